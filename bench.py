@@ -1,0 +1,318 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 quantized-matmul / turbo4 hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+Prints ONE JSON line (rank 0). Workloads (seeded synthetic data):
+  gemv   config 1: Q4_0 x Q8_0 GEMV of the Qwen3-1.7B gate_proj shape (6144 x 2048,
+         W ~ N(0, 0.02) quantized with the reference's Q4_0 rule, x ~ N(0, 1)). One step =
+         quantize x once + one matmul_multi launch over a stack of 72 distinct weight
+         copies (510 MB, > 4x the 126 MB L2, so every step streams from HBM).
+The reference arm (--impl reference) times the reference's CPU algorithm (the oracle
+restatement of RIE's AVX2 path, all host cores) on a bounded sample of the same workload.
+Multi-GPU: one process per GPU; each rank runs its own stack (weak scaling, no collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(name)
+    except Exception:
+        return None
+
+
+class Clocks:
+    """Samples SM clocks / throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in (out or "").splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- workload: config 1 GEMV stack ---------------------------------------------------------
+GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_DISTINCT = 6144, 2048, 72, 8
+
+
+def gemv_weights(seed: int = 1):
+    """GEMV_DISTINCT distinct Q4_0 matrices from N(0, 0.02) with the reference's quantizer."""
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    mats = []
+    for _ in range(GEMV_DISTINCT):
+        wf = rng.normal(0.0, 0.02, (GEMV_ROWS, GEMV_K)).astype(np.float32)
+        mats.append(O.quantize_weight(O.Q4_0, wf))
+    x = rng.standard_normal((1, GEMV_K)).astype(np.float32)
+    return mats, x
+
+
+def gemv_bytes_per_step():
+    w = GEMV_ROWS * GEMV_K // 32 * 18
+    return GEMV_COPIES * (w + GEMV_K * 4 + GEMV_ROWS * 4), w
+
+
+def run_gemv(args, world, rank, local):
+    import torch
+
+    import rust_interference_engine_b200 as rie
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    mats, x = gemv_weights()
+    ws = [rie.Weight.upload(ctx, rie.GgmlType.Q4_0, GEMV_ROWS, GEMV_K, mats[i % GEMV_DISTINCT])
+          for i in range(GEMV_COPIES)]
+    xd = torch.from_numpy(x).cuda()
+    outs = torch.zeros((GEMV_COPIES, GEMV_ROWS), device="cuda")
+    acts = rie.QuantActs(ctx, 1, GEMV_K)
+    jobs = [rie.MatmulJob(w, outs[i], GEMV_ROWS) for i, w in enumerate(ws)]
+
+    def step(ev=None):
+        acts.prepare(xd, 1, GEMV_K, rie.ActFormat.Q8_0)
+        if ev is not None:
+            ev[0].record(stream)
+        rie.matmul_multi(ctx, acts, jobs)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.sync()
+    # parity spot check of the benchmarked output against the oracle
+    import oracle as O
+    want = O.matmul_multi(x, [(O.Q4_0, mats[0], GEMV_K)], n_threads=8)[0][0]
+    got = outs[0].cpu().numpy()
+    max_rel = float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-6))
+
+    kern_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(kern_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = t0.elapsed_time(t1) / args.steps
+    kern_ms = float(np.mean([a.elapsed_time(b) for a, b in kern_ev]))
+    ctx.sync()
+
+    # end to end through the public API with host buffers
+    xh = torch.from_numpy(x).pin_memory()
+    oh = torch.empty((GEMV_COPIES, GEMV_ROWS), pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            barrier(world)
+            torch.cuda.synchronize()
+            e0.record(stream)
+        xd.copy_(xh, non_blocking=True)
+        step()
+        oh.copy_(outs, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    ms = dist_max(ms, world)
+    e2e_ms = dist_max(e2e_ms, world)
+    kern_ms = dist_max(kern_ms, world)
+    step_bytes, w_bytes = gemv_bytes_per_step()
+    peak, peak_kind = peaks()
+    achieved = step_bytes / (kern_ms * 1e-3) / 1e9
+    res = {
+        "metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)",
+        "value": world * step_bytes / (ms * 1e-3) / 1e9,
+        "unit": "GB/s",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)",
+        "config": {"workload": "gemv_q4_0_6144x2048_config1", "rows": GEMV_ROWS, "k": GEMV_K,
+                   "weight_copies_per_step": GEMV_COPIES, "bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2 (510 MB weight stack per step)", "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_0_config1"),
+                     "kernel": "k_gemv<1>", "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
+        "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_COPIES * GEMV_ROWS * 4,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+        "check": {"max_rel_err_vs_oracle": max_rel, "tolerance": 1e-3},
+    }
+    return res
+
+
+def cpu_gemv_sample(seconds: float, threads: int):
+    """The oracle (RIE's AVX2 CPU path restated) on GEMVs of the same workload."""
+    import oracle as O
+    mats, x = gemv_weights()
+    w_bytes = GEMV_ROWS * GEMV_K // 32 * 18
+    per = w_bytes + GEMV_K * 4 + GEMV_ROWS * 4
+    O.matmul_multi(x, [(O.Q4_0, mats[0], GEMV_K)], n_threads=threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.matmul_multi(x, [(O.Q4_0, mats[n % GEMV_DISTINCT], GEMV_K)], n_threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": n * per / el / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "sample": f"{n} GEMVs of 6144x2048 Q4_0 (rotating over {GEMV_DISTINCT} matrices), {el:.1f} s",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
+WORKLOADS = {"gemv": run_gemv}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    world, rank, local = dist_init()
+
+    if args.impl == "reference":
+        if rank == 0:
+            threads = os.cpu_count() or 1
+            samples = []
+            for _ in range(args.warmup):
+                cpu_gemv_sample(0.5, threads)
+            for _ in range(args.steps):
+                samples.append(cpu_gemv_sample(max(args.cpu_seconds / max(args.steps, 1), 0.5), threads))
+            v = float(np.median([s["value"] for s in samples]))
+            cb = dict(samples[0])
+            cb["value"] = v
+            cb["sample"] = f"{args.steps} samples of: " + cb["sample"]
+            print(json.dumps({"impl": "reference", "metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)",
+                              "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+                              "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                              "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "data": "synthetic",
+                              "config": {"workload": "gemv_q4_0_6144x2048_config1"}, "vs_baseline": None,
+                              "cpu_baseline": cb,
+                              "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                  flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    res = WORKLOADS[args.workload](args, world, rank, local)
+    if rank == 0:
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
+                    "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)"})
+        if world == 1:
+            res["cpu_baseline"] = cpu_gemv_sample(args.cpu_seconds, os.cpu_count() or 1)
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

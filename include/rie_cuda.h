@@ -1,0 +1,154 @@
+/*
+ * rie_cuda.h -- C ABI of librie_cuda.so: the B200 (sm_100a) implementation of the Rust
+ * Inference Engine's quantized-matmul + turbo4 KV-cache hot path.
+ *
+ * Conventions follow the reference's C ABI (crates/rie-ffi/include/rie.h:1-78 and
+ * crates/rie-ffi/src/lib.rs:84-157): opaque handles, int32_t status (0 = ok), a
+ * human-readable reason retrievable per context (rcu_last_error) or written into a
+ * caller buffer, no exception or abort ever crosses the boundary, and one context must
+ * not be used from two host threads at once. Device memory handed to the library
+ * (x_dev, out, ...) is plain device pointers; the library never frees caller memory.
+ * All operations are asynchronous on the context's stream; rcu_sync waits for them.
+ *
+ * Each entry point cites the reference interface it replaces (path:line within the
+ * reference project).
+ */
+#ifndef RIE_CUDA_H
+#define RIE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RCU_API __attribute__((visibility("default")))
+#else
+#define RCU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct rcu_ctx rcu_ctx;
+typedef struct rcu_weight rcu_weight;
+typedef struct rcu_acts rcu_acts;
+typedef struct rcu_kv rcu_kv;
+
+enum rcu_status {
+    RCU_OK = 0,
+    RCU_ERR_INVALID = 1,     /* bad argument, shape or handle */
+    RCU_ERR_CUDA = 2,        /* CUDA runtime error (message holds cudaGetErrorString) */
+    RCU_ERR_UNSUPPORTED = 3, /* type/format not implemented on this path */
+    RCU_ERR_OOM = 4,         /* device allocation failed */
+    RCU_ERR_TIMEOUT = 5,     /* a bounded device-side wait expired (see rcu_check_device) */
+    RCU_ERR_RUNTIME = 6      /* reference Error::Runtime (empty batch, context full, ...) */
+};
+
+/* Rounding of the Q8_0 activation quantizer. The reference's SIMD tiers (AVX2
+ * _mm256_cvtps_epi32, NEON vcvtnq_s32_f32: kernels/avx2.rs:173, kernels/neon.rs:478-505)
+ * round half to even; its scalar tier (quant/mod.rs:182, f32::round) rounds half away from
+ * zero. Q8_K quantization is scalar on every tier and always rounds half away. */
+enum rcu_rounding { RCU_ROUND_NEAREST_EVEN = 0, RCU_ROUND_HALF_AWAY = 1 };
+
+/* Activation formats (reference ActFormat, quant/mod.rs:127-132), as bit flags. */
+enum rcu_act_format { RCU_ACT_Q8_0 = 2, RCU_ACT_Q8K = 4 };
+
+/* KV cache formats (reference KvType, model/cpu.rs:12-36). */
+enum rcu_kv_type { RCU_KV_F16 = 0, RCU_KV_Q8_0 = 1, RCU_KV_TURBO4 = 2 };
+
+/* ---- context ------------------------------------------------------------------------ */
+/* Creates a context on `device` issuing work on `stream` (cudaStream_t, NULL = the
+ * legacy default stream). Replaces the CPU backend's thread pool / scratch ownership
+ * (model/cpu.rs:93-177). On failure *out is NULL and err (if non-NULL) holds the reason. */
+RCU_API int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, size_t err_len);
+RCU_API void rcu_ctx_destroy(rcu_ctx *ctx);
+RCU_API int32_t rcu_set_stream(rcu_ctx *ctx, void *stream);
+RCU_API int32_t rcu_set_rounding(rcu_ctx *ctx, int32_t mode);
+/* Last error message of this context ("" if none). Valid until the next call. */
+RCU_API const char *rcu_last_error(const rcu_ctx *ctx);
+/* Waits for all work on the context stream; returns RCU_ERR_TIMEOUT if any bounded
+ * device wait expired since the last check (the bits are then cleared). */
+RCU_API int32_t rcu_sync(rcu_ctx *ctx);
+RCU_API int32_t rcu_check_device(rcu_ctx *ctx, uint32_t *bits_out);
+RCU_API int32_t rcu_version(void);
+
+/* ---- weights (tensor.rs:6-98 Weight) -------------------------------------------------- */
+/* Block layout helpers (quant/mod.rs:69-96). */
+RCU_API uint64_t rcu_row_bytes(uint32_t ggml_type, uint64_t cols);
+/* Copies `rows` rows of raw GGUF block bytes (ggml type id as in gguf: 2 = Q4_0, 12 =
+ * Q4_K, ...) from host memory to the device. No repacking: rows keep the GGUF layout. */
+RCU_API int32_t rcu_weight_upload(rcu_ctx *ctx, uint32_t ggml_type, uint64_t rows, uint64_t cols, const void *host_bytes,
+                          rcu_weight **out);
+/* Zero-copy view of GGUF block bytes already on the device (Weight::from_raw,
+ * tensor.rs:31-35). The base must be 16-byte aligned and rows*row_bytes readable up to
+ * the next multiple of 16. */
+RCU_API int32_t rcu_weight_view(rcu_ctx *ctx, uint32_t ggml_type, uint64_t rows, uint64_t cols, const void *dev_bytes,
+                        rcu_weight **out);
+/* Rows [start, start+n) of w (Weight::slice_rows, tensor.rs:64-69); shares storage. */
+RCU_API int32_t rcu_weight_slice_rows(const rcu_weight *w, uint64_t start, uint64_t n, rcu_weight **out);
+RCU_API void rcu_weight_free(rcu_weight *w);
+RCU_API const void *rcu_weight_device_ptr(const rcu_weight *w);
+
+/* ---- activations (kernels/matmul.rs:19-97 QuantActs) ---------------------------------- */
+RCU_API int32_t rcu_acts_create(rcu_ctx *ctx, uint64_t max_tok, uint64_t max_k, rcu_acts **out);
+RCU_API void rcu_acts_free(rcu_acts *acts);
+/* QuantActs::prepare (matmul.rs:34-71): quantize x_dev (n_tok x k f32, row-major, device)
+ * once into every format in `formats` (RCU_ACT_* bits). Q8_0 follows the context's
+ * rounding mode; Q8_K follows quant/mod.rs:191-218. */
+RCU_API int32_t rcu_acts_prepare(rcu_ctx *ctx, rcu_acts *acts, const float *x_dev, uint64_t n_tok, uint64_t k,
+                         uint32_t formats);
+/* Writes the prepared blocks to host memory in the reference's own block layout
+ * (BlockQ8_0 = 48 bytes: qs[32], f32 d, f32 s; BlockQ8K = 304 bytes: qs[256],
+ * i16 bsums[16], f32 d; quant/mod.rs:139-168). Synchronous. */
+RCU_API int32_t rcu_acts_export(rcu_ctx *ctx, const rcu_acts *acts, uint32_t format, void *host_out);
+
+/* ---- matmul (kernels/matmul.rs:110-176) ----------------------------------------------- */
+typedef struct rcu_job {
+    const rcu_weight *w; /* rows x k weight */
+    float *out;          /* device: out[t * ld + r] = W[r] . X[t] */
+    uint64_t ld;         /* leading dimension (usually w->rows) */
+} rcu_job;
+/* matmul_multi: every job shares the prepared activations and runs in one launch.
+ * Tokens <= 8 use the HBM-streaming GEMV; more tokens use the int8 tensor-core GEMM. */
+RCU_API int32_t rcu_matmul_multi(rcu_ctx *ctx, const rcu_acts *acts, const rcu_job *jobs, uint64_t n_jobs);
+RCU_API int32_t rcu_matmul(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, float *out);
+/* Exact per-block integer sums of weight row `row` with activation row `tok`
+ * (the int32 `s`/`sumi`/`summ` of quant/reference.rs:221-386): one int32 per 32-block
+ * for Q4_0/Q4_1/Q5_0/Q5_1/Q8_0, (sumi, summ) per superblock for Q4_K/Q5_K, sumi per
+ * superblock for Q6_K. out_dev must hold that many int32. */
+RCU_API int32_t rcu_block_sums(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, uint64_t row, uint64_t tok,
+                       int32_t *out_dev);
+
+/* ---- turbo4 (turbo.rs) --------------------------------------------------------------- */
+/* row_bytes_4 (turbo.rs:136-138): f16 scale per rotation block + hd/2 code bytes. */
+RCU_API uint64_t rcu_turbo4_row_bytes(uint64_t hd);
+/* quantize_4 (turbo.rs:167-171) of n_rows rows of hd f32 (device) with the KV_SEED
+ * rotation, written as reference-format rows (scales then Q4_0-order nibbles). */
+RCU_API int32_t rcu_turbo4_quantize(rcu_ctx *ctx, const float *x_dev, uint64_t n_rows, uint64_t hd, uint8_t *rows_dev);
+/* Rotation::apply / apply_inverse (turbo.rs:108-117) of n_rows rows, in place. */
+RCU_API int32_t rcu_turbo4_rotate(rcu_ctx *ctx, float *x_dev, uint64_t n_rows, uint64_t hd, int32_t inverse);
+
+/* ---- KV cache + attention (model/cpu.rs:38-50, 300-328, 550-658) ------------------- */
+/* One layer's cache: n_head_kv heads x `slots` positions of head_dim values, in the given
+ * format. Sliding-window layers pass slots = window + max_batch (cpu.rs:111). */
+RCU_API int32_t rcu_kv_create(rcu_ctx *ctx, int32_t kv_type, uint64_t n_head_kv, uint64_t head_dim, uint64_t slots,
+                      rcu_kv **out);
+RCU_API void rcu_kv_free(rcu_kv *kv);
+/* KV append of n_tok tokens at positions pos0.. (slot = pos % slots): k_dev, v_dev are
+ * n_tok x (n_head_kv*head_dim) f32 on the device (post-RoPE keys). */
+RCU_API int32_t rcu_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k_dev, const float *v_dev, uint64_t n_tok, uint64_t pos0);
+/* Reads/writes the cache as reference-layout rows [kv_head][slot][row] (f16 bits, Q8_0
+ * blocks, or row_bytes_4 turbo rows) for parity checks. Synchronous, host buffers. */
+RCU_API int32_t rcu_kv_export(rcu_ctx *ctx, const rcu_kv *kv, void *k_host, void *v_host);
+RCU_API int32_t rcu_kv_import(rcu_ctx *ctx, rcu_kv *kv, const void *k_host, const void *v_host);
+/* attention() (model/cpu.rs:552-634): causal GQA attention of n_tok queries at positions
+ * pos0.. over the cache; q_dev is n_tok x (n_head*head_dim) f32 (already scaled by
+ * attn_scale), out_dev the same shape. window = 0 means full attention; softcap <= 0
+ * means none. */
+RCU_API int32_t rcu_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q_dev, uint64_t n_tok, uint64_t n_head,
+                      uint64_t pos0, uint64_t window, float softcap, float *out_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RIE_CUDA_H */

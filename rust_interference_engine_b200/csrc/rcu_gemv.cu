@@ -1,0 +1,564 @@
+// rcu_gemv.cu -- decode GEMV: y[t][r] = W[r] . X[t] for up to 8 activation rows, over
+// weights kept in their GGUF block layout (Q4_0/Q4_1/Q5_0/Q5_1/Q8_0 x Q8_0 activations,
+// Q4_K/Q5_K/Q6_K x Q8_K activations). Replaces kernels/matmul.rs:136-241 (matmul_multi,
+// compute_rows) and the vec_dot family of kernels/mod.rs:134-232 for the decode case.
+//
+// Design (HBM-bound; every weight byte is read exactly once per call):
+//   * persistent CTAs, one per SM; each walks a static list of row tiles covering all jobs
+//     of the call (several weights share one launch, like matmul_multi's single region);
+//   * warp 8 is a TMA producer: 1-D bulk copies (cp.async.bulk) stream whole row tiles
+//     (contiguous GGUF bytes) into a ring of shared-memory stages, completion counted on
+//     mbarriers, L2 evict-first;
+//   * warps 0..7 consume: the quantized activations of the call sit in shared memory;
+//     each lane unpacks GGUF blocks from the stage with word loads + funnel shifts and
+//     forms the exact per-block int32 sums with dp4a, then combines in f32 like the
+//     reference (d_w * d_a * s [+ m_w * s_a]); warp shuffles reduce each row.
+//   * large rows are split over 2/4/8 warps; the last warp to finish combines the
+//     partials in a fixed order (deterministic, no block-wide barrier inside the loop).
+//   * every wait is bounded (2 s) and reports through the context's device error word.
+#include <algorithm>
+
+#include "rcu_blocks.cuh"
+#include "rcu_kernels.h"
+
+namespace rcu {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxJobs = 96;
+constexpr int kMaxTok = 8;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kHdrBytes = 4096;  // barriers + reduction scratch
+
+struct GemvJobDev {
+    const uint8_t *w;
+    float *out;
+    uint64_t ld;
+    uint32_t rows, row_bytes;
+    int32_t type;
+    uint32_t rows_per_tile, tile_begin, wpr, rw;
+};
+
+struct GemvParams {
+    GemvJobDev jobs[kMaxJobs];
+    int32_t n_jobs;
+    uint32_t total_tiles, stages, stage_bytes, stage_off;
+    uint32_t k, n_tok, tok0, formats;
+    // shared-memory offsets of the staged activations
+    uint32_t o_q0, o_d0, o_s0, o_sum0, o_qk, o_dk, o_bsk;
+    ActsView acts;
+    uint32_t *err;
+};
+
+struct SmemHdr {
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
+    int cnt[kMaxStages][8];
+    float red[kMaxStages][8][kMaxTok];  // [stage][row in tile * wpr + part][token]
+};
+static_assert(sizeof(SmemHdr) <= kHdrBytes, "header too large");
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Publish one warp's finished row sums v[t] (valid in every lane). With wpr > 1 the last
+// of the row's warps to arrive adds the parts in order 0..wpr-1 and stores the row.
+template <int T>
+__device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb, uint32_t row, int row_in_tile,
+                                         int part, const float (&v)[T], int lane) {
+    if (jb.wpr == 1) {
+        if (lane < T) {
+            float x = v[0];
+#pragma unroll
+            for (int t = 1; t < T; t++)
+                if (lane == t) x = v[t];
+            jb.out[(uint64_t)lane * jb.ld + row] = x;
+        }
+        return;
+    }
+    if (lane < T) {
+        float x = v[0];
+#pragma unroll
+        for (int t = 1; t < T; t++)
+            if (lane == t) x = v[t];
+        h->red[s][row_in_tile * jb.wpr + part][lane] = x;
+    }
+    __syncwarp();
+    __threadfence_block();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(&h->cnt[s][row_in_tile], 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == (int)jb.wpr - 1) {
+        __threadfence_block();
+        if (lane < T) {
+            float acc = 0.0f;
+            for (uint32_t q = 0; q < jb.wpr; q++) acc += *((volatile float *)&h->red[s][row_in_tile * jb.wpr + q][lane]);
+            jb.out[(uint64_t)lane * jb.ld + row] = acc;
+        }
+        __syncwarp();
+        if (lane == 0) h->cnt[s][row_in_tile] = 0;
+    }
+}
+
+// ---- 32-value block types ---------------------------------------------------------------
+template <int TYPE, int T>
+__device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
+                                       uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
+    constexpr uint32_t BB = blk_bytes_c<TYPE>();
+    const uint32_t nb = p.k / QK;
+    uint32_t row_first, nr, b_begin, b_end;
+    int part = 0;
+    if (jb.wpr == 1) {
+        row_first = warp * jb.rw;
+        nr = jb.rw;
+        b_begin = 0;
+        b_end = nb;
+    } else {
+        row_first = warp / jb.wpr;
+        part = warp % jb.wpr;
+        nr = 1;
+        b_begin = part * nb / jb.wpr;
+        b_end = (part + 1) * nb / jb.wpr;
+    }
+    if (row_first >= nrows) return;
+    if (row_first + nr > nrows) nr = nrows - row_first;
+    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_q0);
+    const float *ad = reinterpret_cast<const float *>(sm + p.o_d0);
+    const float *as = reinterpret_cast<const float *>(sm + p.o_s0);
+    const int32_t *asm_ = reinterpret_cast<const int32_t *>(sm + p.o_sum0);
+    float acc[4][T];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int t = 0; t < T; t++) acc[r][t] = 0.0f;
+    for (uint32_t b = b_begin + lane; b < b_end; b += 32) {
+        uint32_t a[T][8];
+        int asum[T];
+        float da[T], sa[T];
+#pragma unroll
+        for (int t = 0; t < T; t++) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(aq + (size_t)t * p.k + (size_t)b * QK);
+            const uint4 x0 = src[0], x1 = src[1];
+            a[t][0] = x0.x, a[t][1] = x0.y, a[t][2] = x0.z, a[t][3] = x0.w;
+            a[t][4] = x1.x, a[t][5] = x1.y, a[t][6] = x1.z, a[t][7] = x1.w;
+            asum[t] = asm_[t * nb + b];
+            da[t] = ad[t * nb + b];
+            sa[t] = as[t * nb + b];
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            if ((uint32_t)r < nr) {
+                BlkW w;
+                dec_blk<TYPE>(wsm, (row_first + r) * jb.row_bytes + b * BB, w);
+#pragma unroll
+                for (int t = 0; t < T; t++) {
+                    const int si = blk_int<TYPE>(w, a[t], asum[t]);
+                    float c = (w.d * da[t]) * (float)si;  // f16(d) * ab.d * s
+                    if (TYPE == T_Q4_1 || TYPE == T_Q5_1) c += w.m * sa[t];
+                    acc[r][t] += c;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        if ((uint32_t)r < nr) {
+            float v[T];
+#pragma unroll
+            for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
+            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
+        }
+    }
+}
+
+// ---- 256-value superblock types: 4 groups of 8 lanes per warp ----------------------------
+template <int TYPE, int T>
+__device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
+                                       uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
+    constexpr uint32_t BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
+    const uint32_t nsb = p.k / QK_K;
+    uint32_t row_first, nr, b_begin, b_end;
+    int part = 0;
+    if (jb.wpr == 1) {
+        row_first = warp * jb.rw;
+        nr = jb.rw;
+        b_begin = 0;
+        b_end = nsb;
+    } else {
+        row_first = warp / jb.wpr;
+        part = warp % jb.wpr;
+        nr = 1;
+        b_begin = part * nsb / jb.wpr;
+        b_end = (part + 1) * nsb / jb.wpr;
+    }
+    if (row_first >= nrows) return;
+    if (row_first + nr > nrows) nr = nrows - row_first;
+    const int g = lane >> 3, sub = lane & 7;
+    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_qk);
+    const float *adk = reinterpret_cast<const float *>(sm + p.o_dk);
+    const int16_t *abs_ = reinterpret_cast<const int16_t *>(sm + p.o_bsk);
+    float acc[4][T];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int t = 0; t < T; t++) acc[r][t] = 0.0f;
+    for (uint32_t sb = b_begin + g; sb < b_end; sb += 4) {
+        if (TYPE == T_Q6_K) {
+            SbAct6 a[T];
+            const int n = sub >> 2, lq = sub & 3;
+#pragma unroll
+            for (int t = 0; t < T; t++) {
+                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + 128 * n + 8 * lq;
+#pragma unroll
+                for (int k = 0; k < 4; k++) a[t].a[k] = *reinterpret_cast<const uint2 *>(base + 32 * k);
+                a[t].d = adk[t * nsb + sb];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                if ((uint32_t)r < nr) {
+                    SbW6 w;
+                    dec_sb_q6k(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+#pragma unroll
+                    for (int t = 0; t < T; t++) {
+                        int sumi = dot_sb_q6k(w, a[t]);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 4);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 2);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
+                        if (sub == 0) acc[r][t] += (w.d * a[t].d) * (float)sumi;
+                    }
+                }
+            }
+        } else {
+            SbAct a[T];
+            const int j = sub >> 1, hh = sub & 1;
+#pragma unroll
+            for (int t = 0; t < T; t++) {
+                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K;
+                a[t].lo = *reinterpret_cast<const uint4 *>(base + 64 * j + 16 * hh);
+                a[t].hi = *reinterpret_cast<const uint4 *>(base + 64 * j + 32 + 16 * hh);
+                a[t].bs2 = *reinterpret_cast<const uint32_t *>(abs_ + (size_t)t * (p.k / 16) + 16 * sb + 2 * sub);
+                a[t].d = adk[t * nsb + sb];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                if ((uint32_t)r < nr) {
+                    SbW w;
+                    dec_sb_k<TYPE>(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+#pragma unroll
+                    for (int t = 0; t < T; t++) {
+                        int summ;
+                        int sumi = dot_sb_k(w, a[t], summ);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 4);
+                        summ += __shfl_xor_sync(0xffffffffu, summ, 4);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 2);
+                        summ += __shfl_xor_sync(0xffffffffu, summ, 2);
+                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
+                        summ += __shfl_xor_sync(0xffffffffu, summ, 1);
+                        // d * sumi - dmin * summ with d = f16(d)*ab.d, dmin = f16(dmin)*ab.d
+                        if (sub == 0) acc[r][t] += (w.d * a[t].d) * (float)sumi - (w.dmin * a[t].d) * (float)summ;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        if ((uint32_t)r < nr) {
+            float v[T];
+#pragma unroll
+            for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
+            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
+        }
+    }
+}
+
+__device__ __forceinline__ int find_job(const GemvParams &p, uint32_t tile) {
+    int lo = 0, hi = p.n_jobs - 1;  // last job whose first tile is <= tile
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.jobs[mid].tile_begin <= tile)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+template <int T>
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    SmemHdr *h = reinterpret_cast<SmemHdr *>(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t S = p.stages;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < S; s++) {
+            mbar_init(&h->full[s], 1);
+            mbar_init(&h->empty[s], kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    for (uint32_t i = threadIdx.x; i < kMaxStages * 8; i += blockDim.x) (&h->cnt[0][0])[i] = 0;
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {  // ---- producer ----
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            uint32_t li = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
+                const uint32_t s = li % S;
+                if (li >= S && !mbar_wait_bounded(&h->empty[s], ((li / S) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                const GemvJobDev &jb = p.jobs[find_job(p, tile)];
+                const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
+                const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
+                const uint32_t bytes = (nrows * jb.row_bytes + 15u) & ~15u;
+                uint8_t *dst = smem + p.stage_off + s * p.stage_bytes;
+                mbar_arrive_expect_tx(&h->full[s], bytes);
+                bulk_g2s(dst, jb.w + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s], pol);
+            }
+            // never leave the CTA with copies in flight: wait for the last phase of each stage
+            const uint32_t issued = li;
+            for (uint32_t s = 0; s < S && s < issued; s++) {
+                const uint32_t last = ((issued - 1 - s) / S) * S + s;  // last li with li % S == s
+                mbar_wait_bounded(&h->full[s], (last / S) & 1, p.err, ERR_TIMEOUT_DRAIN);
+            }
+            (void)ok;
+        }
+        return;
+    }
+
+    // ---- consumers: stage this call's quantized activations -------------------------------
+    {
+        const uint32_t nt = p.n_tok, k = p.k, tid = threadIdx.x, nthr = kConsumerWarps * 32;
+        const ActsView &A = p.acts;
+        if (p.formats & RCU_ACT_Q8_0) {
+            const uint32_t nb = k / QK;
+            const uint4 *src = reinterpret_cast<const uint4 *>(A.q0 + (size_t)p.tok0 * k);
+            uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_q0);
+            for (uint32_t i = tid; i < nt * k / 16; i += nthr) dst[i] = src[i];
+            for (uint32_t i = tid; i < nt * nb; i += nthr) {
+                reinterpret_cast<float *>(smem + p.o_d0)[i] = A.d0[(size_t)p.tok0 * nb + i];
+                reinterpret_cast<float *>(smem + p.o_s0)[i] = A.s0[(size_t)p.tok0 * nb + i];
+                reinterpret_cast<int32_t *>(smem + p.o_sum0)[i] = A.sum0[(size_t)p.tok0 * nb + i];
+            }
+        }
+        if (p.formats & RCU_ACT_Q8K) {
+            const uint32_t nsb = k / QK_K;
+            const uint4 *src = reinterpret_cast<const uint4 *>(A.qk + (size_t)p.tok0 * k);
+            uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_qk);
+            for (uint32_t i = tid; i < nt * k / 16; i += nthr) dst[i] = src[i];
+            for (uint32_t i = tid; i < nt * nsb; i += nthr)
+                reinterpret_cast<float *>(smem + p.o_dk)[i] = A.dk[(size_t)p.tok0 * nsb + i];
+            for (uint32_t i = tid; i < nt * k / 16; i += nthr)
+                reinterpret_cast<int16_t *>(smem + p.o_bsk)[i] = A.bsk[(size_t)p.tok0 * (k / 16) + i];
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+    }
+
+    uint32_t li = 0;
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
+        const uint32_t s = li % S;
+        if (!mbar_wait_bounded(&h->full[s], (li / S) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+        const GemvJobDev &jb = p.jobs[find_job(p, tile)];
+        const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
+        const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
+        const uint8_t *wsm = smem + p.stage_off + s * p.stage_bytes;
+        switch (jb.type) {
+            case T_Q4_0: tile_q<T_Q4_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q4_1: tile_q<T_Q4_1, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_0: tile_q<T_Q5_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_1: tile_q<T_Q5_1, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q8_0: tile_q<T_Q8_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q4_K: tile_k<T_Q4_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_K: tile_k<T_Q5_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q6_K: tile_k<T_Q6_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            default: break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&h->empty[s]);
+    }
+}
+
+// ---- exact per-block integer sums of one (row, token) pair (validation path) ----------
+__global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ wrow, uint32_t row_bytes, int type,
+                                                  ActsView A, uint32_t tok, int32_t *__restrict__ out) {
+    extern __shared__ __align__(16) uint8_t srow[];
+    const int lane = threadIdx.x;
+    for (uint32_t i = lane; i < row_bytes; i += 32) srow[i] = wrow[i];
+    if (lane < 16) srow[row_bytes + lane] = 0;
+    __syncwarp();
+    const uint32_t k = A.k;
+    if (block_size(type) == QK) {
+        const uint32_t nb = k / QK;
+        const int8_t *aq = A.q0 + (size_t)tok * k;
+        for (uint32_t b = lane; b < nb; b += 32) {
+            uint32_t a[8];
+            const uint4 x0 = reinterpret_cast<const uint4 *>(aq + b * QK)[0];
+            const uint4 x1 = reinterpret_cast<const uint4 *>(aq + b * QK)[1];
+            a[0] = x0.x, a[1] = x0.y, a[2] = x0.z, a[3] = x0.w, a[4] = x1.x, a[5] = x1.y, a[6] = x1.z, a[7] = x1.w;
+            const int asum = A.sum0[(size_t)tok * nb + b];
+            BlkW w;
+            int s = 0;
+            switch (type) {
+                case T_Q4_0: dec_blk<T_Q4_0>(srow, b * 18, w); s = blk_int<T_Q4_0>(w, a, asum); break;
+                case T_Q4_1: dec_blk<T_Q4_1>(srow, b * 20, w); s = blk_int<T_Q4_1>(w, a, asum); break;
+                case T_Q5_0: dec_blk<T_Q5_0>(srow, b * 22, w); s = blk_int<T_Q5_0>(w, a, asum); break;
+                case T_Q5_1: dec_blk<T_Q5_1>(srow, b * 24, w); s = blk_int<T_Q5_1>(w, a, asum); break;
+                case T_Q8_0: dec_blk<T_Q8_0>(srow, b * 34, w); s = blk_int<T_Q8_0>(w, a, asum); break;
+            }
+            out[b] = s;
+        }
+        return;
+    }
+    const uint32_t nsb = k / QK_K;
+    const int g = lane >> 3, sub = lane & 7;
+    const int8_t *aq = A.qk + (size_t)tok * k;
+    for (uint32_t sb = g; sb < nsb; sb += 4) {
+        int sumi = 0, summ = 0;
+        if (type == T_Q6_K) {
+            SbAct6 a;
+            const int n = sub >> 2, lq = sub & 3;
+            for (int kk = 0; kk < 4; kk++)
+                a.a[kk] = *reinterpret_cast<const uint2 *>(aq + (size_t)sb * QK_K + 128 * n + 8 * lq + 32 * kk);
+            SbW6 w;
+            dec_sb_q6k(srow, sb * 210, sub, w);
+            sumi = dot_sb_q6k(w, a);
+        } else {
+            SbAct a;
+            const int j = sub >> 1, hh = sub & 1;
+            a.lo = *reinterpret_cast<const uint4 *>(aq + (size_t)sb * QK_K + 64 * j + 16 * hh);
+            a.hi = *reinterpret_cast<const uint4 *>(aq + (size_t)sb * QK_K + 64 * j + 32 + 16 * hh);
+            a.bs2 = *reinterpret_cast<const uint32_t *>(A.bsk + (size_t)tok * (k / 16) + 16 * sb + 2 * sub);
+            SbW w;
+            if (type == T_Q4_K) {
+                dec_sb_k<T_Q4_K>(srow, sb * 144, sub, w);
+            } else {
+                dec_sb_k<T_Q5_K>(srow, sb * 176, sub, w);
+            }
+            sumi = dot_sb_k(w, a, summ);
+        }
+        for (int o = 4; o; o >>= 1) {
+            sumi += __shfl_xor_sync(0xffffffffu, sumi, o);
+            summ += __shfl_xor_sync(0xffffffffu, summ, o);
+        }
+        if (sub == 0) {
+            if (type == T_Q6_K) {
+                out[sb] = sumi;
+            } else {
+                out[2 * sb] = sumi;
+                out[2 * sb + 1] = summ;
+            }
+        }
+    }
+}
+
+int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint64_t row, uint64_t tok,
+                      int32_t *out) {
+    const uint32_t rb = (uint32_t)w->row_bytes;
+    const uint32_t smem = (rb + 16 + 15) & ~15u;
+    if (smem > 48 * 1024) return set_err(ctx, RCU_ERR_UNSUPPORTED, "block_sums: row too long");
+    k_block_sums<<<1, 32, smem, ctx->stream>>>(w->data + row * w->row_bytes, rb, w->type, a, (uint32_t)tok, out);
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
+    return RCU_OK;
+}
+
+// ---- host side -------------------------------------------------------------------------
+static uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
+
+template <int T>
+static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t grid) {
+    static bool attr_set[64] = {};
+    if (!attr_set[ctx->device & 63]) {
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)ctx->max_smem_optin));
+        attr_set[ctx->device & 63] = true;
+    }
+    k_gemv<T><<<grid, kGemvThreads, smem_bytes, ctx->stream>>>(p);
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
+    return RCU_OK;
+}
+
+int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok) {
+    if (n_jobs < 1 || n_jobs > kMaxJobs) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..96 jobs per launch");
+    if (n_tok < 1 || n_tok > kMaxTok) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..8 tokens per launch");
+    GemvParams p{};
+    p.n_jobs = n_jobs;
+    p.k = a.k;
+    p.n_tok = n_tok;
+    p.tok0 = tok0;
+    p.acts = a;
+    p.err = ctx->dev_err;
+    uint32_t tiles = 0, stage_bytes = 0;
+    for (int i = 0; i < n_jobs; i++) {
+        const rcu_weight *w = jobs[i].w;
+        GemvJobDev &jd = p.jobs[i];
+        jd.w = w->data;
+        jd.out = jobs[i].out + (uint64_t)tok0 * jobs[i].ld;
+        jd.ld = jobs[i].ld;
+        jd.rows = (uint32_t)w->rows;
+        jd.row_bytes = (uint32_t)w->row_bytes;
+        jd.type = w->type;
+        p.formats |= act_format(w->type);
+        const uint32_t rb = jd.row_bytes, target = 40u * 1024u;
+        if (8 * rb <= target) {
+            jd.wpr = 1;
+            jd.rw = std::max(1u, std::min(4u, target / (8 * rb)));
+            jd.rows_per_tile = 8 * jd.rw;
+        } else {
+            jd.wpr = 2;
+            while (jd.wpr < 8 && (8 / jd.wpr) * rb > target) jd.wpr *= 2;
+            jd.rw = 1;
+            jd.rows_per_tile = 8 / jd.wpr;
+            const uint32_t units = w->cols / block_size(w->type);
+            if ((jd.rows_per_tile * rb) % 16 != 0 || units < jd.wpr) {
+                jd.wpr = 1;
+                jd.rows_per_tile = 8;
+            }
+        }
+        jd.tile_begin = tiles;
+        tiles += (jd.rows + jd.rows_per_tile - 1) / jd.rows_per_tile;
+        stage_bytes = std::max(stage_bytes, round_up(jd.rows_per_tile * rb, 16) + 16);
+    }
+    p.total_tiles = tiles;
+    p.stage_bytes = stage_bytes;
+    // activations staged in shared memory
+    uint32_t off = kHdrBytes;
+    const uint32_t k = a.k;
+    if (p.formats & RCU_ACT_Q8_0) {
+        const uint32_t nb = k / QK;
+        p.o_q0 = off; off = round_up(off + n_tok * k, 16);
+        p.o_d0 = off; off = round_up(off + n_tok * nb * 4, 16);
+        p.o_s0 = off; off = round_up(off + n_tok * nb * 4, 16);
+        p.o_sum0 = off; off = round_up(off + n_tok * nb * 4, 16);
+    }
+    if (p.formats & RCU_ACT_Q8K) {
+        p.o_qk = off; off = round_up(off + n_tok * k, 16);
+        p.o_dk = off; off = round_up(off + n_tok * (k / QK_K) * 4, 16);
+        p.o_bsk = off; off = round_up(off + n_tok * (k / 16) * 2, 16);
+    }
+    p.stage_off = round_up(off, 128);
+    const uint32_t budget = (uint32_t)ctx->max_smem_optin;
+    if (p.stage_off + 2 * stage_bytes > budget)
+        return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation batch + two weight stages exceed shared memory");
+    p.stages = std::min<uint32_t>(kMaxStages, (budget - p.stage_off) / stage_bytes);
+    const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
+    const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
+    switch (n_tok) {
+        case 1: return launch_t<1>(ctx, p, smem_bytes, grid);
+        case 2: return launch_t<2>(ctx, p, smem_bytes, grid);
+        case 3: return launch_t<3>(ctx, p, smem_bytes, grid);
+        case 4: return launch_t<4>(ctx, p, smem_bytes, grid);
+        case 5: return launch_t<5>(ctx, p, smem_bytes, grid);
+        case 6: return launch_t<6>(ctx, p, smem_bytes, grid);
+        case 7: return launch_t<7>(ctx, p, smem_bytes, grid);
+        default: return launch_t<8>(ctx, p, smem_bytes, grid);
+    }
+}
+
+}  // namespace rcu

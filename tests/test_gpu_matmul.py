@@ -1,0 +1,170 @@
+"""GPU parity of the quantized matmul path against the CPU oracle (through the C ABI).
+
+Contract (north star): Q8_0/Q8_K activation codes and scales bit-exact, per-block int32
+dot sums bit-exact, f32 outputs within 1e-3 relative error (measured like the reference's
+assert_close: |a - b| <= rtol * max|b|, tests/common/mod.rs:25-31).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    import rust_interference_engine_b200 as rie
+    ctx = rie.Context(0, torch.cuda.current_stream())
+    return torch, rie, ctx
+
+
+def close(a, b, rtol=RTOL):
+    scale = max(float(np.max(np.abs(b))), 1e-6)
+    err = float(np.max(np.abs(a - b)))
+    assert err <= rtol * scale, f"max err {err} > {rtol} * {scale}"
+
+
+def gpu_matmul(env, weights, x, rounding=None):
+    """weights: list of (type, uint8 [rows, row_bytes], cols). Returns list of outputs."""
+    torch, rie, ctx = env
+    if rounding is not None:
+        ctx.set_rounding(rounding)
+    n_tok, k = x.shape
+    xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    ws = [rie.Weight.upload(ctx, rie.GgmlType(t), w.shape[0], cols, w) for (t, w, cols) in weights]
+    acts = rie.QuantActs(ctx, n_tok, k)
+    acts.prepare(xd, n_tok, k, rie.formats_for(ws))
+    outs = [torch.full((n_tok, w.rows), float("nan"), device="cuda") for w in ws]
+    rie.matmul_multi(ctx, acts, [rie.MatmulJob(w, o, w.rows) for w, o in zip(ws, outs)])
+    ctx.sync()
+    if rounding is not None:
+        ctx.set_rounding(rie.Rounding.NEAREST_EVEN)
+    return [o.cpu().numpy() for o in outs], acts, ws
+
+
+@pytest.mark.parametrize("rounding", [0, 1])
+def test_q8_0_activation_codes_bit_exact(env, rounding):
+    torch, rie, ctx = env
+    rng = np.random.default_rng(10 + rounding)
+    x = rng.standard_normal((5, 4096)).astype(np.float32)
+    x[0, :32] = 0.0
+    x[1, :64] *= 1e-30
+    x[2, 32:64] = np.arange(32, dtype=np.float32) - 16.0  # ties after scaling
+    ctx.set_rounding(rounding)
+    acts = rie.QuantActs(ctx, 5, 4096)
+    acts.prepare(torch.from_numpy(x).cuda(), 5, 4096, rie.ActFormat.Q8_0)
+    got = acts.export(rie.ActFormat.Q8_0).view(O.BLOCK_Q8_0)
+    ctx.set_rounding(0)
+    want = O.quantize_row_q8_0(x, O.PATH_AVX2 if rounding == 0 else O.PATH_SCALAR).reshape(-1)
+    np.testing.assert_array_equal(got["qs"], want["qs"])
+    np.testing.assert_array_equal(got["d"].view(np.uint32), want["d"].view(np.uint32))
+    np.testing.assert_array_equal(got["s"].view(np.uint32), want["s"].view(np.uint32))
+
+
+def test_q8_k_activation_codes_bit_exact(env):
+    torch, rie, ctx = env
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((4, 4096)).astype(np.float32) * 3
+    x[0, :256] = 0.0
+    x[1, 10], x[1, 20] = 5.0, -5.0  # equal magnitude: the first one wins
+    acts = rie.QuantActs(ctx, 4, 4096)
+    acts.prepare(torch.from_numpy(x).cuda(), 4, 4096, rie.ActFormat.Q8K)
+    got = acts.export(rie.ActFormat.Q8K).view(O.BLOCK_Q8K)
+    want = O.quantize_row_q8_k(x).reshape(-1)
+    np.testing.assert_array_equal(got["qs"], want["qs"])
+    np.testing.assert_array_equal(got["bsums"], want["bsums"])
+    np.testing.assert_array_equal(got["d"].view(np.uint32), want["d"].view(np.uint32))
+
+
+TYPES = [O.Q4_0, O.Q4_1, O.Q5_0, O.Q5_1, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K]
+
+
+@pytest.mark.parametrize("t", TYPES, ids=[O.TYPE_NAMES[t] for t in TYPES])
+def test_block_sums_bit_exact(env, t):
+    torch, rie, ctx = env
+    rng = O.Rng(100 + t)
+    k = 2048
+    w = rng.weight(t, 4, k)
+    x = rng.vec(3 * k, 2.0).reshape(3, k)
+    _, acts, ws = gpu_matmul(env, [(t, w, k)], x)
+    a = O.quantize_acts(t, x, O.PATH_AVX2)
+    n = 2 * (k // 256) if t in (O.Q4_K, O.Q5_K) else k // O.block_size(t)
+    for row in range(4):
+        for tok in range(3):
+            out = torch.zeros(n, dtype=torch.int32, device="cuda")
+            rie.block_sums(ctx, acts, ws[0], row, tok, out)
+            want = O.block_sums(t, w[row], a[tok], k)
+            np.testing.assert_array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("t", TYPES, ids=[O.TYPE_NAMES[t] for t in TYPES])
+@pytest.mark.parametrize("n_tok", [1, 2, 3, 4, 7, 8, 13])
+def test_matmul_matches_oracle(env, t, n_tok):
+    # tests/kernels.rs:144-185 shapes (200 rows x 512) and decode shapes
+    rng = O.Rng(42 + t)
+    for rows, k in ((200, 512), (333, 4096)):
+        w = rng.weight(t, rows, k)
+        x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+        got = gpu_matmul(env, [(t, w, k)], x)[0][0]
+        want = O.matmul_multi(x, [(t, w, k)], n_threads=4)[0]
+        close(got, want)
+
+
+def test_matmul_multi_mixed_types(env):
+    rng = O.Rng(7)
+    k = 4096
+    specs = [(O.Q4_K, 96), (O.Q6_K, 64), (O.Q8_0, 40), (O.Q4_0, 100), (O.Q5_K, 17)]
+    weights = [(t, rng.weight(t, r, k), k) for t, r in specs]
+    for n_tok in (1, 3):
+        x = rng.vec(n_tok * k, 1.5).reshape(n_tok, k)
+        got, _, _ = gpu_matmul(env, weights, x)
+        want = O.matmul_multi(x, weights, n_threads=4)
+        for g, w_ in zip(got, want):
+            close(g, w_)
+
+
+@pytest.mark.parametrize("t,k", [(O.Q6_K, 12288), (O.Q4_K, 12288), (O.Q8_0, 14336), (O.Q4_0, 768), (O.Q6_K, 768)])
+def test_long_and_ragged_rows(env, t, k):
+    # long rows are split over several warps; 768-wide Q6_K rows are not 16-byte multiples
+    rng = O.Rng(3 + k)
+    w = rng.weight(t, 41, k)
+    x = rng.vec(2 * k, 1.0).reshape(2, k)
+    got = gpu_matmul(env, [(t, w, k)], x)[0][0]
+    want = O.matmul_multi(x, [(t, w, k)], n_threads=4)[0]
+    close(got, want)
+
+
+def test_config1_gemv_shape(env):
+    # W 6144x2048 ~ N(0, 0.02) -> Q4_0 (quant/mod.rs:279-298), x ~ N(0, 1)
+    rng = np.random.default_rng(1)
+    wf = rng.normal(0.0, 0.02, (6144, 2048)).astype(np.float32)
+    w = O.quantize_weight(O.Q4_0, wf)
+    x = rng.standard_normal((1, 2048)).astype(np.float32)
+    got = gpu_matmul(env, [(O.Q4_0, w, 2048)], x)[0][0]
+    want = O.matmul_multi(x, [(O.Q4_0, w, 2048)], n_threads=8)[0]
+    close(got, want)
+    # and against float math on the dequantized operands
+    ref = O.dequantize(O.Q4_0, w, 2048).astype(np.float64) @ O.dequantize_q8(O.quantize_row_q8_0(x))[0].astype(np.float64)
+    close(got[0], ref.astype(np.float32))
+
+
+def test_errors_are_reported(env):
+    torch, rie, ctx = env
+    rng = O.Rng(1)
+    w = rie.Weight.upload(ctx, rie.GgmlType.Q4_0, 8, 512, rng.weight(O.Q4_0, 8, 512))
+    acts = rie.QuantActs(ctx, 2, 1024)
+    x = torch.zeros(2, 1024, device="cuda")
+    acts.prepare(x, 2, 1024, rie.ActFormat.Q8_0)
+    out = torch.zeros(2, 8, device="cuda")
+    with pytest.raises(rie.RcuError, match="inner dimension"):
+        rie.matmul(ctx, acts, w, out)
+    with pytest.raises(rie.RcuError, match="empty batch"):
+        acts.prepare(x, 0, 1024, rie.ActFormat.Q8_0)
+    with pytest.raises(rie.RcuError, match="multiple of 256"):
+        acts.prepare(x, 1, 992, rie.ActFormat.Q8K)
+    with pytest.raises(rie.RcuError):
+        rie.Weight.upload(ctx, rie.GgmlType.Q4_K, 2, 100, np.zeros(0, np.uint8))
+    assert ctx.device_error_bits() == 0

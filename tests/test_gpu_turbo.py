@@ -1,0 +1,138 @@
+"""GPU parity of the turbo4 / KV-cache path against the CPU oracle (through the C ABI).
+
+Encoding (rotation + 4-bit codes + f16 scales) and the f16 / Q8_0 KV stores are
+bit-exact; attention outputs are within 2e-3 (turbo4, north star) or 1e-3 (f16, Q8_0)
+of the oracle, relative to the largest output magnitude.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    import rust_interference_engine_b200 as rie
+    ctx = rie.Context(0, torch.cuda.current_stream())
+    return torch, rie, ctx
+
+
+def close(a, b, rtol):
+    scale = max(float(np.max(np.abs(b))), 1e-6)
+    err = float(np.max(np.abs(a - b)))
+    assert err <= rtol * scale, f"max err {err} > {rtol} * {scale}"
+
+
+@pytest.mark.parametrize("hd", [64, 96, 128, 256, 512])
+def test_rotation_bit_exact(env, hd):
+    torch, rie, ctx = env
+    x = np.random.default_rng(hd).standard_normal((9, hd)).astype(np.float32)
+    for inverse in (False, True):
+        xd = torch.from_numpy(x).cuda()
+        rie.turbo.rotate(ctx, xd, 9, hd, inverse)
+        ctx.sync()
+        want = O.rotate(x, inverse=inverse)
+        np.testing.assert_array_equal(xd.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("hd", [64, 96, 128, 256])
+def test_turbo4_encode_bit_exact(env, hd):
+    torch, rie, ctx = env
+    rng = np.random.default_rng(7 + hd)
+    x = rng.standard_normal((300, hd)).astype(np.float32)
+    x[0] = 0.0                      # zero row: rms 0, scale 0
+    x[1, 5], x[1, 77 % hd] = 20.0, -9.0  # outlier channels (turbo.rs:540-541)
+    x[2] *= 1e-20
+    out = torch.zeros((300, rie.turbo.row_bytes_4(hd)), dtype=torch.uint8, device="cuda")
+    rie.turbo.quantize_4(ctx, torch.from_numpy(x).cuda(), 300, hd, out)
+    ctx.sync()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.turbo_quantize_4(x))
+
+
+@pytest.mark.parametrize("kv_type", [O.KV_F16, O.KV_Q8_0, O.KV_TURBO4], ids=["f16", "q8_0", "turbo4"])
+def test_kv_store_bit_exact(env, kv_type):
+    torch, rie, ctx = env
+    n_kv, hd, slots = 2, 128, 16
+    cache = rie.LayerCache(ctx, rie.KvType(kv_type), n_kv, hd, slots)
+    rng = np.random.default_rng(3)
+    k = rng.standard_normal((5, n_kv * hd)).astype(np.float32) * 2
+    v = rng.standard_normal((5, n_kv * hd)).astype(np.float32)
+    cache.store(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), 5, 14)  # wraps the ring
+    ctx.sync()
+    gk, gv = cache.export()
+    rb = O.kv_row_bytes(kv_type, hd)
+    wk = np.zeros((n_kv * slots, rb), np.uint8)
+    wv = np.zeros_like(wk)
+    for t in range(5):
+        slot = (14 + t) % slots
+        for h in range(n_kv):
+            wk[h * slots + slot] = O.kv_store(kv_type, k[t, h * hd:(h + 1) * hd], O.PATH_SCALAR if kv_type == O.KV_Q8_0 else None)
+            wv[h * slots + slot] = O.kv_store(kv_type, v[t, h * hd:(h + 1) * hd], O.PATH_SCALAR if kv_type == O.KV_Q8_0 else None)
+    np.testing.assert_array_equal(gk, wk)
+    np.testing.assert_array_equal(gv, wv)
+
+
+def _attn_case(env, kv_type, n_head, n_kv, hd, slots, n_tok, pos0, window=0, softcap=0.0, seed=0):
+    torch, rie, ctx = env
+    rng = np.random.default_rng(seed)
+    rb = O.kv_row_bytes(kv_type, hd)
+    kf = rng.standard_normal((n_kv * slots, hd)).astype(np.float32)
+    vf = rng.standard_normal((n_kv * slots, hd)).astype(np.float32)
+    kc = O.kv_store(kv_type, kf)
+    vc = O.kv_store(kv_type, vf)
+    cache = rie.LayerCache(ctx, rie.KvType(kv_type), n_kv, hd, slots)
+    cache.import_(kc, vc)
+    q = (rng.standard_normal((n_tok, n_head * hd)) / np.sqrt(hd)).astype(np.float32)
+    out = torch.zeros((n_tok, n_head * hd), device="cuda")
+    rie.attention(ctx, cache, torch.from_numpy(q).cuda(), n_tok, n_head, pos0, out, window, softcap)
+    ctx.sync()
+    want = O.attention(q, kc, vc, n_head, n_kv, hd, pos0, slots, kv_type, window=window, softcap=softcap,
+                       n_threads=8)
+    return out.cpu().numpy(), want
+
+
+@pytest.mark.parametrize("kv_type,tol", [(O.KV_F16, 1e-3), (O.KV_Q8_0, 1e-3), (O.KV_TURBO4, 2e-3)],
+                         ids=["f16", "q8_0", "turbo4"])
+def test_attention_matches_oracle(env, kv_type, tol):
+    for (n_head, n_kv, hd, slots, n_tok, pos0) in [(4, 2, 64, 24, 3, 20), (32, 8, 128, 700, 1, 640),
+                                                   (64, 8, 128, 1100, 1, 1050), (8, 8, 128, 64, 5, 40),
+                                                   (16, 1, 64, 600, 2, 598)]:
+        got, want = _attn_case(env, kv_type, n_head, n_kv, hd, slots, n_tok, pos0, seed=n_head + pos0)
+        close(got, want, tol)
+
+
+def test_attention_sliding_window_and_softcap(env):
+    got, want = _attn_case(env, O.KV_F16, 8, 4, 64, 40, 4, 100, window=37, softcap=30.0, seed=5)
+    close(got, want, 1e-3)
+    got, want = _attn_case(env, O.KV_TURBO4, 8, 2, 128, 300, 2, 1000, window=290, seed=6)
+    close(got, want, 2e-3)
+
+
+def test_turbo_attention_equals_attention_over_reconstruction(env):
+    # model/cpu.rs:665-718 run on the GPU: turbo cache vs f16 cache of the reconstruction
+    torch, rie, ctx = env
+    n_head, n_kv, hd, slots = 4, 2, 64, 24
+    rng = np.random.default_rng(0x1234)
+    x = (rng.random((2, n_kv * slots, hd)).astype(np.float32) - 0.5) * 3
+    tq = [O.turbo_quantize_4(x[i]) for i in range(2)]
+    rec = [np.stack([O.turbo_dequantize_4(r, hd) for r in tq[i]]) for i in range(2)]
+    f16 = [O.f32_to_f16(rec[i]).view(np.uint8).reshape(n_kv * slots, -1) for i in range(2)]
+    q = ((rng.random((3, n_head * hd)).astype(np.float32) - 0.5) * 0.2)
+    outs = []
+    for ty, (kc, vc) in ((O.KV_TURBO4, tq), (O.KV_F16, f16)):
+        cache = rie.LayerCache(ctx, rie.KvType(ty), n_kv, hd, slots)
+        cache.import_(kc, vc)
+        o = torch.zeros((3, n_head * hd), device="cuda")
+        rie.attention(ctx, cache, torch.from_numpy(q).cuda(), 3, n_head, 20, o)
+        ctx.sync()
+        outs.append(o.cpu().numpy())
+    assert np.max(np.abs(outs[0] - outs[1])) < 5e-3
+
+
+def test_config5_shape_turbo_attention(env):
+    # BASELINE config 5 geometry (64 q / 8 kv heads x 128) at a shortened context
+    got, want = _attn_case(env, O.KV_TURBO4, 64, 8, 128, 4096, 1, 4095, seed=9)
+    close(got, want, 2e-3)
