@@ -262,7 +262,144 @@ def cpu_gemv_sample(seconds: float, threads: int):
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
-WORKLOADS = {"gemv": run_gemv}
+# ---- workload: config 2 prefill GEMM -----------------------------------------------------
+PF_M, PF_K, PF_N = 512, 4096, (14336, 4096)
+
+
+def measured_int8_peak(torch):
+    """cuBLAS int8 GEMM throughput (torch._int_mm, 8192^3, best of 5) as the tensor peak."""
+    try:
+        a = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = 1e9
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        return 2 * 8192 ** 3 / (best * 1e-3) / 1e12, "measured (cuBLAS int8 via torch._int_mm, 8192^3 burst)"
+    except Exception as e:  # pragma: no cover
+        return 4500.0, f"nominal 4.5 POPS dense int8 ({type(e).__name__})"
+
+
+def run_prefill(args, world, rank, local):
+    import torch
+
+    import oracle as O
+    import rust_interference_engine_b200 as rie
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((PF_M, PF_K)).astype(np.float32)
+    mats = [O.quantize_weight(O.Q4_0, rng.normal(0.0, 0.02, (n, PF_K)).astype(np.float32)) for n in PF_N]
+    ws = [rie.Weight.upload(ctx, rie.GgmlType.Q4_0, n, PF_K, m) for n, m in zip(PF_N, mats)]
+    xd = torch.from_numpy(x).cuda()
+    outs = [torch.zeros((PF_M, n), device="cuda") for n in PF_N]
+    acts = rie.QuantActs(ctx, PF_M, PF_K)
+    jobs = [rie.MatmulJob(w, o, w.rows) for w, o in zip(ws, outs)]
+    flops = sum(2 * PF_M * PF_K * n for n in PF_N)
+
+    def step(ev=None):
+        acts.prepare(xd, PF_M, PF_K, rie.ActFormat.Q8_0)
+        if ev is not None:
+            ev[0].record(stream)
+        rie.matmul_multi(ctx, acts, jobs)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    ctx.sync()
+    want = O.matmul_multi(x[:64], [(O.Q4_0, mats[1], PF_K)], n_threads=8)[0]
+    got = outs[1][:64].cpu().numpy()
+    max_rel = float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-6))
+    kern_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(kern_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = dist_max(t0.elapsed_time(t1) / args.steps, world)
+    kern_ms = dist_max(float(np.mean([a.elapsed_time(b) for a, b in kern_ev])), world)
+    xh = torch.from_numpy(x).pin_memory()
+    ohs = [torch.empty(o.shape, pin_memory=True) for o in outs]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            barrier(world)
+            torch.cuda.synchronize()
+            e0.record(stream)
+        xd.copy_(xh, non_blocking=True)
+        step()
+        for oh, o in zip(ohs, outs):
+            oh.copy_(o, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dist_max(e0.elapsed_time(e1) / args.steps, world)
+    peak, peak_kind = measured_int8_peak(torch)
+    achieved = flops / (kern_ms * 1e-3) / 1e12
+    return {
+        "metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)",
+        "value": world * flops / (ms * 1e-3) / 1e12,
+        "unit": "TOPS",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, f32 block-scale epilogue)",
+        "config": {"workload": "prefill_q4_0_m512_k4096_config2", "m": PF_M, "k": PF_K, "n": list(PF_N),
+                   "ops_per_step": flops, "l2": "weights 42 MB + activations (L2-resident re-use by design)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": profile_traffic("gemm_q4_0_config2"),
+                     "kernel": "k_gemm<Q4_0>", "launch_ms": kern_ms},
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                "h2d_bytes_per_step": PF_M * PF_K * 4, "d2h_bytes_per_step": sum(PF_M * n * 4 for n in PF_N),
+                "ms_per_step": e2e_ms},
+        "gpu_launches": (1 + len(PF_N)) * args.steps,
+        "clocks": clk.summary(),
+        "check": {"max_rel_err_vs_oracle": max_rel, "tolerance": 1e-3},
+    }
+
+
+def cpu_prefill_sample(seconds: float, threads: int):
+    """The oracle's AVX2 matmul (4-token tiles, RIE's chunking) on 64-token slices of config 2."""
+    import oracle as O
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((64, PF_K)).astype(np.float32)
+    w = O.quantize_weight(O.Q4_0, rng.normal(0.0, 0.02, (PF_N[1], PF_K)).astype(np.float32))
+    O.matmul_multi(x, [(O.Q4_0, w, PF_K)], n_threads=threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.matmul_multi(x, [(O.Q4_0, w, PF_K)], n_threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    ops = n * 2 * 64 * PF_K * PF_N[1]
+    return {"value": ops / el / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{n} matmuls of 64 tokens x 4096 x 4096 (Q4_0), {el:.1f} s",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
+WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample)}
+META = {  # metric / unit / config of each workload, shared by both arms
+    "gemv": {"metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)", "unit": "GB/s",
+             "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "workload": "gemv_q4_0_6144x2048_config1"},
+    "prefill": {"metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)", "unit": "TOPS",
+                "dtype": "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, f32 block-scale epilogue)",
+                "workload": "prefill_q4_0_m512_k4096_config2"},
+}
 
 
 def main():
@@ -280,33 +417,34 @@ def main():
         if rank == 0:
             threads = os.cpu_count() or 1
             samples = []
+            cpu_fn = WORKLOADS[args.workload][1]
             for _ in range(args.warmup):
-                cpu_gemv_sample(0.5, threads)
+                cpu_fn(0.2, threads)
             for _ in range(args.steps):
-                samples.append(cpu_gemv_sample(max(args.cpu_seconds / max(args.steps, 1), 0.5), threads))
+                samples.append(cpu_fn(max(args.cpu_seconds / max(args.steps, 1), 0.5), threads))
             v = float(np.median([s["value"] for s in samples]))
             cb = dict(samples[0])
             cb["value"] = v
             cb["sample"] = f"{args.steps} samples of: " + cb["sample"]
-            print(json.dumps({"impl": "reference", "metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)",
-                              "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-                              "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                              "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "data": "synthetic",
-                              "config": {"workload": "gemv_q4_0_6144x2048_config1"}, "vs_baseline": None,
-                              "cpu_baseline": cb,
-                              "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-                  flush=True)
+            m = META[args.workload]
+            print(json.dumps({"impl": "reference", "metric": m["metric"], "value": v, "unit": m["unit"],
+                              "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                              "higher_is_better": True, "scaling": "weak", "dtype": m["dtype"], "data": "synthetic",
+                              "config": {"workload": m["workload"]}, "vs_baseline": None, "cpu_baseline": cb,
+                              "e2e": {"value": v, "unit": m["unit"], "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
         return
 
-    res = WORKLOADS[args.workload](args, world, rank, local)
+    run_fn, cpu_fn = WORKLOADS[args.workload]
+    res = run_fn(args, world, rank, local)
     if rank == 0:
         res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
                     "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)"})
         if world == 1:
-            res["cpu_baseline"] = cpu_gemv_sample(args.cpu_seconds, os.cpu_count() or 1)
+            res["cpu_baseline"] = cpu_fn(args.cpu_seconds, os.cpu_count() or 1)
         print(json.dumps(res), flush=True)
     if world > 1:
         import torch.distributed as dist

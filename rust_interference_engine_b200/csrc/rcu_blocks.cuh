@@ -10,11 +10,12 @@
 
 namespace rcu {
 
-// n consecutive 32-bit words starting at an even byte offset.
+// n consecutive 32-bit words starting at an even byte offset `off` from a 4-byte aligned
+// base (the aligned words around the span are loaded and funnel-shifted into place).
 template <int N>
-__device__ __forceinline__ void ld_words(const uint8_t *base, uint32_t off, uint32_t (&out)[N]) {
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(base + (off & ~3u));
-    const uint32_t sh = (off & 3u) * 8u;
+__device__ __forceinline__ void ld_words(const uint8_t *base, uint64_t off, uint32_t (&out)[N]) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(base + (off & ~(uint64_t)3));
+    const uint32_t sh = (uint32_t)(off & 3u) * 8u;
     uint32_t r[N + 1];
 #pragma unroll
     for (int i = 0; i <= N; i++) r[i] = w[i];
@@ -85,7 +86,7 @@ __device__ __forceinline__ void dec_q5_1(const uint8_t *b, uint32_t off, BlkW &o
     }
 }
 // Q8_0 (reference.rs:95-100, :283-293)
-__device__ __forceinline__ void dec_q8_0(const uint8_t *b, uint32_t off, BlkW &o) {
+__device__ __forceinline__ void dec_q8_0(const uint8_t *b, uint64_t off, BlkW &o) {
     uint32_t w[9];
     ld_words<9>(b, off, w);
     o.d = f16_bits_to_f32(w[0]);
@@ -105,9 +106,13 @@ __device__ __forceinline__ void dec_blk(const uint8_t *b, uint32_t off, BlkW &o)
 // Exact integer block sum s of the reference (offset-coded types subtract 8 / 16 x sum(a)).
 template <int TYPE>
 __device__ __forceinline__ int blk_int(const BlkW &w, const uint32_t (&a)[8], int asum) {
-    int s = 0;
+    int s0 = 0, s1 = 0;  // two chains halve the dp4a dependency latency
 #pragma unroll
-    for (int i = 0; i < 8; i++) s = dp4a(w.v[i], a[i], s);
+    for (int i = 0; i < 8; i += 2) {
+        s0 = dp4a(w.v[i], a[i], s0);
+        s1 = dp4a(w.v[i + 1], a[i + 1], s1);
+    }
+    int s = s0 + s1;
     if (TYPE == T_Q4_0) s -= 8 * asum;
     if (TYPE == T_Q5_0) s -= 16 * asum;
     return s;

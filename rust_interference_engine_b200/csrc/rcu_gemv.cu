@@ -23,12 +23,13 @@
 
 namespace rcu {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kConsumerWarps = 16;  // upper bound; 1-2 token launches use 16, more tokens 8
+
 constexpr int kMaxJobs = 96;
 constexpr int kMaxTok = 8;
 constexpr int kMaxStages = 8;
-constexpr uint32_t kHdrBytes = 4096;  // barriers + reduction scratch
+constexpr int kMaxRw = 2;  // weight rows per warp per tile
+constexpr uint32_t kHdrBytes = 6144;  // barriers + reduction scratch
 
 struct GemvJobDev {
     const uint8_t *w;
@@ -53,8 +54,8 @@ struct GemvParams {
 struct SmemHdr {
     uint64_t full[kMaxStages];
     uint64_t empty[kMaxStages];
-    int cnt[kMaxStages][8];
-    float red[kMaxStages][8][kMaxTok];  // [stage][row in tile * wpr + part][token]
+    int cnt[kMaxStages][kConsumerWarps];
+    float red[kMaxStages][kConsumerWarps][kMaxTok];  // [stage][row in tile * wpr + part][token]
 };
 static_assert(sizeof(SmemHdr) <= kHdrBytes, "header too large");
 
@@ -129,9 +130,9 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
     const float *ad = reinterpret_cast<const float *>(sm + p.o_d0);
     const float *as = reinterpret_cast<const float *>(sm + p.o_s0);
     const int32_t *asm_ = reinterpret_cast<const int32_t *>(sm + p.o_sum0);
-    float acc[4][T];
+    float acc[kMaxRw][T];
 #pragma unroll
-    for (int r = 0; r < 4; r++)
+    for (int r = 0; r < kMaxRw; r++)
 #pragma unroll
         for (int t = 0; t < T; t++) acc[r][t] = 0.0f;
     for (uint32_t b = b_begin + lane; b < b_end; b += 32) {
@@ -149,7 +150,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
             sa[t] = as[t * nb + b];
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < kMaxRw; r++) {
             if ((uint32_t)r < nr) {
                 BlkW w;
                 dec_blk<TYPE>(wsm, (row_first + r) * jb.row_bytes + b * BB, w);
@@ -164,7 +165,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
         }
     }
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
+    for (int r = 0; r < kMaxRw; r++) {
         if ((uint32_t)r < nr) {
             float v[T];
 #pragma unroll
@@ -200,34 +201,48 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
     const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_qk);
     const float *adk = reinterpret_cast<const float *>(sm + p.o_dk);
     const int16_t *abs_ = reinterpret_cast<const int16_t *>(sm + p.o_bsk);
-    float acc[4][T];
+    float acc[kMaxRw][T];
 #pragma unroll
-    for (int r = 0; r < 4; r++)
+    for (int r = 0; r < kMaxRw; r++)
 #pragma unroll
         for (int t = 0; t < T; t++) acc[r][t] = 0.0f;
-    for (uint32_t sb = b_begin + g; sb < b_end; sb += 4) {
+    // The trip count is uniform across the warp (shuffles below need every lane); groups
+    // past the end of the row work on zeros and contribute nothing.
+    for (uint32_t sb0 = b_begin; sb0 < b_end; sb0 += 4) {
+        const uint32_t sb = sb0 + g;
+        const bool act = sb < b_end;
         if (TYPE == T_Q6_K) {
             SbAct6 a[T];
             const int n = sub >> 2, lq = sub & 3;
 #pragma unroll
             for (int t = 0; t < T; t++) {
-                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + 128 * n + 8 * lq;
+                if (act) {
+                    const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + 128 * n + 8 * lq;
 #pragma unroll
-                for (int k = 0; k < 4; k++) a[t].a[k] = *reinterpret_cast<const uint2 *>(base + 32 * k);
-                a[t].d = adk[t * nsb + sb];
+                    for (int k = 0; k < 4; k++) a[t].a[k] = *reinterpret_cast<const uint2 *>(base + 32 * k);
+                    a[t].d = adk[t * nsb + sb];
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) a[t].a[k] = make_uint2(0, 0);
+                    a[t].d = 0.0f;
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 4; r++) {
+            for (int r = 0; r < kMaxRw; r++) {
                 if ((uint32_t)r < nr) {
                     SbW6 w;
-                    dec_sb_q6k(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+                    if (act) {
+                        dec_sb_q6k(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+                    } else {
+                        w = SbW6{};
+                    }
 #pragma unroll
                     for (int t = 0; t < T; t++) {
                         int sumi = dot_sb_q6k(w, a[t]);
                         sumi += __shfl_xor_sync(0xffffffffu, sumi, 4);
                         sumi += __shfl_xor_sync(0xffffffffu, sumi, 2);
                         sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
-                        if (sub == 0) acc[r][t] += (w.d * a[t].d) * (float)sumi;
+                        if (sub == 0 && act) acc[r][t] += (w.d * a[t].d) * (float)sumi;
                     }
                 }
             }
@@ -236,17 +251,27 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
             const int j = sub >> 1, hh = sub & 1;
 #pragma unroll
             for (int t = 0; t < T; t++) {
-                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K;
-                a[t].lo = *reinterpret_cast<const uint4 *>(base + 64 * j + 16 * hh);
-                a[t].hi = *reinterpret_cast<const uint4 *>(base + 64 * j + 32 + 16 * hh);
-                a[t].bs2 = *reinterpret_cast<const uint32_t *>(abs_ + (size_t)t * (p.k / 16) + 16 * sb + 2 * sub);
-                a[t].d = adk[t * nsb + sb];
+                if (act) {
+                    const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K;
+                    a[t].lo = *reinterpret_cast<const uint4 *>(base + 64 * j + 16 * hh);
+                    a[t].hi = *reinterpret_cast<const uint4 *>(base + 64 * j + 32 + 16 * hh);
+                    a[t].bs2 = *reinterpret_cast<const uint32_t *>(abs_ + (size_t)t * (p.k / 16) + 16 * sb + 2 * sub);
+                    a[t].d = adk[t * nsb + sb];
+                } else {
+                    a[t].lo = a[t].hi = make_uint4(0, 0, 0, 0);
+                    a[t].bs2 = 0;
+                    a[t].d = 0.0f;
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 4; r++) {
+            for (int r = 0; r < kMaxRw; r++) {
                 if ((uint32_t)r < nr) {
                     SbW w;
-                    dec_sb_k<TYPE>(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+                    if (act) {
+                        dec_sb_k<TYPE>(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
+                    } else {
+                        w = SbW{};
+                    }
 #pragma unroll
                     for (int t = 0; t < T; t++) {
                         int summ;
@@ -258,14 +283,15 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
                         sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
                         summ += __shfl_xor_sync(0xffffffffu, summ, 1);
                         // d * sumi - dmin * summ with d = f16(d)*ab.d, dmin = f16(dmin)*ab.d
-                        if (sub == 0) acc[r][t] += (w.d * a[t].d) * (float)sumi - (w.dmin * a[t].d) * (float)summ;
+                        if (sub == 0 && act)
+                            acc[r][t] += (w.d * a[t].d) * (float)sumi - (w.dmin * a[t].d) * (float)summ;
                     }
                 }
             }
         }
     }
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
+    for (int r = 0; r < kMaxRw; r++) {
         if ((uint32_t)r < nr) {
             float v[T];
 #pragma unroll
@@ -287,8 +313,8 @@ __device__ __forceinline__ int find_job(const GemvParams &p, uint32_t tile) {
     return lo;
 }
 
-template <int T>
-__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant__ GemvParams p) {
+template <int T, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     SmemHdr *h = reinterpret_cast<SmemHdr *>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -296,14 +322,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; s++) {
             mbar_init(&h->full[s], 1);
-            mbar_init(&h->empty[s], kConsumerWarps);
+            mbar_init(&h->empty[s], NW);
         }
         fence_mbar_init();
     }
-    for (uint32_t i = threadIdx.x; i < kMaxStages * 8; i += blockDim.x) (&h->cnt[0][0])[i] = 0;
+    for (uint32_t i = threadIdx.x; i < kMaxStages * kConsumerWarps; i += blockDim.x) (&h->cnt[0][0])[i] = 0;
     __syncthreads();
 
-    if (warp == kConsumerWarps) {  // ---- producer ----
+    if (warp == NW) {  // ---- producer ----
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             uint32_t li = 0;
@@ -335,7 +361,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
 
     // ---- consumers: stage this call's quantized activations -------------------------------
     {
-        const uint32_t nt = p.n_tok, k = p.k, tid = threadIdx.x, nthr = kConsumerWarps * 32;
+        const uint32_t nt = p.n_tok, k = p.k, tid = threadIdx.x, nthr = NW * 32;
         const ActsView &A = p.acts;
         if (p.formats & RCU_ACT_Q8_0) {
             const uint32_t nb = k / QK;
@@ -358,7 +384,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
             for (uint32_t i = tid; i < nt * k / 16; i += nthr)
                 reinterpret_cast<int16_t *>(smem + p.o_bsk)[i] = A.bsk[(size_t)p.tok0 * (k / 16) + i];
         }
-        named_bar_sync(1, kConsumerWarps * 32);
+        named_bar_sync(1, NW * 32);
     }
 
     uint32_t li = 0;
@@ -419,9 +445,11 @@ __global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ w
     const uint32_t nsb = k / QK_K;
     const int g = lane >> 3, sub = lane & 7;
     const int8_t *aq = A.qk + (size_t)tok * k;
-    for (uint32_t sb = g; sb < nsb; sb += 4) {
+    for (uint32_t sb0 = 0; sb0 < nsb; sb0 += 4) {
+        const uint32_t sb = sb0 + g;
+        const bool act = sb < nsb;  // uniform trip count: shuffles below need every lane
         int sumi = 0, summ = 0;
-        if (type == T_Q6_K) {
+        if (act && type == T_Q6_K) {
             SbAct6 a;
             const int n = sub >> 2, lq = sub & 3;
             for (int kk = 0; kk < 4; kk++)
@@ -429,7 +457,7 @@ __global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ w
             SbW6 w;
             dec_sb_q6k(srow, sb * 210, sub, w);
             sumi = dot_sb_q6k(w, a);
-        } else {
+        } else if (act) {
             SbAct a;
             const int j = sub >> 1, hh = sub & 1;
             a.lo = *reinterpret_cast<const uint4 *>(aq + (size_t)sb * QK_K + 64 * j + 16 * hh);
@@ -447,7 +475,7 @@ __global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ w
             sumi += __shfl_xor_sync(0xffffffffu, sumi, o);
             summ += __shfl_xor_sync(0xffffffffu, summ, o);
         }
-        if (sub == 0) {
+        if (sub == 0 && act) {
             if (type == T_Q6_K) {
                 out[sb] = sumi;
             } else {
@@ -471,15 +499,15 @@ int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint
 // ---- host side -------------------------------------------------------------------------
 static uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
-template <int T>
+template <int T, int NW>
 static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t grid) {
     static bool attr_set[64] = {};
     if (!attr_set[ctx->device & 63]) {
-        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)ctx->max_smem_optin));
         attr_set[ctx->device & 63] = true;
     }
-    k_gemv<T><<<grid, kGemvThreads, smem_bytes, ctx->stream>>>(p);
+    k_gemv<T, NW><<<grid, (NW + 1) * 32, smem_bytes, ctx->stream>>>(p);
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
@@ -505,20 +533,22 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
         jd.row_bytes = (uint32_t)w->row_bytes;
         jd.type = w->type;
         p.formats |= act_format(w->type);
-        const uint32_t rb = jd.row_bytes, target = 40u * 1024u;
-        if (8 * rb <= target) {
+        // Tile = kConsumerWarps * rw rows (or kConsumerWarps / wpr rows when a row is split
+        // over wpr warps), about 24-48 KB of contiguous GGUF bytes per bulk copy.
+        const uint32_t rb = jd.row_bytes, target = 48u * 1024u, nw = n_tok <= 2 ? 16u : 8u;
+        if (nw * rb <= target) {
             jd.wpr = 1;
-            jd.rw = std::max(1u, std::min(4u, target / (8 * rb)));
-            jd.rows_per_tile = 8 * jd.rw;
+            jd.rw = std::max(1u, std::min<uint32_t>(kMaxRw, target / (nw * rb)));
+            jd.rows_per_tile = nw * jd.rw;
         } else {
             jd.wpr = 2;
-            while (jd.wpr < 8 && (8 / jd.wpr) * rb > target) jd.wpr *= 2;
+            while (jd.wpr < nw && (nw / jd.wpr) * rb > target) jd.wpr *= 2;
             jd.rw = 1;
-            jd.rows_per_tile = 8 / jd.wpr;
+            jd.rows_per_tile = nw / jd.wpr;
             const uint32_t units = w->cols / block_size(w->type);
             if ((jd.rows_per_tile * rb) % 16 != 0 || units < jd.wpr) {
                 jd.wpr = 1;
-                jd.rows_per_tile = 8;
+                jd.rows_per_tile = nw;
             }
         }
         jd.tile_begin = tiles;
@@ -550,14 +580,14 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
     switch (n_tok) {
-        case 1: return launch_t<1>(ctx, p, smem_bytes, grid);
-        case 2: return launch_t<2>(ctx, p, smem_bytes, grid);
-        case 3: return launch_t<3>(ctx, p, smem_bytes, grid);
-        case 4: return launch_t<4>(ctx, p, smem_bytes, grid);
-        case 5: return launch_t<5>(ctx, p, smem_bytes, grid);
-        case 6: return launch_t<6>(ctx, p, smem_bytes, grid);
-        case 7: return launch_t<7>(ctx, p, smem_bytes, grid);
-        default: return launch_t<8>(ctx, p, smem_bytes, grid);
+        case 1: return launch_t<1, 16>(ctx, p, smem_bytes, grid);
+        case 2: return launch_t<2, 16>(ctx, p, smem_bytes, grid);
+        case 3: return launch_t<3, 8>(ctx, p, smem_bytes, grid);
+        case 4: return launch_t<4, 8>(ctx, p, smem_bytes, grid);
+        case 5: return launch_t<5, 8>(ctx, p, smem_bytes, grid);
+        case 6: return launch_t<6, 8>(ctx, p, smem_bytes, grid);
+        case 7: return launch_t<7, 8>(ctx, p, smem_bytes, grid);
+        default: return launch_t<8, 8>(ctx, p, smem_bytes, grid);
     }
 }
 

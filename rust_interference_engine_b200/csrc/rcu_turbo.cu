@@ -114,9 +114,7 @@ __device__ void encode_rotated_row(const float *y, uint32_t d, uint8_t *out, uin
                 den = __fadd_rn(den, __fmul_rn(cq, cq));
             }
             const float s = den > 0.0f ? num / den : 0.0f;
-            const unsigned short hs = __half_as_ushort(__float2half_rn(s));
-            out[2 * bi] = (uint8_t)hs;
-            out[2 * bi + 1] = (uint8_t)(hs >> 8);
+            *reinterpret_cast<unsigned short *>(out + 2 * bi) = __half_as_ushort(__float2half_rn(s));
         }
     }
     __syncwarp();
@@ -164,11 +162,7 @@ __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restr
             float d;
             const int q = quant32(src[b * 32 + lane], RCU_ROUND_HALF_AWAY, d);
             uint8_t *ob = dst + b * 34;
-            if (lane == 0) {
-                const unsigned short hs = __half_as_ushort(__float2half_rn(d));
-                ob[0] = (uint8_t)hs;
-                ob[1] = (uint8_t)(hs >> 8);
-            }
+            if (lane == 0) *reinterpret_cast<unsigned short *>(ob) = __half_as_ushort(__float2half_rn(d));
             ob[2 + lane] = (uint8_t)(int8_t)q;
         }
         return;
@@ -284,21 +278,21 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
     for (uint32_t i = c0 + threadIdx.x; i < c1; i += kAttnThreads) {
         const uint64_t slot = (start + i) % p.slots;
         const uint64_t row = (uint64_t)g * p.slots + slot;
-        const uint8_t *kr = p.kc + row * p.row_bytes;
+        const uint64_t kro = row * p.row_bytes;  // byte offset of the row (rows may be only 2-aligned)
         float s[kMaxGroup];
         for (uint32_t hh = 0; hh < group; hh++) s[hh] = 0.0f;
         if (KV == RCU_KV_TURBO4) {
             const uint32_t b = turbo_block(hd), nb = hd / b, cpb = b / 32;
             for (uint32_t bi = 0; bi < nb; bi++) {
                 uint32_t sw[1];
-                ld_words<1>(kr, 2 * bi, sw);
+                ld_words<1>(p.kc, kro + 2 * bi, sw);
                 const float scale = f16_bits_to_f32(sw[0]);
                 float dcs[kMaxGroup];
                 for (uint32_t hh = 0; hh < group; hh++) dcs[hh] = 0.0f;
                 for (uint32_t c = 0; c < cpb; c++) {
                     const uint32_t cc = bi * cpb + c;
                     uint32_t w[4];
-                    ld_words<4>(kr, 2 * nb + 16 * cc, w);
+                    ld_words<4>(p.kc, kro + 2 * nb + 16 * cc, w);
                     uint32_t lv[8];
 #pragma unroll
                     for (int i2 = 0; i2 < 4; i2++) {
@@ -325,7 +319,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
         } else if (KV == RCU_KV_Q8_0) {
             for (uint32_t bi = 0; bi < hd / 32; bi++) {
                 BlkW w;
-                dec_q8_0(kr, bi * 34, w);
+                dec_q8_0(p.kc, kro + bi * 34, w);
                 for (uint32_t hh = 0; hh < group; hh++) {
                     const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][bi * 32]);
                     const uint4 q0 = qv[0], q1 = qv[1];
@@ -335,7 +329,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
                 }
             }
         } else {
-            const __half2 *kh = reinterpret_cast<const __half2 *>(kr);
+            const __half2 *kh = reinterpret_cast<const __half2 *>(p.kc + kro);
             for (uint32_t d2 = 0; d2 < hd / 2; d2++) {
                 const float2 kv = __half22float2(kh[d2]);
                 for (uint32_t hh = 0; hh < group; hh++) s[hh] += kv.x * qf[hh][2 * d2] + kv.y * qf[hh][2 * d2 + 1];
@@ -374,7 +368,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
     const uint32_t d0 = lane * dpl;
     for (uint32_t i = c0 + warp; i < c1; i += kAttnWarps) {
         const uint64_t slot = (start + i) % p.slots;
-        const uint8_t *vr = p.vc + ((uint64_t)g * p.slots + slot) * p.row_bytes;
+        const uint64_t vro = ((uint64_t)g * p.slots + slot) * p.row_bytes;
+        const uint8_t *vr = p.vc + vro;
         float val[kMaxAttnHd / 32];
         if (KV == RCU_KV_TURBO4) {
             const uint32_t b = turbo_block(hd), nb = hd / b;
@@ -383,14 +378,14 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
                 const uint32_t byte = vr[2 * nb + 16 * c + (m2 & 15)];
                 const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
                 uint32_t sw[1];
-                ld_words<1>(vr, 2 * (dd / b), sw);
+                ld_words<1>(p.vc, vro + 2 * (dd / b), sw);
                 val[e] = f16_bits_to_f32(sw[0]) * inv46 * (float)c_levels[code];
             }
         } else if (KV == RCU_KV_Q8_0) {
             for (uint32_t e = 0; e < dpl; e++) {
                 const uint32_t dd = d0 + e, bi = dd / 32;
                 uint32_t sw[1];
-                ld_words<1>(vr, bi * 34, sw);
+                ld_words<1>(p.vc, vro + bi * 34, sw);
                 val[e] = f16_bits_to_f32(sw[0]) * (float)(int8_t)vr[bi * 34 + 2 + dd % 32];
             }
         } else {

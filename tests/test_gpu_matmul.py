@@ -168,3 +168,26 @@ def test_errors_are_reported(env):
     with pytest.raises(rie.RcuError):
         rie.Weight.upload(ctx, rie.GgmlType.Q4_K, 2, 100, np.zeros(0, np.uint8))
     assert ctx.device_error_bits() == 0
+
+
+@pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 512), (64, 333, 4096), (100, 1000, 2048), (128, 256, 4096),
+                                          (200, 130, 1024), (512, 4096, 4096)])
+def test_prefill_gemm_q4_0(env, n_tok, rows, k):
+    # tcgen05 int8 GEMM path (n_tok >= 32): ragged token and row tiles, several K
+    rng = O.Rng(1000 + n_tok + rows)
+    w = rng.weight(O.Q4_0, rows, k)
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    got = gpu_matmul(env, [(O.Q4_0, w, k)], x)[0][0]
+    want = O.matmul_multi(x, [(O.Q4_0, w, k)], n_threads=8)[0]
+    close(got, want)
+
+
+def test_prefill_gemm_config2(env):
+    # M = 512 tokens x K = 4096, N = 4096 and 14336, W ~ N(0, 0.02) -> Q4_0
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((512, 4096)).astype(np.float32)
+    for n in (4096, 14336):
+        w = O.quantize_weight(O.Q4_0, rng.normal(0.0, 0.02, (n, 4096)).astype(np.float32))
+        got = gpu_matmul(env, [(O.Q4_0, w, 4096)], x)[0][0]
+        want = O.matmul_multi(x, [(O.Q4_0, w, 4096)], n_threads=8)[0]
+        close(got, want)
