@@ -148,6 +148,49 @@ RCU_API int32_t rcu_kv_import(rcu_ctx *ctx, rcu_kv *kv, const void *k_host, cons
 RCU_API int32_t rcu_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q_dev, uint64_t n_tok, uint64_t n_head,
                       uint64_t pos0, uint64_t window, float softcap, float *out_dev);
 
+/* ---- transformer forward (model/mod.rs Model + Backend trait, model/cpu.rs) --------- */
+typedef struct rcu_model rcu_model;
+typedef struct rcu_backend rcu_backend;
+/* Hyper-parameters (reference ModelConfig, model/config.rs:54-104), flattened. Optional
+ * features use 0 / <= 0 for "absent". */
+typedef struct rcu_model_config {
+    uint32_t n_vocab, n_embd, n_layer, n_head, n_head_kv, head_dim, n_ff;
+    uint32_t rope_dim;
+    int32_t rope_neox;                /* 1: rotate (x[i], x[i+dim/2]); 0: (x[2i], x[2i+1]) */
+    float rope_base, rope_freq_scale;
+    float rms_eps, attn_scale, embd_scale, residual_scale, logit_scale;
+    float attn_softcap, final_softcap;
+    uint32_t swa_window, swa_pattern;
+    float rope_base_swa;
+    int32_t act;                      /* 0 SiLU, 1 GELU (tanh) */
+    uint32_t n_expert, n_expert_used, n_ff_exp;
+    int32_t expert_norm_topk, expert_unit_weights;
+} rcu_model_config;
+/* Model::load (model/mod.rs:112-247) without the file: the caller hands over every GGUF
+ * tensor by its GGUF name ("token_embd.weight", "blk.0.attn_q.weight", ...). */
+RCU_API int32_t rcu_model_create(rcu_ctx *ctx, const rcu_model_config *cfg, rcu_model **out);
+RCU_API void rcu_model_free(rcu_model *m);
+RCU_API int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                                     const void *host_bytes);
+/* CpuBackend::with_kv_type (model/cpu.rs:100-177): KV caches and scratch for n_ctx
+ * positions and batches of up to max_batch tokens. Validates the model's tensors. */
+RCU_API int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type,
+                                   rcu_backend **out);
+RCU_API void rcu_backend_free(rcu_backend *b);
+RCU_API uint64_t rcu_backend_max_batch(const rcu_backend *b);
+RCU_API uint64_t rcu_backend_n_ctx(const rcu_backend *b);
+/* Backend::forward (model/mod.rs:313): evaluate tokens at positions pos..pos+n; writes the
+ * last token's logits (n_vocab floats) or all n rows when all_logits. Host buffers;
+ * synchronous. Errors as the reference: empty batch, batch > max, context full, token id
+ * out of range (RCU_ERR_RUNTIME). */
+RCU_API int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, uint64_t pos,
+                                    int32_t all_logits, float *logits, uint64_t logits_len);
+/* Same on device buffers, asynchronous on the context stream (tokens_dev: n uint32). */
+RCU_API int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, uint64_t n, uint64_t pos,
+                                           int32_t all_logits, float *logits_dev);
+/* Backend::hidden (model/mod.rs:318): final normed rows of the last forward (rows x n_embd). */
+RCU_API int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out);
+
 #ifdef __cplusplus
 }
 #endif

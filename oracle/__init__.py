@@ -33,8 +33,8 @@ BLOCK_Q8K = np.dtype({"names": ["qs", "bsums", "d"], "formats": [("i1", 256), ("
 
 
 def build(force: bool = False) -> str:
-    src = os.path.join(_HERE, "rie_oracle.cpp")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("rie_oracle.cpp", "rie_oracle_model.cpp", "rie_oracle.h")]
+    if force or not os.path.exists(_LIB_PATH) or any(os.path.getmtime(_LIB_PATH) < os.path.getmtime(s) for s in srcs):
         subprocess.run(["make", "-C", _HERE, "-B" if force else "liboracle.so"], check=True,
                        stdout=subprocess.DEVNULL)
     return _LIB_PATH
@@ -77,6 +77,11 @@ def _declare(L):
         "orc_kv_store": (None, [I, P, S, P, I]),
         "orc_rmsnorm": (None, [P, P, P, S, F, I]), "orc_rope_table": (None, [S, F, F, S, P, P]),
         "orc_rope_apply": (None, [P, S, I, P, P]), "orc_silu": (F, [F]), "orc_dot_f32": (F, [P, P, S, I]),
+        "orc_model_create": (P, [P]), "orc_model_free": (None, [P]),
+        "orc_model_set_tensor": (I, [P, C.c_char_p, I, U64, U64, P]),
+        "orc_backend_create": (P, [P, U64, U64, I, I, I]), "orc_backend_free": (None, [P]),
+        "orc_backend_forward": (I, [P, P, U64, U64, I, P]), "orc_backend_error": (C.c_char_p, [P]),
+        "orc_backend_hidden": (I, [P, P, U64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -368,3 +373,60 @@ def rope_apply(x, neox, c, s) -> np.ndarray:
     y = np.array(x, dtype=np.float32, copy=True)
     lib().orc_rope_apply(_p(y), y.size, int(neox), _p(np.ascontiguousarray(c)), _p(np.ascontiguousarray(s)))
     return y
+
+
+# ---- transformer forward (model/cpu.rs:210-409) -------------------------------------------
+class ModelConfig(C.Structure):
+    """Same field order as orc_model_config / rcu_model_config."""
+    _fields_ = [("n_vocab", C.c_uint32), ("n_embd", C.c_uint32), ("n_layer", C.c_uint32), ("n_head", C.c_uint32),
+                ("n_head_kv", C.c_uint32), ("head_dim", C.c_uint32), ("n_ff", C.c_uint32), ("rope_dim", C.c_uint32),
+                ("rope_neox", C.c_int32), ("rope_base", C.c_float), ("rope_freq_scale", C.c_float),
+                ("rms_eps", C.c_float), ("attn_scale", C.c_float), ("embd_scale", C.c_float),
+                ("residual_scale", C.c_float), ("logit_scale", C.c_float), ("attn_softcap", C.c_float),
+                ("final_softcap", C.c_float), ("swa_window", C.c_uint32), ("swa_pattern", C.c_uint32),
+                ("rope_base_swa", C.c_float), ("act", C.c_int32), ("n_expert", C.c_uint32),
+                ("n_expert_used", C.c_uint32), ("n_ff_exp", C.c_uint32), ("expert_norm_topk", C.c_int32),
+                ("expert_unit_weights", C.c_int32)]
+
+
+class OracleModel:
+    def __init__(self, cfg: ModelConfig):
+        self.cfg = cfg
+        self.ptr = lib().orc_model_create(C.byref(cfg))
+
+    def set_tensor(self, name: str, t: int, rows: int, cols: int, data) -> None:
+        a = np.ascontiguousarray(data).view(np.uint8)
+        assert a.size == rows * row_bytes(t, cols), name
+        lib().orc_model_set_tensor(self.ptr, name.encode(), t, rows, cols, _p(a))
+
+    def __del__(self):
+        try:
+            lib().orc_model_free(self.ptr)
+        except Exception:
+            pass
+
+
+class OracleBackend:
+    """CpuBackend of the reference, restated (forward / hidden)."""
+
+    def __init__(self, model: OracleModel, n_ctx: int, max_batch: int, kv_type: int = KV_F16, n_threads: int = 8,
+                 path: int | None = None):
+        self.model = model
+        self.n_vocab = model.cfg.n_vocab
+        self.ptr = lib().orc_backend_create(model.ptr, n_ctx, max_batch, kv_type, n_threads,
+                                            default_path() if path is None else path)
+
+    def forward(self, tokens, pos: int, all_logits: bool = False) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        n = tok.size
+        out = np.zeros(((n if all_logits else 1), self.n_vocab), dtype=np.float32)
+        st = lib().orc_backend_forward(self.ptr, _p(tok), n, pos, int(all_logits), _p(out))
+        if st != 0:
+            raise RuntimeError(lib().orc_backend_error(self.ptr).decode())
+        return out
+
+    def __del__(self):
+        try:
+            lib().orc_backend_free(self.ptr)
+        except Exception:
+            pass

@@ -1,0 +1,598 @@
+// rcu_forward.cu -- device forward scheduler: the transformer layer loop of the reference's
+// CPU backend (crates/rie-core/src/model/cpu.rs:210-409, dense_ffn :431-467) over the
+// quantized matmul, KV-cache and attention kernels of this library.
+//
+// Per layer and batch: RMSNorm -> Q8 activations -> one matmul_multi for Q,K,V ->
+// bias / per-head q,k RMSNorm / RoPE / attn_scale -> KV append -> attention -> Wo ->
+// post-norm + residual -> RMSNorm -> gate+up in one launch -> SwiGLU/GELU -> down ->
+// post-norm + residual; then the output norm and head. All work is queued on the context
+// stream; the host only validates arguments and launches.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "rcu_blocks.cuh"
+#include "rcu_kernels.h"
+
+namespace rcu {
+
+struct LayerW {
+    const rcu_weight *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr;
+    const rcu_weight *gate = nullptr, *up = nullptr, *down = nullptr;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    const float *bq = nullptr, *bk = nullptr, *bv = nullptr, *post_attn = nullptr, *post_ffn = nullptr;
+    bool swa = false;
+};
+
+}  // namespace rcu
+
+struct rcu_model {
+    rcu_ctx *ctx = nullptr;
+    rcu_model_config cfg{};
+    std::map<std::string, rcu_weight *> w;
+    std::map<std::string, float *> vec;  // 1-D float tensors as device f32
+    std::vector<rcu_weight *> slices;
+};
+
+struct rcu_backend {
+    rcu_model *m = nullptr;
+    rcu_ctx *ctx = nullptr;
+    uint64_t n_ctx = 0, max_batch = 0;
+    int kv_type = 0;
+    std::vector<rcu::LayerW> layers;
+    const rcu_weight *embd = nullptr, *out = nullptr;
+    const float *out_norm = nullptr;
+    std::vector<rcu_kv *> kv;
+    rcu_acts *acts = nullptr;
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
+    float *g = nullptr, *u = nullptr, *logits = nullptr, *inv_freq = nullptr, *inv_freq_swa = nullptr;
+    uint32_t *tokens = nullptr;
+    uint32_t ff_max = 0;
+    uint64_t hidden_rows = 0;
+    std::vector<void *> allocs;
+};
+
+namespace rcu {
+
+// ---- kernels ---------------------------------------------------------------------------
+
+// Dequantize one GGUF block (reference.rs:53-215) into y (block_size values).
+__device__ void dequant_block(int t, const uint8_t *b, float *y, int lane, int nl) {
+    auto f16 = [&](int off) { return __half2float(__ushort_as_half((unsigned short)(b[off] | (b[off + 1] << 8)))); };
+    switch (t) {
+        case T_Q4_0: {
+            const float d = f16(0);
+            for (int j = lane; j < 16; j += nl) {
+                y[j] = (float)((b[2 + j] & 0xF) - 8) * d;
+                y[j + 16] = (float)((b[2 + j] >> 4) - 8) * d;
+            }
+            break;
+        }
+        case T_Q4_1: {
+            const float d = f16(0), m = f16(2);
+            for (int j = lane; j < 16; j += nl) {
+                y[j] = (float)(b[4 + j] & 0xF) * d + m;
+                y[j + 16] = (float)(b[4 + j] >> 4) * d + m;
+            }
+            break;
+        }
+        case T_Q5_0: case T_Q5_1: {
+            const bool one = t == T_Q5_1;
+            const float d = f16(0), m = one ? f16(2) : 0.0f;
+            const int o = one ? 4 : 2;
+            const uint32_t qh = b[o] | (b[o + 1] << 8) | (b[o + 2] << 16) | ((uint32_t)b[o + 3] << 24);
+            for (int j = lane; j < 16; j += nl) {
+                const uint32_t xh0 = ((qh >> j) << 4) & 0x10, xh1 = (qh >> (j + 12)) & 0x10;
+                const uint32_t a = (b[o + 4 + j] & 0xFu) | xh0, c = (b[o + 4 + j] >> 4) | xh1;
+                y[j] = one ? (float)a * d + m : (float)((int)a - 16) * d;
+                y[j + 16] = one ? (float)c * d + m : (float)((int)c - 16) * d;
+            }
+            break;
+        }
+        case T_Q8_0: {
+            const float d = f16(0);
+            for (int j = lane; j < 32; j += nl) y[j] = (float)(int8_t)b[2 + j] * d;
+            break;
+        }
+        case T_Q4_K: case T_Q5_K: {
+            const float d = f16(0), mn = f16(2);
+            const uint32_t s[3] = {(uint32_t)b[4] | (b[5] << 8) | (b[6] << 16) | ((uint32_t)b[7] << 24),
+                                   (uint32_t)b[8] | (b[9] << 8) | (b[10] << 16) | ((uint32_t)b[11] << 24),
+                                   (uint32_t)b[12] | (b[13] << 8) | (b[14] << 16) | ((uint32_t)b[15] << 24)};
+            for (int i = lane; i < 256; i += nl) {
+                const int j = i / 64, l = i % 32, hi = (i / 32) & 1;
+                uint32_t sc, m;
+                scale_min_k4(2 * j + hi, s, sc, m);
+                uint32_t q;
+                if (t == T_Q4_K) {
+                    q = hi ? (b[16 + 32 * j + l] >> 4) : (b[16 + 32 * j + l] & 0xF);
+                } else {
+                    q = (hi ? (b[48 + 32 * j + l] >> 4) : (b[48 + 32 * j + l] & 0xF)) +
+                        ((b[16 + l] & ((hi ? 2u : 1u) << (2 * j))) ? 16u : 0u);
+                }
+                y[i] = d * (float)sc * (float)q - mn * (float)m;
+            }
+            break;
+        }
+        case T_Q6_K: {
+            const float d = f16(208);
+            for (int i = lane; i < 256; i += nl) {
+                const int n = i / 128, r = i % 128, k = r / 32, l = r % 32, is = l / 16;
+                const uint8_t *ql = b + 64 * n, *qh = b + 128 + 32 * n;
+                const int8_t *sc = (const int8_t *)(b + 192 + 8 * n);
+                const int lo = (k & 1) ? ql[l + 32] : ql[l];
+                const int q = (((k < 2) ? (lo & 0xF) : (lo >> 4)) | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+                y[i] = d * (float)sc[is + 2 * k] * (float)q;
+            }
+            break;
+        }
+        default: break;
+    }
+}
+
+__global__ void k_embed(const uint32_t *__restrict__ tokens, int type, const uint8_t *__restrict__ w, uint64_t row_bytes,
+                        uint32_t e, float scale, float *__restrict__ x) {
+    const uint32_t t = blockIdx.x;
+    const uint8_t *row = w + (uint64_t)tokens[t] * row_bytes;
+    float *y = x + (uint64_t)t * e;
+    if (type == T_F32) {
+        for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) y[i] = reinterpret_cast<const float *>(row)[i] * scale;
+        return;
+    }
+    if (type == T_F16) {
+        for (uint32_t i = threadIdx.x; i < e; i += blockDim.x)
+            y[i] = __half2float(reinterpret_cast<const __half *>(row)[i]) * scale;
+        return;
+    }
+    const int bs = block_size(type), bb = block_bytes(type);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (uint32_t blk = warp; blk < e / bs; blk += nw) {
+        dequant_block(type, row + (uint64_t)blk * bb, y + (uint64_t)blk * bs, lane, 32);
+        __syncwarp();
+        if (scale != 1.0f)
+            for (int i = lane; i < bs; i += 32) y[blk * bs + i] *= scale;
+    }
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+
+// out = x / rms(x) * w per row (ops.rs:7-14): (x * scale) * w.
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, uint32_t e, float eps,
+                          float *__restrict__ out) {
+    __shared__ float red[32];
+    const float *xr = x + (uint64_t)blockIdx.x * e;
+    float *orow = out + (uint64_t)blockIdx.x * e;
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)e + eps);
+    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
+}
+
+// x += post_norm(o) * rs, with the optional post-norm in place on o (ops.rs:17-24).
+__global__ void k_residual(float *__restrict__ x, float *__restrict__ o, const float *__restrict__ post_w, uint32_t e,
+                           float eps, float rs) {
+    __shared__ float red[32];
+    float *xr = x + (uint64_t)blockIdx.x * e;
+    float *orow = o + (uint64_t)blockIdx.x * e;
+    float scale = 1.0f;
+    if (post_w) {
+        float ss = 0.0f;
+        for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) ss += orow[i] * orow[i];
+        ss = block_sum(ss, red);
+        scale = 1.0f / sqrtf(ss / (float)e + eps);
+    }
+    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) {
+        float v = orow[i];
+        if (post_w) v *= scale * post_w[i];
+        xr[i] += rs == 1.0f ? v : v * rs;
+    }
+}
+
+// Per head vector: bias, q/k RMSNorm (x *= scale*w), RoPE, attn_scale (q only).
+// Vectors: [t][0..n_head) = q heads, [t][n_head..n_head+n_kv) = k heads, then v heads (bias).
+__global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, float *__restrict__ v,
+                           const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
+                           const float *__restrict__ qn, const float *__restrict__ kn, const float *__restrict__ inv_freq,
+                           uint32_t n_tok, uint32_t n_head, uint32_t n_kv, uint32_t hd, uint32_t rope_dim, int neox,
+                           uint64_t pos0, float eps, float attn_scale) {
+    __shared__ float buf[4][512];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t per_tok = n_head + 2 * n_kv;
+    const uint64_t item = (uint64_t)blockIdx.x * 4 + warp;
+    if (item >= (uint64_t)n_tok * per_tok) return;
+    const uint32_t t = (uint32_t)(item / per_tok), j = (uint32_t)(item % per_tok);
+    float *vec;
+    const float *bias, *norm;
+    bool is_q = false, rope = true;
+    if (j < n_head) {
+        vec = q + ((uint64_t)t * n_head + j) * hd, bias = bq ? bq + j * hd : nullptr, norm = qn, is_q = true;
+    } else if (j < n_head + n_kv) {
+        vec = k + ((uint64_t)t * n_kv + (j - n_head)) * hd, bias = bk ? bk + (j - n_head) * hd : nullptr, norm = kn;
+    } else {
+        vec = v + ((uint64_t)t * n_kv + (j - n_head - n_kv)) * hd, bias = bv ? bv + (j - n_head - n_kv) * hd : nullptr;
+        norm = nullptr, rope = false;
+    }
+    float *s = buf[warp];
+    for (uint32_t i = lane; i < hd; i += 32) s[i] = vec[i] + (bias ? bias[i] : 0.0f);
+    __syncwarp();
+    if (norm) {
+        float ss = 0.0f;
+        for (uint32_t i = lane; i < hd; i += 32) ss += s[i] * s[i];
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float scale = 1.0f / sqrtf(ss / (float)hd + eps);
+        for (uint32_t i = lane; i < hd; i += 32) s[i] *= scale * norm[i];
+        __syncwarp();
+    }
+    if (rope) {
+        const uint32_t half = rope_dim / 2;
+        const float pos = (float)(pos0 + t);
+        for (uint32_t i = lane; i < half; i += 32) {
+            float sn, cs;
+            sincosf(pos * inv_freq[i], &sn, &cs);
+            const uint32_t i0 = neox ? i : 2 * i, i1 = neox ? i + half : 2 * i + 1;
+            const float a = s[i0], b = s[i1];
+            s[i0] = a * cs - b * sn;
+            s[i1] = a * sn + b * cs;
+        }
+        __syncwarp();
+    }
+    for (uint32_t i = lane; i < hd; i += 32) vec[i] = is_q ? s[i] * attn_scale : s[i];
+}
+
+__global__ void k_glu(float *__restrict__ g, const float *__restrict__ u, uint64_t n, int act) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float a = g[i];
+    float f;
+    if (act == 1) {
+        f = 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a)));
+    } else {
+        f = a / (1.0f + expf(-a));
+    }
+    g[i] = f * u[i];
+}
+
+__global__ void k_logit_post(float *__restrict__ l, uint64_t n, float scale, float cap) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float v = l[i];
+    if (scale != 1.0f) v /= scale;
+    if (cap > 0.0f) v = cap * tanhf(v / cap);
+    l[i] = v;
+}
+
+// ---- host helpers -------------------------------------------------------------------------
+static int dalloc(rcu_backend *b, void **p, size_t bytes) {
+    RCU_CUDA_TRY(b->ctx, cudaMalloc(p, bytes));
+    b->allocs.push_back(*p);
+    return RCU_OK;
+}
+
+static int matmul(rcu_backend *b, const float *x, uint32_t n, uint32_t k, std::vector<rcu_job> jobs) {
+    uint32_t fmt = 0;
+    for (auto &j : jobs) fmt |= act_format(j.w->type);
+    int st = rcu_acts_prepare(b->ctx, b->acts, x, n, k, fmt);
+    if (st) return st;
+    return rcu_matmul_multi(b->ctx, b->acts, jobs.data(), jobs.size());
+}
+
+static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits) {
+    rcu_ctx *ctx = b->ctx;
+    const rcu_model_config &c = b->m->cfg;
+    cudaStream_t s = ctx->stream;
+    const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
+    k_embed<<<(uint32_t)n, 128, 0, s>>>(b->tokens, b->embd->type, b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x);
+    for (uint32_t il = 0; il < c.n_layer; il++) {
+        const LayerW &L = b->layers[il];
+        k_rmsnorm<<<(uint32_t)n, 256, 0, s>>>(b->x, L.attn_norm, e, c.rms_eps, b->xn);
+        int st = matmul(b, b->xn, (uint32_t)n, e, {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}});
+        if (st) return st;
+        const bool swa_rope = L.swa && c.rope_base_swa > 0.0f;
+        const uint64_t items = n * (c.n_head + 2 * c.n_head_kv);
+        k_qkv_post<<<(uint32_t)((items + 3) / 4), 128, 0, s>>>(b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
+                                                              swa_rope ? b->inv_freq_swa : b->inv_freq, (uint32_t)n,
+                                                              c.n_head, c.n_head_kv, hd, c.rope_dim, c.rope_neox, pos0,
+                                                              c.rms_eps, c.attn_scale);
+        st = rcu_kv_store(ctx, b->kv[il], b->k, b->v, n, pos0);
+        if (st) return st;
+        st = rcu_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, L.swa ? c.swa_window : 0, c.attn_softcap, b->att);
+        if (st) return st;
+        st = matmul(b, b->att, (uint32_t)n, qd, {{L.wo, b->o, e}});
+        if (st) return st;
+        k_residual<<<(uint32_t)n, 256, 0, s>>>(b->x, b->o, L.post_attn, e, c.rms_eps, c.residual_scale);
+        k_rmsnorm<<<(uint32_t)n, 256, 0, s>>>(b->x, L.ffn_norm, e, c.rms_eps, b->xn);
+        const uint32_t ff = (uint32_t)L.gate->rows;
+        st = matmul(b, b->xn, (uint32_t)n, e, {{L.gate, b->g, ff}, {L.up, b->u, ff}});
+        if (st) return st;
+        const uint64_t ng = n * ff;
+        k_glu<<<(uint32_t)((ng + 255) / 256), 256, 0, s>>>(b->g, b->u, ng, c.act);
+        st = matmul(b, b->g, (uint32_t)n, ff, {{L.down, b->o, e}});
+        if (st) return st;
+        k_residual<<<(uint32_t)n, 256, 0, s>>>(b->x, b->o, L.post_ffn, e, c.rms_eps, c.residual_scale);
+    }
+    const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
+    k_rmsnorm<<<(uint32_t)m, 256, 0, s>>>(b->x + first * e, b->out_norm, e, c.rms_eps, b->xn);
+    b->hidden_rows = m;
+    int st = matmul(b, b->xn, (uint32_t)m, e, {{b->out, logits, c.n_vocab}});
+    if (st) return st;
+    if (c.logit_scale != 1.0f || c.final_softcap > 0.0f) {
+        const uint64_t nl = m * c.n_vocab;
+        k_logit_post<<<(uint32_t)((nl + 255) / 256), 256, 0, s>>>(logits, nl, c.logit_scale, c.final_softcap);
+    }
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
+    return RCU_OK;
+}
+
+static bool ends_with(const std::string &s, const char *suf) {
+    const size_t n = std::strlen(suf);
+    return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
+}
+
+}  // namespace rcu
+
+using namespace rcu;
+
+extern "C" {
+
+int32_t rcu_model_create(rcu_ctx *ctx, const rcu_model_config *cfg, rcu_model **out) {
+    if (!ctx || !cfg || !out) return set_err(ctx, RCU_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const rcu_model_config &c = *cfg;
+    if (!c.n_vocab || !c.n_embd || !c.n_layer || !c.n_head || !c.n_head_kv || !c.head_dim)
+        return set_err(ctx, RCU_ERR_INVALID, "model config: zero dimension");
+    if (c.n_head % c.n_head_kv) return set_err(ctx, RCU_ERR_INVALID, "n_head not divisible by n_head_kv");
+    if (c.rope_dim > c.head_dim || c.rope_dim % 2) return set_err(ctx, RCU_ERR_INVALID, "invalid rope dimension");
+    if (c.head_dim > 256 || c.head_dim % 32) return set_err(ctx, RCU_ERR_UNSUPPORTED, "head_dim must be a multiple of 32, <= 256");
+    if (c.n_expert) return set_err(ctx, RCU_ERR_UNSUPPORTED, "mixture-of-experts layers are not supported by this backend yet");
+    rcu_model *m = new (std::nothrow) rcu_model();
+    if (!m) return RCU_ERR_OOM;
+    m->ctx = ctx;
+    m->cfg = c;
+    *out = m;
+    return RCU_OK;
+}
+
+void rcu_model_free(rcu_model *m) {
+    if (!m) return;
+    for (auto &kv : m->w) rcu_weight_free(kv.second);
+    for (auto *s : m->slices) rcu_weight_free(s);
+    cudaSetDevice(m->ctx->device);
+    for (auto &kv : m->vec) cudaFree(kv.second);
+    delete m;
+}
+
+int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                             const void *host_bytes) {
+    if (!m || !name || !host_bytes) return RCU_ERR_INVALID;
+    rcu_ctx *ctx = m->ctx;
+    const std::string n(name);
+    if (rows == 1 && (ggml_type == T_F32 || ggml_type == T_F16 || ggml_type == T_BF16)) {
+        std::vector<float> v(cols);
+        for (uint64_t i = 0; i < cols; i++) {
+            if (ggml_type == T_F32) {
+                std::memcpy(&v[i], (const uint8_t *)host_bytes + 4 * i, 4);
+            } else {
+                uint16_t h;
+                std::memcpy(&h, (const uint8_t *)host_bytes + 2 * i, 2);
+                if (ggml_type == T_BF16) {
+                    uint32_t u = (uint32_t)h << 16;
+                    std::memcpy(&v[i], &u, 4);
+                } else {
+                    v[i] = __half2float(__ushort_as_half(h));
+                }
+            }
+        }
+        float *d = nullptr;
+        RCU_CUDA_TRY(ctx, cudaMalloc(&d, cols * 4));
+        RCU_CUDA_TRY(ctx, cudaMemcpy(d, v.data(), cols * 4, cudaMemcpyHostToDevice));
+        auto it = m->vec.find(n);
+        if (it != m->vec.end()) cudaFree(it->second);
+        m->vec[n] = d;
+        return RCU_OK;
+    }
+    rcu_weight *w = nullptr;
+    if (ggml_type == T_F32 || ggml_type == T_F16) {  // float matrices (embeddings only on this path)
+        const uint64_t rb = cols * (ggml_type == T_F32 ? 4 : 2);
+        uint8_t *d = nullptr;
+        RCU_CUDA_TRY(ctx, cudaMalloc(&d, rows * rb + 256));
+        RCU_CUDA_TRY(ctx, cudaMemcpy(d, host_bytes, rows * rb, cudaMemcpyHostToDevice));
+        w = new rcu_weight();
+        w->ctx = ctx, w->type = (int)ggml_type, w->rows = rows, w->cols = cols, w->row_bytes = rb, w->data = d;
+        w->owned = true, w->padded = true;
+    } else {
+        const int32_t st = rcu_weight_upload(ctx, ggml_type, rows, cols, host_bytes, &w);
+        if (st) return st;
+    }
+    auto it = m->w.find(n);
+    if (it != m->w.end()) rcu_weight_free(it->second);
+    m->w[n] = w;
+    return RCU_OK;
+}
+
+int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type, rcu_backend **out) {
+    if (!m || !out) return RCU_ERR_INVALID;
+    *out = nullptr;
+    rcu_ctx *ctx = m->ctx;
+    const rcu_model_config &c = m->cfg;
+    if (n_ctx == 0) return set_err(ctx, RCU_ERR_INVALID, "n_ctx must be positive");
+    if (kv_type < RCU_KV_F16 || kv_type > RCU_KV_TURBO4) return set_err(ctx, RCU_ERR_INVALID, "unknown kv type");
+    rcu_backend *b = new (std::nothrow) rcu_backend();
+    if (!b) return RCU_ERR_OOM;
+    b->m = m;
+    b->ctx = ctx;
+    b->n_ctx = n_ctx;
+    b->max_batch = std::max<uint64_t>(1, std::min<uint64_t>(max_batch, n_ctx));  // cpu.rs:102
+    b->kv_type = kv_type;
+    auto fail = [&](int st) {
+        rcu_backend_free(b);
+        return st;
+    };
+    auto W = [&](const std::string &n) -> const rcu_weight * {
+        auto it = m->w.find(n);
+        return it == m->w.end() ? nullptr : it->second;
+    };
+    auto V = [&](const std::string &n) -> const float * {
+        auto it = m->vec.find(n);
+        return it == m->vec.end() ? nullptr : it->second;
+    };
+    auto need = [&](bool ok, const std::string &what) { return ok ? RCU_OK : set_err(ctx, RCU_ERR_INVALID, "missing or bad tensor " + what); };
+    const uint32_t e = c.n_embd, qd = c.n_head * c.head_dim, kvd = c.n_head_kv * c.head_dim;
+    b->embd = W("token_embd.weight");
+    if (int st = need(b->embd && b->embd->cols == e, "token_embd.weight")) return fail(st);
+    b->out = W("output.weight");
+    if (!b->out) b->out = b->embd;
+    if (int st = need(b->out->cols == e && b->out->rows >= c.n_vocab && gemv_supported(b->out->type), "output.weight"))
+        return fail(st);
+    if (b->out->rows > c.n_vocab) {
+        rcu_weight *s = nullptr;
+        if (int st = rcu_weight_slice_rows(b->out, 0, c.n_vocab, &s)) return fail(st);
+        m->slices.push_back(s);
+        b->out = s;
+    }
+    b->out_norm = V("output_norm.weight");
+    if (int st = need(b->out_norm != nullptr, "output_norm.weight")) return fail(st);
+    for (uint32_t il = 0; il < c.n_layer; il++) {
+        const std::string p = "blk." + std::to_string(il) + ".";
+        LayerW L;
+        if (const rcu_weight *qkv = W(p + "attn_qkv.weight")) {
+            if (int st = need(qkv->rows == (uint64_t)qd + 2 * kvd, p + "attn_qkv.weight")) return fail(st);
+            rcu_weight *a = nullptr, *bb = nullptr, *cc = nullptr;
+            if (int st = rcu_weight_slice_rows(qkv, 0, qd, &a)) return fail(st);
+            m->slices.push_back(a);
+            if (int st = rcu_weight_slice_rows(qkv, qd, kvd, &bb)) return fail(st);
+            m->slices.push_back(bb);
+            if (int st = rcu_weight_slice_rows(qkv, qd + kvd, kvd, &cc)) return fail(st);
+            m->slices.push_back(cc);
+            L.wq = a, L.wk = bb, L.wv = cc;
+        } else {
+            L.wq = W(p + "attn_q.weight"), L.wk = W(p + "attn_k.weight"), L.wv = W(p + "attn_v.weight");
+        }
+        L.wo = W(p + "attn_output.weight");
+        L.gate = W(p + "ffn_gate.weight");
+        L.up = W(p + "ffn_up.weight");
+        L.down = W(p + "ffn_down.weight");
+        if (!L.gate && L.up && L.up->rows == 2ull * c.n_ff) {
+            rcu_weight *g = nullptr, *u = nullptr;
+            if (int st = rcu_weight_slice_rows(L.up, 0, c.n_ff, &g)) return fail(st);
+            m->slices.push_back(g);
+            if (int st = rcu_weight_slice_rows(L.up, c.n_ff, c.n_ff, &u)) return fail(st);
+            m->slices.push_back(u);
+            L.gate = g, L.up = u;
+        }
+        const rcu_weight *mats[7] = {L.wq, L.wk, L.wv, L.wo, L.gate, L.up, L.down};
+        const uint64_t shp[7][2] = {{qd, e}, {kvd, e}, {kvd, e}, {e, qd}, {c.n_ff, e}, {c.n_ff, e}, {e, c.n_ff}};
+        const char *names[7] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+        for (int i = 0; i < 7; i++)
+            if (int st = need(mats[i] && mats[i]->rows == shp[i][0] && mats[i]->cols == shp[i][1] && gemv_supported(mats[i]->type),
+                              p + names[i]))
+                return fail(st);
+        L.attn_norm = V(p + "attn_norm.weight");
+        L.ffn_norm = V(p + "ffn_norm.weight");
+        if (int st = need(L.attn_norm && L.ffn_norm, p + "attn_norm/ffn_norm")) return fail(st);
+        L.q_norm = V(p + "attn_q_norm.weight"), L.k_norm = V(p + "attn_k_norm.weight");
+        L.bq = V(p + "attn_q.bias"), L.bk = V(p + "attn_k.bias"), L.bv = V(p + "attn_v.bias");
+        L.post_attn = V(p + "post_attention_norm.weight"), L.post_ffn = V(p + "post_ffw_norm.weight");
+        L.swa = c.swa_window > 0 && c.swa_pattern > 0 && (il % c.swa_pattern) < c.swa_pattern - 1;
+        b->ff_max = std::max<uint32_t>(b->ff_max, (uint32_t)L.gate->rows);
+        b->layers.push_back(L);
+        const uint64_t slots = L.swa ? std::min<uint64_t>(c.swa_window + b->max_batch, n_ctx) : n_ctx;
+        rcu_kv *kv = nullptr;
+        if (int st = rcu_kv_create(ctx, kv_type, c.n_head_kv, c.head_dim, slots, &kv)) return fail(st);
+        b->kv.push_back(kv);
+    }
+    const uint64_t T = b->max_batch;
+    const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(e, qd), b->ff_max);
+    if (int st = rcu_acts_create(ctx, T, kmax, &b->acts)) return fail(st);
+    struct {
+        float **p;
+        uint64_t n;
+    } bufs[] = {{&b->x, T * e}, {&b->xn, T * e}, {&b->q, T * qd}, {&b->k, T * kvd}, {&b->v, T * kvd}, {&b->att, T * qd},
+                {&b->o, T * e}, {&b->g, T * b->ff_max}, {&b->u, T * b->ff_max}, {&b->logits, T * (uint64_t)c.n_vocab}};
+    for (auto &bf : bufs)
+        if (int st = dalloc(b, (void **)bf.p, bf.n * sizeof(float))) return fail(st);
+    if (int st = dalloc(b, (void **)&b->tokens, T * sizeof(uint32_t))) return fail(st);
+    // RoPE inverse frequencies (ops.rs:65-79), computed like the reference in f32 on the host
+    auto freqs = [&](float base, float fs, float **dst) -> int {
+        const uint32_t half = c.rope_dim / 2;
+        std::vector<float> f(std::max<uint32_t>(half, 1));
+        for (uint32_t i = 0; i < half; i++) f[i] = std::pow(base, -2.0f * (float)i / (float)c.rope_dim) * fs;
+        if (int st = dalloc(b, (void **)dst, f.size() * 4)) return st;
+        RCU_CUDA_TRY(ctx, cudaMemcpy(*dst, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
+        return RCU_OK;
+    };
+    if (int st = freqs(c.rope_base, c.rope_freq_scale, &b->inv_freq)) return fail(st);
+    if (int st = freqs(c.rope_base_swa > 0.0f ? c.rope_base_swa : c.rope_base, 1.0f, &b->inv_freq_swa)) return fail(st);
+    *out = b;
+    return RCU_OK;
+}
+
+void rcu_backend_free(rcu_backend *b) {
+    if (!b) return;
+    for (auto *kv : b->kv) rcu_kv_free(kv);
+    rcu_acts_free(b->acts);
+    cudaSetDevice(b->ctx->device);
+    for (void *p : b->allocs) cudaFree(p);
+    delete b;
+}
+
+uint64_t rcu_backend_max_batch(const rcu_backend *b) { return b ? b->max_batch : 0; }
+uint64_t rcu_backend_n_ctx(const rcu_backend *b) { return b ? b->n_ctx : 0; }
+
+static int32_t check_forward(rcu_backend *b, uint64_t n, uint64_t pos) {
+    if (n == 0) return set_err(b->ctx, RCU_ERR_RUNTIME, "empty batch");  // cpu.rs:215-231
+    if (n > b->max_batch)
+        return set_err(b->ctx, RCU_ERR_RUNTIME,
+                       "batch of " + std::to_string(n) + " tokens exceeds max batch " + std::to_string(b->max_batch));
+    if (pos + n > b->n_ctx)
+        return set_err(b->ctx, RCU_ERR_RUNTIME, "context window full (" + std::to_string(b->n_ctx) + " tokens)");
+    return RCU_OK;
+}
+
+int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, uint64_t pos, int32_t all_logits,
+                            float *logits, uint64_t logits_len) {
+    if (!b || !tokens || !logits) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
+    if (int32_t st = check_forward(b, n, pos)) return st;
+    const uint64_t rows = all_logits ? n : 1;
+    if (logits_len < rows * b->m->cfg.n_vocab) return set_err(b->ctx, RCU_ERR_RUNTIME, "logits buffer too small");
+    for (uint64_t i = 0; i < n; i++)
+        if (tokens[i] >= b->embd->rows) return set_err(b->ctx, RCU_ERR_RUNTIME, "token id " + std::to_string(tokens[i]) + " out of range");
+    rcu_ctx *ctx = b->ctx;
+    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int32_t st = forward_dev(b, n, pos, all_logits != 0, b->logits)) return st;
+    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(logits, b->logits, rows * b->m->cfg.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return rcu_sync(ctx);
+}
+
+int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, uint64_t n, uint64_t pos,
+                                   int32_t all_logits, float *logits_dev) {
+    if (!b || !tokens_dev || !logits_dev) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
+    if (int32_t st = check_forward(b, n, pos)) return st;
+    rcu_ctx *ctx = b->ctx;
+    if (tokens_dev != b->tokens)
+        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens_dev, n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    return forward_dev(b, n, pos, all_logits != 0, logits_dev);
+}
+
+int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out) {
+    if (!b || !host_out) return RCU_ERR_INVALID;
+    const uint64_t n = b->hidden_rows * b->m->cfg.n_embd;
+    if (rows_out) *rows_out = b->hidden_rows;
+    if (cap < n) return set_err(b->ctx, RCU_ERR_INVALID, "hidden buffer too small");
+    RCU_CUDA_TRY(b->ctx, cudaMemcpyAsync(host_out, b->xn, n * 4, cudaMemcpyDeviceToHost, b->ctx->stream));
+    RCU_CUDA_TRY(b->ctx, cudaStreamSynchronize(b->ctx->stream));
+    return RCU_OK;
+}
+
+}  // extern "C"
