@@ -1,0 +1,214 @@
+"""Transformer forward on the device: the reference's `Backend` trait (model/mod.rs:303-320)
+implemented by the CUDA library's scheduler (rcu_model_* / rcu_backend_* of rie_cuda.h).
+
+  Model(ctx, config)                  Model::load without the file: tensors by GGUF name
+  CudaBackend(model, n_ctx, ...)      CpuBackend::with_kv_type (model/cpu.rs:100-177)
+  CudaBackend.forward(tokens, pos)    Backend::forward (model/mod.rs:313)
+  CudaBackend.hidden()                Backend::hidden (model/mod.rs:318)
+  synthetic_tensors(spec, gen)        the tensor set of SyntheticSpec::build (testing.rs:229-383)
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import GgmlType, KvType, _check, _dptr, _lib
+
+
+class ModelConfig(C.Structure):
+    """rcu_model_config (flattened reference ModelConfig, model/config.rs:54-104)."""
+    _fields_ = [("n_vocab", C.c_uint32), ("n_embd", C.c_uint32), ("n_layer", C.c_uint32), ("n_head", C.c_uint32),
+                ("n_head_kv", C.c_uint32), ("head_dim", C.c_uint32), ("n_ff", C.c_uint32), ("rope_dim", C.c_uint32),
+                ("rope_neox", C.c_int32), ("rope_base", C.c_float), ("rope_freq_scale", C.c_float),
+                ("rms_eps", C.c_float), ("attn_scale", C.c_float), ("embd_scale", C.c_float),
+                ("residual_scale", C.c_float), ("logit_scale", C.c_float), ("attn_softcap", C.c_float),
+                ("final_softcap", C.c_float), ("swa_window", C.c_uint32), ("swa_pattern", C.c_uint32),
+                ("rope_base_swa", C.c_float), ("act", C.c_int32), ("n_expert", C.c_uint32),
+                ("n_expert_used", C.c_uint32), ("n_ff_exp", C.c_uint32), ("expert_norm_topk", C.c_int32),
+                ("expert_unit_weights", C.c_int32)]
+
+
+
+
+@dataclass
+class SyntheticSpec:
+    """Shape of a synthetic transformer (testing.rs:93-124)."""
+    arch: str = "qwen3"
+    n_vocab: int = 384
+    n_embd: int = 256
+    n_layer: int = 2
+    n_head: int = 4
+    n_head_kv: int = 2
+    head_dim: int = 64
+    n_ff: int = 512
+    rope_dim: int = 64
+    wtype: int = GgmlType.Q4_0
+    embd_type: int = GgmlType.Q8_0
+    tied_output: bool = False
+    qkv_bias: bool = False
+    qk_norm: bool = True
+    post_norms: bool = False
+    fused: bool = False
+    swa_window: int = 0
+    rope_base: float = 10000.0
+    rms_eps: float = 1e-6
+    type_overrides: dict = field(default_factory=dict)  # per-tensor-suffix ggml type (Q4_K_M style mixes)
+
+    @classmethod
+    def tiny(cls, arch: str, wtype: int) -> "SyntheticSpec":  # testing.rs:127-154
+        return cls(arch=arch, wtype=wtype, embd_type=GgmlType.Q8_0 if GgmlType(wtype).block_size > 1 else wtype,
+                   qkv_bias=arch == "qwen2", qk_norm=arch in ("qwen3", "gemma3"),
+                   post_norms=arch in ("gemma2", "gemma3"), fused=arch == "phi3",
+                   swa_window=5 if arch in ("gemma2", "gemma3") else 0)
+
+    def config(self) -> ModelConfig:
+        """ModelConfig::from_gguf rules for the synthetic metadata (model/config.rs:106-247)."""
+        gemma = self.arch in ("gemma", "gemma2", "gemma3")
+        c = ModelConfig()
+        c.n_vocab, c.n_embd, c.n_layer = self.n_vocab, self.n_embd, self.n_layer
+        c.n_head, c.n_head_kv, c.head_dim, c.n_ff = self.n_head, self.n_head_kv, self.head_dim, self.n_ff
+        c.rope_dim = self.rope_dim
+        c.rope_neox = int(self.arch in ("qwen2", "qwen3", "phi3", "gemma", "gemma2", "gemma3", "qwen3moe", "qwen2moe"))
+        c.rope_base = 1_000_000.0 if self.arch == "gemma3" else self.rope_base
+        c.rope_freq_scale = 1.0
+        c.rms_eps = self.rms_eps
+        c.attn_scale = 1.0 / np.sqrt(np.float32(self.head_dim))
+        c.embd_scale = float(np.sqrt(np.float32(self.n_embd))) if gemma else 1.0
+        c.residual_scale = 1.0
+        c.logit_scale = 1.0
+        c.attn_softcap = 50.0 if self.arch == "gemma2" else 0.0
+        c.final_softcap = 30.0 if self.arch == "gemma2" else 0.0
+        c.swa_window = self.swa_window
+        c.swa_pattern = 2 if self.arch == "gemma2" else (6 if self.arch == "gemma3" else 0)
+        c.rope_base_swa = 10000.0 if self.arch == "gemma3" else 0.0
+        c.act = 1 if gemma else 0
+        return c
+
+    def type_of(self, name: str) -> int:
+        for suffix, t in self.type_overrides.items():
+            if name.endswith(suffix):
+                return t
+        return self.wtype
+
+
+def synthetic_tensors(spec: SyntheticSpec, weight, vec_f32, norm):
+    """Yield (name, ggml_type, rows, cols, bytes) in SyntheticSpec::build order (testing.rs:314-381).
+
+    weight(type, rows, cols) -> uint8 GGUF bytes; vec_f32(n, scale) / norm(n) -> float32."""
+    e, ff = spec.n_embd, spec.n_ff
+    qd, kvd, hd = spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim, spec.head_dim
+    yield "token_embd.weight", spec.embd_type, spec.n_vocab, e, weight(spec.embd_type, spec.n_vocab, e)
+    yield "output_norm.weight", GgmlType.F32, 1, e, norm(e)
+    if not spec.tied_output:
+        yield "output.weight", spec.embd_type, spec.n_vocab, e, weight(spec.embd_type, spec.n_vocab, e)
+    for il in range(spec.n_layer):
+        p = f"blk.{il}."
+        yield p + "attn_norm.weight", GgmlType.F32, 1, e, norm(e)
+        if spec.fused:
+            t = spec.type_of("attn_qkv.weight")
+            yield p + "attn_qkv.weight", t, qd + 2 * kvd, e, weight(t, qd + 2 * kvd, e)
+        else:
+            for nm, rows in (("attn_q.weight", qd), ("attn_k.weight", kvd), ("attn_v.weight", kvd)):
+                t = spec.type_of(nm)
+                yield p + nm, t, rows, e, weight(t, rows, e)
+        if spec.qkv_bias:
+            yield p + "attn_q.bias", GgmlType.F32, 1, qd, vec_f32(qd, 0.1)
+            yield p + "attn_k.bias", GgmlType.F32, 1, kvd, vec_f32(kvd, 0.1)
+            yield p + "attn_v.bias", GgmlType.F32, 1, kvd, vec_f32(kvd, 0.1)
+        if spec.qk_norm:
+            yield p + "attn_q_norm.weight", GgmlType.F32, 1, hd, norm(hd)
+            yield p + "attn_k_norm.weight", GgmlType.F32, 1, hd, norm(hd)
+        t = spec.type_of("attn_output.weight")
+        yield p + "attn_output.weight", t, e, qd, weight(t, e, qd)
+        if spec.post_norms:
+            yield p + "post_attention_norm.weight", GgmlType.F32, 1, e, norm(e)
+            yield p + "post_ffw_norm.weight", GgmlType.F32, 1, e, norm(e)
+        yield p + "ffn_norm.weight", GgmlType.F32, 1, e, norm(e)
+        if spec.fused:
+            t = spec.type_of("ffn_up.weight")
+            yield p + "ffn_up.weight", t, 2 * ff, e, weight(t, 2 * ff, e)
+            t = spec.type_of("ffn_down.weight")
+            yield p + "ffn_down.weight", t, e, ff, weight(t, e, ff)
+        else:
+            for nm, rows, cols in (("ffn_gate.weight", ff, e), ("ffn_up.weight", ff, e), ("ffn_down.weight", e, ff)):
+                t = spec.type_of(nm)
+                yield p + nm, t, rows, cols, weight(t, rows, cols)
+
+
+class Model:
+    def __init__(self, ctx, cfg: ModelConfig):
+        self.ctx, self.cfg = ctx, cfg
+        lib = _lib.load()
+        self.ptr = C.c_void_p()
+        _check(ctx.ptr, lib.rcu_model_create(ctx.ptr, C.byref(cfg), C.byref(self.ptr)))
+
+    def set_tensor(self, name: str, ty: int, rows: int, cols: int, data) -> None:
+        a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        _check(self.ctx.ptr, _lib.load().rcu_model_set_tensor(self.ptr, name.encode(), int(ty), rows, cols,
+                                                              a.ctypes.data_as(C.c_void_p)))
+
+    def free(self):
+        if getattr(self, "ptr", None):
+            _lib.load().rcu_model_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class CudaBackend:
+    """`impl Backend for CudaBackend`: forward / hidden / max_batch / n_ctx."""
+
+    def __init__(self, model: Model, n_ctx: int, max_batch: int, kv_type: KvType = KvType.F16):
+        self.model, self.ctx = model, model.ctx
+        self.ptr = C.c_void_p()
+        _check(self.ctx.ptr, _lib.load().rcu_backend_create(model.ptr, n_ctx, max_batch, int(kv_type),
+                                                            C.byref(self.ptr)))
+        self.n_vocab = model.cfg.n_vocab
+        self.n_embd = model.cfg.n_embd
+
+    def name(self) -> str:
+        return "CUDA (sm_100a)"
+
+    def max_batch(self) -> int:
+        return int(_lib.load().rcu_backend_max_batch(self.ptr))
+
+    def n_ctx(self) -> int:
+        return int(_lib.load().rcu_backend_n_ctx(self.ptr))
+
+    def forward(self, tokens, pos: int, all_logits: bool = False) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        rows = tok.size if all_logits else 1
+        out = np.zeros((rows, self.n_vocab), dtype=np.float32)
+        _check(self.ctx.ptr, _lib.load().rcu_backend_forward(self.ptr, tok.ctypes.data_as(C.c_void_p), tok.size, pos,
+                                                             int(all_logits), out.ctypes.data_as(C.c_void_p),
+                                                             out.size))
+        return out
+
+    def forward_device(self, tokens_dev, n: int, pos: int, logits_dev, all_logits: bool = False) -> None:
+        _check(self.ctx.ptr, _lib.load().rcu_backend_forward_device(self.ptr, C.c_void_p(_dptr(tokens_dev)), n, pos,
+                                                                    int(all_logits), C.c_void_p(_dptr(logits_dev))))
+
+    def hidden(self) -> np.ndarray | None:
+        rows = C.c_uint64(0)
+        cap = 4096 * self.n_embd
+        buf = np.zeros(cap, dtype=np.float32)
+        _check(self.ctx.ptr, _lib.load().rcu_backend_hidden(self.ptr, buf.ctypes.data_as(C.c_void_p), cap,
+                                                            C.byref(rows)))
+        return buf[: rows.value * self.n_embd].reshape(rows.value, self.n_embd) if rows.value else None
+
+    def free(self):
+        if getattr(self, "ptr", None):
+            _lib.load().rcu_backend_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,115 @@
+"""Device forward scheduler vs the oracle's restatement of the reference CPU forward
+(model/cpu.rs:210-409) on the synthetic model families of testing.rs (tiny presets).
+
+Logits are compared like the reference's own model tests compare two implementations
+(tests/model.rs:340-375, assert_close against the larger magnitude), here at 1e-3 for the
+int8 paths (the two sides see the same quantized activations up to f32 accumulation order).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-3
+
+
+def close(a, b, rtol=RTOL, what=""):
+    scale = max(float(np.max(np.abs(b))), 1e-6)
+    err = float(np.max(np.abs(a - b)))
+    assert err <= rtol * scale, f"{what}: max err {err} > {rtol} * {scale}"
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+    import rust_interference_engine_b200 as rie
+    from rust_interference_engine_b200 import model as M
+    ctx = rie.Context(0, torch.cuda.current_stream())
+    return torch, rie, M, ctx
+
+
+def build_pair(env, spec, kv_type, n_ctx=64, max_batch=16, seed=1):
+    torch, rie, M, ctx = env
+    rng = O.Rng(seed)
+    cfg = spec.config()
+    gm = M.Model(ctx, cfg)
+    om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(cfg)))
+    weight = lambda t, r, c: rng.weight(int(t), r, c)
+    vec = lambda n, s: rng.vec(n, s)
+    norm = lambda n: (1.0 + 0.1 * rng.vec(n, 1.0)).astype(np.float32)
+    for name, t, rows, cols, data in M.synthetic_tensors(spec, weight, vec, norm):
+        gm.set_tensor(name, int(t), rows, cols, data)
+        om.set_tensor(name, int(t), rows, cols, data)
+    gb = M.CudaBackend(gm, n_ctx, max_batch, rie.KvType(kv_type))
+    ob = O.OracleBackend(om, n_ctx, max_batch, kv_type=kv_type, n_threads=8)
+    return gb, ob, (gm, om)
+
+
+def run_compare(env, spec, kv_type, rtol=RTOL):
+    gb, ob, keep = build_pair(env, spec, kv_type)
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, spec.n_vocab, 7).astype(np.uint32)
+    g = gb.forward(prompt, 0, all_logits=True)
+    o = ob.forward(prompt, 0, all_logits=True)
+    close(g, o, rtol, "prompt")
+    pos = len(prompt)
+    for step in range(3):
+        tok = np.array([int(np.argmax(o[-1]))], dtype=np.uint32)
+        g = gb.forward(tok, pos)
+        o = ob.forward(tok, pos)
+        close(g, o, rtol, f"decode step {step}")
+        pos += 1
+    return gb
+
+
+WT = [O.Q4_0, O.Q8_0, O.Q4_K, O.Q6_K, O.Q5_0, O.Q5_K, O.Q4_1]
+
+
+@pytest.mark.parametrize("wtype", WT, ids=[O.TYPE_NAMES[t] for t in WT])
+def test_qwen3_forward_matches_oracle(env, wtype):
+    from rust_interference_engine_b200 import model as M
+    run_compare(env, M.SyntheticSpec.tiny("qwen3", wtype), O.KV_F16)
+
+
+@pytest.mark.parametrize("arch", ["llama", "qwen2", "gemma2", "phi3"])
+def test_arch_variants_match_oracle(env, arch):
+    from rust_interference_engine_b200 import model as M
+    spec = M.SyntheticSpec.tiny(arch, O.Q4_K if arch != "phi3" else O.Q4_0)
+    run_compare(env, spec, O.KV_F16)
+
+
+@pytest.mark.parametrize("kv", [O.KV_Q8_0, O.KV_TURBO4], ids=["q8_0", "turbo4"])
+def test_quantized_kv_forward_matches_oracle(env, kv):
+    from rust_interference_engine_b200 import model as M
+    run_compare(env, M.SyntheticSpec.tiny("qwen3", O.Q4_K), kv, rtol=2e-3)
+
+
+def test_q4_k_m_mix_and_hidden(env):
+    from rust_interference_engine_b200 import model as M
+    # Qwen3 Q4_K_M-style mix: attn_v and ffn_down in Q6_K, the rest Q4_K; embeddings Q6_K
+    spec = M.SyntheticSpec.tiny("qwen3", O.Q4_K)
+    spec.embd_type = O.Q6_K
+    spec.type_overrides = {"attn_v.weight": O.Q6_K, "ffn_down.weight": O.Q6_K}
+    gb, ob, keep = build_pair(env, spec, O.KV_F16)
+    toks = np.arange(5, dtype=np.uint32) * 7
+    g = gb.forward(toks, 0)
+    o = ob.forward(toks, 0)
+    close(g, o)
+    h = gb.hidden()
+    assert h is not None and h.shape == (1, spec.n_embd)
+
+
+def test_forward_errors(env):
+    torch, rie, M, ctx = env
+    gb, ob, keep = build_pair(env, M.SyntheticSpec.tiny("qwen3", O.Q4_0), O.KV_F16, n_ctx=16, max_batch=4)
+    with pytest.raises(rie.RcuError, match="empty batch"):
+        gb.forward(np.zeros(0, np.uint32), 0)
+    with pytest.raises(rie.RcuError, match="exceeds max batch"):
+        gb.forward(np.zeros(5, np.uint32), 0)
+    with pytest.raises(rie.RcuError, match="context window full"):
+        gb.forward(np.zeros(2, np.uint32), 15)
+    with pytest.raises(rie.RcuError, match="out of range"):
+        gb.forward(np.array([10_000], np.uint32), 0)
+    # the backend stays usable after rejected calls
+    close(gb.forward(np.array([3, 4], np.uint32), 0), ob.forward(np.array([3, 4], np.uint32), 0))
