@@ -191,6 +191,19 @@ RCU_API int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *token
 /* Backend::hidden (model/mod.rs:318): final normed rows of the last forward (rows x n_embd). */
 RCU_API int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out);
 
+/* ---- allocation-free matmul (no counterpart in the reference) ------------------------ */
+/* W . X for f32 activations x_dev (n_tok x w->cols, device), out_dev[t * ld + r], without
+ * allocating any device memory: the activations are quantized into a fixed scratch area
+ * compiled into this library (about 322 KB, kept on every GPU that loads it until exit).
+ * For callers that cannot cudaMalloc at matmul time, e.g. because all device memory is
+ * owned by their own pool or by PyTorch's caching allocator. Limits: n_tok <= 8 and
+ * w->cols <= 16384 (larger calls return RCU_ERR_INVALID). All calls share the scratch, so
+ * calls that overlap on the GPU race; order them (one stream per device). The first call
+ * on a device looks the scratch address up once (cudaGetSymbolAddress): make that first
+ * call before any stream capture. */
+RCU_API int32_t rcu_matmul_f32_static(rcu_ctx *ctx, const rcu_weight *w, const float *x_dev, uint64_t n_tok,
+                                      float *out_dev, uint64_t ld);
+
 #ifdef __cplusplus
 }
 #endif

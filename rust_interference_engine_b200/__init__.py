@@ -28,7 +28,7 @@ from . import _lib
 from ._lib import RcuError, RcuJob
 
 __all__ = ["GgmlType", "ActFormat", "KvType", "Rounding", "Context", "Weight", "QuantActs", "MatmulJob",
-           "matmul", "matmul_multi", "formats_for", "block_sums", "LayerCache", "attention", "turbo", "RcuError"]
+           "matmul", "matmul_multi", "matmul_f32_static", "formats_for", "block_sums", "LayerCache", "attention", "turbo", "RcuError"]
 
 
 class GgmlType(enum.IntEnum):  # quant/mod.rs:15-68 (GGUF ids)
@@ -270,6 +270,18 @@ def matmul_multi(ctx: Context, acts: QuantActs, jobs: Sequence[MatmulJob]) -> No
 
 def matmul(ctx: Context, acts: QuantActs, w: Weight, out) -> None:  # matmul.rs:130-133
     matmul_multi(ctx, acts, [MatmulJob(w, out, w.rows)])
+
+
+def matmul_f32_static(ctx: Context, w: Weight, x, n_tok: int, out, ld: int | None = None) -> None:
+    """W . X for f32 activations without allocating device memory.
+
+    For callers that cannot cudaMalloc when they run a matmul (their device memory belongs
+    to a pool such as PyTorch's caching allocator, or allocation would stall a decode step):
+    the activations are quantized into a fixed scratch area inside the library. At most 8
+    tokens and rows of at most 16384 values; calls that overlap on the GPU share that
+    scratch and must not run concurrently."""
+    _check(ctx.ptr, ctx._lib.rcu_matmul_f32_static(ctx.ptr, w.ptr, C.c_void_p(_dptr(x)), n_tok,
+                                                   C.c_void_p(_dptr(out)), w.rows if ld is None else ld))
 
 
 def block_sums(ctx: Context, acts: QuantActs, w: Weight, row: int, tok: int, out) -> None:

@@ -57,6 +57,7 @@ SIGNATURES = {
     "rcu_backend_forward": (I32, [P, P, U64, U64, I32, P, U64]),
     "rcu_backend_forward_device": (I32, [P, P, U64, U64, I32, P]),
     "rcu_backend_hidden": (I32, [P, P, U64, C.POINTER(U64)]),
+    "rcu_matmul_f32_static": (I32, [P, P, P, U64, P, U64]),
 }
 
 
