@@ -372,6 +372,215 @@ def run_prefill(args, world, rank, local):
     }
 
 
+# ---- workload: config 3 Qwen3-8B-shape Q4_K_M decode ------------------------------------
+QWEN3_8B = dict(arch="qwen3", n_vocab=151936, n_embd=4096, n_layer=36, n_head=32, n_head_kv=8, head_dim=128,
+                n_ff=12288, rope_dim=128, rope_base=1_000_000.0, rms_eps=1e-6)
+DEC_PROMPT = 512
+
+
+def qwen3_8b_spec(n_layer=None):
+    from rust_interference_engine_b200 import GgmlType as G
+    from rust_interference_engine_b200.model import SyntheticSpec
+    kw = dict(QWEN3_8B)
+    if n_layer is not None:
+        kw["n_layer"] = n_layer
+    return SyntheticSpec(wtype=G.Q4_K, embd_type=G.Q6_K, qk_norm=True,
+                         type_overrides={"attn_v.weight": G.Q6_K, "ffn_down.weight": G.Q6_K}, **kw)
+
+
+class RandomBlocks:
+    """random_weight semantics (testing.rs:46-91) at numpy speed: random bytes with valid f16
+    scale fields U[0.5, 1) x per-type scale (negative 30 % of the time where the reference
+    allows it). The bytes differ from the reference's xorshift stream; the distribution is
+    the one `rie bench --synthetic` uses."""
+
+    SCALE = {2: 0.01, 3: 0.01, 6: 0.005, 7: 0.005, 8: 0.001, 12: 0.001, 13: 0.0007, 14: 0.0001}
+    OFFS = {2: [0], 6: [0], 8: [0], 3: [0, 2], 7: [0, 2], 12: [0, 2], 13: [0, 2], 14: [208]}
+    BB = {2: 18, 3: 20, 6: 22, 7: 24, 8: 34, 12: 144, 13: 176, 14: 210}
+    BS = {2: 32, 3: 32, 6: 32, 7: 32, 8: 32, 12: 256, 13: 256, 14: 256}
+
+    def __init__(self, seed):
+        self.rng = np.random.default_rng(seed)
+
+    def weight(self, t, rows, cols):
+        t = int(t)
+        nb = rows * cols // self.BS[t]
+        data = np.frombuffer(self.rng.bytes(nb * self.BB[t]), dtype=np.uint8).reshape(nb, self.BB[t]).copy()
+        for i, off in enumerate(self.OFFS[t]):
+            v = (self.rng.random(nb, dtype=np.float32) * 0.5 + 0.5) * self.SCALE[t]
+            if i == 0 and t in (2, 6, 8, 14):
+                v = np.where(self.rng.random(nb, dtype=np.float32) < 0.3, -v, v)
+            if i == 1 and t in (3, 7):
+                v = -v * 8.0
+            data[:, off:off + 2] = v.astype(np.float16).view(np.uint8).reshape(nb, 2)
+        return data.reshape(-1)
+
+    def vec(self, n, scale):
+        return (self.rng.random(n, dtype=np.float32) * 2 - 1) * scale
+
+    def norm(self, n):
+        return (1.0 + 0.1 * (self.rng.random(n, dtype=np.float32) * 2 - 1)).astype(np.float32)
+
+
+def weight_bytes_per_token(spec):
+    from rust_interference_engine_b200 import GgmlType as G
+    e, ff, qd, kvd = spec.n_embd, spec.n_ff, spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim
+    per_layer = sum(G(spec.type_of(n)).row_bytes(c) * r for n, r, c in (
+        ("attn_q.weight", qd, e), ("attn_k.weight", kvd, e), ("attn_v.weight", kvd, e), ("attn_output.weight", e, qd),
+        ("ffn_gate.weight", ff, e), ("ffn_up.weight", ff, e), ("ffn_down.weight", e, ff)))
+    head = G(spec.embd_type).row_bytes(e) * spec.n_vocab
+    return spec.n_layer * per_layer + head
+
+
+def run_decode(args, world, rank, local):
+    import torch
+
+    import rust_interference_engine_b200 as rie
+    from rust_interference_engine_b200 import model as M
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    spec = qwen3_8b_spec()
+    gen = RandomBlocks(3)
+    model = M.Model(ctx, spec.config())
+    t_build = time.perf_counter()
+    for name, t, rows, cols, data in M.synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
+        model.set_tensor(name, int(t), rows, cols, data)
+    t_build = time.perf_counter() - t_build
+    n_gen = max(args.warmup, 3) + args.steps
+    n_ctx = DEC_PROMPT + n_gen + 1
+    be = M.CudaBackend(model, n_ctx, 64, rie.KvType.F16)
+    prompt = np.random.default_rng(4).integers(0, spec.n_vocab, DEC_PROMPT).astype(np.uint32)
+    gen_tokens = torch.from_numpy(np.random.default_rng(5).integers(0, spec.n_vocab, n_gen).astype(np.int32)).cuda()
+    logits = torch.zeros(spec.n_vocab, device="cuda")
+    prompt_d = torch.from_numpy(prompt.astype(np.int32)).cuda()
+
+    def prefill():
+        for p0 in range(0, DEC_PROMPT, 64):  # Engine::eval_tokens chunks at n_batch (engine.rs:263-269)
+            be.forward_device(prompt_d[p0:], min(64, DEC_PROMPT - p0), p0, logits)
+
+    prefill()  # warm: kernel attributes, L2
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    prefill()
+    p1.record(stream)
+    torch.cuda.synchronize()
+    pp_tps = DEC_PROMPT / (p0.elapsed_time(p1) * 1e-3)
+    pos = DEC_PROMPT
+    for i in range(max(args.warmup, 3)):  # the second decode step captures the CUDA graph
+        be.forward_device(gen_tokens[i:], 1, pos, logits)
+        pos += 1
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            be.forward_device(gen_tokens[max(args.warmup, 3) + i:], 1, pos + i, logits)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = dist_max(t0.elapsed_time(t1) / args.steps, world)
+    finite = bool(torch.isfinite(logits).all())
+
+    # e2e: the host API (Backend::forward), token in and logits out through host memory
+    be2 = M.CudaBackend(model, n_ctx, 64, rie.KvType.F16)
+    for p0_ in range(0, DEC_PROMPT, 64):
+        be2.forward(prompt[p0_:p0_ + 64], p0_, False)
+    pos2, tok = DEC_PROMPT, np.array([1], dtype=np.uint32)
+    for i in range(max(args.warmup, 3)):
+        be2.forward(tok, pos2)
+        pos2 += 1
+    e0 = time.perf_counter()
+    for i in range(args.steps):
+        out = be2.forward(tok, pos2)
+        tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)  # greedy, as Engine::bench
+        pos2 += 1
+    e2e_s = time.perf_counter() - e0
+    e2e_tps = args.steps / e2e_s
+    del be2
+
+    # dominant kernel: the gate+up GEMV launch (2 x 12288 x 4096 Q4_K), timed alone over
+    # 8 layers' worth of distinct weights (453 MB > L2)
+    gu = [rie.Weight.upload(ctx, rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd, gen.weight(rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd))
+          for _ in range(16)]
+    xg = torch.randn(1, spec.n_embd, device="cuda")
+    acts = rie.QuantActs(ctx, 1, spec.n_embd)
+    acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
+    og = torch.zeros(2, spec.n_ff, device="cuda")
+    jobs = [[rie.MatmulJob(gu[2 * i], og[0]), rie.MatmulJob(gu[2 * i + 1], og[1])] for i in range(8)]
+    for j in jobs:
+        rie.matmul_multi(ctx, acts, j)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 40
+    g0.record(stream)
+    for r in range(reps):
+        rie.matmul_multi(ctx, acts, jobs[r % 8])
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gemv_ms = g0.elapsed_time(g1) / reps
+    gemv_bytes = 2 * rie.GgmlType.Q4_K.row_bytes(spec.n_embd) * spec.n_ff
+    peak, peak_kind = peaks()
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    wbytes = weight_bytes_per_token(spec)
+    kv_bytes = 2 * spec.n_layer * spec.n_head_kv * spec.head_dim * 2 * (pos + args.steps // 2)
+    return {
+        "metric": "Qwen3-8B-shape Q4_K_M decode tg tok/s (config 3, batch 1)",
+        "value": world * 1000.0 / ms,
+        "unit": "tok/s",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "int8 x Q4_K/Q6_K blocks (Q8_K activations), f32 glue, f16 KV",
+        "config": {"workload": "qwen3_8b_q4_k_m_decode_config3", "layers": spec.n_layer, "hidden": spec.n_embd,
+                   "ffn": spec.n_ff, "heads": f"{spec.n_head}/{spec.n_head_kv}x{spec.head_dim}",
+                   "vocab": spec.n_vocab, "prompt": DEC_PROMPT, "context_at_timing": pos,
+                   "weight_bytes_per_token": wbytes, "kv": "f16", "batch": 1,
+                   "l2": "inputs larger than L2 (4.9 GB of weights streamed per token)",
+                   "parallelism": f"replicas x{world}", "decode": "CUDA graph replay per token",
+                   "pp_tok_s": pp_tps, "model_build_s": t_build},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_gate_up"),
+                     "kernel": "k_gemv<1,16> (gate+up, 2 x 12288 x 4096 Q4_K)", "bytes_per_launch": gemv_bytes,
+                     "launch_ms": gemv_ms,
+                     "whole_step_weight_gb_s": (wbytes + kv_bytes) / (ms * 1e-3) / 1e9},
+        "e2e": {"value": world * e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": spec.n_vocab * 4, "ms_per_step": 1000.0 * e2e_s / args.steps,
+                "api": "CudaBackend.forward (rcu_backend_forward, host tokens/logits, greedy)"},
+        "gpu_launches": args.steps * (17 * spec.n_layer + 5),
+        "clocks": clk.summary(),
+        "check": {"logits_finite": finite},
+    }
+
+
+def cpu_decode_sample(seconds: float, threads: int):
+    """The oracle's restated CPU forward (AVX2 tier, all host threads) decoding on the same
+    model shape: a 16-token prompt, then single-token steps until `seconds` elapse."""
+    import oracle as O
+    from rust_interference_engine_b200.model import synthetic_tensors
+    spec = qwen3_8b_spec()
+    gen = RandomBlocks(3)
+    om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(spec.config())))
+    for name, t, rows, cols, data in synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
+        om.set_tensor(name, int(t), rows, cols, data)
+    ob = O.OracleBackend(om, 256, 16, kv_type=O.KV_F16, n_threads=threads)
+    ob.forward(np.arange(16, dtype=np.uint32), 0)
+    n, pos, t0 = 0, 16, time.perf_counter()
+    tok = np.array([1], dtype=np.uint32)
+    while True:
+        out = ob.forward(tok, pos)
+        tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
+        n, pos = n + 1, pos + 1
+        el = time.perf_counter() - t0
+        if el >= seconds or pos >= 255:
+            break
+    return {"value": n / el, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of the 36-layer Qwen3-8B-shape Q4_K_M model at context 16-{pos}, {el:.1f} s",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
 def cpu_prefill_sample(seconds: float, threads: int):
     """The oracle's AVX2 matmul (4-token tiles, RIE's chunking) on 64-token slices of config 2."""
     import oracle as O
@@ -392,8 +601,12 @@ def cpu_prefill_sample(seconds: float, threads: int):
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
-WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample)}
+WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample),
+             "decode": (run_decode, cpu_decode_sample)}
 META = {  # metric / unit / config of each workload, shared by both arms
+    "decode": {"metric": "Qwen3-8B-shape Q4_K_M decode tg tok/s (config 3, batch 1)", "unit": "tok/s",
+               "dtype": "int8 x Q4_K/Q6_K blocks (Q8_K activations), f32 glue, f16 KV",
+               "workload": "qwen3_8b_q4_k_m_decode_config3"},
     "gemv": {"metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)", "unit": "GB/s",
              "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "workload": "gemv_q4_0_6144x2048_config1"},
     "prefill": {"metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)", "unit": "TOPS",
@@ -405,9 +618,9 @@ META = {  # metric / unit / config of each workload, shared by both arms
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -8,6 +8,7 @@
 // post-norm + residual; then the output norm and head. All work is queued on the context
 // stream; the host only validates arguments and launches.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -49,9 +50,19 @@ struct rcu_backend {
     float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
     float *g = nullptr, *u = nullptr, *logits = nullptr, *inv_freq = nullptr, *inv_freq_swa = nullptr;
     uint32_t *tokens = nullptr;
+    uint64_t *pos_dev = nullptr;  // position of the batch, read by the kernels (graph replay)
+    float *attn_scratch = nullptr;
     uint32_t ff_max = 0;
     uint64_t hidden_rows = 0;
     std::vector<void *> allocs;
+    // The backend runs on its own stream (stream capture needs a non-default stream) and
+    // joins the context stream with events on entry and exit.
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    bool use_graphs = true;
+    int decode_calls = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
 };
 
 namespace rcu {
@@ -206,7 +217,7 @@ __global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, float *
                            const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
                            const float *__restrict__ qn, const float *__restrict__ kn, const float *__restrict__ inv_freq,
                            uint32_t n_tok, uint32_t n_head, uint32_t n_kv, uint32_t hd, uint32_t rope_dim, int neox,
-                           uint64_t pos0, float eps, float attn_scale) {
+                           const uint64_t *__restrict__ pos_ptr, float eps, float attn_scale) {
     __shared__ float buf[4][512];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t per_tok = n_head + 2 * n_kv;
@@ -237,7 +248,7 @@ __global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, float *
     }
     if (rope) {
         const uint32_t half = rope_dim / 2;
-        const float pos = (float)(pos0 + t);
+        const float pos = (float)(*pos_ptr + t);
         for (uint32_t i = lane; i < half; i += 32) {
             float sn, cs;
             sincosf(pos * inv_freq[i], &sn, &cs);
@@ -264,6 +275,8 @@ __global__ void k_glu(float *__restrict__ g, const float *__restrict__ u, uint64
     g[i] = f * u[i];
 }
 
+__global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos) { *pos_dev = pos; }
+
 __global__ void k_logit_post(float *__restrict__ l, uint64_t n, float scale, float cap) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -288,7 +301,10 @@ static int matmul(rcu_backend *b, const float *x, uint32_t n, uint32_t k, std::v
     return rcu_matmul_multi(b->ctx, b->acts, jobs.data(), jobs.size());
 }
 
-static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits) {
+// One forward of n tokens at the position stored in b->pos_dev (pos0 is its host copy, used
+// to size the attention grid unless `fixed_grid`, which sizes it for the whole cache so the
+// launch sequence does not depend on the position and can be replayed as a graph).
+static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
     rcu_ctx *ctx = b->ctx;
     const rcu_model_config &c = b->m->cfg;
     cudaStream_t s = ctx->stream;
@@ -303,11 +319,13 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         const uint64_t items = n * (c.n_head + 2 * c.n_head_kv);
         k_qkv_post<<<(uint32_t)((items + 3) / 4), 128, 0, s>>>(b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
                                                               swa_rope ? b->inv_freq_swa : b->inv_freq, (uint32_t)n,
-                                                              c.n_head, c.n_head_kv, hd, c.rope_dim, c.rope_neox, pos0,
-                                                              c.rms_eps, c.attn_scale);
-        st = rcu_kv_store(ctx, b->kv[il], b->k, b->v, n, pos0);
+                                                              c.n_head, c.n_head_kv, hd, c.rope_dim, c.rope_neox,
+                                                              b->pos_dev, c.rms_eps, c.attn_scale);
+        st = launch_kv_store(ctx, b->kv[il], b->k, b->v, n, pos0, b->pos_dev);
         if (st) return st;
-        st = rcu_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, L.swa ? c.swa_window : 0, c.attn_softcap, b->att);
+        const uint64_t window = L.swa ? c.swa_window : 0;
+        st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, b->att,
+                              fixed_grid ? attention_max_splits(b->kv[il], window) : 0, b->attn_scratch);
         if (st) return st;
         st = matmul(b, b->att, (uint32_t)n, qd, {{L.wo, b->o, e}});
         if (st) return st;
@@ -523,6 +541,18 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
     for (auto &bf : bufs)
         if (int st = dalloc(b, (void **)bf.p, bf.n * sizeof(float))) return fail(st);
     if (int st = dalloc(b, (void **)&b->tokens, T * sizeof(uint32_t))) return fail(st);
+    if (int st = dalloc(b, (void **)&b->pos_dev, sizeof(uint64_t))) return fail(st);
+    uint64_t scratch = 0;  // split-context attention partials, sized for the longest layer
+    for (uint32_t il = 0; il < c.n_layer; il++) {
+        const uint64_t window = b->layers[il].swa ? c.swa_window : 0;
+        scratch = std::max<uint64_t>(scratch, attention_scratch_bytes(b->kv[il], T, c.n_head,
+                                                                      attention_max_splits(b->kv[il], window)));
+    }
+    if (int st = dalloc(b, (void **)&b->attn_scratch, scratch)) return fail(st);
+    RCU_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    RCU_CUDA_TRY(ctx, cudaEventCreateWithFlags(&b->ev_in, cudaEventDisableTiming));
+    RCU_CUDA_TRY(ctx, cudaEventCreateWithFlags(&b->ev_out, cudaEventDisableTiming));
+    if (const char *g = std::getenv("RIE_CUDA_GRAPHS")) b->use_graphs = std::strcmp(g, "0") != 0;
     // RoPE inverse frequencies (ops.rs:65-79), computed like the reference in f32 on the host
     auto freqs = [&](float base, float fs, float **dst) -> int {
         const uint32_t half = c.rope_dim / 2;
@@ -540,6 +570,13 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
 
 void rcu_backend_free(rcu_backend *b) {
     if (!b) return;
+    cudaSetDevice(b->ctx->device);
+    if (b->stream) cudaStreamSynchronize(b->stream);
+    if (b->graph_exec) cudaGraphExecDestroy(b->graph_exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    if (b->ev_in) cudaEventDestroy(b->ev_in);
+    if (b->ev_out) cudaEventDestroy(b->ev_out);
+    if (b->stream) cudaStreamDestroy(b->stream);
     for (auto *kv : b->kv) rcu_kv_free(kv);
     rcu_acts_free(b->acts);
     cudaSetDevice(b->ctx->device);
@@ -560,6 +597,58 @@ static int32_t check_forward(rcu_backend *b, uint64_t n, uint64_t pos) {
     return RCU_OK;
 }
 
+// Runs one forward on the backend stream, joined to the context stream by events. Single
+// token, last-logits calls (decode) are captured once into a CUDA graph and replayed: every
+// kernel reads the token and position from device memory and the attention grid covers the
+// whole cache, so the launch sequence does not change between steps.
+static int32_t run_forward(rcu_backend *b, const uint32_t *tokens, bool tokens_on_host, uint64_t n, uint64_t pos,
+                           bool all_logits, float *logits) {
+    rcu_ctx *ctx = b->ctx;
+    cudaStream_t caller = ctx->stream;
+    RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_in, caller));
+    RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(b->stream, b->ev_in, 0));
+    ctx->stream = b->stream;
+    struct Restore {
+        rcu_ctx *c;
+        cudaStream_t s;
+        ~Restore() { c->stream = s; }
+    } restore{ctx, caller};
+    const cudaMemcpyKind kind = tokens_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    if (tokens != b->tokens) RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens, n * 4, kind, b->stream));
+    k_set_pos<<<1, 1, 0, b->stream>>>(b->pos_dev, pos);  // by value: no host buffer to keep alive
+    const bool decode = n == 1 && !all_logits && logits == b->logits;
+    if (decode && b->use_graphs && b->graph_exec) {
+        RCU_CUDA_TRY(ctx, cudaGraphLaunch(b->graph_exec, b->stream));
+    } else if (decode && b->use_graphs && b->decode_calls >= 1) {
+        // the first decode ran eagerly (kernel attributes set, all lazily created state made);
+        // capture the second one and replay it from then on
+        RCU_CUDA_TRY(ctx, cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+        const int st = forward_dev(b, 1, pos, false, b->logits, true);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(b->stream, &g);
+        if (st) {
+            if (g) cudaGraphDestroy(g);
+            return st;
+        }
+        if (e != cudaSuccess) return cuda_err(ctx, e, "cudaStreamEndCapture");
+        cudaGraphExec_t ge = nullptr;
+        const cudaError_t e2 = cudaGraphInstantiate(&ge, g, 0);
+        if (e2 != cudaSuccess) {
+            cudaGraphDestroy(g);
+            return cuda_err(ctx, e2, "cudaGraphInstantiate");
+        }
+        b->graph = g;
+        b->graph_exec = ge;
+        RCU_CUDA_TRY(ctx, cudaGraphLaunch(b->graph_exec, b->stream));
+    } else {
+        if (int32_t st = forward_dev(b, n, pos, all_logits, logits, decode && b->use_graphs)) return st;
+    }
+    if (decode) b->decode_calls++;
+    RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_out, b->stream));
+    RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(caller, b->ev_out, 0));
+    return RCU_OK;
+}
+
 int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, uint64_t pos, int32_t all_logits,
                             float *logits, uint64_t logits_len) {
     if (!b || !tokens || !logits) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
@@ -569,8 +658,7 @@ int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, 
     for (uint64_t i = 0; i < n; i++)
         if (tokens[i] >= b->embd->rows) return set_err(b->ctx, RCU_ERR_RUNTIME, "token id " + std::to_string(tokens[i]) + " out of range");
     rcu_ctx *ctx = b->ctx;
-    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens, n * 4, cudaMemcpyHostToDevice, ctx->stream));
-    if (int32_t st = forward_dev(b, n, pos, all_logits != 0, b->logits)) return st;
+    if (int32_t st = run_forward(b, tokens, true, n, pos, all_logits != 0, b->logits)) return st;
     RCU_CUDA_TRY(ctx, cudaMemcpyAsync(logits, b->logits, rows * b->m->cfg.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return rcu_sync(ctx);
 }
@@ -579,10 +667,13 @@ int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, u
                                    int32_t all_logits, float *logits_dev) {
     if (!b || !tokens_dev || !logits_dev) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
     if (int32_t st = check_forward(b, n, pos)) return st;
-    rcu_ctx *ctx = b->ctx;
-    if (tokens_dev != b->tokens)
-        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens_dev, n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
-    return forward_dev(b, n, pos, all_logits != 0, logits_dev);
+    // decode steps run through the backend's own logits buffer (and graph), then copy out
+    const bool decode = n == 1 && !all_logits;
+    if (int32_t st = run_forward(b, tokens_dev, false, n, pos, all_logits != 0, decode ? b->logits : logits_dev)) return st;
+    if (decode && logits_dev != b->logits)
+        RCU_CUDA_TRY(b->ctx, cudaMemcpyAsync(logits_dev, b->logits, b->m->cfg.n_vocab * 4, cudaMemcpyDeviceToDevice,
+                                             b->ctx->stream));
+    return RCU_OK;
 }
 
 int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out) {
@@ -590,6 +681,7 @@ int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, 
     const uint64_t n = b->hidden_rows * b->m->cfg.n_embd;
     if (rows_out) *rows_out = b->hidden_rows;
     if (cap < n) return set_err(b->ctx, RCU_ERR_INVALID, "hidden buffer too small");
+    RCU_CUDA_TRY(b->ctx, cudaStreamSynchronize(b->stream));
     RCU_CUDA_TRY(b->ctx, cudaMemcpyAsync(host_out, b->xn, n * 4, cudaMemcpyDeviceToHost, b->ctx->stream));
     RCU_CUDA_TRY(b->ctx, cudaStreamSynchronize(b->ctx->stream));
     return RCU_OK;

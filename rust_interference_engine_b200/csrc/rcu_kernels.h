@@ -20,4 +20,15 @@ int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
 int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint64_t row, uint64_t tok,
                       int32_t *out);
 
+// KV append / attention with the position either by value (pos_ptr == nullptr) or read
+// from device memory (graph replay). n_split == 0 sizes the split grid from pos0; scratch
+// == nullptr uses the context's growable scratch (may allocate).
+int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
+                    const uint64_t *pos_ptr);
+int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
+                     const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
+                     float *scratch);
+uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window);
+uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split);
+
 }  // namespace rcu

@@ -141,8 +141,9 @@ __device__ __forceinline__ int quant32(float v, int rounding, float &d_out) {
 // One warp per (token, kv head, k|v). Rows land at slot (pos0 + t) % slots.
 __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restrict__ k, const float *__restrict__ v,
                                                   uint32_t n_tok, uint32_t n_kv, uint32_t hd, uint32_t slots,
-                                                  uint64_t pos0, uint32_t row_bytes, uint8_t *__restrict__ kc,
-                                                  uint8_t *__restrict__ vc) {
+                                                  uint64_t pos0, const uint64_t *__restrict__ pos_ptr, uint32_t row_bytes,
+                                                  uint8_t *__restrict__ kc, uint8_t *__restrict__ vc) {
+    if (pos_ptr) pos0 = *pos_ptr;
     __shared__ float xs[4][kMaxHd];
     __shared__ uint8_t qs[4][kMaxHd];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,7 +205,6 @@ __global__ void __launch_bounds__(128) k_turbo_rotate(float *__restrict__ x, uin
 // ---- attention ----------------------------------------------------------------------------
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr uint32_t kChunk = 256;
 constexpr int kMaxGroup = 16;
 constexpr int kMaxAttnHd = 256;
 
@@ -212,8 +212,9 @@ struct AttnParams {
     const uint8_t *kc, *vc;
     const float *q;
     float *o_part, *m_part, *l_part;
-    uint32_t n_tok, n_head, n_kv, hd, slots, window, n_split, row_bytes;
+    uint32_t n_tok, n_head, n_kv, hd, slots, window, n_split, rows_per_split, row_bytes;
     uint64_t pos0;
+    const uint64_t *pos_ptr;  // when set, the position is read from device memory (graph replay)
     float softcap;
     int rounding;
 };
@@ -226,18 +227,22 @@ __device__ __forceinline__ uint32_t lut16(uint32_t idx, uint32_t t0, uint32_t t1
     return (lo & ~m) | (hi & m);
 }
 
-template <int KV>
+// One CTA = (KV head g, query token t, split): scores rows [c0, c1) of the cache for the
+// G query heads of the group in 64-row sub-chunks with an online softmax, and writes an
+// un-normalised partial output with its running max / sum.
+template <int KV, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_constant__ AttnParams p) {
+    constexpr int SUB = 64, DPL = kMaxAttnHd / 32;
     const uint32_t g = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
-    const uint32_t group = p.n_head / p.n_kv, hd = p.hd;
+    const uint32_t hd = p.hd, dpl = hd / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t pt = p.pos0 + t;
+    const uint64_t pt = (p.pos_ptr ? *p.pos_ptr : p.pos0) + t;
     const uint64_t start = p.window > 0 ? (pt + 1 > p.window ? pt + 1 - p.window : 0) : 0;
     const uint32_t len = (uint32_t)(pt + 1 - start);
-    const uint32_t c0 = split * kChunk, c1 = min(len, c0 + kChunk);
-    const uint64_t part_base = ((uint64_t)t * p.n_head + (uint64_t)g * group) * p.n_split + split;
+    const uint32_t c0 = split * p.rows_per_split, c1 = min(len, c0 + p.rows_per_split);
+    const uint64_t part_base = ((uint64_t)t * p.n_head + (uint64_t)g * G) * p.n_split + split;
     if (c0 >= len) {
-        for (uint32_t hh = warp; hh < group; hh += kAttnWarps) {
+        for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
             const uint64_t pb = part_base + (uint64_t)hh * p.n_split;
             if (lane == 0) {
                 p.m_part[pb] = -INFINITY;
@@ -247,16 +252,16 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
         }
         return;
     }
-    __shared__ float qf[kMaxGroup][kMaxAttnHd];        // f32 query (f16 cache) / rotation scratch
-    __shared__ __align__(16) int8_t qi[kMaxGroup][kMaxAttnHd];
-    __shared__ float qd[kMaxGroup][kMaxAttnHd / 32];
-    __shared__ float sc[kMaxGroup][kChunk];
+    __shared__ __align__(16) float qf[G][kMaxAttnHd];  // f32 query (f16 cache) / rotation scratch
+    __shared__ __align__(16) int8_t qi[G][kMaxAttnHd];
+    __shared__ float qd[G][kMaxAttnHd / 32];
+    __shared__ float sc[G][SUB];
     __shared__ float red[kAttnWarps][kMaxAttnHd];
-    __shared__ float mrow[kMaxGroup], lrow[kMaxGroup];
+    __shared__ float mrun[G], lrun[G], alpha[G];
 
     // 1. queries of this group: rotate (turbo) and quantize to Q8_0 (turbo / Q8_0 caches)
-    for (uint32_t hh = warp; hh < group; hh += kAttnWarps) {
-        const float *qsrc = p.q + ((uint64_t)t * p.n_head + g * group + hh) * hd;
+    for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
+        const float *qsrc = p.q + ((uint64_t)t * p.n_head + g * G + hh) * hd;
         for (uint32_t d = lane; d < hd; d += 32) qf[hh][d] = qsrc[d];
         __syncwarp();
         if (KV == RCU_KV_TURBO4) rotate_row(qf[hh], hd, false, lane);
@@ -268,137 +273,166 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
                 if (lane == 0) qd[hh][b] = d;
             }
         }
+        if (lane == 0) {
+            mrun[hh] = -INFINITY;
+            lrun[hh] = 0.0f;
+        }
         __syncwarp();
     }
     __syncthreads();
 
-    // 2. scores: one cache row per thread, every head of the group
     const uint32_t tb[4] = {0xc6b6a182u, 0xfaeee2d5u, 0x2b1e1206u, 0x7e5f4a3au};  // c_levels as bytes
     const float inv46 = 1.0f / 46.0f;
-    for (uint32_t i = c0 + threadIdx.x; i < c1; i += kAttnThreads) {
-        const uint64_t slot = (start + i) % p.slots;
-        const uint64_t row = (uint64_t)g * p.slots + slot;
-        const uint64_t kro = row * p.row_bytes;  // byte offset of the row (rows may be only 2-aligned)
-        float s[kMaxGroup];
-        for (uint32_t hh = 0; hh < group; hh++) s[hh] = 0.0f;
-        if (KV == RCU_KV_TURBO4) {
-            const uint32_t b = turbo_block(hd), nb = hd / b, cpb = b / 32;
-            for (uint32_t bi = 0; bi < nb; bi++) {
-                uint32_t sw[1];
-                ld_words<1>(p.kc, kro + 2 * bi, sw);
-                const float scale = f16_bits_to_f32(sw[0]);
-                float dcs[kMaxGroup];
-                for (uint32_t hh = 0; hh < group; hh++) dcs[hh] = 0.0f;
-                for (uint32_t c = 0; c < cpb; c++) {
-                    const uint32_t cc = bi * cpb + c;
-                    uint32_t w[4];
-                    ld_words<4>(p.kc, kro + 2 * nb + 16 * cc, w);
-                    uint32_t lv[8];
+    float acc[G][DPL];
 #pragma unroll
-                    for (int i2 = 0; i2 < 4; i2++) {
-                        lv[i2] = lut16(w[i2] & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
-                        lv[4 + i2] = lut16((w[i2] >> 4) & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
-                    }
-                    for (uint32_t hh = 0; hh < group; hh++) {
-                        const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][cc * 32]);
-                        const uint4 q0 = qv[0], q1 = qv[1];
-                        int acc = dp4a(lv[0], q0.x, 0);
-                        acc = dp4a(lv[1], q0.y, acc);
-                        acc = dp4a(lv[2], q0.z, acc);
-                        acc = dp4a(lv[3], q0.w, acc);
-                        acc = dp4a(lv[4], q1.x, acc);
-                        acc = dp4a(lv[5], q1.y, acc);
-                        acc = dp4a(lv[6], q1.z, acc);
-                        acc = dp4a(lv[7], q1.w, acc);
-                        dcs[hh] += qd[hh][cc] * (float)acc;  // dot_chunks: s += d_q * acc
-                    }
-                }
-                for (uint32_t hh = 0; hh < group; hh++) s[hh] += scale * dcs[hh];
-            }
-            for (uint32_t hh = 0; hh < group; hh++) s[hh] *= inv46;
-        } else if (KV == RCU_KV_Q8_0) {
-            for (uint32_t bi = 0; bi < hd / 32; bi++) {
-                BlkW w;
-                dec_q8_0(p.kc, kro + bi * 34, w);
-                for (uint32_t hh = 0; hh < group; hh++) {
-                    const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][bi * 32]);
-                    const uint4 q0 = qv[0], q1 = qv[1];
-                    const uint32_t a[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                    const int si = blk_int<T_Q8_0>(w, a, 0);
-                    s[hh] += (w.d * qd[hh][bi]) * (float)si;
-                }
-            }
-        } else {
-            const __half2 *kh = reinterpret_cast<const __half2 *>(p.kc + kro);
-            for (uint32_t d2 = 0; d2 < hd / 2; d2++) {
-                const float2 kv = __half22float2(kh[d2]);
-                for (uint32_t hh = 0; hh < group; hh++) s[hh] += kv.x * qf[hh][2 * d2] + kv.y * qf[hh][2 * d2 + 1];
-            }
-        }
-        for (uint32_t hh = 0; hh < group; hh++) {
-            float v = s[hh];
-            if (p.softcap > 0.0f) v = p.softcap * tanhf(v / p.softcap);
-            sc[hh][i - c0] = v;
-        }
-    }
-    __syncthreads();
-    // 3. chunk max / exp / sum per head
-    for (uint32_t hh = warp; hh < group; hh += kAttnWarps) {
-        float m = -INFINITY;
-        for (uint32_t i = lane; i < c1 - c0; i += 32) m = fmaxf(m, sc[hh][i]);
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (uint32_t i = lane; i < c1 - c0; i += 32) {
-            const float e = expf(sc[hh][i] - m);
-            sc[hh][i] = e;
-            l += e;
-        }
-        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            mrow[hh] = m;
-            lrow[hh] = l;
-        }
-    }
-    __syncthreads();
-    // 4. weighted V sum: warp w takes rows i = c0 + w (mod 4); lane owns dims lane*dpl..
-    const uint32_t dpl = hd / 32;  // dims per lane (hd multiple of 32)
-    float acc[kMaxGroup][kMaxAttnHd / 32];
-    for (uint32_t hh = 0; hh < group; hh++)
-        for (uint32_t e = 0; e < dpl; e++) acc[hh][e] = 0.0f;
+    for (int hh = 0; hh < G; hh++)
+#pragma unroll
+        for (int e = 0; e < DPL; e++) acc[hh][e] = 0.0f;
     const uint32_t d0 = lane * dpl;
-    for (uint32_t i = c0 + warp; i < c1; i += kAttnWarps) {
-        const uint64_t slot = (start + i) % p.slots;
-        const uint64_t vro = ((uint64_t)g * p.slots + slot) * p.row_bytes;
-        const uint8_t *vr = p.vc + vro;
-        float val[kMaxAttnHd / 32];
-        if (KV == RCU_KV_TURBO4) {
-            const uint32_t b = turbo_block(hd), nb = hd / b;
-            for (uint32_t e = 0; e < dpl; e++) {
-                const uint32_t dd = d0 + e, c = dd / 32, m2 = dd % 32;
-                const uint32_t byte = vr[2 * nb + 16 * c + (m2 & 15)];
-                const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
-                uint32_t sw[1];
-                ld_words<1>(p.vc, vro + 2 * (dd / b), sw);
-                val[e] = f16_bits_to_f32(sw[0]) * inv46 * (float)c_levels[code];
+
+    for (uint32_t s0 = c0; s0 < c1; s0 += SUB) {
+        const uint32_t s1 = min(c1, s0 + SUB);
+        // 2. scores: two threads per row, each half of the head dimension
+        {
+            const uint32_t r = threadIdx.x >> 1, half = threadIdx.x & 1;
+            const uint32_t i = s0 + r;
+            float s[G];
+#pragma unroll
+            for (int hh = 0; hh < G; hh++) s[hh] = 0.0f;
+            if (i < s1) {
+                const uint64_t row = (uint64_t)g * p.slots + (start + i) % p.slots;
+                const uint64_t kro = row * p.row_bytes;
+                if (KV == RCU_KV_TURBO4) {
+                    const uint32_t b = turbo_block(hd), nb = hd / b, nch = hd / 32;
+                    for (uint32_t cc = half * (nch / 2); cc < (half + 1) * (nch / 2) + (half ? nch % 2 : 0); cc++) {
+                        uint32_t sw[1];
+                        ld_words<1>(p.kc, kro + 2 * ((cc * 32) / b), sw);
+                        const float scale = f16_bits_to_f32(sw[0]);
+                        uint32_t w[4];
+                        ld_words<4>(p.kc, kro + 2 * nb + 16 * cc, w);
+                        uint32_t lv[8];
+#pragma unroll
+                        for (int i2 = 0; i2 < 4; i2++) {
+                            lv[i2] = lut16(w[i2] & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
+                            lv[4 + i2] = lut16((w[i2] >> 4) & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
+                        }
+#pragma unroll
+                        for (int hh = 0; hh < G; hh++) {
+                            const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][cc * 32]);
+                            const uint4 q0 = qv[0], q1 = qv[1];
+                            int a0 = dp4a(lv[0], q0.x, 0), a1 = dp4a(lv[1], q0.y, 0);
+                            a0 = dp4a(lv[2], q0.z, a0);
+                            a1 = dp4a(lv[3], q0.w, a1);
+                            a0 = dp4a(lv[4], q1.x, a0);
+                            a1 = dp4a(lv[5], q1.y, a1);
+                            a0 = dp4a(lv[6], q1.z, a0);
+                            a1 = dp4a(lv[7], q1.w, a1);
+                            s[hh] += scale * (qd[hh][cc] * (float)(a0 + a1));
+                        }
+                    }
+                } else if (KV == RCU_KV_Q8_0) {
+                    const uint32_t nbk = hd / 32;
+                    for (uint32_t bi = half * (nbk / 2); bi < (half + 1) * (nbk / 2) + (half ? nbk % 2 : 0); bi++) {
+                        BlkW w;
+                        dec_q8_0(p.kc, kro + bi * 34, w);
+#pragma unroll
+                        for (int hh = 0; hh < G; hh++) {
+                            const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][bi * 32]);
+                            const uint4 q0 = qv[0], q1 = qv[1];
+                            const uint32_t a[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                            s[hh] += (w.d * qd[hh][bi]) * (float)blk_int<T_Q8_0>(w, a, 0);
+                        }
+                    }
+                } else {
+                    const uint4 *kh = reinterpret_cast<const uint4 *>(p.kc + kro) + half * (hd / 16);
+                    for (uint32_t c = 0; c < hd / 16; c++) {  // 8 halves per 16-byte load
+                        const uint4 raw = kh[c];
+                        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                        const uint32_t dbase = half * (hd / 2) + 8 * c;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float2 kv = __half22float2(h2[j]);
+#pragma unroll
+                            for (int hh = 0; hh < G; hh++)
+                                s[hh] += kv.x * qf[hh][dbase + 2 * j] + kv.y * qf[hh][dbase + 2 * j + 1];
+                        }
+                    }
+                }
             }
-        } else if (KV == RCU_KV_Q8_0) {
-            for (uint32_t e = 0; e < dpl; e++) {
-                const uint32_t dd = d0 + e, bi = dd / 32;
-                uint32_t sw[1];
-                ld_words<1>(p.vc, vro + bi * 34, sw);
-                val[e] = f16_bits_to_f32(sw[0]) * (float)(int8_t)vr[bi * 34 + 2 + dd % 32];
+#pragma unroll
+            for (int hh = 0; hh < G; hh++) {
+                float v = s[hh] + __shfl_xor_sync(0xffffffffu, s[hh], 1);
+                if (KV == RCU_KV_TURBO4) v *= inv46;
+                if (p.softcap > 0.0f) v = p.softcap * tanhf(v / p.softcap);
+                if (half == 0 && r < SUB) sc[hh][r] = i < s1 ? v : -INFINITY;
             }
-        } else {
-            const unsigned short *vh = reinterpret_cast<const unsigned short *>(vr);
-            for (uint32_t e = 0; e < dpl; e++) val[e] = __half2float(__ushort_as_half(vh[d0 + e]));
         }
-        for (uint32_t hh = 0; hh < group; hh++) {
-            const float w = sc[hh][i - c0];
-            for (uint32_t e = 0; e < dpl; e++) acc[hh][e] += w * val[e];
+        __syncthreads();
+        // 3. online softmax per head
+        for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
+            const float v0 = sc[hh][lane], v1 = sc[hh][lane + 32];
+            float m = fmaxf(v0, v1);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float m_old = mrun[hh], m_new = fmaxf(m_old, m);
+            const float e0 = v0 == -INFINITY ? 0.0f : expf(v0 - m_new), e1 = v1 == -INFINITY ? 0.0f : expf(v1 - m_new);
+            sc[hh][lane] = e0;
+            sc[hh][lane + 32] = e1;
+            float l = e0 + e1;
+            for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) {
+                const float a = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
+                alpha[hh] = a;
+                lrun[hh] = lrun[hh] * a + l;
+                mrun[hh] = m_new;
+            }
         }
+        __syncthreads();
+        // 4. weighted V sum: warp w takes rows s0 + w (mod 4); lane owns dims lane*dpl..
+#pragma unroll
+        for (int hh = 0; hh < G; hh++) {
+            const float a = alpha[hh];
+#pragma unroll
+            for (int e = 0; e < DPL; e++) acc[hh][e] *= a;
+        }
+        for (uint32_t i = s0 + warp; i < s1; i += kAttnWarps) {
+            const uint64_t vro = ((uint64_t)g * p.slots + (start + i) % p.slots) * p.row_bytes;
+            const uint8_t *vr = p.vc + vro;
+            float val[DPL];
+#pragma unroll
+            for (int e = 0; e < DPL; e++) {
+                if ((uint32_t)e >= dpl) break;
+                const uint32_t dd = d0 + e;
+                if (KV == RCU_KV_TURBO4) {
+                    const uint32_t b = turbo_block(hd), nb = hd / b, c = dd / 32, m2 = dd % 32;
+                    const uint32_t byte = vr[2 * nb + 16 * c + (m2 & 15)];
+                    const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
+                    uint32_t sw[1];
+                    ld_words<1>(p.vc, vro + 2 * (dd / b), sw);
+                    val[e] = f16_bits_to_f32(sw[0]) * inv46 * (float)c_levels[code];
+                } else if (KV == RCU_KV_Q8_0) {
+                    const uint32_t bi = dd / 32;
+                    uint32_t sw[1];
+                    ld_words<1>(p.vc, vro + bi * 34, sw);
+                    val[e] = f16_bits_to_f32(sw[0]) * (float)(int8_t)vr[bi * 34 + 2 + dd % 32];
+                } else {
+                    val[e] = __half2float(reinterpret_cast<const __half *>(vr)[dd]);
+                }
+            }
+#pragma unroll
+            for (int hh = 0; hh < G; hh++) {
+                const float w = sc[hh][i - s0];
+#pragma unroll
+                for (int e = 0; e < DPL; e++)
+                    if ((uint32_t)e < dpl) acc[hh][e] += w * val[e];
+            }
+        }
+        __syncthreads();
     }
-    for (uint32_t hh = 0; hh < group; hh++) {
-        for (uint32_t e = 0; e < dpl; e++) red[warp][d0 + e] = acc[hh][e];
+#pragma unroll
+    for (int hh = 0; hh < G; hh++) {
+#pragma unroll
+        for (int e = 0; e < DPL; e++)
+            if ((uint32_t)e < dpl) red[warp][d0 + e] = acc[hh][e];
         __syncthreads();
         for (uint32_t d = threadIdx.x; d < hd; d += kAttnThreads) {
             float o = 0.0f;
@@ -407,10 +441,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
         }
         __syncthreads();
     }
-    if (threadIdx.x < group) {
+    if (threadIdx.x < G) {
         const uint64_t pb = part_base + (uint64_t)threadIdx.x * p.n_split;
-        p.m_part[pb] = mrow[threadIdx.x];
-        p.l_part[pb] = lrow[threadIdx.x];
+        p.m_part[pb] = mrun[threadIdx.x];
+        p.l_part[pb] = lrun[threadIdx.x];
     }
 }
 
@@ -465,6 +499,103 @@ static int scratch_get(rcu_ctx *ctx, size_t bytes, void **out) {
         sc.n = bytes;
     }
     *out = sc.p;
+    return RCU_OK;
+}
+
+
+int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
+                    const uint64_t *pos_ptr) {
+    const uint64_t items = n_tok * kv->n_kv * 2;
+    k_kv_store<<<(uint32_t)((items + 3) / 4), 128, 0, ctx->stream>>>(kv->type, k, v, (uint32_t)n_tok, (uint32_t)kv->n_kv,
+                                                                     (uint32_t)kv->hd, (uint32_t)kv->slots, pos0, pos_ptr,
+                                                                     (uint32_t)kv->row_bytes, kv->k, kv->v);
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
+    return RCU_OK;
+}
+
+// Rows per CTA: a multiple of 64, chosen so that n_kv x n_tok x splits covers about two
+// waves of SMs; both numbers depend only on (max_len, n_tok, n_kv), never on the position.
+static void split_plan(uint64_t max_len, uint64_t n_tok, uint64_t n_kv, int num_sms, uint32_t *n_split,
+                       uint32_t *rows_per_split) {
+    const uint64_t n_sub = (max_len + 63) / 64;
+    const uint64_t want = std::max<uint64_t>(1, (2 * (uint64_t)num_sms) / std::max<uint64_t>(1, n_kv * n_tok));
+    const uint64_t splits = std::max<uint64_t>(1, std::min(n_sub, want));
+    const uint64_t subs_per = (n_sub + splits - 1) / splits;
+    *rows_per_split = (uint32_t)(subs_per * 64);
+    *n_split = (uint32_t)((max_len + *rows_per_split - 1) / *rows_per_split);
+}
+
+uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window) {
+    const uint64_t max_len = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
+    return (uint32_t)((max_len + 63) / 64);  // upper bound of any plan (64-row splits)
+}
+
+uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split) {
+    return n_tok * n_head * n_split * (kv->hd + 2) * sizeof(float);
+}
+
+template <int KV>
+static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, dim3 cgrid, float *out) {
+    switch (group) {
+        case 1: k_attn_partial<KV, 1><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        case 2: k_attn_partial<KV, 2><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        case 4: k_attn_partial<KV, 4><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        case 8: k_attn_partial<KV, 8><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        case 16: k_attn_partial<KV, 16><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4, 8 or 16");
+    }
+    k_attn_combine<KV><<<cgrid, 32, 0, ctx->stream>>>(p, out);
+    return RCU_OK;
+}
+
+int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
+                     const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
+                     float *scratch) {
+    const uint64_t group = n_head / kv->n_kv;
+    if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
+    AttnParams p{};
+    p.kc = kv->k;
+    p.vc = kv->v;
+    p.q = q;
+    p.n_tok = (uint32_t)n_tok;
+    p.n_head = (uint32_t)n_head;
+    p.n_kv = (uint32_t)kv->n_kv;
+    p.hd = (uint32_t)kv->hd;
+    p.slots = (uint32_t)kv->slots;
+    p.window = (uint32_t)window;
+    p.pos0 = pos0;
+    p.pos_ptr = pos_ptr;
+    p.softcap = softcap;
+    p.rounding = ctx->rounding;
+    p.row_bytes = (uint32_t)kv->row_bytes;
+    // fixed plans (graph replay) cover the whole cache; otherwise the current length
+    uint64_t max_len;
+    if (n_split != 0) {
+        max_len = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
+    } else {
+        const uint64_t last = pos0 + n_tok - 1;
+        max_len = window > 0 ? std::min<uint64_t>(window, last + 1) : last + 1;
+    }
+    split_plan(max_len, n_tok, kv->n_kv, ctx->num_sms, &p.n_split, &p.rows_per_split);
+    const uint64_t parts = n_tok * n_head * p.n_split;
+    void *scr = scratch;
+    if (!scr) {
+        int st = scratch_get(ctx, parts * (kv->hd + 2) * sizeof(float), &scr);
+        if (st) return st;
+    }
+    p.o_part = (float *)scr;
+    p.m_part = p.o_part + parts * kv->hd;
+    p.l_part = p.m_part + parts;
+    dim3 grid((uint32_t)kv->n_kv, (uint32_t)n_tok, p.n_split);
+    dim3 cgrid((uint32_t)n_head, (uint32_t)n_tok);
+    int st = RCU_OK;
+    switch (kv->type) {
+        case RCU_KV_F16: st = dispatch_group<RCU_KV_F16>(ctx, p, (int)group, grid, cgrid, out); break;
+        case RCU_KV_Q8_0: st = dispatch_group<RCU_KV_Q8_0>(ctx, p, (int)group, grid, cgrid, out); break;
+        default: st = dispatch_group<RCU_KV_TURBO4>(ctx, p, (int)group, grid, cgrid, out); break;
+    }
+    if (st) return st;
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
 
@@ -545,13 +676,7 @@ int32_t rcu_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k_dev, const float *
     if (!ctx || !kv || !k_dev || !v_dev) return set_err(ctx, RCU_ERR_INVALID, "null argument");
     if (n_tok == 0) return RCU_OK;
     if (n_tok > kv->slots) return set_err(ctx, RCU_ERR_INVALID, "kv_store: more tokens than slots");
-    const uint64_t items = n_tok * kv->n_kv * 2;
-    k_kv_store<<<(uint32_t)((items + 3) / 4), 128, 0, ctx->stream>>>(kv->type, k_dev, v_dev, (uint32_t)n_tok,
-                                                                     (uint32_t)kv->n_kv, (uint32_t)kv->hd,
-                                                                     (uint32_t)kv->slots, pos0, (uint32_t)kv->row_bytes,
-                                                                     kv->k, kv->v);
-    RCU_CUDA_TRY(ctx, cudaGetLastError());
-    return RCU_OK;
+    return rcu::launch_kv_store(ctx, kv, k_dev, v_dev, n_tok, pos0, nullptr);
 }
 
 int32_t rcu_kv_export(rcu_ctx *ctx, const rcu_kv *kv, void *k_host, void *v_host) {
@@ -577,51 +702,10 @@ int32_t rcu_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q_dev, uint64
     if (!ctx || !kv || !q_dev || !out_dev) return set_err(ctx, RCU_ERR_INVALID, "null argument");
     if (n_tok == 0) return set_err(ctx, RCU_ERR_RUNTIME, "empty batch");
     if (n_head % kv->n_kv) return set_err(ctx, RCU_ERR_INVALID, "n_head not divisible by n_head_kv");
-    const uint64_t group = n_head / kv->n_kv;
-    if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
     const uint64_t last = pos0 + n_tok - 1;
     const uint64_t max_len = window > 0 ? std::min<uint64_t>(window, last + 1) : last + 1;
     if (max_len > kv->slots) return set_err(ctx, RCU_ERR_RUNTIME, "context window full");
-    AttnParams p{};
-    p.kc = kv->k;
-    p.vc = kv->v;
-    p.q = q_dev;
-    p.n_tok = (uint32_t)n_tok;
-    p.n_head = (uint32_t)n_head;
-    p.n_kv = (uint32_t)kv->n_kv;
-    p.hd = (uint32_t)kv->hd;
-    p.slots = (uint32_t)kv->slots;
-    p.window = (uint32_t)window;
-    p.pos0 = pos0;
-    p.softcap = softcap;
-    p.rounding = ctx->rounding;
-    p.row_bytes = (uint32_t)kv->row_bytes;
-    p.n_split = (uint32_t)((max_len + kChunk - 1) / kChunk);
-    const uint64_t parts = n_tok * n_head * p.n_split;
-    void *scr = nullptr;
-    int st = scratch_get(ctx, parts * (kv->hd + 2) * sizeof(float), &scr);
-    if (st) return st;
-    p.o_part = (float *)scr;
-    p.m_part = p.o_part + parts * kv->hd;
-    p.l_part = p.m_part + parts;
-    dim3 grid((uint32_t)kv->n_kv, (uint32_t)n_tok, p.n_split);
-    dim3 cgrid((uint32_t)n_head, (uint32_t)n_tok);
-    switch (kv->type) {
-        case RCU_KV_F16:
-            k_attn_partial<RCU_KV_F16><<<grid, kAttnThreads, 0, ctx->stream>>>(p);
-            k_attn_combine<RCU_KV_F16><<<cgrid, 32, 0, ctx->stream>>>(p, out_dev);
-            break;
-        case RCU_KV_Q8_0:
-            k_attn_partial<RCU_KV_Q8_0><<<grid, kAttnThreads, 0, ctx->stream>>>(p);
-            k_attn_combine<RCU_KV_Q8_0><<<cgrid, 32, 0, ctx->stream>>>(p, out_dev);
-            break;
-        default:
-            k_attn_partial<RCU_KV_TURBO4><<<grid, kAttnThreads, 0, ctx->stream>>>(p);
-            k_attn_combine<RCU_KV_TURBO4><<<cgrid, 32, 0, ctx->stream>>>(p, out_dev);
-            break;
-    }
-    RCU_CUDA_TRY(ctx, cudaGetLastError());
-    return RCU_OK;
+    return rcu::launch_attention(ctx, kv, q_dev, n_tok, n_head, pos0, nullptr, window, softcap, out_dev, 0, nullptr);
 }
 
 }  // extern "C"

@@ -125,3 +125,17 @@ def test_forward_errors(env):
         gb.forward(np.array([10_000], np.uint32), 0)
     # the backend stays usable after rejected calls
     close(gb.forward(np.array([3, 4], np.uint32), 0), ob.forward(np.array([3, 4], np.uint32), 0))
+
+
+def test_long_decode_replays_graph(env):
+    # decode steps 2.. replay one captured CUDA graph; positions, KV slots and the attention
+    # length are read from device memory on every replay
+    from rust_interference_engine_b200 import model as M
+    gb, ob, keep = build_pair(env, M.SyntheticSpec.tiny("qwen3", O.Q4_K), O.KV_F16, n_ctx=300)
+    toks = np.random.default_rng(3).integers(0, 384, 40).astype(np.uint32)
+    close(gb.forward(toks[:16], 0), ob.forward(toks[:16], 0))
+    for i in range(16, 40):
+        close(gb.forward(toks[i:i + 1], i), ob.forward(toks[i:i + 1], i), what=f"pos {i}")
+    # a batch in between leaves the graph valid
+    close(gb.forward(toks[:8], 40), ob.forward(toks[:8], 40))
+    close(gb.forward(toks[8:9], 48), ob.forward(toks[8:9], 48))
