@@ -2,11 +2,12 @@
 // CPU backend (crates/rie-core/src/model/cpu.rs:210-409, dense_ffn :431-467) over the
 // quantized matmul, KV-cache and attention kernels of this library.
 //
-// Per layer and batch: RMSNorm -> Q8 activations -> one matmul_multi for Q,K,V ->
-// bias / per-head q,k RMSNorm / RoPE / attn_scale -> KV append -> attention -> Wo ->
-// post-norm + residual -> RMSNorm -> gate+up in one launch -> SwiGLU/GELU -> down ->
-// post-norm + residual; then the output norm and head. All work is queued on the context
-// stream; the host only validates arguments and launches.
+// Per layer and batch: [residual +] RMSNorm + Q8 activations -> one matmul_multi for Q,K,V
+// -> bias / per-head q,k RMSNorm / RoPE / attn_scale + KV append -> attention (merge +
+// Q8 activations) -> Wo -> post-norm + residual + RMSNorm + Q8 activations -> gate+up in
+// one launch -> SwiGLU/GELU + Q8 activations -> down; the down residual is added by the
+// next norm. Ten launches per layer, all queued on the backend stream; the host only
+// validates arguments and launches.
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -14,6 +15,7 @@
 #include <string>
 #include <vector>
 
+#include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
 
@@ -52,6 +54,7 @@ struct rcu_backend {
     uint32_t *tokens = nullptr;
     uint64_t *pos_dev = nullptr;  // position of the batch, read by the kernels (graph replay)
     float *attn_scratch = nullptr;
+    bool fused_merge = true;  // attention merge quantizes for Wo in the same kernel
     uint32_t ff_max = 0;
     uint64_t hidden_rows = 0;
     std::vector<void *> allocs;
@@ -178,101 +181,98 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return s;
 }
 
-// out = x / rms(x) * w per row (ops.rs:7-14): (x * scale) * w.
-__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, uint32_t e, float eps,
-                          float *__restrict__ out) {
+// Residual + RMSNorm + activation quantization in one pass over a token row (one CTA of
+// 1024 threads per token, value i of the row in thread i % 1024, slot i / 1024):
+//   x += post_norm(o) * rs        when o is given (ops.rs:17-24, cpu.rs:330-345)
+//   xn = (x * (1 / rms(x))) * w   (ops.rs:7-14)
+// then xn is quantized into the matmul activations (ActOut formats) and, when xn_f32 is
+// given, stored as f32. Each thread writes back only the x values it read, so x may be
+// updated in place.
+constexpr int kNormThreads = 1024;
+template <int NIT>
+__global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, const float *__restrict__ o,
+                                                         const float *__restrict__ post_w, float rs,
+                                                         const float *__restrict__ w, uint32_t e, float eps,
+                                                         float *__restrict__ xn_f32, const ActOut ao) {
     __shared__ float red[32];
-    const float *xr = x + (uint64_t)blockIdx.x * e;
-    float *orow = out + (uint64_t)blockIdx.x * e;
+    __shared__ Q8kShared sh;
+    const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *xr = x + (uint64_t)t * e;
+    float v[NIT];
+#pragma unroll
+    for (int j = 0; j < NIT; j++) {
+        const uint32_t i = tid + kNormThreads * j;
+        v[j] = i < e ? xr[i] : 0.0f;
+    }
+    if (o) {
+        const float *orow = o + (uint64_t)t * e;
+        float ov[NIT];
+#pragma unroll
+        for (int j = 0; j < NIT; j++) {
+            const uint32_t i = tid + kNormThreads * j;
+            ov[j] = i < e ? orow[i] : 0.0f;
+        }
+        if (post_w) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NIT; j++) ss += ov[j] * ov[j];
+            ss = block_sum(ss, red);
+            const float scale = 1.0f / sqrtf(ss / (float)e + eps);
+#pragma unroll
+            for (int j = 0; j < NIT; j++) {
+                const uint32_t i = tid + kNormThreads * j;
+                if (i < e) ov[j] *= scale * post_w[i];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NIT; j++) {
+            const uint32_t i = tid + kNormThreads * j;
+            v[j] += rs == 1.0f ? ov[j] : ov[j] * rs;
+            if (i < e) xr[i] = v[j];
+        }
+    }
     float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) ss += xr[i] * xr[i];
+#pragma unroll
+    for (int j = 0; j < NIT; j++) ss += v[j] * v[j];
     ss = block_sum(ss, red);
     const float scale = 1.0f / sqrtf(ss / (float)e + eps);
-    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
-}
-
-// x += post_norm(o) * rs, with the optional post-norm in place on o (ops.rs:17-24).
-__global__ void k_residual(float *__restrict__ x, float *__restrict__ o, const float *__restrict__ post_w, uint32_t e,
-                           float eps, float rs) {
-    __shared__ float red[32];
-    float *xr = x + (uint64_t)blockIdx.x * e;
-    float *orow = o + (uint64_t)blockIdx.x * e;
-    float scale = 1.0f;
-    if (post_w) {
-        float ss = 0.0f;
-        for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) ss += orow[i] * orow[i];
-        ss = block_sum(ss, red);
-        scale = 1.0f / sqrtf(ss / (float)e + eps);
-    }
-    for (uint32_t i = threadIdx.x; i < e; i += blockDim.x) {
-        float v = orow[i];
-        if (post_w) v *= scale * post_w[i];
-        xr[i] += rs == 1.0f ? v : v * rs;
-    }
-}
-
-// Per head vector: bias, q/k RMSNorm (x *= scale*w), RoPE, attn_scale (q only).
-// Vectors: [t][0..n_head) = q heads, [t][n_head..n_head+n_kv) = k heads, then v heads (bias).
-__global__ void k_qkv_post(float *__restrict__ q, float *__restrict__ k, float *__restrict__ v,
-                           const float *__restrict__ bq, const float *__restrict__ bk, const float *__restrict__ bv,
-                           const float *__restrict__ qn, const float *__restrict__ kn, const float *__restrict__ inv_freq,
-                           uint32_t n_tok, uint32_t n_head, uint32_t n_kv, uint32_t hd, uint32_t rope_dim, int neox,
-                           const uint64_t *__restrict__ pos_ptr, float eps, float attn_scale) {
-    __shared__ float buf[4][512];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t per_tok = n_head + 2 * n_kv;
-    const uint64_t item = (uint64_t)blockIdx.x * 4 + warp;
-    if (item >= (uint64_t)n_tok * per_tok) return;
-    const uint32_t t = (uint32_t)(item / per_tok), j = (uint32_t)(item % per_tok);
-    float *vec;
-    const float *bias, *norm;
-    bool is_q = false, rope = true;
-    if (j < n_head) {
-        vec = q + ((uint64_t)t * n_head + j) * hd, bias = bq ? bq + j * hd : nullptr, norm = qn, is_q = true;
-    } else if (j < n_head + n_kv) {
-        vec = k + ((uint64_t)t * n_kv + (j - n_head)) * hd, bias = bk ? bk + (j - n_head) * hd : nullptr, norm = kn;
-    } else {
-        vec = v + ((uint64_t)t * n_kv + (j - n_head - n_kv)) * hd, bias = bv ? bv + (j - n_head - n_kv) * hd : nullptr;
-        norm = nullptr, rope = false;
-    }
-    float *s = buf[warp];
-    for (uint32_t i = lane; i < hd; i += 32) s[i] = vec[i] + (bias ? bias[i] : 0.0f);
-    __syncwarp();
-    if (norm) {
-        float ss = 0.0f;
-        for (uint32_t i = lane; i < hd; i += 32) ss += s[i] * s[i];
-        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float scale = 1.0f / sqrtf(ss / (float)hd + eps);
-        for (uint32_t i = lane; i < hd; i += 32) s[i] *= scale * norm[i];
-        __syncwarp();
-    }
-    if (rope) {
-        const uint32_t half = rope_dim / 2;
-        const float pos = (float)(*pos_ptr + t);
-        for (uint32_t i = lane; i < half; i += 32) {
-            float sn, cs;
-            sincosf(pos * inv_freq[i], &sn, &cs);
-            const uint32_t i0 = neox ? i : 2 * i, i1 = neox ? i + half : 2 * i + 1;
-            const float a = s[i0], b = s[i1];
-            s[i0] = a * cs - b * sn;
-            s[i1] = a * sn + b * cs;
+#pragma unroll
+    for (int j = 0; j < NIT; j++) {
+        const uint32_t i = tid + kNormThreads * j;
+        const float xn = i < e ? v[j] * scale * w[i] : 0.0f;
+        if (xn_f32 && i < e) xn_f32[(uint64_t)t * e + i] = xn;
+        const uint32_t i0 = kNormThreads * j + 32 * warp;  // first value of this warp's block
+        if ((ao.fmt & RCU_ACT_Q8_0) && i0 < e) q8_0_block(xn, (uint64_t)t * (e / QK) + i0 / QK, lane, ao);
+        if (ao.fmt & RCU_ACT_Q8K) {
+            const uint32_t g0 = kNormThreads * j + QK_K * (warp / 8);
+            q8_k_block(xn, tid % QK_K, warp & ~7u, (uint64_t)t * (e / QK_K) + g0 / QK_K, g0 < e, ao, sh, j & 1);
         }
-        __syncwarp();
     }
-    for (uint32_t i = lane; i < hd; i += 32) vec[i] = is_q ? s[i] * attn_scale : s[i];
 }
 
-__global__ void k_glu(float *__restrict__ g, const float *__restrict__ u, uint64_t n, int act) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const float a = g[i];
-    float f;
-    if (act == 1) {
-        f = 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a)));
-    } else {
-        f = a / (1.0f + expf(-a));
+// g = act(g) * u (SwiGLU / GELU-tanh, ops.rs:41-58) quantized for the down matmul; one
+// value per thread, grid (ceil(ff / 1024), tokens).
+__global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, const float *__restrict__ u, uint32_t ff,
+                                                int act, const ActOut ao) {
+    __shared__ Q8kShared sh;
+    const uint32_t t = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t i = blockIdx.x * 1024 + tid;
+    float f = 0.0f;
+    if (i < ff) {
+        const float a = g[(uint64_t)t * ff + i];
+        if (act == 1) {
+            f = 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a)));
+        } else {
+            f = a / (1.0f + expf(-a));
+        }
+        f *= u[(uint64_t)t * ff + i];
     }
-    g[i] = f * u[i];
+    const uint32_t i0 = blockIdx.x * 1024 + 32 * warp;
+    if ((ao.fmt & RCU_ACT_Q8_0) && i0 < ff) q8_0_block(f, (uint64_t)t * (ff / QK) + i0 / QK, lane, ao);
+    if (ao.fmt & RCU_ACT_Q8K) {
+        const uint32_t g0 = blockIdx.x * 1024 + QK_K * (warp / 8);
+        q8_k_block(f, tid % QK_K, warp & ~7u, (uint64_t)t * (ff / QK_K) + g0 / QK_K, g0 < ff, ao, sh, 0);
+    }
 }
 
 __global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos) { *pos_dev = pos; }
@@ -293,58 +293,94 @@ static int dalloc(rcu_backend *b, void **p, size_t bytes) {
     return RCU_OK;
 }
 
-static int matmul(rcu_backend *b, const float *x, uint32_t n, uint32_t k, std::vector<rcu_job> jobs) {
-    uint32_t fmt = 0;
-    for (auto &j : jobs) fmt |= act_format(j.w->type);
-    int st = rcu_acts_prepare(b->ctx, b->acts, x, n, k, fmt);
-    if (st) return st;
+// Activation formats the weights of one matmul_multi call consume.
+static uint32_t formats(std::initializer_list<const rcu_weight *> ws) {
+    uint32_t f = 0;
+    for (auto *w : ws) f |= act_format(w->type);
+    return f;
+}
+
+static ActOut acts_out(rcu_backend *b, uint32_t fmt) { return act_out(b->acts->v, fmt, b->ctx->rounding); }
+
+// Matmuls over activations that a fused producer kernel already quantized into b->acts.
+static int matmul(rcu_backend *b, uint32_t n, uint32_t k, uint32_t fmt, std::vector<rcu_job> jobs) {
+    b->acts->v.n_tok = n;
+    b->acts->v.k = k;
+    b->acts->v.have = fmt;
     return rcu_matmul_multi(b->ctx, b->acts, jobs.data(), jobs.size());
+}
+
+// x (+)= post_norm(o) * rs; quantized RMSNorm(x) * w into b->acts (and f32 into xn_f32).
+static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const float *post_w, const float *w,
+                  float *xn_f32, uint32_t fmt) {
+    const rcu_model_config &c = b->m->cfg;
+    const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
+    const ActOut ao = acts_out(b, fmt);
+    const float rs = c.residual_scale, eps = c.rms_eps;
+    cudaStream_t s = b->ctx->stream;
+    const dim3 grid((uint32_t)n);
+    if (nit <= 1) k_norm_q<1><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
+    else if (nit <= 2) k_norm_q<2><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
+    else if (nit <= 4) k_norm_q<4><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
+    else if (nit <= 8) k_norm_q<8><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
+    else if (nit <= 16) k_norm_q<16><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
+    else return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
+    return RCU_OK;
 }
 
 // One forward of n tokens at the position stored in b->pos_dev (pos0 is its host copy, used
 // to size the attention grid unless `fixed_grid`, which sizes it for the whole cache so the
 // launch sequence does not depend on the position and can be replayed as a graph).
+// Per layer: norm+quantize, QKV matmul, q/k post-processing + KV append, attention with the
+// merge quantizing for Wo, Wo, residual+norm+quantize, gate+up, GLU+quantize, down; the
+// down residual is folded into the next layer's (or the output) norm.
 static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
     rcu_ctx *ctx = b->ctx;
     const rcu_model_config &c = b->m->cfg;
     cudaStream_t s = ctx->stream;
     const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
     k_embed<<<(uint32_t)n, 128, 0, s>>>(b->tokens, b->embd->type, b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x);
+    const float *pend_o = nullptr, *pend_post = nullptr;  // residual not yet added to x
+    int st;
     for (uint32_t il = 0; il < c.n_layer; il++) {
         const LayerW &L = b->layers[il];
-        k_rmsnorm<<<(uint32_t)n, 256, 0, s>>>(b->x, L.attn_norm, e, c.rms_eps, b->xn);
-        int st = matmul(b, b->xn, (uint32_t)n, e, {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}});
-        if (st) return st;
+        const uint32_t fqkv = formats({L.wq, L.wk, L.wv});
+        if ((st = norm_q(b, n, b->x, pend_o, pend_post, L.attn_norm, nullptr, fqkv))) return st;
+        if ((st = matmul(b, (uint32_t)n, e, fqkv, {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}}))) return st;
         const bool swa_rope = L.swa && c.rope_base_swa > 0.0f;
-        const uint64_t items = n * (c.n_head + 2 * c.n_head_kv);
-        k_qkv_post<<<(uint32_t)((items + 3) / 4), 128, 0, s>>>(b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
-                                                              swa_rope ? b->inv_freq_swa : b->inv_freq, (uint32_t)n,
-                                                              c.n_head, c.n_head_kv, hd, c.rope_dim, c.rope_neox,
-                                                              b->pos_dev, c.rms_eps, c.attn_scale);
-        st = launch_kv_store(ctx, b->kv[il], b->k, b->v, n, pos0, b->pos_dev);
-        if (st) return st;
+        QkvPostParams qp{b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
+                         swa_rope ? b->inv_freq_swa : b->inv_freq, b->pos_dev, (uint32_t)n, c.n_head, hd,
+                         c.rope_dim, c.rope_neox, c.rms_eps, c.attn_scale};
+        if ((st = launch_qkv_post_store(ctx, b->kv[il], qp))) return st;
         const uint64_t window = L.swa ? c.swa_window : 0;
-        st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, b->att,
-                              fixed_grid ? attention_max_splits(b->kv[il], window) : 0, b->attn_scratch);
+        const uint32_t fo = formats({L.wo});
+        const ActOut ao = acts_out(b, fo);
+        const uint32_t nsp = fixed_grid ? attention_max_splits(b->kv[il], window) : 0;
+        if (b->fused_merge) {
+            st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, nullptr,
+                                  nsp, b->attn_scratch, &ao);
+        } else {
+            st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, b->att,
+                                  nsp, b->attn_scratch, nullptr);
+            if (!st) st = launch_quantize(ctx, b->acts->v, b->att, (uint32_t)n, qd, fo);
+        }
         if (st) return st;
-        st = matmul(b, b->att, (uint32_t)n, qd, {{L.wo, b->o, e}});
-        if (st) return st;
-        k_residual<<<(uint32_t)n, 256, 0, s>>>(b->x, b->o, L.post_attn, e, c.rms_eps, c.residual_scale);
-        k_rmsnorm<<<(uint32_t)n, 256, 0, s>>>(b->x, L.ffn_norm, e, c.rms_eps, b->xn);
+        if ((st = matmul(b, (uint32_t)n, qd, fo, {{L.wo, b->o, e}}))) return st;
+        const uint32_t fgu = formats({L.gate, L.up});
+        if ((st = norm_q(b, n, b->x, b->o, L.post_attn, L.ffn_norm, nullptr, fgu))) return st;
         const uint32_t ff = (uint32_t)L.gate->rows;
-        st = matmul(b, b->xn, (uint32_t)n, e, {{L.gate, b->g, ff}, {L.up, b->u, ff}});
-        if (st) return st;
-        const uint64_t ng = n * ff;
-        k_glu<<<(uint32_t)((ng + 255) / 256), 256, 0, s>>>(b->g, b->u, ng, c.act);
-        st = matmul(b, b->g, (uint32_t)n, ff, {{L.down, b->o, e}});
-        if (st) return st;
-        k_residual<<<(uint32_t)n, 256, 0, s>>>(b->x, b->o, L.post_ffn, e, c.rms_eps, c.residual_scale);
+        if ((st = matmul(b, (uint32_t)n, e, fgu, {{L.gate, b->g, ff}, {L.up, b->u, ff}}))) return st;
+        const uint32_t fd = formats({L.down});
+        k_glu_q<<<dim3((ff + 1023) / 1024, (uint32_t)n), 1024, 0, s>>>(b->g, b->u, ff, c.act, acts_out(b, fd));
+        if ((st = matmul(b, (uint32_t)n, ff, fd, {{L.down, b->o, e}}))) return st;
+        pend_o = b->o;
+        pend_post = L.post_ffn;
     }
     const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
-    k_rmsnorm<<<(uint32_t)m, 256, 0, s>>>(b->x + first * e, b->out_norm, e, c.rms_eps, b->xn);
+    const uint32_t fout = formats({b->out});
+    if ((st = norm_q(b, m, b->x + first * e, pend_o + first * e, pend_post, b->out_norm, b->xn, fout))) return st;
     b->hidden_rows = m;
-    int st = matmul(b, b->xn, (uint32_t)m, e, {{b->out, logits, c.n_vocab}});
-    if (st) return st;
+    if ((st = matmul(b, (uint32_t)m, e, fout, {{b->out, logits, c.n_vocab}}))) return st;
     if (c.logit_scale != 1.0f || c.final_softcap > 0.0f) {
         const uint64_t nl = m * c.n_vocab;
         k_logit_post<<<(uint32_t)((nl + 255) / 256), 256, 0, s>>>(logits, nl, c.logit_scale, c.final_softcap);
@@ -544,6 +580,8 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
     if (int st = dalloc(b, (void **)&b->pos_dev, sizeof(uint64_t))) return fail(st);
     uint64_t scratch = 0;  // split-context attention partials, sized for the longest layer
     for (uint32_t il = 0; il < c.n_layer; il++) {
+        b->fused_merge = b->fused_merge &&
+                         attention_fused_merge_ok(c.n_head, c.head_dim, act_format(b->layers[il].wo->type));
         const uint64_t window = b->layers[il].swa ? c.swa_window : 0;
         scratch = std::max<uint64_t>(scratch, attention_scratch_bytes(b->kv[il], T, c.n_head,
                                                                       attention_max_splits(b->kv[il], window)));

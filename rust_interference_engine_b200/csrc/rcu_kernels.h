@@ -25,9 +25,27 @@ int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint
 // == nullptr uses the context's growable scratch (may allocate).
 int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
                     const uint64_t *pos_ptr);
+// aq != nullptr fuses the activation quantization (for the Wo matmul) into the merge; out
+// may then be nullptr.
+struct ActOut;
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
                      const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
-                     float *scratch);
+                     float *scratch, const ActOut *aq);
+
+// Bias, q/k norm, RoPE and attn_scale on the fused QKV output, with k and v appended to the
+// cache at slot (*pos_ptr + t) % slots (q is updated in place).
+struct QkvPostParams {
+    float *q;
+    const float *k, *v;
+    const float *bq, *bk, *bv, *qn, *kn, *inv_freq;
+    const uint64_t *pos_ptr;
+    uint32_t n_tok, n_head, hd, rope_dim;
+    int neox;
+    float eps, attn_scale;
+};
+int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p);
+// Whether the merge can quantize in the same kernel for this head shape and act format.
+bool attention_fused_merge_ok(uint64_t n_head, uint64_t hd, uint32_t fmt);
 uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window);
 uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split);
 

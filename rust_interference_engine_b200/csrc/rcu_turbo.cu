@@ -16,6 +16,7 @@
 #include <cstring>
 #include <vector>
 
+#include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
 
@@ -138,6 +139,27 @@ __device__ __forceinline__ int quant32(float v, int rounding, float &d_out) {
 }
 
 // ---- KV append ----------------------------------------------------------------------------
+// Encodes one warp-owned shared row x (hd values; turbo rotates it in place) into cache row dst.
+__device__ void store_row(int type, float *x, uint32_t hd, uint8_t *dst, uint8_t *qtmp, int lane) {
+    if (type == RCU_KV_F16) {
+        unsigned short *o = reinterpret_cast<unsigned short *>(dst);
+        for (uint32_t i = lane; i < hd; i += 32) o[i] = __half_as_ushort(__float2half_rn(x[i]));
+        return;
+    }
+    if (type == RCU_KV_Q8_0) {  // store_q8_0 (cpu.rs:637-647): scalar rounding, f16 scale
+        for (uint32_t b = 0; b < hd / 32; b++) {
+            float d;
+            const int q = quant32(x[b * 32 + lane], RCU_ROUND_HALF_AWAY, d);
+            uint8_t *ob = dst + b * 34;
+            if (lane == 0) *reinterpret_cast<unsigned short *>(ob) = __half_as_ushort(__float2half_rn(d));
+            ob[2 + lane] = (uint8_t)(int8_t)q;
+        }
+        return;
+    }
+    rotate_row(x, hd, false, lane);
+    encode_rotated_row(x, hd, dst, qtmp, lane);
+}
+
 // One warp per (token, kv head, k|v). Rows land at slot (pos0 + t) % slots.
 __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restrict__ k, const float *__restrict__ v,
                                                   uint32_t n_tok, uint32_t n_kv, uint32_t hd, uint32_t slots,
@@ -153,26 +175,71 @@ __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restr
     const float *src = (which ? v : k) + ((uint64_t)t * n_kv + h) * hd;
     const uint64_t slot = (pos0 + t) % slots;
     uint8_t *dst = (which ? vc : kc) + ((uint64_t)h * slots + slot) * row_bytes;
-    if (type == RCU_KV_F16) {
-        unsigned short *o = reinterpret_cast<unsigned short *>(dst);
-        for (uint32_t i = lane; i < hd; i += 32) o[i] = __half_as_ushort(__float2half_rn(src[i]));
-        return;
-    }
-    if (type == RCU_KV_Q8_0) {  // store_q8_0 (cpu.rs:637-647): scalar rounding, f16 scale
-        for (uint32_t b = 0; b < hd / 32; b++) {
-            float d;
-            const int q = quant32(src[b * 32 + lane], RCU_ROUND_HALF_AWAY, d);
-            uint8_t *ob = dst + b * 34;
-            if (lane == 0) *reinterpret_cast<unsigned short *>(ob) = __half_as_ushort(__float2half_rn(d));
-            ob[2 + lane] = (uint8_t)(int8_t)q;
-        }
-        return;
-    }
     float *x = xs[warp];
     for (uint32_t i = lane; i < hd; i += 32) x[i] = src[i];
     __syncwarp();
-    rotate_row(x, hd, false, lane);
-    encode_rotated_row(x, hd, dst, qs[warp], lane);
+    store_row(type, x, hd, dst, qs[warp], lane);
+}
+
+// Per head vector of the fused QKV output, one warp each: bias, q/k RMSNorm (x *= scale*w),
+// RoPE (ops.rs:65-99), then q heads are scaled by attn_scale and written back, while k and v
+// heads go straight into the cache at slot (pos + t) % slots (cpu.rs:280-328).
+// Vectors: [t][0..n_head) = q heads, [t][n_head..n_head+n_kv) = k heads, then v heads.
+__global__ void __launch_bounds__(128) k_qkv_post_store(QkvPostParams p, int type, uint32_t n_kv, uint32_t slots,
+                                                        uint32_t row_bytes, uint8_t *__restrict__ kc,
+                                                        uint8_t *__restrict__ vc) {
+    __shared__ float buf[4][kMaxHd];
+    __shared__ uint8_t qs[4][kMaxHd];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t hd = p.hd, per_tok = p.n_head + 2 * n_kv;
+    const uint64_t item = (uint64_t)blockIdx.x * 4 + warp;
+    if (item >= (uint64_t)p.n_tok * per_tok) return;
+    const uint32_t t = (uint32_t)(item / per_tok), j = (uint32_t)(item % per_tok);
+    const float *src, *bias, *norm;
+    int kind;  // 0 q, 1 k, 2 v
+    uint32_t h;
+    if (j < p.n_head) {
+        h = j, kind = 0, norm = p.qn;
+        src = p.q + ((uint64_t)t * p.n_head + h) * hd, bias = p.bq ? p.bq + h * hd : nullptr;
+    } else if (j < p.n_head + n_kv) {
+        h = j - p.n_head, kind = 1, norm = p.kn;
+        src = p.k + ((uint64_t)t * n_kv + h) * hd, bias = p.bk ? p.bk + h * hd : nullptr;
+    } else {
+        h = j - p.n_head - n_kv, kind = 2, norm = nullptr;
+        src = p.v + ((uint64_t)t * n_kv + h) * hd, bias = p.bv ? p.bv + h * hd : nullptr;
+    }
+    float *x = buf[warp];
+    for (uint32_t i = lane; i < hd; i += 32) x[i] = src[i] + (bias ? bias[i] : 0.0f);
+    __syncwarp();
+    if (norm) {
+        float ss = 0.0f;
+        for (uint32_t i = lane; i < hd; i += 32) ss += x[i] * x[i];
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float scale = 1.0f / sqrtf(ss / (float)hd + p.eps);
+        for (uint32_t i = lane; i < hd; i += 32) x[i] *= scale * norm[i];
+        __syncwarp();
+    }
+    const uint64_t pos = *p.pos_ptr + t;
+    if (kind != 2) {
+        const uint32_t half = p.rope_dim / 2;
+        const float fpos = (float)pos;
+        for (uint32_t i = lane; i < half; i += 32) {
+            float sn, cs;
+            sincosf(fpos * p.inv_freq[i], &sn, &cs);
+            const uint32_t i0 = p.neox ? i : 2 * i, i1 = p.neox ? i + half : 2 * i + 1;
+            const float a = x[i0], b = x[i1];
+            x[i0] = a * cs - b * sn;
+            x[i1] = a * sn + b * cs;
+        }
+        __syncwarp();
+    }
+    if (kind == 0) {
+        float *dst = p.q + ((uint64_t)t * p.n_head + h) * hd;
+        for (uint32_t i = lane; i < hd; i += 32) dst[i] = x[i] * p.attn_scale;
+        return;
+    }
+    uint8_t *dst = (kind == 1 ? kc : vc) + ((uint64_t)h * slots + pos % slots) * row_bytes;
+    store_row(type, x, hd, dst, qs[warp], lane);
 }
 
 // quantize_4 of arbitrary rows (turbo.rs:167-171), reference row layout out.
@@ -206,6 +273,8 @@ __global__ void __launch_bounds__(128) k_turbo_rotate(float *__restrict__ x, uin
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxGroup = 16;
+constexpr uint32_t kCombineMaxSplits = 256;  // split-plan cap (fused merge keeps weights in smem)
+constexpr uint32_t kCombineMaxHeads = 8;
 constexpr int kMaxAttnHd = 256;
 
 struct AttnParams {
@@ -503,6 +572,19 @@ static int scratch_get(rcu_ctx *ctx, size_t bytes, void **out) {
 }
 
 
+int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p) {
+    if (p.hd != kv->hd) return set_err(ctx, RCU_ERR_INVALID, "qkv post: head_dim differs from the cache's");
+    if (kv->type == RCU_KV_TURBO4) {
+        if (int st = ensure_signs(ctx)) return st;
+    }
+    const uint64_t items = (uint64_t)p.n_tok * (p.n_head + 2 * kv->n_kv);
+    k_qkv_post_store<<<(uint32_t)((items + 3) / 4), 128, 0, ctx->stream>>>(p, kv->type, (uint32_t)kv->n_kv,
+                                                                         (uint32_t)kv->slots, (uint32_t)kv->row_bytes,
+                                                                         kv->k, kv->v);
+    RCU_CUDA_TRY(ctx, cudaGetLastError());
+    return RCU_OK;
+}
+
 int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
                     const uint64_t *pos_ptr) {
     const uint64_t items = n_tok * kv->n_kv * 2;
@@ -519,7 +601,7 @@ static void split_plan(uint64_t max_len, uint64_t n_tok, uint64_t n_kv, int num_
                        uint32_t *rows_per_split) {
     const uint64_t n_sub = (max_len + 63) / 64;
     const uint64_t want = std::max<uint64_t>(1, (2 * (uint64_t)num_sms) / std::max<uint64_t>(1, n_kv * n_tok));
-    const uint64_t splits = std::max<uint64_t>(1, std::min(n_sub, want));
+    const uint64_t splits = std::max<uint64_t>(1, std::min<uint64_t>(std::min(n_sub, want), kCombineMaxSplits));
     const uint64_t subs_per = (n_sub + splits - 1) / splits;
     *rows_per_split = (uint32_t)(subs_per * 64);
     *n_split = (uint32_t)((max_len + *rows_per_split - 1) / *rows_per_split);
@@ -534,8 +616,77 @@ uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_he
     return n_tok * n_head * n_split * (kv->hd + 2) * sizeof(float);
 }
 
+// Merge of the splits fused with the activation quantization of the Wo matmul: one CTA per
+// (token, run of hpc heads), one output value per thread (hpc * hd threads: whole Q8_0
+// blocks, and whole Q8_K blocks when that format is asked for).
 template <int KV>
-static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, dim3 cgrid, float *out) {
+__global__ void __launch_bounds__(1024) k_attn_combine_q(const __grid_constant__ AttnParams p, uint32_t hpc,
+                                                         float *__restrict__ out, const ActOut ao) {
+    __shared__ float fac[kCombineMaxHeads][kCombineMaxSplits];
+    __shared__ __align__(16) float ob[1024];
+    __shared__ Q8kShared sh;
+    const uint32_t t = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hd = p.hd;
+    const uint32_t h0 = blockIdx.x * hpc, nw = blockDim.x >> 5;
+    // 1. per-head merge weights exp(m_s - M) / L
+    for (uint32_t hh = warp; hh < hpc; hh += nw) {
+        const uint64_t base = ((uint64_t)t * p.n_head + h0 + hh) * p.n_split;
+        float M = -INFINITY;
+        for (uint32_t s = lane; s < p.n_split; s += 32) M = fmaxf(M, p.m_part[base + s]);
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        for (uint32_t s = lane; s < p.n_split; s += 32) {
+            const float m = p.m_part[base + s];
+            const float f = m == -INFINITY ? 0.0f : expf(m - M);
+            fac[hh][s] = f;
+            L += f * p.l_part[base + s];
+        }
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float invL = 1.0f / L;
+        for (uint32_t s = lane; s < p.n_split; s += 32) fac[hh][s] *= invL;
+    }
+    __syncthreads();
+    // 2. one dimension per thread
+    const uint32_t hh = tid / hd, d = tid % hd;
+    const uint64_t base = ((uint64_t)t * p.n_head + h0 + hh) * p.n_split;
+    float acc = 0.0f;
+    for (uint32_t s = 0; s < p.n_split; s++) {
+        const float f = fac[hh][s];
+        if (f != 0.0f) acc += f * p.o_part[(base + s) * hd + d];
+    }
+    if (KV == RCU_KV_TURBO4) {
+        ob[tid] = acc;
+        __syncthreads();
+        if (warp < hpc) rotate_row(ob + warp * hd, hd, true, lane);
+        __syncthreads();
+        acc = ob[tid];
+    }
+    const uint64_t row_k = (uint64_t)p.n_head * hd, col = (uint64_t)h0 * hd + tid;
+    if (out) out[t * row_k + col] = acc;
+    // 3. quantize (the CTA covers whole blocks)
+    if (ao.fmt & RCU_ACT_Q8_0) q8_0_block(acc, (t * row_k + col) / QK, lane, ao);
+    if (ao.fmt & RCU_ACT_Q8K) {
+        const uint64_t g0 = (uint64_t)h0 * hd + QK_K * (warp / 8);
+        q8_k_block(acc, tid % QK_K, warp & ~7u, (t * row_k + g0) / QK_K, true, ao, sh, 0);
+    }
+}
+
+// Heads per CTA of the fused merge for this shape, or 0 when the fused kernel cannot cover it.
+static uint32_t combine_heads(uint64_t n_head, uint64_t hd, uint32_t fmt) {
+    uint32_t h = 1;
+    if (fmt & RCU_ACT_Q8K) {
+        while ((h * hd) % QK_K) h++;
+    } else {
+        while (2 * h * hd <= 256 && n_head % (2 * h) == 0) h *= 2;
+    }
+    if (h > kCombineMaxHeads || h * hd > 1024 || n_head % h) return 0;
+    return h;
+}
+
+bool attention_fused_merge_ok(uint64_t n_head, uint64_t hd, uint32_t fmt) { return combine_heads(n_head, hd, fmt) != 0; }
+
+template <int KV>
+static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, float *out, const ActOut *aq,
+                          uint32_t hpc) {
     switch (group) {
         case 1: k_attn_partial<KV, 1><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
         case 2: k_attn_partial<KV, 2><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
@@ -544,14 +695,20 @@ static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 gri
         case 16: k_attn_partial<KV, 16><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
         default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4, 8 or 16");
     }
-    k_attn_combine<KV><<<cgrid, 32, 0, ctx->stream>>>(p, out);
+    if (aq) {
+        k_attn_combine_q<KV><<<dim3(p.n_head / hpc, p.n_tok), hpc * p.hd, 0, ctx->stream>>>(p, hpc, out, *aq);
+    } else {
+        k_attn_combine<KV><<<dim3(p.n_head, p.n_tok), 32, 0, ctx->stream>>>(p, out);
+    }
     return RCU_OK;
 }
 
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
                      const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
-                     float *scratch) {
+                     float *scratch, const ActOut *aq) {
     const uint64_t group = n_head / kv->n_kv;
+    const uint32_t hpc = aq ? combine_heads(n_head, kv->hd, aq->fmt) : 0;
+    if (aq && !hpc) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: no fused merge for this head shape");
     if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
     AttnParams p{};
     p.kc = kv->k;
@@ -587,12 +744,11 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
     p.m_part = p.o_part + parts * kv->hd;
     p.l_part = p.m_part + parts;
     dim3 grid((uint32_t)kv->n_kv, (uint32_t)n_tok, p.n_split);
-    dim3 cgrid((uint32_t)n_head, (uint32_t)n_tok);
     int st = RCU_OK;
     switch (kv->type) {
-        case RCU_KV_F16: st = dispatch_group<RCU_KV_F16>(ctx, p, (int)group, grid, cgrid, out); break;
-        case RCU_KV_Q8_0: st = dispatch_group<RCU_KV_Q8_0>(ctx, p, (int)group, grid, cgrid, out); break;
-        default: st = dispatch_group<RCU_KV_TURBO4>(ctx, p, (int)group, grid, cgrid, out); break;
+        case RCU_KV_F16: st = dispatch_group<RCU_KV_F16>(ctx, p, (int)group, grid, out, aq, hpc); break;
+        case RCU_KV_Q8_0: st = dispatch_group<RCU_KV_Q8_0>(ctx, p, (int)group, grid, out, aq, hpc); break;
+        default: st = dispatch_group<RCU_KV_TURBO4>(ctx, p, (int)group, grid, out, aq, hpc); break;
     }
     if (st) return st;
     RCU_CUDA_TRY(ctx, cudaGetLastError());
@@ -705,7 +861,8 @@ int32_t rcu_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q_dev, uint64
     const uint64_t last = pos0 + n_tok - 1;
     const uint64_t max_len = window > 0 ? std::min<uint64_t>(window, last + 1) : last + 1;
     if (max_len > kv->slots) return set_err(ctx, RCU_ERR_RUNTIME, "context window full");
-    return rcu::launch_attention(ctx, kv, q_dev, n_tok, n_head, pos0, nullptr, window, softcap, out_dev, 0, nullptr);
+    return rcu::launch_attention(ctx, kv, q_dev, n_tok, n_head, pos0, nullptr, window, softcap, out_dev, 0, nullptr,
+                                 nullptr);
 }
 
 }  // extern "C"
