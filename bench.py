@@ -130,23 +130,35 @@ def barrier(world: int):
 
 # ---- workload: config 1 GEMV stack ---------------------------------------------------------
 GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_DISTINCT = 6144, 2048, 72, 8
+GEMV_TYPE = "Q4_0"  # config 1; --wtype runs the same shape in another GGUF type
+BLOCK = {"Q4_0": (32, 18), "Q4_1": (32, 20), "Q5_0": (32, 22), "Q5_1": (32, 24), "Q8_0": (32, 34),
+         "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210)}
 
 
 def gemv_weights(seed: int = 1):
-    """GEMV_DISTINCT distinct Q4_0 matrices from N(0, 0.02) with the reference's quantizer."""
+    """GEMV_DISTINCT distinct matrices from N(0, 0.02) with the reference's quantizer."""
     import oracle as O
     rng = np.random.default_rng(seed)
     mats = []
     for _ in range(GEMV_DISTINCT):
         wf = rng.normal(0.0, 0.02, (GEMV_ROWS, GEMV_K)).astype(np.float32)
-        mats.append(O.quantize_weight(O.Q4_0, wf))
+        mats.append(O.quantize_weight(getattr(O, GEMV_TYPE), wf))
     x = rng.standard_normal((1, GEMV_K)).astype(np.float32)
     return mats, x
 
 
 def gemv_bytes_per_step():
-    w = GEMV_ROWS * GEMV_K // 32 * 18
+    bs, bb = BLOCK[GEMV_TYPE]
+    w = GEMV_ROWS * GEMV_K // bs * bb
     return GEMV_COPIES * (w + GEMV_K * 4 + GEMV_ROWS * 4), w
+
+
+def gemv_meta():
+    kq = GEMV_TYPE.endswith("_K")
+    tag = "config 1" if GEMV_TYPE == "Q4_0" else "config-1 shape"
+    return {"metric": f"quant-matmul HBM GB/s ({GEMV_TYPE} x {'Q8_K' if kq else 'Q8_0'} GEMV, {tag})", "unit": "GB/s",
+            "dtype": f"int8 ({GEMV_TYPE} x {'Q8_K' if kq else 'Q8_0'} blocks, f32 combine)",
+            "workload": f"gemv_{GEMV_TYPE.lower()}_{GEMV_ROWS}x{GEMV_K}" + ("_config1" if GEMV_TYPE == "Q4_0" else "")}
 
 
 def run_gemv(args, world, rank, local):
@@ -157,15 +169,16 @@ def run_gemv(args, world, rank, local):
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
     mats, x = gemv_weights()
-    ws = [rie.Weight.upload(ctx, rie.GgmlType.Q4_0, GEMV_ROWS, GEMV_K, mats[i % GEMV_DISTINCT])
+    ws = [rie.Weight.upload(ctx, getattr(rie.GgmlType, GEMV_TYPE), GEMV_ROWS, GEMV_K, mats[i % GEMV_DISTINCT])
           for i in range(GEMV_COPIES)]
+    fmt = rie.ActFormat.Q8K if GEMV_TYPE.endswith("_K") else rie.ActFormat.Q8_0
     xd = torch.from_numpy(x).cuda()
     outs = torch.zeros((GEMV_COPIES, GEMV_ROWS), device="cuda")
     acts = rie.QuantActs(ctx, 1, GEMV_K)
     jobs = [rie.MatmulJob(w, outs[i], GEMV_ROWS) for i, w in enumerate(ws)]
 
     def step(ev=None):
-        acts.prepare(xd, 1, GEMV_K, rie.ActFormat.Q8_0)
+        acts.prepare(xd, 1, GEMV_K, fmt)
         if ev is not None:
             ev[0].record(stream)
         rie.matmul_multi(ctx, acts, jobs)
@@ -177,7 +190,7 @@ def run_gemv(args, world, rank, local):
     ctx.sync()
     # parity spot check of the benchmarked output against the oracle
     import oracle as O
-    want = O.matmul_multi(x, [(O.Q4_0, mats[0], GEMV_K)], n_threads=8)[0][0]
+    want = O.matmul_multi(x, [(getattr(O, GEMV_TYPE), mats[0], GEMV_K)], n_threads=8)[0][0]
     got = outs[0].cpu().numpy()
     max_rel = float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-6))
 
@@ -219,20 +232,22 @@ def run_gemv(args, world, rank, local):
     step_bytes, w_bytes = gemv_bytes_per_step()
     peak, peak_kind = peaks()
     achieved = step_bytes / (kern_ms * 1e-3) / 1e9
+    gm = gemv_meta()
     res = {
-        "metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)",
+        "metric": gm["metric"],
         "value": world * step_bytes / (ms * 1e-3) / 1e9,
         "unit": "GB/s",
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
-        "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)",
-        "config": {"workload": "gemv_q4_0_6144x2048_config1", "rows": GEMV_ROWS, "k": GEMV_K,
+        "dtype": gm["dtype"],
+        "config": {"workload": gm["workload"], "rows": GEMV_ROWS, "k": GEMV_K,
                    "weight_copies_per_step": GEMV_COPIES, "bytes_per_step": step_bytes,
-                   "l2": "inputs larger than L2 (510 MB weight stack per step)", "parallelism": f"replicas x{world}"},
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e6:.0f} MB weight stack per step)",
+                   "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_0_config1"),
-                     "kernel": "k_gemv<1>", "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
+                     "peak_source": peak_kind, "traffic": profile_traffic(gm["workload"]),
+                     "kernel": "k_gemv<1,16>", "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
         "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_COPIES * GEMV_ROWS * 4,
                 "ms_per_step": e2e_ms},
@@ -247,18 +262,19 @@ def cpu_gemv_sample(seconds: float, threads: int):
     """The oracle (RIE's AVX2 CPU path restated) on GEMVs of the same workload."""
     import oracle as O
     mats, x = gemv_weights()
-    w_bytes = GEMV_ROWS * GEMV_K // 32 * 18
+    _, w_bytes = gemv_bytes_per_step()
     per = w_bytes + GEMV_K * 4 + GEMV_ROWS * 4
-    O.matmul_multi(x, [(O.Q4_0, mats[0], GEMV_K)], n_threads=threads)
+    t = getattr(O, GEMV_TYPE)
+    O.matmul_multi(x, [(t, mats[0], GEMV_K)], n_threads=threads)
     n, t0 = 0, time.perf_counter()
     while True:
-        O.matmul_multi(x, [(O.Q4_0, mats[n % GEMV_DISTINCT], GEMV_K)], n_threads=threads)
+        O.matmul_multi(x, [(t, mats[n % GEMV_DISTINCT], GEMV_K)], n_threads=threads)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": n * per / el / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port", "sample": f"{n} GEMVs of 6144x2048 Q4_0 (rotating over {GEMV_DISTINCT} matrices), {el:.1f} s",
+    return {"value": n * per / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} GEMVs of {GEMV_ROWS}x{GEMV_K} {GEMV_TYPE} (rotating over {GEMV_DISTINCT} matrices), {el:.1f} s",
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
@@ -625,7 +641,12 @@ def main():
     ap.add_argument("--workload", default="decode", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--wtype", default="Q4_0", choices=sorted(BLOCK),
+                    help="GGUF type of the gemv workload (config 1 is Q4_0)")
     args = ap.parse_args()
+    global GEMV_TYPE
+    GEMV_TYPE = args.wtype
+    META["gemv"] = gemv_meta()
     world, rank, local = dist_init()
 
     if args.impl == "reference":

@@ -26,22 +26,43 @@ __device__ __forceinline__ void ld_words(const uint8_t *base, uint64_t off, uint
 // Spread 4 bits (h & 0xF) to bit 4 of each byte.
 __device__ __forceinline__ uint32_t spread4_bit4(uint32_t h) { return (((h & 0xFu) * 0x00204081u) & 0x01010101u) << 4; }
 
+// dp4a with unsigned weight bytes: codes 0..255 (e.g. a nibble in the high half of a byte,
+// i.e. 16 x nibble) times signed activation bytes.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Two int16 halves of a times the two low int8 bytes of b, plus c.
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Byte i (0..3) of w as a sign-extended int (i is a compile-time or lane constant).
+__device__ __forceinline__ int sbyte(uint32_t w, uint32_t i) { return (int)(int8_t)((w >> (8 * i)) & 0xffu); }
+
 // ---- 32-value blocks (activations: 32 int8 codes as 8 words, their exact sum) --------
-struct BlkW {  // decoded weight block: 8 words of unsigned/signed codes in element order
-    uint32_t v[8];
-    float d, m;  // f16 scale (and min for Q4_1/Q5_1) as f32
+// A block at an even byte offset is read as the aligned words around it; one funnel shift
+// per word (by 16 or by 32, i.e. none) puts each field in place.
+struct BlkW {  // decoded weight block
+    uint32_t v[8];  // Q4: v[0..3] low nibbles, v[4..7] = 16 x high nibbles; Q5/Q8: codes
+    float d, m;     // f16 scale (and min for Q4_1/Q5_1) as f32
 };
 
-// Q4_0 (reference.rs:55-62, :221-233): codes nib-8, we keep nib and subtract 8*sum(a).
+// Q4_0 (reference.rs:55-62, :221-233): codes nib-8; we keep nib and subtract 8*sum(a).
 __device__ __forceinline__ void dec_q4_0(const uint8_t *b, uint32_t off, BlkW &o) {
-    uint32_t w[5];
-    ld_words<5>(b, off, w);  // bytes off .. off+20
-    o.d = f16_bits_to_f32(w[0]);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(b + (off & ~3u));
+    const uint32_t sh = (off & 3u) * 8u;  // 0 or 16
+    uint32_t r[5];
+#pragma unroll
+    for (int i = 0; i < 5; i++) r[i] = w[i];
+    o.d = f16_bits_to_f32(__funnelshift_rc(r[0], r[1], sh));
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16);
+        const uint32_t q = __funnelshift_rc(r[i], r[i + 1], sh + 16);
         o.v[i] = q & 0x0F0F0F0Fu;
-        o.v[4 + i] = (q >> 4) & 0x0F0F0F0Fu;
+        o.v[4 + i] = q & 0xF0F0F0F0u;
     }
     o.m = 0.0f;
 }
@@ -55,43 +76,49 @@ __device__ __forceinline__ void dec_q4_1(const uint8_t *b, uint32_t off, BlkW &o
     for (int i = 0; i < 4; i++) {
         const uint32_t q = w[1 + i];
         o.v[i] = q & 0x0F0F0F0Fu;
-        o.v[4 + i] = (q >> 4) & 0x0F0F0F0Fu;
+        o.v[4 + i] = q & 0xF0F0F0F0u;
     }
 }
 // Q5_0 (reference.rs:72-82, :249-264): 5th bit j of qh -> element j, bit j+16 -> j+16.
 __device__ __forceinline__ void dec_q5_0(const uint8_t *b, uint32_t off, BlkW &o) {
-    uint32_t w[6];
-    ld_words<6>(b, off, w);  // d(2) qh(4) qs(16)
-    o.d = f16_bits_to_f32(w[0]);
-    const uint32_t qh = __funnelshift_r(w[0], w[1], 16);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(b + (off & ~3u));
+    const uint32_t sh = (off & 3u) * 8u;
+    uint32_t r[6];
+#pragma unroll
+    for (int i = 0; i < 6; i++) r[i] = w[i];
+    o.d = f16_bits_to_f32(__funnelshift_rc(r[0], r[1], sh));
+    const uint32_t qh = __funnelshift_rc(r[0], r[1], sh + 16);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint32_t q = __funnelshift_r(w[1 + i], w[2 + i], 16);
+        const uint32_t q = __funnelshift_rc(r[1 + i], r[2 + i], sh + 16);
         o.v[i] = (q & 0x0F0F0F0Fu) | spread4_bit4(qh >> (4 * i));
         o.v[4 + i] = ((q >> 4) & 0x0F0F0F0Fu) | spread4_bit4(qh >> (16 + 4 * i));
     }
     o.m = 0.0f;
 }
-// Q5_1 (reference.rs:83-94, :266-281): 24-byte blocks are 4-aligned.
+// Q5_1 (reference.rs:83-94, :266-281): 24-byte blocks are 8-aligned.
 __device__ __forceinline__ void dec_q5_1(const uint8_t *b, uint32_t off, BlkW &o) {
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(b + off);
-    o.d = f16_bits_to_f32(w[0]);
-    o.m = f16_bits_to_f32(w[0] >> 16);
-    const uint32_t qh = w[1];
+    const uint2 *w = reinterpret_cast<const uint2 *>(b + off);
+    const uint2 h = w[0], q01 = w[1], q23 = w[2];
+    o.d = f16_bits_to_f32(h.x);
+    o.m = f16_bits_to_f32(h.x >> 16);
+    const uint32_t qh = h.y, qw[4] = {q01.x, q01.y, q23.x, q23.y};
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint32_t q = w[2 + i];
-        o.v[i] = (q & 0x0F0F0F0Fu) | spread4_bit4(qh >> (4 * i));
-        o.v[4 + i] = ((q >> 4) & 0x0F0F0F0Fu) | spread4_bit4(qh >> (16 + 4 * i));
+        o.v[i] = (qw[i] & 0x0F0F0F0Fu) | spread4_bit4(qh >> (4 * i));
+        o.v[4 + i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | spread4_bit4(qh >> (16 + 4 * i));
     }
 }
 // Q8_0 (reference.rs:95-100, :283-293)
 __device__ __forceinline__ void dec_q8_0(const uint8_t *b, uint64_t off, BlkW &o) {
-    uint32_t w[9];
-    ld_words<9>(b, off, w);
-    o.d = f16_bits_to_f32(w[0]);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(b + (off & ~(uint64_t)3));
+    const uint32_t sh = (uint32_t)(off & 3u) * 8u;
+    uint32_t r[9];
 #pragma unroll
-    for (int i = 0; i < 8; i++) o.v[i] = __funnelshift_r(w[i], w[i + 1], 16);
+    for (int i = 0; i < 9; i++) r[i] = w[i];
+    o.d = f16_bits_to_f32(__funnelshift_rc(r[0], r[1], sh));
+#pragma unroll
+    for (int i = 0; i < 8; i++) o.v[i] = __funnelshift_rc(r[i], r[i + 1], sh + 16);
     o.m = 0.0f;
 }
 
@@ -106,6 +133,16 @@ __device__ __forceinline__ void dec_blk(const uint8_t *b, uint32_t off, BlkW &o)
 // Exact integer block sum s of the reference (offset-coded types subtract 8 / 16 x sum(a)).
 template <int TYPE>
 __device__ __forceinline__ int blk_int(const BlkW &w, const uint32_t (&a)[8], int asum) {
+    if (TYPE == T_Q4_0 || TYPE == T_Q4_1) {
+        int lo = 0, hi = 0;  // hi accumulates 16 x (high nibble . a)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            lo = dp4a_us(w.v[i], a[i], lo);
+            hi = dp4a_us(w.v[4 + i], a[4 + i], hi);
+        }
+        const int s = lo + (hi >> 4);
+        return TYPE == T_Q4_0 ? s - 8 * asum : s;
+    }
     int s0 = 0, s1 = 0;  // two chains halve the dp4a dependency latency
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
@@ -113,7 +150,6 @@ __device__ __forceinline__ int blk_int(const BlkW &w, const uint32_t (&a)[8], in
         s1 = dp4a(w.v[i + 1], a[i + 1], s1);
     }
     int s = s0 + s1;
-    if (TYPE == T_Q4_0) s -= 8 * asum;
     if (TYPE == T_Q5_0) s -= 16 * asum;
     return s;
 }
@@ -122,11 +158,7 @@ constexpr int blk_bytes_c() {
     return TYPE == T_Q4_0 ? 18 : TYPE == T_Q4_1 ? 20 : TYPE == T_Q5_0 ? 22 : TYPE == T_Q5_1 ? 24 : 34;
 }
 
-// ---- 256-value superblocks, 8 cooperating lanes per superblock ----------------------
-// Lane `sub` (0..7) of the group owns elements [64j + 16h, +16) and [64j + 32 + 16h, +16)
-// with j = sub/2, h = sub%2 (Q4_K/Q5_K), and the scale/min index `sub` for the min term.
-
-// get_scale_min_k4 (reference.rs:8-14) on the 12 scale bytes held in 3 words.
+// get_scale_min_k4 (reference.rs:8-14) on the 12 scale bytes held in 3 words (dequantize path).
 __device__ __forceinline__ void scale_min_k4(int j, const uint32_t (&s)[3], uint32_t &sc, uint32_t &mn) {
     auto byte = [&](int i) -> uint32_t { return (s[i >> 2] >> (8 * (i & 3))) & 0xffu; };
     if (j < 4) {
@@ -138,110 +170,111 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint32_t (&s)[3], uint
     }
 }
 
-struct SbAct {  // one lane's share of a Q8_K activation superblock
-    uint4 lo, hi;  // 16 codes for the low-nibble and high-nibble sub-blocks
-    uint32_t bs2;  // bsums[2*sub] | bsums[2*sub+1] << 16 (i16 pair)
-    float d;
+// ---- 256-value superblocks, 8 cooperating lanes per superblock ----------------------
+// Q4_K / Q5_K: lane `sub` (0..7) owns elements [64j + 16h, +16) (sub-block 2j) and
+// [64j + 32 + 16h, +16) (sub-block 2j+1) with j = sub/2, h = sub%2, and the min of
+// sub-block `sub` (whose 32 activations are Q8_K bsums 2*sub and 2*sub+1). The lane's share
+// of the superblock's exact sums is
+//   I = sc[2j] * (w_lo . a_lo) + sc[2j+1] * (w_hi . a_hi),  M = mn[sub] * (bsums pair)
+// and the eight lanes' shares add up to the reference's sumi / summ (reference.rs:295-350).
+struct KLane {  // lane constants
+    uint32_t sub, j, h, sh16, csh;
+    bool hi;
 };
-struct SbW {  // one lane's share of a decoded Q4_K / Q5_K weight superblock
-    uint32_t lo[4], hi[4];
-    int sc_lo, sc_hi, mn;
-    float d, dmin;
-};
-
-// Q4_K (reference.rs:153-168) and Q5_K (reference.rs:169-189) decode of lane `sub`.
+__device__ __forceinline__ KLane k_lane(uint32_t sub) {
+    KLane l;
+    l.sub = sub;
+    l.j = sub >> 1;
+    l.h = sub & 1;
+    l.sh16 = 16 * (l.j & 1);
+    l.csh = 8 * (sub & 3);
+    l.hi = sub >= 4;
+    return l;
+}
+// Scales sc[2j], sc[2j+1] and min mn[sub] from the 12 scale bytes s0..s2
+// (get_scale_min_k4, reference.rs:8-14).
+__device__ __forceinline__ void k_scales(const KLane &l, uint32_t s0, uint32_t s1, uint32_t s2, int &sc_lo, int &sc_hi,
+                                         int &mn) {
+    const uint32_t a = s0 >> l.sh16, b = s2 >> l.sh16;
+    const uint32_t pair = l.hi ? ((b & 0x0F0Fu) | ((a >> 2) & 0x3030u)) : a;
+    sc_lo = (int)(pair & 63u);
+    sc_hi = (int)((pair >> 8) & 63u);
+    const uint32_t c = s1 >> l.csh, d = s2 >> l.csh;
+    const uint32_t m = l.hi ? (((d >> 4) & 0x0Fu) | ((c >> 2) & 0x30u)) : c;
+    mn = (int)(m & 63u);
+}
+// Lane share (I, M) of one Q4_K (144 B) or Q5_K (176 B) superblock at 16-aligned `sb`;
+// alo / ahi: the lane's 16 + 16 activation codes, bs2: bsums[2*sub] | bsums[2*sub+1] << 16.
+// Returns the packed f16 pair (d, dmin).
 template <int TYPE>
-__device__ __forceinline__ void dec_sb_k(const uint8_t *base, uint32_t off, int sub, SbW &o) {
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(base + off);
-    o.d = f16_bits_to_f32(hdr.x);
-    o.dmin = f16_bits_to_f32(hdr.x >> 16);
-    const uint32_t s[3] = {hdr.y, hdr.z, hdr.w};
-    const int j = sub >> 1, h = sub & 1;
-    uint32_t a, b, c, m;
-    scale_min_k4(2 * j, s, a, m);
-    scale_min_k4(2 * j + 1, s, b, m);
-    scale_min_k4(sub, s, c, m);
-    o.sc_lo = (int)a;
-    o.sc_hi = (int)b;
-    o.mn = (int)m;
-    uint4 q, qh = make_uint4(0, 0, 0, 0);
+__device__ __forceinline__ uint32_t k_lane_dot(const KLane &l, const uint8_t *sb, const uint4 &alo, const uint4 &ahi,
+                                               uint32_t bs2, int &I, int &M) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(sb);
+    int sc_lo, sc_hi, mn;
+    k_scales(l, hdr.y, hdr.z, hdr.w, sc_lo, sc_hi, mn);
+    const uint32_t al[4] = {alo.x, alo.y, alo.z, alo.w}, ah[4] = {ahi.x, ahi.y, ahi.z, ahi.w};
+    int s1 = 0, s2 = 0;
     if (TYPE == T_Q4_K) {
-        q = *reinterpret_cast<const uint4 *>(base + off + 16 + 32 * j + 16 * h);
-    } else {  // qh[32] at 16, ql[128] at 48
-        qh = *reinterpret_cast<const uint4 *>(base + off + 16 + 16 * h);
-        q = *reinterpret_cast<const uint4 *>(base + off + 48 + 32 * j + 16 * h);
-    }
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+        const uint4 q = *reinterpret_cast<const uint4 *>(sb + 16 + 32 * l.j + 16 * l.h);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        o.lo[i] = qw[i] & 0x0F0F0F0Fu;
-        o.hi[i] = (qw[i] >> 4) & 0x0F0F0F0Fu;
-        if (TYPE == T_Q5_K) {
-            o.lo[i] |= ((hw[i] >> (2 * j)) & 0x01010101u) << 4;
-            o.hi[i] |= ((hw[i] >> (2 * j + 1)) & 0x01010101u) << 4;
+        for (int i = 0; i < 4; i++) {
+            s1 = dp4a_us(qw[i] & 0x0F0F0F0Fu, al[i], s1);
+            s2 = dp4a_us(qw[i] & 0xF0F0F0F0u, ah[i], s2);
+        }
+        s2 >>= 4;  // exact: every term was 16 x nibble x a
+    } else {  // qh[32] at 16, ql[128] at 48
+        const uint4 qh = *reinterpret_cast<const uint4 *>(sb + 16 + 16 * l.h);
+        const uint4 q = *reinterpret_cast<const uint4 *>(sb + 48 + 32 * l.j + 16 * l.h);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t lo = (qw[i] & 0x0F0F0F0Fu) | (((hw[i] >> (2 * l.j)) & 0x01010101u) << 4);
+            const uint32_t hi = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * l.j + 1)) & 0x01010101u) << 4);
+            s1 = dp4a_us(lo, al[i], s1);
+            s2 = dp4a_us(hi, ah[i], s2);
         }
     }
-}
-// Lane share of sumi (sum_j s1*sc[2j] + s2*sc[2j+1]) and summ ((bsum pair) * mn[sub]).
-__device__ __forceinline__ int dot_sb_k(const SbW &w, const SbAct &a, int &summ) {
-    const uint32_t alo[4] = {a.lo.x, a.lo.y, a.lo.z, a.lo.w};
-    const uint32_t ahi[4] = {a.hi.x, a.hi.y, a.hi.z, a.hi.w};
-    int s1 = 0, s2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        s1 = dp4a(w.lo[i], alo[i], s1);
-        s2 = dp4a(w.hi[i], ahi[i], s2);
-    }
-    const int bsum = (int)(int16_t)(a.bs2 & 0xffffu) + (int)(int16_t)(a.bs2 >> 16);
-    summ = bsum * w.mn;
-    return s1 * w.sc_lo + s2 * w.sc_hi;
+    I = s1 * sc_lo + s2 * sc_hi;
+    M = dp2a_lo(bs2, (uint32_t)mn * 0x0101u, 0);
+    return hdr.x;
 }
 
-// Q6_K (reference.rs:190-207, :352-386). Lane `sub`: half n = sub/4, positions
-// l in [8*lq, 8*lq+8) with lq = sub%4, covering elements 128n + 32k + l (k = 0..3).
-struct SbAct6 {
-    uint2 a[4];  // 8 codes for each k
-    float d;
+// Q6_K (reference.rs:190-207, :352-386). Lane `sub`: half n = sub/4, positions l in
+// [8*lq, 8*lq+8) with lq = sub%4, covering elements 128n + 32k + l (k = 0..3). Exact:
+//   sumi = sum_e sc[e/16] * q6[e] * a[e] - 32 * sum_g sc[g] * bsums[g]
+// the lane's share of the second sum is its groups 2*sub, 2*sub+1 (one dp2a).
+struct Q6Lane {
+    uint32_t n, lq, is, sub;
 };
-struct SbW6 {
-    uint32_t q[4][2];  // unsigned 6-bit codes (0..63), 8 per k
-    int sc[4];
-    float d;
-};
-__device__ __forceinline__ void dec_sb_q6k(const uint8_t *base, uint32_t off, int sub, SbW6 &o) {
-    const int n = sub >> 2, lq = sub & 3, is = lq >> 1;
-    uint32_t A[2], B[2], H[2], S[2], D[1];
-    ld_words<2>(base, off + 64 * n + 8 * lq, A);
-    ld_words<2>(base, off + 64 * n + 32 + 8 * lq, B);
-    ld_words<2>(base, off + 128 + 32 * n + 8 * lq, H);
-    ld_words<2>(base, off + 192 + 8 * n, S);
-    ld_words<1>(base, off + 208, D);
-    o.d = f16_bits_to_f32(D[0]);
+__device__ __forceinline__ Q6Lane q6_lane(uint32_t sub) { return Q6Lane{sub >> 2, sub & 3, (sub & 3) >> 1, sub}; }
+// Superblock at an even offset `off` from a 4-aligned base; a[k]: the lane's 8 activation
+// codes of group k; bs2 = bsums[2*sub] | bsums[2*sub+1] << 16. Returns the f16 d bits.
+__device__ __forceinline__ uint32_t q6_lane_dot(const Q6Lane &l, const uint8_t *base, uint32_t off, const uint2 (&a)[4],
+                                                uint32_t bs2, int &I) {
+    uint32_t A[2], B[2], H[2], S[2];
+    ld_words<2>(base, off + 64 * l.n + 8 * l.lq, A);
+    ld_words<2>(base, off + 64 * l.n + 32 + 8 * l.lq, B);
+    ld_words<2>(base, off + 128 + 32 * l.n + 8 * l.lq, H);
+    ld_words<2>(base, off + 192 + 8 * l.n, S);
+    const uint32_t scp = *reinterpret_cast<const uint16_t *>(base + off + 192 + 2 * l.sub);
+    const uint32_t dbits = *reinterpret_cast<const uint16_t *>(base + off + 208);
+    int acc = 0;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
+        int s = 0;
 #pragma unroll
         for (int w = 0; w < 2; w++) {
             const uint32_t src = (k & 1) ? B[w] : A[w];
             const uint32_t lo4 = (k < 2) ? (src & 0x0F0F0F0Fu) : ((src >> 4) & 0x0F0F0F0Fu);
-            o.q[k][w] = lo4 | (((H[w] >> (2 * k)) & 0x03030303u) << 4);
+            const uint32_t q = lo4 | (((H[w] >> (2 * k)) & 0x03030303u) << 4);
+            s = dp4a_us(q, w ? a[k].y : a[k].x, s);
         }
-        const int scb = 2 * k + is;  // scale byte index within this half (0..7)
-        o.sc[k] = (int)(int8_t)((S[scb >> 2] >> (8 * (scb & 3))) & 0xffu);
+        const uint32_t sci = l.is + 2 * k;  // scale byte within this half: 0..7
+        acc += sbyte(S[sci >> 2], sci & 3) * s;
     }
-}
-// Lane share of sumi: sum_k sc_k * (sum q6*a - 32 * sum a), exact.
-__device__ __forceinline__ int dot_sb_q6k(const SbW6 &w, const SbAct6 &a) {
-    int sumi = 0;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        int acc = dp4a(w.q[k][0], a.a[k].x, 0);
-        acc = dp4a(w.q[k][1], a.a[k].y, acc);
-        int asum = dp4a(0x01010101u, a.a[k].x, 0);
-        asum = dp4a(0x01010101u, a.a[k].y, asum);
-        sumi += w.sc[k] * (acc - 32 * asum);
-    }
-    return sumi;
+    I = acc - 32 * dp2a_lo(bs2, scp, 0);
+    return dbits;
 }
 
 }  // namespace rcu

@@ -2,6 +2,7 @@
 // activations and the matmul dispatcher. Status codes and error strings follow the
 // reference's C ABI conventions (crates/rie-ffi/src/lib.rs:84-157): nothing throws or
 // aborts across the boundary; every failure returns a status and records a message.
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -73,6 +74,7 @@ int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, s
     c->stream = (cudaStream_t)stream;
     c->num_sms = prop.multiProcessorCount;
     c->max_smem_optin = prop.sharedMemPerBlockOptin;
+    if (const char *v = std::getenv("RIE_CUDA_PDL")) c->pdl = std::strcmp(v, "0") != 0;
     e = cudaMalloc(&c->dev_err, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(cuda_err(c, e, "cudaMalloc(err)"));
     e = cudaMemset(c->dev_err, 0, sizeof(uint32_t));

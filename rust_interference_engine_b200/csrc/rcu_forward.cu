@@ -148,6 +148,8 @@ __device__ void dequant_block(int t, const uint8_t *b, float *y, int lane, int n
 
 __global__ void k_embed(const uint32_t *__restrict__ tokens, int type, const uint8_t *__restrict__ w, uint64_t row_bytes,
                         uint32_t e, float scale, float *__restrict__ x) {
+    pdl_wait();
+    pdl_trigger();
     const uint32_t t = blockIdx.x;
     const uint8_t *row = w + (uint64_t)tokens[t] * row_bytes;
     float *y = x + (uint64_t)t * e;
@@ -194,6 +196,8 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
                                                          const float *__restrict__ post_w, float rs,
                                                          const float *__restrict__ w, uint32_t e, float eps,
                                                          float *__restrict__ xn_f32, const ActOut ao) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     __shared__ Q8kShared sh;
     const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -254,6 +258,8 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
 // value per thread, grid (ceil(ff / 1024), tokens).
 __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, const float *__restrict__ u, uint32_t ff,
                                                 int act, const ActOut ao) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ Q8kShared sh;
     const uint32_t t = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t i = blockIdx.x * 1024 + tid;
@@ -275,9 +281,15 @@ __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, con
     }
 }
 
-__global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos) { *pos_dev = pos; }
+__global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos) {
+    pdl_wait();
+    pdl_trigger();
+    *pos_dev = pos;
+}
 
 __global__ void k_logit_post(float *__restrict__ l, uint64_t n, float scale, float cap) {
+    pdl_wait();
+    pdl_trigger();
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     float v = l[i];
@@ -317,14 +329,10 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
     const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
     const ActOut ao = acts_out(b, fmt);
     const float rs = c.residual_scale, eps = c.rms_eps;
-    cudaStream_t s = b->ctx->stream;
-    const dim3 grid((uint32_t)n);
-    if (nit <= 1) k_norm_q<1><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
-    else if (nit <= 2) k_norm_q<2><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
-    else if (nit <= 4) k_norm_q<4><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
-    else if (nit <= 8) k_norm_q<8><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
-    else if (nit <= 16) k_norm_q<16><<<grid, kNormThreads, 0, s>>>(x, o, post_w, rs, w, e, eps, xn_f32, ao);
-    else return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
+    auto kern = nit <= 1 ? k_norm_q<1> : nit <= 2 ? k_norm_q<2> : nit <= 4 ? k_norm_q<4> : nit <= 8 ? k_norm_q<8> : k_norm_q<16>;
+    if (nit > 16) return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
+    RCU_CUDA_TRY(b->ctx, launch_k(b->ctx, kern, dim3((uint32_t)n), dim3(kNormThreads), 0, x, o, post_w, rs, w, e, eps,
+                                  xn_f32, ao));
     return RCU_OK;
 }
 
@@ -339,7 +347,7 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
     const rcu_model_config &c = b->m->cfg;
     cudaStream_t s = ctx->stream;
     const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
-    k_embed<<<(uint32_t)n, 128, 0, s>>>(b->tokens, b->embd->type, b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type, b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x));
     const float *pend_o = nullptr, *pend_post = nullptr;  // residual not yet added to x
     int st;
     for (uint32_t il = 0; il < c.n_layer; il++) {
@@ -371,7 +379,7 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         const uint32_t ff = (uint32_t)L.gate->rows;
         if ((st = matmul(b, (uint32_t)n, e, fgu, {{L.gate, b->g, ff}, {L.up, b->u, ff}}))) return st;
         const uint32_t fd = formats({L.down});
-        k_glu_q<<<dim3((ff + 1023) / 1024, (uint32_t)n), 1024, 0, s>>>(b->g, b->u, ff, c.act, acts_out(b, fd));
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3(dim3((ff + 1023) / 1024, (uint32_t)n)), dim3(1024), 0, b->g, b->u, ff, c.act, acts_out(b, fd)));
         if ((st = matmul(b, (uint32_t)n, ff, fd, {{L.down, b->o, e}}))) return st;
         pend_o = b->o;
         pend_post = L.post_ffn;
@@ -383,7 +391,7 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
     if ((st = matmul(b, (uint32_t)m, e, fout, {{b->out, logits, c.n_vocab}}))) return st;
     if (c.logit_scale != 1.0f || c.final_softcap > 0.0f) {
         const uint64_t nl = m * c.n_vocab;
-        k_logit_post<<<(uint32_t)((nl + 255) / 256), 256, 0, s>>>(logits, nl, c.logit_scale, c.final_softcap);
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_logit_post), dim3((uint32_t)((nl + 255) / 256)), dim3(256), 0, logits, nl, c.logit_scale, c.final_softcap));
     }
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
@@ -646,14 +654,18 @@ static int32_t run_forward(rcu_backend *b, const uint32_t *tokens, bool tokens_o
     RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_in, caller));
     RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(b->stream, b->ev_in, 0));
     ctx->stream = b->stream;
+    ctx->early_weights = true;  // model weights are written only at load time
     struct Restore {
         rcu_ctx *c;
         cudaStream_t s;
-        ~Restore() { c->stream = s; }
+        ~Restore() {
+            c->stream = s;
+            c->early_weights = false;
+        }
     } restore{ctx, caller};
     const cudaMemcpyKind kind = tokens_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
     if (tokens != b->tokens) RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens, n * 4, kind, b->stream));
-    k_set_pos<<<1, 1, 0, b->stream>>>(b->pos_dev, pos);  // by value: no host buffer to keep alive
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_set_pos), dim3(1), dim3(1), 0, b->pos_dev, pos));  // by value: no host buffer to keep alive
     const bool decode = n == 1 && !all_logits && logits == b->logits;
     if (decode && b->use_graphs && b->graph_exec) {
         RCU_CUDA_TRY(ctx, cudaGraphLaunch(b->graph_exec, b->stream));

@@ -45,6 +45,7 @@ struct GemvParams {
     int32_t n_jobs;
     uint32_t total_tiles, stages, stage_bytes, stage_off;
     uint32_t k, n_tok, tok0, formats;
+    uint32_t early_weights;  // producer may load weights before the previous kernel ends
     // shared-memory offsets of the staged activations
     uint32_t o_q0, o_d0, o_s0, o_sum0, o_qk, o_dk, o_bsk;
     ActsView acts;
@@ -104,7 +105,7 @@ __device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb
     }
 }
 
-// ---- 32-value block types ---------------------------------------------------------------
+// ---- 32-value block types: one block per lane per step ----------------------------------
 template <int TYPE, int T>
 __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
                                        uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
@@ -130,6 +131,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
     const float *ad = reinterpret_cast<const float *>(sm + p.o_d0);
     const float *as = reinterpret_cast<const float *>(sm + p.o_s0);
     const int32_t *asm_ = reinterpret_cast<const int32_t *>(sm + p.o_sum0);
+    const uint32_t rb = jb.row_bytes, wrow0 = row_first * rb;
     float acc[kMaxRw][T];
 #pragma unroll
     for (int r = 0; r < kMaxRw; r++)
@@ -145,15 +147,15 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
             const uint4 x0 = src[0], x1 = src[1];
             a[t][0] = x0.x, a[t][1] = x0.y, a[t][2] = x0.z, a[t][3] = x0.w;
             a[t][4] = x1.x, a[t][5] = x1.y, a[t][6] = x1.z, a[t][7] = x1.w;
-            asum[t] = asm_[t * nb + b];
+            asum[t] = (TYPE == T_Q4_0 || TYPE == T_Q5_0) ? asm_[t * nb + b] : 0;
             da[t] = ad[t * nb + b];
-            sa[t] = as[t * nb + b];
+            sa[t] = (TYPE == T_Q4_1 || TYPE == T_Q5_1) ? as[t * nb + b] : 0.0f;
         }
 #pragma unroll
         for (int r = 0; r < kMaxRw; r++) {
             if ((uint32_t)r < nr) {
                 BlkW w;
-                dec_blk<TYPE>(wsm, (row_first + r) * jb.row_bytes + b * BB, w);
+                dec_blk<TYPE>(wsm, wrow0 + r * rb + b * BB, w);
 #pragma unroll
                 for (int t = 0; t < T; t++) {
                     const int si = blk_int<TYPE>(w, a[t], asum[t]);
@@ -175,7 +177,10 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
     }
 }
 
-// ---- 256-value superblock types: 4 groups of 8 lanes per warp ----------------------------
+// ---- 256-value superblock types: 4 groups of 8 lanes per warp, a superblock per group -----
+// Each lane keeps its own f32 partial of every row; one warp reduction per row at the end
+// (the sum of per-lane partials differs from the reference's per-superblock order only by
+// f32 rounding).
 template <int TYPE, int T>
 __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
                                        uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
@@ -197,94 +202,69 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
     }
     if (row_first >= nrows) return;
     if (row_first + nr > nrows) nr = nrows - row_first;
-    const int g = lane >> 3, sub = lane & 7;
+    const uint32_t g = lane >> 3, sub = lane & 7;
     const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_qk);
     const float *adk = reinterpret_cast<const float *>(sm + p.o_dk);
-    const int16_t *abs_ = reinterpret_cast<const int16_t *>(sm + p.o_bsk);
+    const uint32_t *abs2 = reinterpret_cast<const uint32_t *>(sm + p.o_bsk);  // bsums pairs
+    const uint32_t rb = jb.row_bytes, wrow0 = row_first * rb;
     float acc[kMaxRw][T];
 #pragma unroll
     for (int r = 0; r < kMaxRw; r++)
 #pragma unroll
         for (int t = 0; t < T; t++) acc[r][t] = 0.0f;
-    // The trip count is uniform across the warp (shuffles below need every lane); groups
-    // past the end of the row work on zeros and contribute nothing.
-    for (uint32_t sb0 = b_begin; sb0 < b_end; sb0 += 4) {
-        const uint32_t sb = sb0 + g;
-        const bool act = sb < b_end;
-        if (TYPE == T_Q6_K) {
-            SbAct6 a[T];
-            const int n = sub >> 2, lq = sub & 3;
+    if (TYPE == T_Q6_K) {
+        const Q6Lane l = q6_lane(sub);
+        const uint32_t aoff = 128 * l.n + 8 * l.lq;
+        for (uint32_t sb = b_begin + g; sb < b_end; sb += 4) {
+            uint2 a[T][4];
+            uint32_t bs2[T];
+            float ad[T];
 #pragma unroll
             for (int t = 0; t < T; t++) {
-                if (act) {
-                    const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + 128 * n + 8 * lq;
+                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + aoff;
 #pragma unroll
-                    for (int k = 0; k < 4; k++) a[t].a[k] = *reinterpret_cast<const uint2 *>(base + 32 * k);
-                    a[t].d = adk[t * nsb + sb];
-                } else {
-#pragma unroll
-                    for (int k = 0; k < 4; k++) a[t].a[k] = make_uint2(0, 0);
-                    a[t].d = 0.0f;
-                }
+                for (int k = 0; k < 4; k++) a[t][k] = *reinterpret_cast<const uint2 *>(base + 32 * k);
+                bs2[t] = abs2[(size_t)t * (p.k / 32) + 8 * sb + sub];
+                ad[t] = adk[t * nsb + sb];
             }
 #pragma unroll
             for (int r = 0; r < kMaxRw; r++) {
                 if ((uint32_t)r < nr) {
-                    SbW6 w;
-                    if (act) {
-                        dec_sb_q6k(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
-                    } else {
-                        w = SbW6{};
-                    }
 #pragma unroll
                     for (int t = 0; t < T; t++) {
-                        int sumi = dot_sb_q6k(w, a[t]);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 4);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 2);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
-                        if (sub == 0 && act) acc[r][t] += (w.d * a[t].d) * (float)sumi;
+                        int I;
+                        const uint32_t db = q6_lane_dot(l, wsm, wrow0 + r * rb + sb * BB, a[t], bs2[t], I);
+                        acc[r][t] += (f16_bits_to_f32(db) * ad[t]) * (float)I;
                     }
                 }
             }
-        } else {
-            SbAct a[T];
-            const int j = sub >> 1, hh = sub & 1;
+        }
+    } else {
+        const KLane l = k_lane(sub);
+        const uint32_t alo_off = 64 * l.j + 16 * l.h;
+        for (uint32_t sb = b_begin + g; sb < b_end; sb += 4) {
+            uint4 alo[T], ahi[T];
+            uint32_t bs2[T];
+            float ad[T];
 #pragma unroll
             for (int t = 0; t < T; t++) {
-                if (act) {
-                    const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K;
-                    a[t].lo = *reinterpret_cast<const uint4 *>(base + 64 * j + 16 * hh);
-                    a[t].hi = *reinterpret_cast<const uint4 *>(base + 64 * j + 32 + 16 * hh);
-                    a[t].bs2 = *reinterpret_cast<const uint32_t *>(abs_ + (size_t)t * (p.k / 16) + 16 * sb + 2 * sub);
-                    a[t].d = adk[t * nsb + sb];
-                } else {
-                    a[t].lo = a[t].hi = make_uint4(0, 0, 0, 0);
-                    a[t].bs2 = 0;
-                    a[t].d = 0.0f;
-                }
+                const int8_t *base = aq + (size_t)t * p.k + (size_t)sb * QK_K + alo_off;
+                alo[t] = *reinterpret_cast<const uint4 *>(base);
+                ahi[t] = *reinterpret_cast<const uint4 *>(base + 32);
+                bs2[t] = abs2[(size_t)t * (p.k / 32) + 8 * sb + sub];
+                ad[t] = adk[t * nsb + sb];
             }
 #pragma unroll
             for (int r = 0; r < kMaxRw; r++) {
                 if ((uint32_t)r < nr) {
-                    SbW w;
-                    if (act) {
-                        dec_sb_k<TYPE>(wsm, (row_first + r) * jb.row_bytes + sb * BB, sub, w);
-                    } else {
-                        w = SbW{};
-                    }
+                    const uint8_t *sbp = wsm + wrow0 + r * rb + sb * BB;
 #pragma unroll
                     for (int t = 0; t < T; t++) {
-                        int summ;
-                        int sumi = dot_sb_k(w, a[t], summ);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 4);
-                        summ += __shfl_xor_sync(0xffffffffu, summ, 4);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 2);
-                        summ += __shfl_xor_sync(0xffffffffu, summ, 2);
-                        sumi += __shfl_xor_sync(0xffffffffu, sumi, 1);
-                        summ += __shfl_xor_sync(0xffffffffu, summ, 1);
+                        int I, M;
+                        const uint32_t dm = k_lane_dot<TYPE>(l, sbp, alo[t], ahi[t], bs2[t], I, M);
                         // d * sumi - dmin * summ with d = f16(d)*ab.d, dmin = f16(dmin)*ab.d
-                        if (sub == 0 && act)
-                            acc[r][t] += (w.d * a[t].d) * (float)sumi - (w.dmin * a[t].d) * (float)summ;
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&dm));
+                        acc[r][t] += (f.x * ad[t]) * (float)I - (f.y * ad[t]) * (float)M;
                     }
                 }
             }
@@ -301,24 +281,13 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
     }
 }
 
-__device__ __forceinline__ int find_job(const GemvParams &p, uint32_t tile) {
-    int lo = 0, hi = p.n_jobs - 1;  // last job whose first tile is <= tile
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (p.jobs[mid].tile_begin <= tile)
-            lo = mid;
-        else
-            hi = mid - 1;
-    }
-    return lo;
-}
-
 template <int T, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     SmemHdr *h = reinterpret_cast<SmemHdr *>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t S = p.stages;
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; s++) {
             mbar_init(&h->full[s], 1);
@@ -330,17 +299,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
     __syncthreads();
 
     if (warp == NW) {  // ---- producer ----
+        if (!p.early_weights) pdl_wait();
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             uint32_t li = 0;
-            bool ok = true;
+            int ji = 0;  // tiles are visited in increasing order: the job index only advances
             for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
                 const uint32_t s = li % S;
-                if (li >= S && !mbar_wait_bounded(&h->empty[s], ((li / S) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-                    ok = false;
-                    break;
-                }
-                const GemvJobDev &jb = p.jobs[find_job(p, tile)];
+                if (li >= S && !mbar_wait_bounded(&h->empty[s], ((li / S) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+                while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
+                const GemvJobDev &jb = p.jobs[ji];
                 const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
                 const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
                 const uint32_t bytes = (nrows * jb.row_bytes + 15u) & ~15u;
@@ -354,12 +322,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
                 const uint32_t last = ((issued - 1 - s) / S) * S + s;  // last li with li % S == s
                 mbar_wait_bounded(&h->full[s], (last / S) & 1, p.err, ERR_TIMEOUT_DRAIN);
             }
-            (void)ok;
         }
         return;
     }
 
     // ---- consumers: stage this call's quantized activations -------------------------------
+    // (with early_weights the producer streams weights before the previous kernel ends;
+    // everything else waits for it)
+    pdl_wait();
     {
         const uint32_t nt = p.n_tok, k = p.k, tid = threadIdx.x, nthr = NW * 32;
         const ActsView &A = p.acts;
@@ -381,17 +351,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
             for (uint32_t i = tid; i < nt * k / 16; i += nthr) dst[i] = src[i];
             for (uint32_t i = tid; i < nt * nsb; i += nthr)
                 reinterpret_cast<float *>(smem + p.o_dk)[i] = A.dk[(size_t)p.tok0 * nsb + i];
-            for (uint32_t i = tid; i < nt * k / 16; i += nthr)
-                reinterpret_cast<int16_t *>(smem + p.o_bsk)[i] = A.bsk[(size_t)p.tok0 * (k / 16) + i];
+            const uint32_t *bsrc = reinterpret_cast<const uint32_t *>(A.bsk + (size_t)p.tok0 * (k / 16));
+            for (uint32_t i = tid; i < nt * k / 32; i += nthr) reinterpret_cast<uint32_t *>(smem + p.o_bsk)[i] = bsrc[i];
         }
         named_bar_sync(1, NW * 32);
     }
 
     uint32_t li = 0;
+    int ji = 0;
     for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
         const uint32_t s = li % S;
         if (!mbar_wait_bounded(&h->full[s], (li / S) & 1, p.err, ERR_TIMEOUT_FULL)) break;
-        const GemvJobDev &jb = p.jobs[find_job(p, tile)];
+        while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
+        const GemvJobDev &jb = p.jobs[ji];
         const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
         const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
         const uint8_t *wsm = smem + p.stage_off + s * p.stage_bytes;
@@ -412,6 +384,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
 }
 
 // ---- exact per-block integer sums of one (row, token) pair (validation path) ----------
+// The same lane decoders as the GEMV; K-quant lane shares are reduced over the 8 lanes.
 __global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ wrow, uint32_t row_bytes, int type,
                                                   ActsView A, uint32_t tok, int32_t *__restrict__ out) {
     extern __shared__ __align__(16) uint8_t srow[];
@@ -443,33 +416,28 @@ __global__ void __launch_bounds__(32) k_block_sums(const uint8_t *__restrict__ w
         return;
     }
     const uint32_t nsb = k / QK_K;
-    const int g = lane >> 3, sub = lane & 7;
+    const uint32_t g = lane >> 3, sub = lane & 7;
     const int8_t *aq = A.qk + (size_t)tok * k;
+    const uint32_t *bs = reinterpret_cast<const uint32_t *>(A.bsk + (size_t)tok * (k / 16));
     for (uint32_t sb0 = 0; sb0 < nsb; sb0 += 4) {
         const uint32_t sb = sb0 + g;
         const bool act = sb < nsb;  // uniform trip count: shuffles below need every lane
         int sumi = 0, summ = 0;
         if (act && type == T_Q6_K) {
-            SbAct6 a;
-            const int n = sub >> 2, lq = sub & 3;
+            const Q6Lane l = q6_lane(sub);
+            uint2 a[4];
             for (int kk = 0; kk < 4; kk++)
-                a.a[kk] = *reinterpret_cast<const uint2 *>(aq + (size_t)sb * QK_K + 128 * n + 8 * lq + 32 * kk);
-            SbW6 w;
-            dec_sb_q6k(srow, sb * 210, sub, w);
-            sumi = dot_sb_q6k(w, a);
+                a[kk] = *reinterpret_cast<const uint2 *>(aq + (size_t)sb * QK_K + 128 * l.n + 8 * l.lq + 32 * kk);
+            q6_lane_dot(l, srow, sb * 210, a, bs[8 * sb + sub], sumi);
         } else if (act) {
-            SbAct a;
-            const int j = sub >> 1, hh = sub & 1;
-            a.lo = *reinterpret_cast<const uint4 *>(aq + (size_t)sb * QK_K + 64 * j + 16 * hh);
-            a.hi = *reinterpret_cast<const uint4 *>(aq + (size_t)sb * QK_K + 64 * j + 32 + 16 * hh);
-            a.bs2 = *reinterpret_cast<const uint32_t *>(A.bsk + (size_t)tok * (k / 16) + 16 * sb + 2 * sub);
-            SbW w;
+            const KLane l = k_lane(sub);
+            const int8_t *base = aq + (size_t)sb * QK_K + 64 * l.j + 16 * l.h;
+            const uint4 alo = *reinterpret_cast<const uint4 *>(base), ahi = *reinterpret_cast<const uint4 *>(base + 32);
             if (type == T_Q4_K) {
-                dec_sb_k<T_Q4_K>(srow, sb * 144, sub, w);
+                k_lane_dot<T_Q4_K>(l, srow + sb * 144, alo, ahi, bs[8 * sb + sub], sumi, summ);
             } else {
-                dec_sb_k<T_Q5_K>(srow, sb * 176, sub, w);
+                k_lane_dot<T_Q5_K>(l, srow + sb * 176, alo, ahi, bs[8 * sb + sub], sumi, summ);
             }
-            sumi = dot_sb_k(w, a, summ);
         }
         for (int o = 4; o; o >>= 1) {
             sumi += __shfl_xor_sync(0xffffffffu, sumi, o);
@@ -507,7 +475,7 @@ static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t g
                                                (int)ctx->max_smem_optin));
         attr_set[ctx->device & 63] = true;
     }
-    k_gemv<T, NW><<<grid, (NW + 1) * 32, smem_bytes, ctx->stream>>>(p);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_gemv<T, NW>), dim3(grid), dim3((NW + 1) * 32), smem_bytes, p));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
@@ -522,6 +490,7 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     p.tok0 = tok0;
     p.acts = a;
     p.err = ctx->dev_err;
+    p.early_weights = ctx->early_weights ? 1u : 0u;
     uint32_t tiles = 0, stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
         const rcu_weight *w = jobs[i].w;

@@ -167,6 +167,10 @@ struct rcu_ctx {
     int num_sms = 148;
     size_t max_smem_optin = 0;
     uint32_t *dev_err = nullptr;  // device error bits
+    bool pdl = true;              // programmatic dependent launch for the kernels of this library
+    // GEMV weights may be streamed before the previous kernel has finished (set while the
+    // forward scheduler runs: its weights are written once, at load time)
+    bool early_weights = false;
     std::string last_error;
 };
 
@@ -189,6 +193,32 @@ struct rcu_acts {
 namespace rcu {
 int set_err(rcu_ctx *c, int code, const std::string &msg);
 int cuda_err(rcu_ctx *c, cudaError_t e, const char *what);
+}  // namespace rcu
+
+namespace rcu {
+// Programmatic dependent launch. Kernels started with launch_k may begin while the kernel
+// before them in the stream is still running. Each of them calls pdl_wait() before its first
+// access to memory that an earlier kernel writes or reads (everything but the weights), and
+// pdl_trigger() to let the kernel after it launch early. pdl_wait() returns once the previous
+// kernel has completed and its writes are visible; on a plain launch both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(const rcu_ctx *ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 }  // namespace rcu
 
 #define RCU_CUDA_TRY(ctx, expr)                                           \

@@ -8,6 +8,8 @@ namespace rcu {
 // One warp per 32-value block, one value per lane.
 __global__ void __launch_bounds__(256) k_quantize_q8_0(const float *__restrict__ x, uint32_t n_tok, uint32_t k,
                                                        const ActOut o) {
+    pdl_wait();
+    pdl_trigger();
     const uint32_t nb = k / QK;
     const uint64_t blk = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (blk >= (uint64_t)n_tok * nb) return;
@@ -17,6 +19,8 @@ __global__ void __launch_bounds__(256) k_quantize_q8_0(const float *__restrict__
 
 // One CTA of 256 threads per 256-value block.
 __global__ void __launch_bounds__(256) k_quantize_q8_k(const float *__restrict__ x, const ActOut o) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ Q8kShared sh;
     const uint64_t blk = blockIdx.x;
     q8_k_block(x[blk * QK_K + threadIdx.x], threadIdx.x, 0, blk, true, o, sh, 0);
@@ -27,12 +31,12 @@ int launch_quantize(rcu_ctx *ctx, const ActsView &a, const float *x, uint32_t n_
     if (formats & RCU_ACT_Q8_0) {
         const uint64_t nblk = (uint64_t)n_tok * (k / QK);
         const uint32_t grid = (uint32_t)((nblk + 7) / 8);
-        k_quantize_q8_0<<<grid, 256, 0, ctx->stream>>>(x, n_tok, k, o);
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_quantize_q8_0), dim3(grid), dim3(256), 0, x, n_tok, k, o));
         RCU_CUDA_TRY(ctx, cudaGetLastError());
     }
     if (formats & RCU_ACT_Q8K) {
         const uint64_t nblk = (uint64_t)n_tok * (k / QK_K);
-        k_quantize_q8_k<<<(uint32_t)nblk, 256, 0, ctx->stream>>>(x, o);
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_quantize_q8_k), dim3((uint32_t)nblk), dim3(256), 0, x, o));
         RCU_CUDA_TRY(ctx, cudaGetLastError());
     }
     return RCU_OK;

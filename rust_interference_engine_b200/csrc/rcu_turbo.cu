@@ -165,6 +165,8 @@ __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restr
                                                   uint32_t n_tok, uint32_t n_kv, uint32_t hd, uint32_t slots,
                                                   uint64_t pos0, const uint64_t *__restrict__ pos_ptr, uint32_t row_bytes,
                                                   uint8_t *__restrict__ kc, uint8_t *__restrict__ vc) {
+    pdl_wait();
+    pdl_trigger();
     if (pos_ptr) pos0 = *pos_ptr;
     __shared__ float xs[4][kMaxHd];
     __shared__ uint8_t qs[4][kMaxHd];
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restr
 __global__ void __launch_bounds__(128) k_qkv_post_store(QkvPostParams p, int type, uint32_t n_kv, uint32_t slots,
                                                         uint32_t row_bytes, uint8_t *__restrict__ kc,
                                                         uint8_t *__restrict__ vc) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float buf[4][kMaxHd];
     __shared__ uint8_t qs[4][kMaxHd];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -301,6 +305,8 @@ __device__ __forceinline__ uint32_t lut16(uint32_t idx, uint32_t t0, uint32_t t1
 // un-normalised partial output with its running max / sum.
 template <int KV, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_constant__ AttnParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int SUB = 64, DPL = kMaxAttnHd / 32;
     const uint32_t g = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
     const uint32_t hd = p.hd, dpl = hd / 32;
@@ -520,6 +526,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
 // Merge the chunks of one (token, head), normalise, rotate back (turbo).
 template <int KV>
 __global__ void __launch_bounds__(32) k_attn_combine(const __grid_constant__ AttnParams p, float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const uint32_t h = blockIdx.x, t = blockIdx.y, lane = threadIdx.x, hd = p.hd;
     const uint64_t base = ((uint64_t)t * p.n_head + h) * p.n_split;
     float M = -INFINITY;
@@ -578,9 +586,7 @@ int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p) {
         if (int st = ensure_signs(ctx)) return st;
     }
     const uint64_t items = (uint64_t)p.n_tok * (p.n_head + 2 * kv->n_kv);
-    k_qkv_post_store<<<(uint32_t)((items + 3) / 4), 128, 0, ctx->stream>>>(p, kv->type, (uint32_t)kv->n_kv,
-                                                                         (uint32_t)kv->slots, (uint32_t)kv->row_bytes,
-                                                                         kv->k, kv->v);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_qkv_post_store), dim3((uint32_t)((items + 3) / 4)), dim3(128), 0, p, kv->type, (uint32_t)kv->n_kv, (uint32_t)kv->slots, (uint32_t)kv->row_bytes, kv->k, kv->v));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
@@ -588,9 +594,7 @@ int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p) {
 int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
                     const uint64_t *pos_ptr) {
     const uint64_t items = n_tok * kv->n_kv * 2;
-    k_kv_store<<<(uint32_t)((items + 3) / 4), 128, 0, ctx->stream>>>(kv->type, k, v, (uint32_t)n_tok, (uint32_t)kv->n_kv,
-                                                                     (uint32_t)kv->hd, (uint32_t)kv->slots, pos0, pos_ptr,
-                                                                     (uint32_t)kv->row_bytes, kv->k, kv->v);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_kv_store), dim3((uint32_t)((items + 3) / 4)), dim3(128), 0, kv->type, k, v, (uint32_t)n_tok, (uint32_t)kv->n_kv, (uint32_t)kv->hd, (uint32_t)kv->slots, pos0, pos_ptr, (uint32_t)kv->row_bytes, kv->k, kv->v));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
@@ -622,6 +626,8 @@ uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_he
 template <int KV>
 __global__ void __launch_bounds__(1024) k_attn_combine_q(const __grid_constant__ AttnParams p, uint32_t hpc,
                                                          float *__restrict__ out, const ActOut ao) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float fac[kCombineMaxHeads][kCombineMaxSplits];
     __shared__ __align__(16) float ob[1024];
     __shared__ Q8kShared sh;
@@ -688,17 +694,17 @@ template <int KV>
 static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, float *out, const ActOut *aq,
                           uint32_t hpc) {
     switch (group) {
-        case 1: k_attn_partial<KV, 1><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
-        case 2: k_attn_partial<KV, 2><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
-        case 4: k_attn_partial<KV, 4><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
-        case 8: k_attn_partial<KV, 8><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
-        case 16: k_attn_partial<KV, 16><<<grid, kAttnThreads, 0, ctx->stream>>>(p); break;
+        case 1: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 1>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
+        case 2: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 2>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
+        case 4: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 4>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
+        case 8: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 8>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
+        case 16: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 16>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
         default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4, 8 or 16");
     }
     if (aq) {
-        k_attn_combine_q<KV><<<dim3(p.n_head / hpc, p.n_tok), hpc * p.hd, 0, ctx->stream>>>(p, hpc, out, *aq);
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_combine_q<KV>), dim3(dim3(p.n_head / hpc, p.n_tok)), dim3(hpc * p.hd), 0, p, hpc, out, *aq));
     } else {
-        k_attn_combine<KV><<<dim3(p.n_head, p.n_tok), 32, 0, ctx->stream>>>(p, out);
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_combine<KV>), dim3(dim3(p.n_head, p.n_tok)), dim3(32), 0, p, out));
     }
     return RCU_OK;
 }
