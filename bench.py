@@ -391,7 +391,7 @@ def run_prefill(args, world, rank, local):
 # ---- workload: config 3 Qwen3-8B-shape Q4_K_M decode ------------------------------------
 QWEN3_8B = dict(arch="qwen3", n_vocab=151936, n_embd=4096, n_layer=36, n_head=32, n_head_kv=8, head_dim=128,
                 n_ff=12288, rope_dim=128, rope_base=1_000_000.0, rms_eps=1e-6)
-DEC_PROMPT = 512
+DEC_PROMPT = 512  # config 3: 512-token prompt (--prompt changes it, e.g. for a short profile)
 
 
 def qwen3_8b_spec(n_layer=None):
@@ -643,9 +643,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--wtype", default="Q4_0", choices=sorted(BLOCK),
                     help="GGUF type of the gemv workload (config 1 is Q4_0)")
+    ap.add_argument("--prompt", type=int, default=512, help="prompt length of the decode workload (config 3: 512)")
     args = ap.parse_args()
-    global GEMV_TYPE
+    global GEMV_TYPE, DEC_PROMPT
     GEMV_TYPE = args.wtype
+    DEC_PROMPT = args.prompt
     META["gemv"] = gemv_meta()
     world, rank, local = dist_init()
 

@@ -105,6 +105,44 @@ __device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb
     }
 }
 
+// Reduce each row's per-lane partials over the warp and store the rows. Two rows share the
+// first butterfly stage (lanes 0-15 end with row 0, lanes 16-31 with row 1).
+template <int T>
+__device__ __forceinline__ void finish_rows(SmemHdr *h, int s, const GemvJobDev &jb, uint32_t r0, uint32_t row_first,
+                                            uint32_t nr, int part, float (&acc)[kMaxRw][T], int lane) {
+    if (kMaxRw == 2 && nr == 2 && jb.wpr == 1) {
+        const bool up = lane & 16;
+        float v[T];
+#pragma unroll
+        for (int t = 0; t < T; t++) {
+            const float give = up ? acc[0][t] : acc[1][t];
+            float keep = up ? acc[1][t] : acc[0][t];
+            keep += __shfl_xor_sync(0xffffffffu, give, 16);
+#pragma unroll
+            for (int o = 8; o; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+            v[t] = keep;
+        }
+        const int tl = lane & 15;
+        if (tl < T) {
+            float x = v[0];
+#pragma unroll
+            for (int t = 1; t < T; t++)
+                if (tl == t) x = v[t];
+            jb.out[(uint64_t)tl * jb.ld + r0 + row_first + (up ? 1 : 0)] = x;
+        }
+        return;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRw; r++) {
+        if ((uint32_t)r < nr) {
+            float v[T];
+#pragma unroll
+            for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
+            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
+        }
+    }
+}
+
 // ---- 32-value block types: one block per lane per step ----------------------------------
 template <int TYPE, int T>
 __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
@@ -166,15 +204,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
             }
         }
     }
-#pragma unroll
-    for (int r = 0; r < kMaxRw; r++) {
-        if ((uint32_t)r < nr) {
-            float v[T];
-#pragma unroll
-            for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
-            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
-        }
-    }
+    finish_rows<T>(h, s, jb, r0, row_first, nr, part, acc, lane);
 }
 
 // ---- 256-value superblock types: 4 groups of 8 lanes per warp, a superblock per group -----
@@ -264,21 +294,13 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
                         const uint32_t dm = k_lane_dot<TYPE>(l, sbp, alo[t], ahi[t], bs2[t], I, M);
                         // d * sumi - dmin * summ with d = f16(d)*ab.d, dmin = f16(dmin)*ab.d
                         const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&dm));
-                        acc[r][t] += (f.x * ad[t]) * (float)I - (f.y * ad[t]) * (float)M;
+                        acc[r][t] = fmaf(ad[t], fmaf(-f.y, (float)M, f.x * (float)I), acc[r][t]);
                     }
                 }
             }
         }
     }
-#pragma unroll
-    for (int r = 0; r < kMaxRw; r++) {
-        if ((uint32_t)r < nr) {
-            float v[T];
-#pragma unroll
-            for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
-            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
-        }
-    }
+    finish_rows<T>(h, s, jb, r0, row_first, nr, part, acc, lane);
 }
 
 template <int T, int NW>
@@ -302,11 +324,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
         if (!p.early_weights) pdl_wait();
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
-            uint32_t li = 0;
+            uint32_t li = 0, s = 0, ph = 0;  // tile count, stage, pass parity (li / S) & 1
             int ji = 0;  // tiles are visited in increasing order: the job index only advances
             for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
-                const uint32_t s = li % S;
-                if (li >= S && !mbar_wait_bounded(&h->empty[s], ((li / S) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+                if (li >= S && !mbar_wait_bounded(&h->empty[s], ph ^ 1u, p.err, ERR_TIMEOUT_EMPTY)) break;
                 while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
                 const GemvJobDev &jb = p.jobs[ji];
                 const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
@@ -315,6 +336,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
                 uint8_t *dst = smem + p.stage_off + s * p.stage_bytes;
                 mbar_arrive_expect_tx(&h->full[s], bytes);
                 bulk_g2s(dst, jb.w + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s], pol);
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
             // never leave the CTA with copies in flight: wait for the last phase of each stage
             const uint32_t issued = li;
@@ -357,11 +382,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
         named_bar_sync(1, NW * 32);
     }
 
-    uint32_t li = 0;
+    uint32_t s = 0, ph = 0;
     int ji = 0;
-    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++li) {
-        const uint32_t s = li % S;
-        if (!mbar_wait_bounded(&h->full[s], (li / S) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+        if (!mbar_wait_bounded(&h->full[s], ph, p.err, ERR_TIMEOUT_FULL)) break;
         while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
         const GemvJobDev &jb = p.jobs[ji];
         const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
@@ -380,6 +404,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&h->empty[s]);
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+        }
     }
 }
 
