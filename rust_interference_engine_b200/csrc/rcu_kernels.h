@@ -22,7 +22,9 @@ int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint
 
 // KV append / attention with the position either by value (pos_ptr == nullptr) or read
 // from device memory (graph replay). n_split == 0 sizes the split grid from pos0; scratch
-// == nullptr uses the context's growable scratch (may allocate).
+// == nullptr uses the context's growable scratch (may allocate). A caller-provided scratch
+// (attention_scratch_bytes) must start zeroed: its leading completion counters reset
+// themselves after every call.
 int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, uint64_t n_tok, uint64_t pos0,
                     const uint64_t *pos_ptr);
 // aq != nullptr fuses the activation quantization (for the Wo matmul) into the merge; out
@@ -44,8 +46,9 @@ struct QkvPostParams {
     float eps, attn_scale;
 };
 int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p);
-// Whether the merge can quantize in the same kernel for this head shape and act format.
-bool attention_fused_merge_ok(uint64_t n_head, uint64_t hd, uint32_t fmt);
+// Whether the merge can quantize in the same kernel for this head shape and act format
+// (a GQA group's output must hold whole activation blocks).
+bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt);
 uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window);
 uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split);
 

@@ -274,25 +274,28 @@ __global__ void __launch_bounds__(128) k_turbo_rotate(float *__restrict__ x, uin
 }
 
 // ---- attention ----------------------------------------------------------------------------
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxGroup = 16;
-constexpr uint32_t kCombineMaxSplits = 256;  // split-plan cap (fused merge keeps weights in smem)
-constexpr uint32_t kCombineMaxHeads = 8;
+constexpr uint32_t kMaxSplits = 256;  // split-plan cap
 constexpr int kMaxAttnHd = 256;
+constexpr uint32_t kSub = 64;  // cache rows per sub-chunk staged in shared memory
 
 struct AttnParams {
     const uint8_t *kc, *vc;
     const float *q;
     float *o_part, *m_part, *l_part;
-    uint32_t n_tok, n_head, n_kv, hd, slots, window, n_split, rows_per_split, row_bytes;
+    uint32_t *done;  // per (token, kv head): CTAs finished; the last one merges and resets it
+    float *out;      // merged output [t][n_head * hd] (f32), may be null
+    ActOut aq;       // quantization of the merged output for the Wo matmul (aq.fmt == 0: none)
+    uint32_t n_tok, n_head, n_kv, hd, slots, window, n_split, rows_per_split, row_bytes, buf_bytes;
     uint64_t pos0;
     const uint64_t *pos_ptr;  // when set, the position is read from device memory (graph replay)
     float softcap;
     int rounding;
 };
 
-// 4 nibble indices (one per byte, 0..15) -> 4 int8 levels, with byte permutes.
+// Byte lookup of 16 entries (the turbo4 levels as int8) for 4 nibble indices at once.
 __device__ __forceinline__ uint32_t lut16(uint32_t idx, uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3) {
     const uint32_t sel = __byte_perm(idx | (idx >> 4), 0, 0x0020) & 0x7777u;
     const uint32_t lo = __byte_perm(t0, t1, sel), hi = __byte_perm(t2, t3, sel);
@@ -300,23 +303,298 @@ __device__ __forceinline__ uint32_t lut16(uint32_t idx, uint32_t t0, uint32_t t1
     return (lo & ~m) | (hi & m);
 }
 
-// One CTA = (KV head g, query token t, split): scores rows [c0, c1) of the cache for the
-// G query heads of the group in 64-row sub-chunks with an online softmax, and writes an
-// un-normalised partial output with its running max / sum.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Where the rows of one staged sub-chunk sit in its shared buffer: the ring of slots may wrap,
+// so a sub-chunk is one or two contiguous byte ranges, each copied from its 16-byte aligned
+// enclosure.
+struct StagedRows {
+    uint32_t n1, d1, d2;  // rows in the first range; byte offset of its first row; same for the second
+    __device__ __forceinline__ uint32_t off(uint32_t r, uint32_t rb) const {
+        return r < n1 ? d1 + r * rb : d2 + (r - n1) * rb;
+    }
+};
+__device__ __forceinline__ StagedRows stage_rows(const uint8_t *cache, uint64_t head_base, uint32_t slots, uint32_t rb,
+                                                 uint64_t first_slot, uint32_t n, uint8_t *buf) {
+    StagedRows sr;
+    const uint64_t room = slots - first_slot;
+    sr.n1 = room < n ? (uint32_t)room : n;
+    const uint64_t b1 = head_base + first_slot * rb, lo1 = b1 & ~15ull, hi1 = (b1 + (uint64_t)sr.n1 * rb + 15) & ~15ull;
+    sr.d1 = (uint32_t)(b1 - lo1);
+    for (uint32_t o = threadIdx.x * 16; o < hi1 - lo1; o += kAttnThreads * 16) cp_async16(buf + o, cache + lo1 + o);
+    sr.d2 = (uint32_t)(hi1 - lo1);
+    if (sr.n1 < n) {
+        const uint64_t b2 = head_base, lo2 = b2 & ~15ull, hi2 = (b2 + (uint64_t)(n - sr.n1) * rb + 15) & ~15ull;
+        uint8_t *buf2 = buf + sr.d2;
+        sr.d2 += (uint32_t)(b2 - lo2);
+        for (uint32_t o = threadIdx.x * 16; o < hi2 - lo2; o += kAttnThreads * 16) cp_async16(buf2 + o, cache + lo2 + o);
+    }
+    return sr;
+}
+
+// One CTA = (KV head g, query token t, split): the G query heads of the group against cache
+// rows [c0, c1) in 64-row sub-chunks (K and V staged in shared memory by cp.async, the next
+// sub-chunk in flight while the current one is scored), online softmax, un-normalised
+// partial output. The last CTA of (t, g) to finish merges the splits (cpu.rs:590-634 softmax
+// and weighted sum), applies the inverse rotation (turbo) and writes the f32 output and/or
+// the quantized activations of the Wo matmul.
 template <int KV, int G>
-__global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnParams p) {
     pdl_wait();
     pdl_trigger();
-    constexpr int SUB = 64, DPL = kMaxAttnHd / 32;
+    constexpr int DPL = kMaxAttnHd / 32;
+    extern __shared__ __align__(16) uint8_t dsm[];
+    __shared__ __align__(16) float qf[G][kMaxAttnHd];  // f32 query (f16 cache) / rotation scratch
+    __shared__ __align__(16) int8_t qi[G][kMaxAttnHd];
+    __shared__ float qd[G][kMaxAttnHd / 32];
+    __shared__ float sc[G][kSub];
+    __shared__ float red[kAttnWarps][kMaxAttnHd];
+    __shared__ float mrun[G], lrun[G], alpha[G];
+    __shared__ Q8kShared qsh;
+    __shared__ uint32_t s_last;
     const uint32_t g = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
-    const uint32_t hd = p.hd, dpl = hd / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t hd = p.hd, dpl = hd / 32, rb = p.row_bytes, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const uint64_t pt = (p.pos_ptr ? *p.pos_ptr : p.pos0) + t;
     const uint64_t start = p.window > 0 ? (pt + 1 > p.window ? pt + 1 - p.window : 0) : 0;
     const uint32_t len = (uint32_t)(pt + 1 - start);
     const uint32_t c0 = split * p.rows_per_split, c1 = min(len, c0 + p.rows_per_split);
     const uint64_t part_base = ((uint64_t)t * p.n_head + (uint64_t)g * G) * p.n_split + split;
-    if (c0 >= len) {
+    const uint64_t head_base = (uint64_t)g * p.slots * rb;
+    // buffers: K of even sub-chunks, K of odd ones, V even, V odd
+    auto kbuf_of = [&](uint32_t b) { return dsm + b * p.buf_bytes; };
+    auto vbuf_of = [&](uint32_t b) { return dsm + (2 + b) * p.buf_bytes; };
+
+    if (c0 < len) {
+        StagedRows kr0, vr0, kr1, vr1;
+        {
+            const uint32_t n = min(kSub, c1 - c0);
+            kr0 = stage_rows(p.kc, head_base, p.slots, rb, (start + c0) % p.slots, n, kbuf_of(0));
+            vr0 = stage_rows(p.vc, head_base, p.slots, rb, (start + c0) % p.slots, n, vbuf_of(0));
+            cp_async_commit();
+        }
+        // 1. queries of this group: rotate (turbo) and quantize to Q8_0 (turbo / Q8_0 caches)
+        for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
+            const float *qsrc = p.q + ((uint64_t)t * p.n_head + g * G + hh) * hd;
+            for (uint32_t d = lane; d < hd; d += 32) qf[hh][d] = qsrc[d];
+            __syncwarp();
+            if (KV == RCU_KV_TURBO4) rotate_row(qf[hh], hd, false, lane);
+            if (KV != RCU_KV_F16) {
+                for (uint32_t b = 0; b < hd / 32; b++) {
+                    float d;
+                    const int q = quant32(qf[hh][b * 32 + lane], p.rounding, d);
+                    qi[hh][b * 32 + lane] = (int8_t)q;
+                    if (lane == 0) qd[hh][b] = d;
+                }
+            }
+            if (lane == 0) {
+                mrun[hh] = -INFINITY;
+                lrun[hh] = 0.0f;
+            }
+            __syncwarp();
+        }
+        const uint32_t tb[4] = {0xc6b6a182u, 0xfaeee2d5u, 0x2b1e1206u, 0x7e5f4a3au};  // c_levels as bytes
+        const float inv46 = 1.0f / 46.0f;
+        float acc[G][DPL];
+#pragma unroll
+        for (int hh = 0; hh < G; hh++)
+#pragma unroll
+            for (int e = 0; e < DPL; e++) acc[hh][e] = 0.0f;
+        const uint32_t d0 = lane * dpl;
+
+        uint32_t sub = 0;
+        for (uint32_t s0 = c0; s0 < c1; s0 += kSub, sub++) {
+            const uint32_t s1 = min(c1, s0 + kSub), cur = sub & 1;
+            if (s1 < c1) {  // prefetch the next sub-chunk into the other buffers
+                const uint32_t n = min(kSub, c1 - s1);
+                const StagedRows a = stage_rows(p.kc, head_base, p.slots, rb, (start + s1) % p.slots, n, kbuf_of(cur ^ 1));
+                const StagedRows b = stage_rows(p.vc, head_base, p.slots, rb, (start + s1) % p.slots, n, vbuf_of(cur ^ 1));
+                if (cur) {
+                    kr0 = a;
+                    vr0 = b;
+                } else {
+                    kr1 = a;
+                    vr1 = b;
+                }
+                cp_async_commit();
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
+            __syncthreads();
+            const uint8_t *kbuf = kbuf_of(cur), *vbuf = vbuf_of(cur);
+            const StagedRows krc = cur ? kr1 : kr0, vrc = cur ? vr1 : vr0;
+            // 2. scores: four threads per row, each a quarter of the head dimension
+            {
+                const uint32_t r = tid >> 2, qq = tid & 3;
+                float s[G];
+#pragma unroll
+                for (int hh = 0; hh < G; hh++) s[hh] = 0.0f;
+                if (s0 + r < s1) {
+                    const uint32_t ro = krc.off(r, rb);
+                    if (KV == RCU_KV_TURBO4) {
+                        const uint32_t b = turbo_block(hd), nb = hd / b;
+                        for (uint32_t cc = qq; cc < hd / 32; cc += 4) {
+                            uint32_t sw[1];
+                            ld_words<1>(kbuf, ro + 2 * ((cc * 32) / b), sw);
+                            const float scale = f16_bits_to_f32(sw[0]);
+                            uint32_t w[4];
+                            ld_words<4>(kbuf, ro + 2 * nb + 16 * cc, w);
+                            uint32_t lv[8];
+#pragma unroll
+                            for (int i2 = 0; i2 < 4; i2++) {
+                                lv[i2] = lut16(w[i2] & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
+                                lv[4 + i2] = lut16((w[i2] >> 4) & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
+                            }
+#pragma unroll
+                            for (int hh = 0; hh < G; hh++) {
+                                const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][cc * 32]);
+                                const uint4 q0 = qv[0], q1 = qv[1];
+                                int a0 = dp4a(lv[0], q0.x, 0), a1 = dp4a(lv[1], q0.y, 0);
+                                a0 = dp4a(lv[2], q0.z, a0);
+                                a1 = dp4a(lv[3], q0.w, a1);
+                                a0 = dp4a(lv[4], q1.x, a0);
+                                a1 = dp4a(lv[5], q1.y, a1);
+                                a0 = dp4a(lv[6], q1.z, a0);
+                                a1 = dp4a(lv[7], q1.w, a1);
+                                s[hh] += scale * (qd[hh][cc] * (float)(a0 + a1));
+                            }
+                        }
+                    } else if (KV == RCU_KV_Q8_0) {
+                        for (uint32_t bi = qq; bi < hd / 32; bi += 4) {
+                            BlkW w;
+                            dec_q8_0(kbuf, ro + bi * 34, w);
+#pragma unroll
+                            for (int hh = 0; hh < G; hh++) {
+                                const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][bi * 32]);
+                                const uint4 q0 = qv[0], q1 = qv[1];
+                                const uint32_t av[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                                s[hh] += (w.d * qd[hh][bi]) * (float)blk_int<T_Q8_0>(w, av, 0);
+                            }
+                        }
+                    } else {
+                        const uint4 *kh = reinterpret_cast<const uint4 *>(kbuf + ro);
+                        const uint32_t per = hd / 32;  // 16-byte chunks (8 halves) per quarter
+                        for (uint32_t c = 0; c < per; c++) {
+                            const uint4 raw = kh[qq * per + c];
+                            const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+                            const uint32_t db = qq * (hd / 4) + 8 * c;
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const float2 kv = __half22float2(h2[j]);
+#pragma unroll
+                                for (int hh = 0; hh < G; hh++)
+                                    s[hh] += kv.x * qf[hh][db + 2 * j] + kv.y * qf[hh][db + 2 * j + 1];
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int hh = 0; hh < G; hh++) {
+                    float v = s[hh] + __shfl_xor_sync(0xffffffffu, s[hh], 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    if (KV == RCU_KV_TURBO4) v *= inv46;
+                    if (p.softcap > 0.0f) v = p.softcap * tanhf(v / p.softcap);
+                    if (qq == 0) sc[hh][r] = s0 + r < s1 ? v : -INFINITY;
+                }
+            }
+            __syncthreads();
+            // 3. online softmax per head
+            for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
+                const float v0 = sc[hh][lane], v1 = sc[hh][lane + 32];
+                float m = fmaxf(v0, v1);
+                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float m_old = mrun[hh], m_new = fmaxf(m_old, m);
+                const float e0 = v0 == -INFINITY ? 0.0f : expf(v0 - m_new), e1 = v1 == -INFINITY ? 0.0f : expf(v1 - m_new);
+                sc[hh][lane] = e0;
+                sc[hh][lane + 32] = e1;
+                float l = e0 + e1;
+                for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+                if (lane == 0) {
+                    const float a = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
+                    alpha[hh] = a;
+                    lrun[hh] = lrun[hh] * a + l;
+                    mrun[hh] = m_new;
+                }
+            }
+            __syncthreads();
+            // 4. weighted V sum: warp w takes rows s0 + w (mod 8); lane owns dims lane*dpl..
+#pragma unroll
+            for (int hh = 0; hh < G; hh++) {
+                const float a = alpha[hh];
+#pragma unroll
+                for (int e = 0; e < DPL; e++) acc[hh][e] *= a;
+            }
+#pragma unroll 2
+            for (uint32_t i = s0 + warp; i < s1; i += kAttnWarps) {
+                const uint32_t ro = vrc.off(i - s0, rb);
+                float val[DPL];
+                if (KV == RCU_KV_F16 && DPL >= 4) {
+                    if (dpl == 4) {
+                        const uint2 raw = *reinterpret_cast<const uint2 *>(vbuf + ro + 2 * d0);
+                        const float2 a0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+                        const float2 a1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+                        val[0] = a0.x, val[1] = a0.y, val[2] = a1.x, val[3] = a1.y;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < DPL; e++)
+                            if ((uint32_t)e < dpl) val[e] = __half2float(reinterpret_cast<const __half *>(vbuf + ro)[d0 + e]);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < DPL; e++) {
+                        if ((uint32_t)e >= dpl) break;
+                        const uint32_t dd = d0 + e;
+                        if (KV == RCU_KV_TURBO4) {
+                            const uint32_t b = turbo_block(hd), nb = hd / b, c = dd / 32, m2 = dd % 32;
+                            const uint32_t byte = vbuf[ro + 2 * nb + 16 * c + (m2 & 15)];
+                            const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
+                            const uint32_t sbits = *reinterpret_cast<const uint16_t *>(vbuf + ro + 2 * (dd / b));
+                            val[e] = f16_bits_to_f32(sbits) * inv46 * (float)c_levels[code];
+                        } else if (KV == RCU_KV_Q8_0) {
+                            const uint32_t bi = dd / 32;
+                            const uint32_t sbits = *reinterpret_cast<const uint16_t *>(vbuf + ro + bi * 34);
+                            val[e] = f16_bits_to_f32(sbits) * (float)(int8_t)vbuf[ro + bi * 34 + 2 + dd % 32];
+                        } else {
+                            val[e] = __half2float(reinterpret_cast<const __half *>(vbuf + ro)[dd]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int hh = 0; hh < G; hh++) {
+                    const float w = sc[hh][i - s0];
+#pragma unroll
+                    for (int e = 0; e < DPL; e++)
+                        if ((uint32_t)e < dpl) acc[hh][e] += w * val[e];
+                }
+            }
+            __syncthreads();  // the buffers of this sub-chunk are refilled two iterations later
+        }
+#pragma unroll
+        for (int hh = 0; hh < G; hh++) {
+#pragma unroll
+            for (int e = 0; e < DPL; e++)
+                if ((uint32_t)e < dpl) red[warp][d0 + e] = acc[hh][e];
+            __syncthreads();
+            for (uint32_t d = tid; d < hd; d += kAttnThreads) {
+                float o = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kAttnWarps; w++) o += red[w][d];
+                p.o_part[(part_base + (uint64_t)hh * p.n_split) * hd + d] = o;
+            }
+            __syncthreads();
+        }
+        if (tid < G) {
+            const uint64_t pb = part_base + (uint64_t)tid * p.n_split;
+            p.m_part[pb] = mrun[tid];
+            p.l_part[pb] = lrun[tid];
+        }
+    } else {
         for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
             const uint64_t pb = part_base + (uint64_t)hh * p.n_split;
             if (lane == 0) {
@@ -325,231 +603,65 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_partial(const __grid_cons
             }
             for (uint32_t d = lane; d < hd; d += 32) p.o_part[pb * hd + d] = 0.0f;
         }
-        return;
     }
-    __shared__ __align__(16) float qf[G][kMaxAttnHd];  // f32 query (f16 cache) / rotation scratch
-    __shared__ __align__(16) int8_t qi[G][kMaxAttnHd];
-    __shared__ float qd[G][kMaxAttnHd / 32];
-    __shared__ float sc[G][SUB];
-    __shared__ float red[kAttnWarps][kMaxAttnHd];
-    __shared__ float mrun[G], lrun[G], alpha[G];
 
-    // 1. queries of this group: rotate (turbo) and quantize to Q8_0 (turbo / Q8_0 caches)
+    // ---- merge: the last CTA of (t, g) ----------------------------------------------------
+    __threadfence();
+    __syncthreads();
+    uint32_t *done = p.done + (uint64_t)t * p.n_kv + g;
+    if (tid == 0) s_last = atomicAdd(done, 1u) == p.n_split - 1 ? 1u : 0u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    float *fac = reinterpret_cast<float *>(dsm);  // [G][n_split]
+    float *vals = fac + ((G * p.n_split + 3) & ~3u);  // [G][hd]
+    const uint64_t base0 = ((uint64_t)t * p.n_head + (uint64_t)g * G) * p.n_split;
     for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
-        const float *qsrc = p.q + ((uint64_t)t * p.n_head + g * G + hh) * hd;
-        for (uint32_t d = lane; d < hd; d += 32) qf[hh][d] = qsrc[d];
-        __syncwarp();
-        if (KV == RCU_KV_TURBO4) rotate_row(qf[hh], hd, false, lane);
-        if (KV != RCU_KV_F16) {
-            for (uint32_t b = 0; b < hd / 32; b++) {
-                float d;
-                const int q = quant32(qf[hh][b * 32 + lane], p.rounding, d);
-                qi[hh][b * 32 + lane] = (int8_t)q;
-                if (lane == 0) qd[hh][b] = d;
-            }
+        const uint64_t base = base0 + (uint64_t)hh * p.n_split;
+        float M = -INFINITY;
+        for (uint32_t s = lane; s < p.n_split; s += 32) M = fmaxf(M, __ldcg(p.m_part + base + s));
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        for (uint32_t s = lane; s < p.n_split; s += 32) {
+            const float m = __ldcg(p.m_part + base + s);
+            const float f = m == -INFINITY ? 0.0f : expf(m - M);
+            fac[hh * p.n_split + s] = f;
+            L += f * __ldcg(p.l_part + base + s);
         }
-        if (lane == 0) {
-            mrun[hh] = -INFINITY;
-            lrun[hh] = 0.0f;
-        }
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float invL = 1.0f / L;
         __syncwarp();
+        for (uint32_t s = lane; s < p.n_split; s += 32) fac[hh * p.n_split + s] *= invL;
     }
     __syncthreads();
-
-    const uint32_t tb[4] = {0xc6b6a182u, 0xfaeee2d5u, 0x2b1e1206u, 0x7e5f4a3au};  // c_levels as bytes
-    const float inv46 = 1.0f / 46.0f;
-    float acc[G][DPL];
-#pragma unroll
-    for (int hh = 0; hh < G; hh++)
-#pragma unroll
-        for (int e = 0; e < DPL; e++) acc[hh][e] = 0.0f;
-    const uint32_t d0 = lane * dpl;
-
-    for (uint32_t s0 = c0; s0 < c1; s0 += SUB) {
-        const uint32_t s1 = min(c1, s0 + SUB);
-        // 2. scores: two threads per row, each half of the head dimension
-        {
-            const uint32_t r = threadIdx.x >> 1, half = threadIdx.x & 1;
-            const uint32_t i = s0 + r;
-            float s[G];
-#pragma unroll
-            for (int hh = 0; hh < G; hh++) s[hh] = 0.0f;
-            if (i < s1) {
-                const uint64_t row = (uint64_t)g * p.slots + (start + i) % p.slots;
-                const uint64_t kro = row * p.row_bytes;
-                if (KV == RCU_KV_TURBO4) {
-                    const uint32_t b = turbo_block(hd), nb = hd / b, nch = hd / 32;
-                    for (uint32_t cc = half * (nch / 2); cc < (half + 1) * (nch / 2) + (half ? nch % 2 : 0); cc++) {
-                        uint32_t sw[1];
-                        ld_words<1>(p.kc, kro + 2 * ((cc * 32) / b), sw);
-                        const float scale = f16_bits_to_f32(sw[0]);
-                        uint32_t w[4];
-                        ld_words<4>(p.kc, kro + 2 * nb + 16 * cc, w);
-                        uint32_t lv[8];
-#pragma unroll
-                        for (int i2 = 0; i2 < 4; i2++) {
-                            lv[i2] = lut16(w[i2] & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
-                            lv[4 + i2] = lut16((w[i2] >> 4) & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
-                        }
-#pragma unroll
-                        for (int hh = 0; hh < G; hh++) {
-                            const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][cc * 32]);
-                            const uint4 q0 = qv[0], q1 = qv[1];
-                            int a0 = dp4a(lv[0], q0.x, 0), a1 = dp4a(lv[1], q0.y, 0);
-                            a0 = dp4a(lv[2], q0.z, a0);
-                            a1 = dp4a(lv[3], q0.w, a1);
-                            a0 = dp4a(lv[4], q1.x, a0);
-                            a1 = dp4a(lv[5], q1.y, a1);
-                            a0 = dp4a(lv[6], q1.z, a0);
-                            a1 = dp4a(lv[7], q1.w, a1);
-                            s[hh] += scale * (qd[hh][cc] * (float)(a0 + a1));
-                        }
-                    }
-                } else if (KV == RCU_KV_Q8_0) {
-                    const uint32_t nbk = hd / 32;
-                    for (uint32_t bi = half * (nbk / 2); bi < (half + 1) * (nbk / 2) + (half ? nbk % 2 : 0); bi++) {
-                        BlkW w;
-                        dec_q8_0(p.kc, kro + bi * 34, w);
-#pragma unroll
-                        for (int hh = 0; hh < G; hh++) {
-                            const uint4 *qv = reinterpret_cast<const uint4 *>(&qi[hh][bi * 32]);
-                            const uint4 q0 = qv[0], q1 = qv[1];
-                            const uint32_t a[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                            s[hh] += (w.d * qd[hh][bi]) * (float)blk_int<T_Q8_0>(w, a, 0);
-                        }
-                    }
-                } else {
-                    const uint4 *kh = reinterpret_cast<const uint4 *>(p.kc + kro) + half * (hd / 16);
-                    for (uint32_t c = 0; c < hd / 16; c++) {  // 8 halves per 16-byte load
-                        const uint4 raw = kh[c];
-                        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
-                        const uint32_t dbase = half * (hd / 2) + 8 * c;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const float2 kv = __half22float2(h2[j]);
-#pragma unroll
-                            for (int hh = 0; hh < G; hh++)
-                                s[hh] += kv.x * qf[hh][dbase + 2 * j] + kv.y * qf[hh][dbase + 2 * j + 1];
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int hh = 0; hh < G; hh++) {
-                float v = s[hh] + __shfl_xor_sync(0xffffffffu, s[hh], 1);
-                if (KV == RCU_KV_TURBO4) v *= inv46;
-                if (p.softcap > 0.0f) v = p.softcap * tanhf(v / p.softcap);
-                if (half == 0 && r < SUB) sc[hh][r] = i < s1 ? v : -INFINITY;
-            }
-        }
-        __syncthreads();
-        // 3. online softmax per head
-        for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
-            const float v0 = sc[hh][lane], v1 = sc[hh][lane + 32];
-            float m = fmaxf(v0, v1);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float m_old = mrun[hh], m_new = fmaxf(m_old, m);
-            const float e0 = v0 == -INFINITY ? 0.0f : expf(v0 - m_new), e1 = v1 == -INFINITY ? 0.0f : expf(v1 - m_new);
-            sc[hh][lane] = e0;
-            sc[hh][lane + 32] = e1;
-            float l = e0 + e1;
-            for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            if (lane == 0) {
-                const float a = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
-                alpha[hh] = a;
-                lrun[hh] = lrun[hh] * a + l;
-                mrun[hh] = m_new;
-            }
-        }
-        __syncthreads();
-        // 4. weighted V sum: warp w takes rows s0 + w (mod 4); lane owns dims lane*dpl..
-#pragma unroll
-        for (int hh = 0; hh < G; hh++) {
-            const float a = alpha[hh];
-#pragma unroll
-            for (int e = 0; e < DPL; e++) acc[hh][e] *= a;
-        }
-        for (uint32_t i = s0 + warp; i < s1; i += kAttnWarps) {
-            const uint64_t vro = ((uint64_t)g * p.slots + (start + i) % p.slots) * p.row_bytes;
-            const uint8_t *vr = p.vc + vro;
-            float val[DPL];
-#pragma unroll
-            for (int e = 0; e < DPL; e++) {
-                if ((uint32_t)e >= dpl) break;
-                const uint32_t dd = d0 + e;
-                if (KV == RCU_KV_TURBO4) {
-                    const uint32_t b = turbo_block(hd), nb = hd / b, c = dd / 32, m2 = dd % 32;
-                    const uint32_t byte = vr[2 * nb + 16 * c + (m2 & 15)];
-                    const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
-                    uint32_t sw[1];
-                    ld_words<1>(p.vc, vro + 2 * (dd / b), sw);
-                    val[e] = f16_bits_to_f32(sw[0]) * inv46 * (float)c_levels[code];
-                } else if (KV == RCU_KV_Q8_0) {
-                    const uint32_t bi = dd / 32;
-                    uint32_t sw[1];
-                    ld_words<1>(p.vc, vro + bi * 34, sw);
-                    val[e] = f16_bits_to_f32(sw[0]) * (float)(int8_t)vr[bi * 34 + 2 + dd % 32];
-                } else {
-                    val[e] = __half2float(reinterpret_cast<const __half *>(vr)[dd]);
-                }
-            }
-#pragma unroll
-            for (int hh = 0; hh < G; hh++) {
-                const float w = sc[hh][i - s0];
-#pragma unroll
-                for (int e = 0; e < DPL; e++)
-                    if ((uint32_t)e < dpl) acc[hh][e] += w * val[e];
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int hh = 0; hh < G; hh++) {
-#pragma unroll
-        for (int e = 0; e < DPL; e++)
-            if ((uint32_t)e < dpl) red[warp][d0 + e] = acc[hh][e];
-        __syncthreads();
-        for (uint32_t d = threadIdx.x; d < hd; d += kAttnThreads) {
-            float o = 0.0f;
-            for (int w = 0; w < kAttnWarps; w++) o += red[w][d];
-            p.o_part[(part_base + (uint64_t)hh * p.n_split) * hd + d] = o;
-        }
-        __syncthreads();
-    }
-    if (threadIdx.x < G) {
-        const uint64_t pb = part_base + (uint64_t)threadIdx.x * p.n_split;
-        p.m_part[pb] = mrun[threadIdx.x];
-        p.l_part[pb] = lrun[threadIdx.x];
-    }
-}
-
-// Merge the chunks of one (token, head), normalise, rotate back (turbo).
-template <int KV>
-__global__ void __launch_bounds__(32) k_attn_combine(const __grid_constant__ AttnParams p, float *__restrict__ out) {
-    pdl_wait();
-    pdl_trigger();
-    const uint32_t h = blockIdx.x, t = blockIdx.y, lane = threadIdx.x, hd = p.hd;
-    const uint64_t base = ((uint64_t)t * p.n_head + h) * p.n_split;
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < p.n_split; s++) M = fmaxf(M, p.m_part[base + s]);
-    float L = 0.0f;
-    for (uint32_t s = 0; s < p.n_split; s++) {
-        const float m = p.m_part[base + s];
-        if (m != -INFINITY) L += expf(m - M) * p.l_part[base + s];
-    }
-    const float invL = 1.0f / L;
-    __shared__ float o[kMaxAttnHd];
-    for (uint32_t d = lane; d < hd; d += 32) {
-        float acc = 0.0f;
+    const uint32_t gv = G * hd;  // values of this group
+    for (uint32_t v = tid; v < gv; v += kAttnThreads) {
+        const uint32_t hh = v / hd, d = v % hd;
+        const uint64_t base = base0 + (uint64_t)hh * p.n_split;
+        float o = 0.0f;
         for (uint32_t s = 0; s < p.n_split; s++) {
-            const float m = p.m_part[base + s];
-            if (m != -INFINITY) acc += expf(m - M) * p.o_part[(base + s) * hd + d];
+            const float f = fac[hh * p.n_split + s];
+            if (f != 0.0f) o += f * __ldcg(p.o_part + (base + s) * hd + d);
         }
-        o[d] = acc * invL;
+        vals[v] = o;
     }
-    __syncwarp();
-    if (KV == RCU_KV_TURBO4) rotate_row(o, hd, true, lane);
-    for (uint32_t d = lane; d < hd; d += 32) out[((uint64_t)t * p.n_head + h) * hd + d] = o[d];
+    __syncthreads();
+    if (KV == RCU_KV_TURBO4) {
+        for (uint32_t hh = warp; hh < G; hh += kAttnWarps) rotate_row(vals + hh * hd, hd, true, lane);
+        __syncthreads();
+    }
+    const uint64_t row_k = (uint64_t)p.n_head * hd, col0 = (uint64_t)g * gv, row0 = (uint64_t)t * row_k + col0;
+    if (p.out)
+        for (uint32_t v = tid; v < gv; v += kAttnThreads) p.out[row0 + v] = vals[v];
+    if (p.aq.fmt) {
+        for (uint32_t v0 = 0; v0 < gv; v0 += kAttnThreads) {  // whole Q8_0 blocks; whole Q8_K blocks when asked
+            const uint32_t v = v0 + tid;
+            const float x = v < gv ? vals[v] : 0.0f;
+            if ((p.aq.fmt & RCU_ACT_Q8_0) && v0 + 32 * warp < gv) q8_0_block(x, (row0 + v0 + 32 * warp) / QK, lane, p.aq);
+            if (p.aq.fmt & RCU_ACT_Q8K) q8_k_block(x, tid, 0, (row0 + v0) / QK_K, v0 < gv, p.aq, qsh, (v0 / kAttnThreads) & 1);
+        }
+    }
+    if (tid == 0) *done = 0u;
 }
 
 static uint64_t kv_row_bytes(int type, uint64_t hd) {
@@ -603,123 +715,72 @@ int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, ui
 // waves of SMs; both numbers depend only on (max_len, n_tok, n_kv), never on the position.
 static void split_plan(uint64_t max_len, uint64_t n_tok, uint64_t n_kv, int num_sms, uint32_t *n_split,
                        uint32_t *rows_per_split) {
-    const uint64_t n_sub = (max_len + 63) / 64;
+    const uint64_t n_sub = (max_len + kSub - 1) / kSub;
     const uint64_t want = std::max<uint64_t>(1, (2 * (uint64_t)num_sms) / std::max<uint64_t>(1, n_kv * n_tok));
-    const uint64_t splits = std::max<uint64_t>(1, std::min<uint64_t>(std::min(n_sub, want), kCombineMaxSplits));
+    const uint64_t splits = std::max<uint64_t>(1, std::min<uint64_t>(std::min(n_sub, want), kMaxSplits));
     const uint64_t subs_per = (n_sub + splits - 1) / splits;
-    *rows_per_split = (uint32_t)(subs_per * 64);
+    *rows_per_split = (uint32_t)(subs_per * kSub);
     *n_split = (uint32_t)((max_len + *rows_per_split - 1) / *rows_per_split);
 }
 
 uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window) {
     const uint64_t max_len = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
-    return (uint32_t)((max_len + 63) / 64);  // upper bound of any plan (64-row splits)
+    return (uint32_t)std::min<uint64_t>((max_len + kSub - 1) / kSub, kMaxSplits);  // bound of any plan
 }
 
+// Scratch: per (token, kv head) completion counters first (zeroed once, self-resetting),
+// then the partial outputs, maxima and sums.
+static uint64_t counters_bytes(uint64_t n_tok, uint64_t n_kv) { return (n_tok * n_kv * 4 + 255) & ~255ull; }
 uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split) {
-    return n_tok * n_head * n_split * (kv->hd + 2) * sizeof(float);
+    return counters_bytes(n_tok, kv->n_kv) + n_tok * n_head * n_split * (kv->hd + 2) * sizeof(float);
 }
 
-// Merge of the splits fused with the activation quantization of the Wo matmul: one CTA per
-// (token, run of hpc heads), one output value per thread (hpc * hd threads: whole Q8_0
-// blocks, and whole Q8_K blocks when that format is asked for).
-template <int KV>
-__global__ void __launch_bounds__(1024) k_attn_combine_q(const __grid_constant__ AttnParams p, uint32_t hpc,
-                                                         float *__restrict__ out, const ActOut ao) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ float fac[kCombineMaxHeads][kCombineMaxSplits];
-    __shared__ __align__(16) float ob[1024];
-    __shared__ Q8kShared sh;
-    const uint32_t t = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hd = p.hd;
-    const uint32_t h0 = blockIdx.x * hpc, nw = blockDim.x >> 5;
-    // 1. per-head merge weights exp(m_s - M) / L
-    for (uint32_t hh = warp; hh < hpc; hh += nw) {
-        const uint64_t base = ((uint64_t)t * p.n_head + h0 + hh) * p.n_split;
-        float M = -INFINITY;
-        for (uint32_t s = lane; s < p.n_split; s += 32) M = fmaxf(M, p.m_part[base + s]);
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = 0.0f;
-        for (uint32_t s = lane; s < p.n_split; s += 32) {
-            const float m = p.m_part[base + s];
-            const float f = m == -INFINITY ? 0.0f : expf(m - M);
-            fac[hh][s] = f;
-            L += f * p.l_part[base + s];
-        }
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float invL = 1.0f / L;
-        for (uint32_t s = lane; s < p.n_split; s += 32) fac[hh][s] *= invL;
-    }
-    __syncthreads();
-    // 2. one dimension per thread
-    const uint32_t hh = tid / hd, d = tid % hd;
-    const uint64_t base = ((uint64_t)t * p.n_head + h0 + hh) * p.n_split;
-    float acc = 0.0f;
-    for (uint32_t s = 0; s < p.n_split; s++) {
-        const float f = fac[hh][s];
-        if (f != 0.0f) acc += f * p.o_part[(base + s) * hd + d];
-    }
-    if (KV == RCU_KV_TURBO4) {
-        ob[tid] = acc;
-        __syncthreads();
-        if (warp < hpc) rotate_row(ob + warp * hd, hd, true, lane);
-        __syncthreads();
-        acc = ob[tid];
-    }
-    const uint64_t row_k = (uint64_t)p.n_head * hd, col = (uint64_t)h0 * hd + tid;
-    if (out) out[t * row_k + col] = acc;
-    // 3. quantize (the CTA covers whole blocks)
-    if (ao.fmt & RCU_ACT_Q8_0) q8_0_block(acc, (t * row_k + col) / QK, lane, ao);
-    if (ao.fmt & RCU_ACT_Q8K) {
-        const uint64_t g0 = (uint64_t)h0 * hd + QK_K * (warp / 8);
-        q8_k_block(acc, tid % QK_K, warp & ~7u, (t * row_k + g0) / QK_K, true, ao, sh, 0);
-    }
+bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt) {
+    const uint64_t gv = (n_head / n_kv) * hd;
+    return (fmt & RCU_ACT_Q8K) ? gv % QK_K == 0 : gv % QK == 0;
 }
 
-// Heads per CTA of the fused merge for this shape, or 0 when the fused kernel cannot cover it.
-static uint32_t combine_heads(uint64_t n_head, uint64_t hd, uint32_t fmt) {
-    uint32_t h = 1;
-    if (fmt & RCU_ACT_Q8K) {
-        while ((h * hd) % QK_K) h++;
-    } else {
-        while (2 * h * hd <= 256 && n_head % (2 * h) == 0) h *= 2;
+template <int KV, int G>
+static int launch_group(rcu_ctx *ctx, const AttnParams &p, dim3 grid, uint32_t dyn) {
+    static int max_dyn[64] = {};  // per device: opt-in limit minus the kernel's static shared memory
+    int &md = max_dyn[ctx->device & 63];
+    if (!md) {
+        cudaFuncAttributes fa;
+        RCU_CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, k_attn<KV, G>));
+        const int lim = (int)ctx->max_smem_optin - (int)fa.sharedSizeBytes;
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_attn<KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        md = lim;
     }
-    if (h > kCombineMaxHeads || h * hd > 1024 || n_head % h) return 0;
-    return h;
+    if ((int)dyn > md) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: cache rows too long for shared memory");
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn<KV, G>), grid, dim3(kAttnThreads), dyn, p));
+    return RCU_OK;
 }
-
-bool attention_fused_merge_ok(uint64_t n_head, uint64_t hd, uint32_t fmt) { return combine_heads(n_head, hd, fmt) != 0; }
 
 template <int KV>
-static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, float *out, const ActOut *aq,
-                          uint32_t hpc) {
+static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, uint32_t dyn) {
     switch (group) {
-        case 1: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 1>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
-        case 2: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 2>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
-        case 4: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 4>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
-        case 8: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 8>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
-        case 16: RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_partial<KV, 16>), dim3(grid), dim3(kAttnThreads), 0, p)); break;
+        case 1: return launch_group<KV, 1>(ctx, p, grid, dyn);
+        case 2: return launch_group<KV, 2>(ctx, p, grid, dyn);
+        case 4: return launch_group<KV, 4>(ctx, p, grid, dyn);
+        case 8: return launch_group<KV, 8>(ctx, p, grid, dyn);
+        case 16: return launch_group<KV, 16>(ctx, p, grid, dyn);
         default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4, 8 or 16");
     }
-    if (aq) {
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_combine_q<KV>), dim3(dim3(p.n_head / hpc, p.n_tok)), dim3(hpc * p.hd), 0, p, hpc, out, *aq));
-    } else {
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn_combine<KV>), dim3(dim3(p.n_head, p.n_tok)), dim3(32), 0, p, out));
-    }
-    return RCU_OK;
 }
 
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
                      const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
                      float *scratch, const ActOut *aq) {
     const uint64_t group = n_head / kv->n_kv;
-    const uint32_t hpc = aq ? combine_heads(n_head, kv->hd, aq->fmt) : 0;
-    if (aq && !hpc) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: no fused merge for this head shape");
     if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
+    if (aq && !attention_fused_merge_ok(n_head, kv->n_kv, kv->hd, aq->fmt))
+        return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: group output does not hold whole activation blocks");
     AttnParams p{};
     p.kc = kv->k;
     p.vc = kv->v;
     p.q = q;
+    p.out = out;
+    if (aq) p.aq = *aq;
     p.n_tok = (uint32_t)n_tok;
     p.n_head = (uint32_t)n_head;
     p.n_kv = (uint32_t)kv->n_kv;
@@ -731,6 +792,7 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
     p.softcap = softcap;
     p.rounding = ctx->rounding;
     p.row_bytes = (uint32_t)kv->row_bytes;
+    p.buf_bytes = (uint32_t)((kSub * kv->row_bytes + 15) & ~15ull) + 64;
     // fixed plans (graph replay) cover the whole cache; otherwise the current length
     uint64_t max_len;
     if (n_split != 0) {
@@ -741,24 +803,26 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
     }
     split_plan(max_len, n_tok, kv->n_kv, ctx->num_sms, &p.n_split, &p.rows_per_split);
     const uint64_t parts = n_tok * n_head * p.n_split;
-    void *scr = scratch;
+    uint8_t *scr = reinterpret_cast<uint8_t *>(scratch);
     if (!scr) {
-        int st = scratch_get(ctx, parts * (kv->hd + 2) * sizeof(float), &scr);
+        void *v = nullptr;
+        int st = scratch_get(ctx, counters_bytes(n_tok, kv->n_kv) + parts * (kv->hd + 2) * sizeof(float), &v);
         if (st) return st;
+        scr = reinterpret_cast<uint8_t *>(v);
+        RCU_CUDA_TRY(ctx, cudaMemsetAsync(scr, 0, counters_bytes(n_tok, kv->n_kv), ctx->stream));
     }
-    p.o_part = (float *)scr;
+    p.done = reinterpret_cast<uint32_t *>(scr);
+    p.o_part = reinterpret_cast<float *>(scr + counters_bytes(n_tok, kv->n_kv));
     p.m_part = p.o_part + parts * kv->hd;
     p.l_part = p.m_part + parts;
+    const uint64_t merge_bytes = 4 * (((group * p.n_split + 3) & ~3ull) + group * kv->hd);
+    const uint32_t dyn = (uint32_t)std::max<uint64_t>(4ull * p.buf_bytes, merge_bytes);
     dim3 grid((uint32_t)kv->n_kv, (uint32_t)n_tok, p.n_split);
-    int st = RCU_OK;
     switch (kv->type) {
-        case RCU_KV_F16: st = dispatch_group<RCU_KV_F16>(ctx, p, (int)group, grid, out, aq, hpc); break;
-        case RCU_KV_Q8_0: st = dispatch_group<RCU_KV_Q8_0>(ctx, p, (int)group, grid, out, aq, hpc); break;
-        default: st = dispatch_group<RCU_KV_TURBO4>(ctx, p, (int)group, grid, out, aq, hpc); break;
+        case RCU_KV_F16: return dispatch_group<RCU_KV_F16>(ctx, p, (int)group, grid, dyn);
+        case RCU_KV_Q8_0: return dispatch_group<RCU_KV_Q8_0>(ctx, p, (int)group, grid, dyn);
+        default: return dispatch_group<RCU_KV_TURBO4>(ctx, p, (int)group, grid, dyn);
     }
-    if (st) return st;
-    RCU_CUDA_TRY(ctx, cudaGetLastError());
-    return RCU_OK;
 }
 
 }  // namespace rcu
