@@ -131,6 +131,7 @@ def barrier(world: int):
 # ---- workload: config 1 GEMV stack ---------------------------------------------------------
 GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_DISTINCT = 6144, 2048, 72, 8
 GEMV_TYPE = "Q4_0"  # config 1; --wtype runs the same shape in another GGUF type
+GEMV_EACH = False  # --shape RxK: weights of another shape, one launch per weight (decode-like)
 BLOCK = {"Q4_0": (32, 18), "Q4_1": (32, 20), "Q5_0": (32, 22), "Q5_1": (32, 24), "Q8_0": (32, 34),
          "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210)}
 
@@ -156,6 +157,8 @@ def gemv_bytes_per_step():
 def gemv_meta():
     kq = GEMV_TYPE.endswith("_K")
     tag = "config 1" if GEMV_TYPE == "Q4_0" else "config-1 shape"
+    if GEMV_EACH:
+        tag = f"{GEMV_ROWS}x{GEMV_K}, one launch per weight"
     return {"metric": f"quant-matmul HBM GB/s ({GEMV_TYPE} x {'Q8_K' if kq else 'Q8_0'} GEMV, {tag})", "unit": "GB/s",
             "dtype": f"int8 ({GEMV_TYPE} x {'Q8_K' if kq else 'Q8_0'} blocks, f32 combine)",
             "workload": f"gemv_{GEMV_TYPE.lower()}_{GEMV_ROWS}x{GEMV_K}" + ("_config1" if GEMV_TYPE == "Q4_0" else "")}
@@ -181,7 +184,11 @@ def run_gemv(args, world, rank, local):
         acts.prepare(xd, 1, GEMV_K, fmt)
         if ev is not None:
             ev[0].record(stream)
-        rie.matmul_multi(ctx, acts, jobs)
+        if GEMV_EACH:
+            for j in jobs:
+                rie.matmul_multi(ctx, acts, [j])
+        else:
+            rie.matmul_multi(ctx, acts, jobs)
         if ev is not None:
             ev[1].record(stream)
 
@@ -251,7 +258,7 @@ def run_gemv(args, world, rank, local):
         "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_COPIES * GEMV_ROWS * 4,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (1 + (GEMV_COPIES if GEMV_EACH else 1)) * args.steps,
         "clocks": clk.summary(),
         "check": {"max_rel_err_vs_oracle": max_rel, "tolerance": 1e-3},
     }
@@ -644,9 +651,16 @@ def main():
     ap.add_argument("--wtype", default="Q4_0", choices=sorted(BLOCK),
                     help="GGUF type of the gemv workload (config 1 is Q4_0)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt length of the decode workload (config 3: 512)")
+    ap.add_argument("--shape", default=None, help="gemv workload: ROWSxK weights, one launch each (e.g. 24576x4096)")
     args = ap.parse_args()
-    global GEMV_TYPE, DEC_PROMPT
+    global GEMV_TYPE, DEC_PROMPT, GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_EACH, GEMV_DISTINCT
     GEMV_TYPE = args.wtype
+    if args.shape:
+        GEMV_ROWS, GEMV_K = (int(v) for v in args.shape.lower().split("x"))
+        bs, bb = BLOCK[GEMV_TYPE]
+        GEMV_COPIES = max(GEMV_DISTINCT, -(-520_000_000 // (GEMV_ROWS * GEMV_K // bs * bb)))
+        GEMV_DISTINCT = max(1, min(GEMV_DISTINCT, 800_000_000 // (GEMV_ROWS * GEMV_K * 4)))  # host f32 draft
+        GEMV_EACH = True
     DEC_PROMPT = args.prompt
     META["gemv"] = gemv_meta()
     world, rank, local = dist_init()

@@ -63,10 +63,12 @@ struct Q8kShared {
 
 // Q8_K of one 256-value block held one value per thread by 8 consecutive warps
 // (j = index in the block, 0..255; the block's first warp is warp `w0` of the CTA).
-// Every thread of the CTA must call this the same number of times (it has a __syncthreads);
+// Every participating thread must call this the same number of times: it synchronises the
+// whole CTA (bar_threads == 0) or the first bar_threads threads on named barrier bar_id.
 // `store` false skips the writes (threads past the end of the row). `parity` alternates.
 __device__ __forceinline__ void q8_k_block(float v, uint32_t j, uint32_t w0, uint64_t blk, bool store,
-                                           const ActOut &o, Q8kShared &sh, int parity) {
+                                           const ActOut &o, Q8kShared &sh, int parity, int bar_id = 0,
+                                           int bar_threads = 0) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // signed value of largest magnitude; ties keep the first index (strict > scan)
     unsigned long long key = ((unsigned long long)__float_as_uint(fabsf(v)) << 32) | (uint32_t)(0xffffffffu - j);
@@ -79,7 +81,10 @@ __device__ __forceinline__ void q8_k_block(float v, uint32_t j, uint32_t w0, uin
         sh.key[parity][warp] = key;
         sh.val[parity][warp] = wv;
     }
-    __syncthreads();
+    if (bar_threads)
+        asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(bar_threads) : "memory");
+    else
+        __syncthreads();
     unsigned long long best = sh.key[parity][w0];
     float mx = sh.val[parity][w0];
 #pragma unroll

@@ -5,6 +5,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -43,6 +44,23 @@ using namespace rcu;
     catch (...) {                                                       \
         return set_err((ctx), RCU_ERR_RUNTIME, "internal exception");   \
     }
+
+namespace rcu {
+cudaError_t prefer_max_shared(const void *kern) {
+    // kernels already configured on the current device; a handful of entries
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void *>> done;
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev)) return e;
+    std::lock_guard<std::mutex> g(mu);
+    for (auto &d : done)
+        if (d.first == dev && d.second == kern) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                               (int)cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess) done.emplace_back(dev, kern);
+    return e;
+}
+}  // namespace rcu
 
 extern "C" {
 

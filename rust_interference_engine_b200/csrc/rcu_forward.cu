@@ -189,24 +189,35 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 //   xn = (x * (1 / rms(x))) * w   (ops.rs:7-14)
 // then xn is quantized into the matmul activations (ActOut formats) and, when xn_f32 is
 // given, stored as f32. Each thread writes back only the x values it read, so x may be
-// updated in place.
+// updated in place. The norm weights, and x when `x_ready` (x was last written by a kernel
+// that has completed before this one starts: three or more launches earlier), are loaded
+// before waiting for the previous kernel, which produced o.
 constexpr int kNormThreads = 1024;
 template <int NIT>
 __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, const float *__restrict__ o,
                                                          const float *__restrict__ post_w, float rs,
                                                          const float *__restrict__ w, uint32_t e, float eps,
-                                                         float *__restrict__ xn_f32, const ActOut ao) {
-    pdl_wait();
-    pdl_trigger();
+                                                         float *__restrict__ xn_f32, const ActOut ao, int x_ready) {
     __shared__ float red[32];
     __shared__ Q8kShared sh;
     const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float *xr = x + (uint64_t)t * e;
-    float v[NIT];
+    float v[NIT], wv[NIT], pw[NIT];
 #pragma unroll
     for (int j = 0; j < NIT; j++) {
         const uint32_t i = tid + kNormThreads * j;
-        v[j] = i < e ? xr[i] : 0.0f;
+        wv[j] = i < e ? w[i] : 0.0f;
+        pw[j] = (post_w && i < e) ? post_w[i] : 0.0f;
+        if (x_ready) v[j] = i < e ? xr[i] : 0.0f;
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!x_ready) {
+#pragma unroll
+        for (int j = 0; j < NIT; j++) {
+            const uint32_t i = tid + kNormThreads * j;
+            v[j] = i < e ? xr[i] : 0.0f;
+        }
     }
     if (o) {
         const float *orow = o + (uint64_t)t * e;
@@ -223,10 +234,7 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
             ss = block_sum(ss, red);
             const float scale = 1.0f / sqrtf(ss / (float)e + eps);
 #pragma unroll
-            for (int j = 0; j < NIT; j++) {
-                const uint32_t i = tid + kNormThreads * j;
-                if (i < e) ov[j] *= scale * post_w[i];
-            }
+            for (int j = 0; j < NIT; j++) ov[j] *= scale * pw[j];
         }
 #pragma unroll
         for (int j = 0; j < NIT; j++) {
@@ -243,7 +251,7 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
 #pragma unroll
     for (int j = 0; j < NIT; j++) {
         const uint32_t i = tid + kNormThreads * j;
-        const float xn = i < e ? v[j] * scale * w[i] : 0.0f;
+        const float xn = i < e ? v[j] * scale * wv[j] : 0.0f;
         if (xn_f32 && i < e) xn_f32[(uint64_t)t * e + i] = xn;
         const uint32_t i0 = kNormThreads * j + 32 * warp;  // first value of this warp's block
         if ((ao.fmt & RCU_ACT_Q8_0) && i0 < e) q8_0_block(xn, (uint64_t)t * (e / QK) + i0 / QK, lane, ao);
@@ -324,7 +332,7 @@ static int matmul(rcu_backend *b, uint32_t n, uint32_t k, uint32_t fmt, std::vec
 
 // x (+)= post_norm(o) * rs; quantized RMSNorm(x) * w into b->acts (and f32 into xn_f32).
 static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const float *post_w, const float *w,
-                  float *xn_f32, uint32_t fmt) {
+                  float *xn_f32, uint32_t fmt, bool x_ready) {
     const rcu_model_config &c = b->m->cfg;
     const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
     const ActOut ao = acts_out(b, fmt);
@@ -332,7 +340,7 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
     auto kern = nit <= 1 ? k_norm_q<1> : nit <= 2 ? k_norm_q<2> : nit <= 4 ? k_norm_q<4> : nit <= 8 ? k_norm_q<8> : k_norm_q<16>;
     if (nit > 16) return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
     RCU_CUDA_TRY(b->ctx, launch_k(b->ctx, kern, dim3((uint32_t)n), dim3(kNormThreads), 0, x, o, post_w, rs, w, e, eps,
-                                  xn_f32, ao));
+                                  xn_f32, ao, x_ready ? 1 : 0));
     return RCU_OK;
 }
 
@@ -345,16 +353,28 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
 static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
     rcu_ctx *ctx = b->ctx;
     const rcu_model_config &c = b->m->cfg;
-    cudaStream_t s = ctx->stream;
     const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type, b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x));
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type, b->embd->data,
+                               b->embd->row_bytes, e, c.embd_scale, b->x));
+    // [residual +] RMSNorm + quantize (its own kernel), then the matmuls that consume it.
+    // x_ready: x was written three or more launches back (the norm kernel may load it early).
+    auto norm_matmul = [&](uint64_t rows, uint64_t row0, const float *o, const float *post, const float *w,
+                           float *xn_f32, bool x_ready, std::vector<rcu_job> jobs) -> int {
+        uint32_t fmt = 0;
+        for (auto &j : jobs) fmt |= act_format(j.w->type);
+        if (int st = norm_q(b, rows, b->x + row0 * e, o ? o + row0 * e : nullptr, post, w, xn_f32, fmt, x_ready))
+            return st;
+        return matmul(b, (uint32_t)rows, e, fmt, jobs);
+    };
     const float *pend_o = nullptr, *pend_post = nullptr;  // residual not yet added to x
     int st;
     for (uint32_t il = 0; il < c.n_layer; il++) {
         const LayerW &L = b->layers[il];
-        const uint32_t fqkv = formats({L.wq, L.wk, L.wv});
-        if ((st = norm_q(b, n, b->x, pend_o, pend_post, L.attn_norm, nullptr, fqkv))) return st;
-        if ((st = matmul(b, (uint32_t)n, e, fqkv, {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}}))) return st;
+        // x comes from k_embed (the launch just before) in layer 0, else from this layer's
+        // previous norm (four launches back)
+        if ((st = norm_matmul(n, 0, pend_o, pend_post, L.attn_norm, nullptr, il > 0,
+                              {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}})))
+            return st;
         const bool swa_rope = L.swa && c.rope_base_swa > 0.0f;
         QkvPostParams qp{b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
                          swa_rope ? b->inv_freq_swa : b->inv_freq, b->pos_dev, (uint32_t)n, c.n_head, hd,
@@ -374,24 +394,25 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         }
         if (st) return st;
         if ((st = matmul(b, (uint32_t)n, qd, fo, {{L.wo, b->o, e}}))) return st;
-        const uint32_t fgu = formats({L.gate, L.up});
-        if ((st = norm_q(b, n, b->x, b->o, L.post_attn, L.ffn_norm, nullptr, fgu))) return st;
         const uint32_t ff = (uint32_t)L.gate->rows;
-        if ((st = matmul(b, (uint32_t)n, e, fgu, {{L.gate, b->g, ff}, {L.up, b->u, ff}}))) return st;
+        if ((st = norm_matmul(n, 0, b->o, L.post_attn, L.ffn_norm, nullptr, true,
+                              {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
+            return st;
         const uint32_t fd = formats({L.down});
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3(dim3((ff + 1023) / 1024, (uint32_t)n)), dim3(1024), 0, b->g, b->u, ff, c.act, acts_out(b, fd)));
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((ff + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, ff,
+                                   c.act, acts_out(b, fd)));
         if ((st = matmul(b, (uint32_t)n, ff, fd, {{L.down, b->o, e}}))) return st;
         pend_o = b->o;
         pend_post = L.post_ffn;
     }
     const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
-    const uint32_t fout = formats({b->out});
-    if ((st = norm_q(b, m, b->x + first * e, pend_o + first * e, pend_post, b->out_norm, b->xn, fout))) return st;
     b->hidden_rows = m;
-    if ((st = matmul(b, (uint32_t)m, e, fout, {{b->out, logits, c.n_vocab}}))) return st;
+    if ((st = norm_matmul(m, first, pend_o, pend_post, b->out_norm, b->xn, true, {{b->out, logits, c.n_vocab}})))
+        return st;
     if (c.logit_scale != 1.0f || c.final_softcap > 0.0f) {
         const uint64_t nl = m * c.n_vocab;
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_logit_post), dim3((uint32_t)((nl + 255) / 256)), dim3(256), 0, logits, nl, c.logit_scale, c.final_softcap));
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_logit_post), dim3((uint32_t)((nl + 255) / 256)), dim3(256), 0, logits, nl,
+                                   c.logit_scale, c.final_softcap));
     }
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;

@@ -204,9 +204,15 @@ namespace rcu {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Every kernel of the library runs with the largest shared-memory carveout, so that an SM
+// never has to drain and re-split L1 / shared memory between consecutive kernels (the GEMV
+// needs the maximum) and a dependent kernel can become resident next to the running one.
+cudaError_t prefer_max_shared(const void *kern);
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(const rcu_ctx *ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             Args... args) {
+    if (cudaError_t e = prefer_max_shared(reinterpret_cast<const void *>(kern))) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;

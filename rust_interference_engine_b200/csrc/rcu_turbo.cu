@@ -345,8 +345,6 @@ __device__ __forceinline__ StagedRows stage_rows(const uint8_t *cache, uint64_t 
 // the quantized activations of the Wo matmul.
 template <int KV, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnParams p) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int DPL = kMaxAttnHd / 32;
     extern __shared__ __align__(16) uint8_t dsm[];
     __shared__ __align__(16) float qf[G][kMaxAttnHd];  // f32 query (f16 cache) / rotation scratch
@@ -370,13 +368,34 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     auto kbuf_of = [&](uint32_t b) { return dsm + b * p.buf_bytes; };
     auto vbuf_of = [&](uint32_t b) { return dsm + (2 + b) * p.buf_bytes; };
 
+    // The first sub-chunk is staged before waiting for the previous kernel: its rows were
+    // written by earlier steps, except the rows of this batch's own positions (written by the
+    // kernel just before), which are copied again after the wait.
+    const uint64_t pos_b = p.pos_ptr ? *p.pos_ptr : p.pos0;
+    const uint32_t fresh0 = pos_b > start ? (uint32_t)(pos_b - start) : 0;  // first row of this batch
+    StagedRows kr0{}, vr0{}, kr1{}, vr1{};
     if (c0 < len) {
-        StagedRows kr0, vr0, kr1, vr1;
-        {
-            const uint32_t n = min(kSub, c1 - c0);
-            kr0 = stage_rows(p.kc, head_base, p.slots, rb, (start + c0) % p.slots, n, kbuf_of(0));
-            vr0 = stage_rows(p.vc, head_base, p.slots, rb, (start + c0) % p.slots, n, vbuf_of(0));
-            cp_async_commit();
+        const uint32_t n = min(kSub, c1 - c0);
+        kr0 = stage_rows(p.kc, head_base, p.slots, rb, (start + c0) % p.slots, n, kbuf_of(0));
+        vr0 = stage_rows(p.vc, head_base, p.slots, rb, (start + c0) % p.slots, n, vbuf_of(0));
+        cp_async_commit();
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (c0 < len) {
+        const uint32_t n0 = min(kSub, c1 - c0);
+        if (c0 + n0 > fresh0) {  // re-copy this batch's rows (2-byte units: rows are 2-aligned)
+            cp_async_wait<0>();
+            __syncthreads();  // every thread's copies of the sub-chunk have landed
+            const uint32_t r_first = fresh0 > c0 ? fresh0 - c0 : 0, hw = rb / 2;
+            for (uint32_t u = tid; u < (n0 - r_first) * hw; u += kAttnThreads) {
+                const uint32_t r = r_first + u / hw, h2 = u % hw;
+                const uint64_t src = head_base + (uint64_t)((start + c0 + r) % p.slots) * rb + 2 * h2;
+                *reinterpret_cast<uint16_t *>(kbuf_of(0) + kr0.off(r, rb) + 2 * h2) =
+                    *reinterpret_cast<const uint16_t *>(p.kc + src);
+                *reinterpret_cast<uint16_t *>(vbuf_of(0) + vr0.off(r, rb) + 2 * h2) =
+                    *reinterpret_cast<const uint16_t *>(p.vc + src);
+            }
         }
         // 1. queries of this group: rotate (turbo) and quantize to Q8_0 (turbo / Q8_0 caches)
         for (uint32_t hh = warp; hh < G; hh += kAttnWarps) {
@@ -638,11 +657,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     for (uint32_t v = tid; v < gv; v += kAttnThreads) {
         const uint32_t hh = v / hd, d = v % hd;
         const uint64_t base = base0 + (uint64_t)hh * p.n_split;
+        const float *src = p.o_part + base * hd + d, *fh = fac + hh * p.n_split;
         float o = 0.0f;
-        for (uint32_t s = 0; s < p.n_split; s++) {
-            const float f = fac[hh * p.n_split + s];
-            if (f != 0.0f) o += f * __ldcg(p.o_part + (base + s) * hd + d);
+        uint32_t s = 0;
+        for (; s + 8 <= p.n_split; s += 8) {  // eight independent loads in flight
+            float x[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) x[j] = __ldcg(src + (uint64_t)(s + j) * hd);
+#pragma unroll
+            for (int j = 0; j < 8; j++) o += fh[s + j] * x[j];
         }
+        for (; s < p.n_split; s++) o += fh[s] * __ldcg(src + (uint64_t)s * hd);
         vals[v] = o;
     }
     __syncthreads();
