@@ -190,6 +190,28 @@ RCU_API int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *token
                                            int32_t all_logits, float *logits_dev);
 /* Backend::hidden (model/mod.rs:318): final normed rows of the last forward (rows x n_embd). */
 RCU_API int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out);
+/* The KV cache of one layer (owned by the backend), e.g. to fill it with rcu_kv_import. */
+RCU_API int32_t rcu_backend_kv(rcu_backend *b, uint64_t layer, rcu_kv **out);
+
+/* ---- tensor parallelism over NCCL (no counterpart in the reference: it has no multi-device
+ * code). One process (or thread) per GPU, each with its own context. -------------------- */
+/* A model holding rank `rank` of `world` shards: rcu_model_set_tensor takes the full GGUF
+ * tensors and keeps this rank's part (q/k/v and gate/up rows by head / FFN row, the output
+ * head's vocabulary rows, attn_output and ffn_down column blocks; the rest replicated). */
+RCU_API int32_t rcu_model_create_tp(rcu_ctx *ctx, const rcu_model_config *cfg, int32_t rank, int32_t world,
+                                    rcu_model **out);
+/* Host-only: the shard rcu_model_set_tensor keeps for (rank, world); out == NULL reports the
+ * shape only. */
+RCU_API int32_t rcu_tp_shard(const rcu_model_config *cfg, const char *name, uint32_t ggml_type, uint64_t rows,
+                             uint64_t cols, const void *host_bytes, int32_t rank, int32_t world, void *out,
+                             uint64_t out_cap, uint64_t *out_rows, uint64_t *out_cols);
+/* Communicator id (128 bytes) made on one rank and handed to every rank. */
+RCU_API int32_t rcu_tp_unique_id(uint8_t *out, uint64_t cap);
+/* rcu_backend_create for a tensor-parallel model: all ranks call it with the same id; Wo and
+ * ffn_down outputs are all-reduced, the vocabulary-parallel logits all-gathered, so every
+ * rank's forward returns the full logits. */
+RCU_API int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type,
+                                      const uint8_t *comm_id, rcu_backend **out);
 
 /* ---- allocation-free matmul (no counterpart in the reference) ------------------------ */
 /* W . X for f32 activations x_dev (n_tok x w->cols, device), out_dev[t * ld + r], without

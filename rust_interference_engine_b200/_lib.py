@@ -58,6 +58,11 @@ SIGNATURES = {
     "rcu_backend_forward_device": (I32, [P, P, U64, U64, I32, P]),
     "rcu_backend_hidden": (I32, [P, P, U64, C.POINTER(U64)]),
     "rcu_matmul_f32_static": (I32, [P, P, P, U64, P, U64]),
+    "rcu_backend_kv": (I32, [P, U64, C.POINTER(P)]),
+    "rcu_model_create_tp": (I32, [P, P, I32, I32, C.POINTER(P)]),
+    "rcu_tp_shard": (I32, [P, C.c_char_p, U32, U64, U64, P, I32, I32, P, U64, C.POINTER(U64), C.POINTER(U64)]),
+    "rcu_tp_unique_id": (I32, [P, U64]),
+    "rcu_backend_create_tp": (I32, [P, U64, U64, I32, P, C.POINTER(P)]),
 }
 
 

@@ -45,6 +45,20 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def nccl_link() -> list:
+    """Link NCCL by soname (libnccl.so.2): the process uses whichever copy it loads first
+    (the one PyTorch brings, when present)."""
+    for d in ("/usr/lib/x86_64-linux-gnu", "/usr/local/cuda/lib64"):
+        if os.path.exists(os.path.join(d, "libnccl.so.2")):
+            return ["-L" + d, "-l:libnccl.so.2"]
+    try:
+        import nvidia.nccl  # pip wheel layout
+        d = os.path.join(os.path.dirname(nvidia.nccl.__file__), "lib")
+        return ["-L" + d, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + d]
+    except Exception:
+        return ["-l:libnccl.so.2"]
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
@@ -66,7 +80,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError("nvcc failed")
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcuda"]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcuda", *nccl_link()]
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB)
     return LIB

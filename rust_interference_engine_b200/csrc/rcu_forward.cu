@@ -15,6 +15,8 @@
 #include <string>
 #include <vector>
 
+#include <nccl.h>
+
 #include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
@@ -34,6 +36,7 @@ struct LayerW {
 struct rcu_model {
     rcu_ctx *ctx = nullptr;
     rcu_model_config cfg{};
+    int tp_rank = 0, tp_world = 1;  // tensor-parallel shard held by this model
     std::map<std::string, rcu_weight *> w;
     std::map<std::string, float *> vec;  // 1-D float tensors as device f32
     std::vector<rcu_weight *> slices;
@@ -42,6 +45,9 @@ struct rcu_model {
 struct rcu_backend {
     rcu_model *m = nullptr;
     rcu_ctx *ctx = nullptr;
+    rcu_model_config cfg{};  // this rank's dimensions (heads, FFN rows, vocab rows) under TP
+    ncclComm_t comm = nullptr;  // tensor-parallel communicator (world > 1)
+    float *logits_local = nullptr, *logits_gather = nullptr;
     uint64_t n_ctx = 0, max_batch = 0;
     int kv_type = 0;
     std::vector<rcu::LayerW> layers;
@@ -333,7 +339,7 @@ static int matmul(rcu_backend *b, uint32_t n, uint32_t k, uint32_t fmt, std::vec
 // x (+)= post_norm(o) * rs; quantized RMSNorm(x) * w into b->acts (and f32 into xn_f32).
 static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const float *post_w, const float *w,
                   float *xn_f32, uint32_t fmt, bool x_ready) {
-    const rcu_model_config &c = b->m->cfg;
+    const rcu_model_config &c = b->cfg;
     const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
     const ActOut ao = acts_out(b, fmt);
     const float rs = c.residual_scale, eps = c.rms_eps;
@@ -350,9 +356,33 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
 // Per layer: norm+quantize, QKV matmul, q/k post-processing + KV append, attention with the
 // merge quantizing for Wo, Wo, residual+norm+quantize, gate+up, GLU+quantize, down; the
 // down residual is folded into the next layer's (or the output) norm.
+static int nccl_err(rcu_ctx *ctx, ncclResult_t r, const char *what) {
+    return set_err(ctx, RCU_ERR_RUNTIME, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+// [P][rows][cols] (rank-major, as all-gather leaves it) -> [rows][P * cols]
+__global__ void k_unshard_cols(const float *__restrict__ src, float *__restrict__ dst, uint32_t P, uint32_t rows,
+                               uint32_t cols) {
+    pdl_wait();
+    pdl_trigger();
+    const uint64_t n = (uint64_t)P * rows * cols;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t c = i % cols, r = (i / cols) % rows, p = i / ((uint64_t)cols * rows);
+        dst[r * (uint64_t)P * cols + p * cols + c] = src[i];
+    }
+}
+
 static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
     rcu_ctx *ctx = b->ctx;
-    const rcu_model_config &c = b->m->cfg;
+    const rcu_model_config &c = b->cfg;
+    const int P = b->m->tp_world;
+    // tensor parallel: the row-parallel outputs (Wo, down) are partial sums over this rank's
+    // slice of K; all-reduce them before the residual add
+    auto all_reduce = [&](float *buf, uint64_t count) -> int {
+        if (P == 1) return RCU_OK;
+        const ncclResult_t r = ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, b->comm, ctx->stream);
+        return r == ncclSuccess ? RCU_OK : nccl_err(ctx, r, "ncclAllReduce");
+    };
     const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
     RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type, b->embd->data,
                                b->embd->row_bytes, e, c.embd_scale, b->x));
@@ -394,6 +424,7 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         }
         if (st) return st;
         if ((st = matmul(b, (uint32_t)n, qd, fo, {{L.wo, b->o, e}}))) return st;
+        if ((st = all_reduce(b->o, n * e))) return st;
         const uint32_t ff = (uint32_t)L.gate->rows;
         if ((st = norm_matmul(n, 0, b->o, L.post_attn, L.ffn_norm, nullptr, true,
                               {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
@@ -402,15 +433,27 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((ff + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, ff,
                                    c.act, acts_out(b, fd)));
         if ((st = matmul(b, (uint32_t)n, ff, fd, {{L.down, b->o, e}}))) return st;
+        if ((st = all_reduce(b->o, n * e))) return st;
         pend_o = b->o;
         pend_post = L.post_ffn;
     }
     const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
     b->hidden_rows = m;
-    if ((st = norm_matmul(m, first, pend_o, pend_post, b->out_norm, b->xn, true, {{b->out, logits, c.n_vocab}})))
+    // vocab-parallel head: each rank computes its rows of the vocabulary, then all-gather
+    float *lg = P == 1 ? logits : b->logits_local;
+    if ((st = norm_matmul(m, first, pend_o, pend_post, b->out_norm, b->xn, true, {{b->out, lg, c.n_vocab}})))
         return st;
+    const uint64_t vocab = (uint64_t)c.n_vocab * P;
+    if (P > 1) {
+        float *dst = m == 1 ? logits : b->logits_gather;
+        const ncclResult_t r = ncclAllGather(lg, dst, m * c.n_vocab, ncclFloat32, b->comm, ctx->stream);
+        if (r != ncclSuccess) return nccl_err(ctx, r, "ncclAllGather");
+        if (m > 1)
+            RCU_CUDA_TRY(ctx, launch_k(ctx, (k_unshard_cols), dim3(ctx->num_sms * 4), dim3(256), 0, b->logits_gather,
+                                       logits, (uint32_t)P, (uint32_t)m, (uint32_t)c.n_vocab));
+    }
     if (c.logit_scale != 1.0f || c.final_softcap > 0.0f) {
-        const uint64_t nl = m * c.n_vocab;
+        const uint64_t nl = m * vocab;
         RCU_CUDA_TRY(ctx, launch_k(ctx, (k_logit_post), dim3((uint32_t)((nl + 255) / 256)), dim3(256), 0, logits, nl,
                                    c.logit_scale, c.final_softcap));
     }
@@ -423,6 +466,91 @@ static bool ends_with(const std::string &s, const char *suf) {
     return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
 }
 
+// ---- tensor-parallel sharding (host side) ---------------------------------------------------
+// Column-parallel (rows split): q/k/v (by head), gate/up, the vocabulary rows of the output
+// head, q/k/v biases. Row-parallel (columns split, whole blocks): attn_output, ffn_down.
+// Everything else (embeddings, norms) is replicated.
+enum TpKind { TP_REPL = 0, TP_ROWS = 1, TP_COLS = 2, TP_QKV = 3, TP_UPGATE = 4 };
+static int tp_kind(const std::string &n, const rcu_model_config &c, uint64_t rows) {
+    if (n == "output.weight") return TP_ROWS;  // (not "blk.N.attn_output.weight")
+    if (ends_with(n, ".attn_output.weight") || ends_with(n, ".ffn_down.weight")) return TP_COLS;
+    if (ends_with(n, ".attn_qkv.weight")) return TP_QKV;
+    if (ends_with(n, ".ffn_up.weight") && rows == 2ull * c.n_ff) return TP_UPGATE;
+    for (const char *suf : {".attn_q.weight", ".attn_k.weight", ".attn_v.weight", ".ffn_gate.weight", ".ffn_up.weight",
+                            ".attn_q.bias", ".attn_k.bias", ".attn_v.bias"})
+        if (ends_with(n, suf)) return TP_ROWS;
+    return TP_REPL;
+}
+
+// Shard of one tensor for `rank` of `world`. 1-D tensors (rows == 1) split their elements.
+// out == nullptr only reports the shape; otherwise out holds out_cap bytes.
+static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &name, uint32_t type, uint64_t rows,
+                    uint64_t cols, const uint8_t *host, int rank, int world, std::vector<uint8_t> *out, uint64_t *out_rows,
+                    uint64_t *out_cols) {
+    const int kind = world > 1 ? tp_kind(name, c, rows) : TP_REPL;
+    const bool vec1d = rows == 1 && (type == T_F32 || type == T_F16 || type == T_BF16) && kind == TP_ROWS;
+    const uint64_t rb = vec1d ? (type == T_F32 ? 4 : 2) * cols : rcu_row_bytes(type, cols);
+    if (!vec1d && rb == 0) return set_err(ctx, RCU_ERR_INVALID, "tensor " + name + ": bad row length");
+    auto bad = [&](const char *why) { return set_err(ctx, RCU_ERR_INVALID, "tensor parallel: " + name + " " + why); };
+    auto copy_rows = [&](uint64_t r0, uint64_t nr, uint64_t at) {
+        if (out) std::memcpy(out->data() + at * rb, host + r0 * rb, nr * rb);
+    };
+    switch (kind) {
+        case TP_REPL:
+            *out_rows = rows, *out_cols = cols;
+            if (out) out->assign(host, host + rows * rb);
+            return RCU_OK;
+        case TP_ROWS: {
+            if (vec1d) {  // bias vector: split elements
+                if (cols % world) return bad("length not divisible by the tensor-parallel degree");
+                const uint64_t es = rb / cols, n = cols / world;
+                *out_rows = 1, *out_cols = n;
+                if (out) out->assign(host + rank * n * es, host + (rank + 1) * n * es);
+                return RCU_OK;
+            }
+            uint64_t total = rows;
+            if (name == "output.weight") total = c.n_vocab;  // padded vocab rows are dropped
+            if (total % world) return bad("rows not divisible by the tensor-parallel degree");
+            const uint64_t n = total / world;
+            *out_rows = n, *out_cols = cols;
+            if (out) out->resize(n * rb);
+            copy_rows(rank * n, n, 0);
+            return RCU_OK;
+        }
+        case TP_QKV: {
+            const uint64_t qd = (uint64_t)c.n_head * c.head_dim, kvd = (uint64_t)c.n_head_kv * c.head_dim;
+            if (rows != qd + 2 * kvd || qd % world || kvd % world) return bad("q/k/v rows do not split evenly");
+            const uint64_t nq = qd / world, nk = kvd / world;
+            *out_rows = nq + 2 * nk, *out_cols = cols;
+            if (out) out->resize((nq + 2 * nk) * rb);
+            copy_rows(rank * nq, nq, 0);
+            copy_rows(qd + rank * nk, nk, nq);
+            copy_rows(qd + kvd + rank * nk, nk, nq + nk);
+            return RCU_OK;
+        }
+        case TP_UPGATE: {
+            if (c.n_ff % world) return bad("FFN rows not divisible by the tensor-parallel degree");
+            const uint64_t nf = c.n_ff / world;
+            *out_rows = 2 * nf, *out_cols = cols;
+            if (out) out->resize(2 * nf * rb);
+            copy_rows(rank * nf, nf, 0);
+            copy_rows(c.n_ff + rank * nf, nf, nf);
+            return RCU_OK;
+        }
+        default: {  // TP_COLS: each row keeps its rank's run of whole blocks
+            const uint64_t bs = block_size(type);
+            if (cols % world || (cols / world) % bs) return bad("columns do not split into whole blocks");
+            const uint64_t nc = cols / world, srb = rcu_row_bytes(type, nc);
+            *out_rows = rows, *out_cols = nc;
+            if (out) {
+                out->resize(rows * srb);
+                for (uint64_t r = 0; r < rows; r++) std::memcpy(out->data() + r * srb, host + r * rb + rank * srb, srb);
+            }
+            return RCU_OK;
+        }
+    }
+}
+
 }  // namespace rcu
 
 using namespace rcu;
@@ -430,6 +558,11 @@ using namespace rcu;
 extern "C" {
 
 int32_t rcu_model_create(rcu_ctx *ctx, const rcu_model_config *cfg, rcu_model **out) {
+    return rcu_model_create_tp(ctx, cfg, 0, 1, out);
+}
+
+int32_t rcu_model_create_tp(rcu_ctx *ctx, const rcu_model_config *cfg, int32_t rank, int32_t world, rcu_model **out) {
+    if (world < 1 || rank < 0 || rank >= world) return set_err(ctx, RCU_ERR_INVALID, "bad tensor-parallel rank/world");
     if (!ctx || !cfg || !out) return set_err(ctx, RCU_ERR_INVALID, "null argument");
     *out = nullptr;
     const rcu_model_config &c = *cfg;
@@ -443,7 +576,24 @@ int32_t rcu_model_create(rcu_ctx *ctx, const rcu_model_config *cfg, rcu_model **
     if (!m) return RCU_ERR_OOM;
     m->ctx = ctx;
     m->cfg = c;
+    m->tp_rank = rank;
+    m->tp_world = world;
     *out = m;
+    return RCU_OK;
+}
+
+int32_t rcu_tp_shard(const rcu_model_config *cfg, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                     const void *host_bytes, int32_t rank, int32_t world, void *out, uint64_t out_cap,
+                     uint64_t *out_rows, uint64_t *out_cols) {
+    if (!cfg || !name || !out_rows || !out_cols || (out && !host_bytes)) return RCU_ERR_INVALID;
+    if (world < 1 || rank < 0 || rank >= world) return RCU_ERR_INVALID;
+    rcu_ctx scratch_ctx;  // error text only
+    std::vector<uint8_t> buf;
+    const int st = tp_shard(&scratch_ctx, *cfg, name, ggml_type, rows, cols, (const uint8_t *)host_bytes, rank, world,
+                            out ? &buf : nullptr, out_rows, out_cols);
+    if (st || !out) return st;
+    if (buf.size() > out_cap) return RCU_ERR_INVALID;
+    std::memcpy(out, buf.data(), buf.size());
     return RCU_OK;
 }
 
@@ -461,6 +611,14 @@ int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type,
     if (!m || !name || !host_bytes) return RCU_ERR_INVALID;
     rcu_ctx *ctx = m->ctx;
     const std::string n(name);
+    std::vector<uint8_t> shard;  // this rank's part of a tensor-parallel tensor
+    if (m->tp_world > 1 && tp_kind(n, m->cfg, rows) != TP_REPL) {
+        uint64_t r2 = 0, c2 = 0;
+        if (int st = tp_shard(ctx, m->cfg, n, ggml_type, rows, cols, (const uint8_t *)host_bytes, m->tp_rank,
+                              m->tp_world, &shard, &r2, &c2))
+            return st;
+        rows = r2, cols = c2, host_bytes = shard.data();
+    }
     if (rows == 1 && (ggml_type == T_F32 || ggml_type == T_F16 || ggml_type == T_BF16)) {
         std::vector<float> v(cols);
         for (uint64_t i = 0; i < cols; i++) {
@@ -505,14 +663,36 @@ int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type,
 }
 
 int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type, rcu_backend **out) {
+    return rcu_backend_create_tp(m, n_ctx, max_batch, kv_type, nullptr, out);
+}
+
+int32_t rcu_tp_unique_id(uint8_t *out, uint64_t cap) {
+    if (!out || cap < sizeof(ncclUniqueId)) return RCU_ERR_INVALID;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return RCU_ERR_RUNTIME;
+    std::memcpy(out, &id, sizeof(id));
+    return RCU_OK;
+}
+
+int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type, const uint8_t *uid,
+                              rcu_backend **out) {
     if (!m || !out) return RCU_ERR_INVALID;
     *out = nullptr;
     rcu_ctx *ctx = m->ctx;
-    const rcu_model_config &c = m->cfg;
+    const int P = m->tp_world;
+    if (P > 1 && !uid) return set_err(ctx, RCU_ERR_INVALID, "tensor-parallel backend needs the communicator id");
     if (n_ctx == 0) return set_err(ctx, RCU_ERR_INVALID, "n_ctx must be positive");
     if (kv_type < RCU_KV_F16 || kv_type > RCU_KV_TURBO4) return set_err(ctx, RCU_ERR_INVALID, "unknown kv type");
+    if (m->cfg.n_head % P || m->cfg.n_head_kv % P || m->cfg.n_ff % P || m->cfg.n_vocab % P)
+        return set_err(ctx, RCU_ERR_INVALID, "heads, KV heads, FFN rows and vocabulary must divide by the tensor-parallel degree");
     rcu_backend *b = new (std::nothrow) rcu_backend();
     if (!b) return RCU_ERR_OOM;
+    b->cfg = m->cfg;
+    b->cfg.n_head /= P;
+    b->cfg.n_head_kv /= P;
+    b->cfg.n_ff /= P;
+    b->cfg.n_vocab /= P;
+    const rcu_model_config &c = b->cfg;
     b->m = m;
     b->ctx = ctx;
     b->n_ctx = n_ctx;
@@ -535,7 +715,16 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
     b->embd = W("token_embd.weight");
     if (int st = need(b->embd && b->embd->cols == e, "token_embd.weight")) return fail(st);
     b->out = W("output.weight");
-    if (!b->out) b->out = b->embd;
+    if (!b->out) {  // tied head: this rank's vocabulary rows of the embedding
+        if (P > 1) {
+            rcu_weight *s = nullptr;
+            if (int st = rcu_weight_slice_rows(b->embd, (uint64_t)m->tp_rank * c.n_vocab, c.n_vocab, &s)) return fail(st);
+            m->slices.push_back(s);
+            b->out = s;
+        } else {
+            b->out = b->embd;
+        }
+    }
     if (int st = need(b->out->cols == e && b->out->rows >= c.n_vocab && gemv_supported(b->out->type), "output.weight"))
         return fail(st);
     if (b->out->rows > c.n_vocab) {
@@ -602,7 +791,9 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
         float **p;
         uint64_t n;
     } bufs[] = {{&b->x, T * e}, {&b->xn, T * e}, {&b->q, T * qd}, {&b->k, T * kvd}, {&b->v, T * kvd}, {&b->att, T * qd},
-                {&b->o, T * e}, {&b->g, T * b->ff_max}, {&b->u, T * b->ff_max}, {&b->logits, T * (uint64_t)c.n_vocab}};
+                {&b->o, T * e}, {&b->g, T * b->ff_max}, {&b->u, T * b->ff_max},
+                {&b->logits, T * (uint64_t)c.n_vocab * P}, {&b->logits_local, P > 1 ? T * (uint64_t)c.n_vocab : 1},
+                {&b->logits_gather, P > 1 ? T * (uint64_t)c.n_vocab * P : 1}};
     for (auto &bf : bufs)
         if (int st = dalloc(b, (void **)bf.p, bf.n * sizeof(float))) return fail(st);
     if (int st = dalloc(b, (void **)&b->tokens, T * sizeof(uint32_t))) return fail(st);
@@ -632,7 +823,20 @@ int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int
     };
     if (int st = freqs(c.rope_base, c.rope_freq_scale, &b->inv_freq)) return fail(st);
     if (int st = freqs(c.rope_base_swa > 0.0f ? c.rope_base_swa : c.rope_base, 1.0f, &b->inv_freq_swa)) return fail(st);
+    if (P > 1) {  // every rank of the model calls this with the same id
+        ncclUniqueId id;
+        std::memcpy(&id, uid, sizeof(id));
+        RCU_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+        const ncclResult_t r = ncclCommInitRank(&b->comm, P, id, m->tp_rank);
+        if (r != ncclSuccess) return fail(nccl_err(ctx, r, "ncclCommInitRank"));
+    }
     *out = b;
+    return RCU_OK;
+}
+
+int32_t rcu_backend_kv(rcu_backend *b, uint64_t layer, rcu_kv **out) {
+    if (!b || !out || layer >= b->kv.size()) return RCU_ERR_INVALID;
+    *out = b->kv[layer];
     return RCU_OK;
 }
 
@@ -642,6 +846,7 @@ void rcu_backend_free(rcu_backend *b) {
     if (b->stream) cudaStreamSynchronize(b->stream);
     if (b->graph_exec) cudaGraphExecDestroy(b->graph_exec);
     if (b->graph) cudaGraphDestroy(b->graph);
+    if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its collectives
     if (b->ev_in) cudaEventDestroy(b->ev_in);
     if (b->ev_out) cudaEventDestroy(b->ev_out);
     if (b->stream) cudaStreamDestroy(b->stream);
@@ -726,7 +931,7 @@ int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, 
     if (!b || !tokens || !logits) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
     if (int32_t st = check_forward(b, n, pos)) return st;
     const uint64_t rows = all_logits ? n : 1;
-    if (logits_len < rows * b->m->cfg.n_vocab) return set_err(b->ctx, RCU_ERR_RUNTIME, "logits buffer too small");
+    if (logits_len < rows * b->m->cfg.n_vocab) return set_err(b->ctx, RCU_ERR_RUNTIME, "logits buffer too small");  // full vocabulary
     for (uint64_t i = 0; i < n; i++)
         if (tokens[i] >= b->embd->rows) return set_err(b->ctx, RCU_ERR_RUNTIME, "token id " + std::to_string(tokens[i]) + " out of range");
     rcu_ctx *ctx = b->ctx;

@@ -137,12 +137,50 @@ def synthetic_tensors(spec: SyntheticSpec, weight, vec_f32, norm):
                 yield p + nm, t, rows, cols, weight(t, rows, cols)
 
 
+def tp_unique_id() -> bytes:
+    """Communicator id for a tensor-parallel backend: made on one rank, given to all."""
+    buf = (C.c_uint8 * 128)()
+    st = _lib.load().rcu_tp_unique_id(buf, 128)
+    if st:
+        raise _lib.RcuError(st, "rcu_tp_unique_id failed")
+    return bytes(buf)
+
+
+def tp_shard(cfg: ModelConfig, name: str, ty: int, rows: int, cols: int, data, rank: int, world: int):
+    """The part of a GGUF tensor that rank `rank` of a tensor-parallel model keeps (host-only):
+    (bytes as uint8, rows, cols)."""
+    a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    r, c = C.c_uint64(0), C.c_uint64(0)
+    lib = _lib.load()
+    st = lib.rcu_tp_shard(C.byref(cfg), name.encode(), int(ty), rows, cols, a.ctypes.data_as(C.c_void_p), rank, world,
+                          None, 0, C.byref(r), C.byref(c))
+    if st:
+        raise _lib.RcuError(st, f"rcu_tp_shard({name})")
+    out = np.zeros(a.size, dtype=np.uint8)  # a shard is never larger than the tensor
+    st = lib.rcu_tp_shard(C.byref(cfg), name.encode(), int(ty), rows, cols, a.ctypes.data_as(C.c_void_p), rank, world,
+                          out.ctypes.data_as(C.c_void_p), out.size, C.byref(r), C.byref(c))
+    if st:
+        raise _lib.RcuError(st, f"rcu_tp_shard({name})")
+    if rows == 1 and int(ty) in (0, 1, 30):  # 1-D f32 / f16 / bf16 vector
+        nbytes = c.value * (4 if int(ty) == 0 else 2)
+    else:
+        nbytes = r.value * rcu_row_bytes_host(ty, c.value)
+    return out[:nbytes], r.value, c.value
+
+
+def rcu_row_bytes_host(ty: int, cols: int) -> int:
+    return int(_lib.load().rcu_row_bytes(int(ty), cols))
+
+
 class Model:
-    def __init__(self, ctx, cfg: ModelConfig):
-        self.ctx, self.cfg = ctx, cfg
+    """Model::load without the file. With world > 1 the model holds rank `rank`'s shard of a
+    tensor-parallel split (set_tensor still takes the full tensors)."""
+
+    def __init__(self, ctx, cfg: ModelConfig, rank: int = 0, world: int = 1):
+        self.ctx, self.cfg, self.rank, self.world = ctx, cfg, rank, world
         lib = _lib.load()
         self.ptr = C.c_void_p()
-        _check(ctx.ptr, lib.rcu_model_create(ctx.ptr, C.byref(cfg), C.byref(self.ptr)))
+        _check(ctx.ptr, lib.rcu_model_create_tp(ctx.ptr, C.byref(cfg), rank, world, C.byref(self.ptr)))
 
     def set_tensor(self, name: str, ty: int, rows: int, cols: int, data) -> None:
         a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
@@ -164,11 +202,14 @@ class Model:
 class CudaBackend:
     """`impl Backend for CudaBackend`: forward / hidden / max_batch / n_ctx."""
 
-    def __init__(self, model: Model, n_ctx: int, max_batch: int, kv_type: KvType = KvType.F16):
+    def __init__(self, model: Model, n_ctx: int, max_batch: int, kv_type: KvType = KvType.F16,
+                 comm_id: bytes | None = None):
+        """comm_id: tp_unique_id() of rank 0, for a tensor-parallel model (every rank passes it)."""
         self.model, self.ctx = model, model.ctx
         self.ptr = C.c_void_p()
-        _check(self.ctx.ptr, _lib.load().rcu_backend_create(model.ptr, n_ctx, max_batch, int(kv_type),
-                                                            C.byref(self.ptr)))
+        uid = None if comm_id is None else (C.c_uint8 * len(comm_id)).from_buffer_copy(comm_id)
+        _check(self.ctx.ptr, _lib.load().rcu_backend_create_tp(model.ptr, n_ctx, max_batch, int(kv_type), uid,
+                                                               C.byref(self.ptr)))
         self.n_vocab = model.cfg.n_vocab
         self.n_embd = model.cfg.n_embd
 
@@ -193,6 +234,12 @@ class CudaBackend:
     def forward_device(self, tokens_dev, n: int, pos: int, logits_dev, all_logits: bool = False) -> None:
         _check(self.ctx.ptr, _lib.load().rcu_backend_forward_device(self.ptr, C.c_void_p(_dptr(tokens_dev)), n, pos,
                                                                     int(all_logits), C.c_void_p(_dptr(logits_dev))))
+
+    def kv_cache(self, layer: int):
+        """The rcu_kv handle of one layer's cache (owned by the backend)."""
+        kv = C.c_void_p()
+        _check(self.ctx.ptr, _lib.load().rcu_backend_kv(self.ptr, layer, C.byref(kv)))
+        return kv
 
     def hidden(self) -> np.ndarray | None:
         rows = C.c_uint64(0)
