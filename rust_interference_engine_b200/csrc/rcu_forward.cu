@@ -48,6 +48,15 @@ struct rcu_backend {
     rcu_model_config cfg{};  // this rank's dimensions (heads, FFN rows, vocab rows) under TP
     ncclComm_t comm = nullptr;  // tensor-parallel communicator (world > 1)
     float *logits_local = nullptr, *logits_gather = nullptr;
+    // fused all-reduce over NVLink (tensor parallel, batches of <= 8 tokens): receive buffer
+    // [2 slots][P ranks][max_batch][n_embd], arrival counters [2 per layer][P], the forward
+    // count, and the peers' buffers / counters mapped into this process (CUDA IPC)
+    bool ar_ok = false;
+    float *ar_buf = nullptr;
+    uint32_t *ar_flags = nullptr;
+    uint64_t *ar_epoch = nullptr;
+    float *ar_peer_buf[8] = {};
+    uint32_t *ar_peer_flags[8] = {};
     uint64_t n_ctx = 0, max_batch = 0;
     int kv_type = 0;
     std::vector<rcu::LayerW> layers;
@@ -199,11 +208,52 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 // that has completed before this one starts: three or more launches earlier), are loaded
 // before waiting for the previous kernel, which produced o.
 constexpr int kNormThreads = 1024;
+
+// Tensor parallel with the fused all-reduce: instead of o, the norm sums the P ranks' partial
+// rows that the row-parallel GEMVs pushed into this GPU's receive buffer (in rank order, so
+// every rank computes the same values), after every rank's arrival counter has reached
+// epoch * expect (each producer launch adds `expect` per forward).
+struct ArSum {
+    const float *src;       // [P][stride] receive buffer slot
+    const uint32_t *flag;   // [P] arrival counters of this all-reduce
+    const uint64_t *epoch;  // forwards run with the fused all-reduce, this one included
+    uint32_t expect, P, stride;
+    uint32_t *err;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits (thread 0, bounded) until every rank's partial rows have arrived.
+__device__ __forceinline__ void ar_wait(const ArSum &ar) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        const uint32_t target = (uint32_t)(*ar.epoch * ar.expect);
+        const uint64_t t0 = globaltimer_ns();
+        bool ok = true;
+        for (uint32_t q = 0; q < ar.P && ok; q++) {
+            while ((int32_t)(ld_acquire_sys(ar.flag + q) - target) < 0) {
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(ar.err, (uint32_t)ERR_TIMEOUT_PEER);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+}
+
 template <int NIT>
 __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, const float *__restrict__ o,
                                                          const float *__restrict__ post_w, float rs,
                                                          const float *__restrict__ w, uint32_t e, float eps,
-                                                         float *__restrict__ xn_f32, const ActOut ao, int x_ready) {
+                                                         float *__restrict__ xn_f32, const ActOut ao, int x_ready,
+                                                         const ArSum ar) {
     __shared__ float red[32];
     __shared__ Q8kShared sh;
     const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -225,13 +275,27 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
             v[j] = i < e ? xr[i] : 0.0f;
         }
     }
-    if (o) {
-        const float *orow = o + (uint64_t)t * e;
+    if (o || ar.P) {
         float ov[NIT];
+        if (ar.P) {
+            ar_wait(ar);
 #pragma unroll
-        for (int j = 0; j < NIT; j++) {
-            const uint32_t i = tid + kNormThreads * j;
-            ov[j] = i < e ? orow[i] : 0.0f;
+            for (int j = 0; j < NIT; j++) ov[j] = 0.0f;
+            for (uint32_t q = 0; q < ar.P; q++) {
+                const float *src = ar.src + (uint64_t)q * ar.stride + (uint64_t)t * e;
+#pragma unroll
+                for (int j = 0; j < NIT; j++) {
+                    const uint32_t i = tid + kNormThreads * j;
+                    if (i < e) ov[j] += __ldcg(src + i);
+                }
+            }
+        } else {
+            const float *orow = o + (uint64_t)t * e;
+#pragma unroll
+            for (int j = 0; j < NIT; j++) {
+                const uint32_t i = tid + kNormThreads * j;
+                ov[j] = i < e ? orow[i] : 0.0f;
+            }
         }
         if (post_w) {
             float ss = 0.0f;
@@ -295,10 +359,11 @@ __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, con
     }
 }
 
-__global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos) {
+__global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos, uint64_t *epoch) {
     pdl_wait();
     pdl_trigger();
     *pos_dev = pos;
+    if (epoch) *epoch += 1;  // a forward with the fused all-reduce starts
 }
 
 __global__ void k_logit_post(float *__restrict__ l, uint64_t n, float scale, float cap) {
@@ -338,7 +403,7 @@ static int matmul(rcu_backend *b, uint32_t n, uint32_t k, uint32_t fmt, std::vec
 
 // x (+)= post_norm(o) * rs; quantized RMSNorm(x) * w into b->acts (and f32 into xn_f32).
 static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const float *post_w, const float *w,
-                  float *xn_f32, uint32_t fmt, bool x_ready) {
+                  float *xn_f32, uint32_t fmt, bool x_ready, const ArSum &ar) {
     const rcu_model_config &c = b->cfg;
     const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
     const ActOut ao = acts_out(b, fmt);
@@ -346,7 +411,7 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
     auto kern = nit <= 1 ? k_norm_q<1> : nit <= 2 ? k_norm_q<2> : nit <= 4 ? k_norm_q<4> : nit <= 8 ? k_norm_q<8> : k_norm_q<16>;
     if (nit > 16) return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
     RCU_CUDA_TRY(b->ctx, launch_k(b->ctx, kern, dim3((uint32_t)n), dim3(kNormThreads), 0, x, o, post_w, rs, w, e, eps,
-                                  xn_f32, ao, x_ready ? 1 : 0));
+                                  xn_f32, ao, x_ready ? 1 : 0, ar));
     return RCU_OK;
 }
 
@@ -389,20 +454,52 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
     // [residual +] RMSNorm + quantize (its own kernel), then the matmuls that consume it.
     // x_ready: x was written three or more launches back (the norm kernel may load it early).
     auto norm_matmul = [&](uint64_t rows, uint64_t row0, const float *o, const float *post, const float *w,
-                           float *xn_f32, bool x_ready, std::vector<rcu_job> jobs) -> int {
+                           float *xn_f32, bool x_ready, const ArSum &ar, std::vector<rcu_job> jobs) -> int {
         uint32_t fmt = 0;
         for (auto &j : jobs) fmt |= act_format(j.w->type);
-        if (int st = norm_q(b, rows, b->x + row0 * e, o ? o + row0 * e : nullptr, post, w, xn_f32, fmt, x_ready))
+        ArSum a = ar;
+        if (a.P) a.src += row0 * e;
+        if (int st = norm_q(b, rows, b->x + row0 * e, o ? o + row0 * e : nullptr, post, w, xn_f32, fmt, x_ready, a))
             return st;
         return matmul(b, (uint32_t)rows, e, fmt, jobs);
     };
+    // Row-parallel matmul (Wo, down) of all-reduce number j. Fused (NVLink): the GEMV pushes
+    // this rank's partial rows into every rank's receive buffer and the next norm sums them;
+    // otherwise into b->o followed by an NCCL all-reduce.
+    const bool fused = P > 1 && b->ar_ok && n <= 8;
+    const int rank = b->m->tp_rank;
+    auto row_parallel = [&](const rcu_weight *w, uint32_t k, uint32_t j, ArSum *sum) -> int {
+        const uint32_t fmt = formats({w});
+        *sum = ArSum{};
+        if (!fused) {
+            if (int st = matmul(b, (uint32_t)n, k, fmt, {{w, b->o, e}})) return st;
+            return all_reduce(b->o, n * e);
+        }
+        const uint64_t stride = b->max_batch * e, slot = (uint64_t)(j & 1) * P * stride;
+        ArPush push{};
+        for (int q = 0; q < P; q++) {
+            if (q != rank) push.dst[push.n_dst++] = b->ar_peer_buf[q] + slot + rank * stride;
+            push.flag[push.n_flag++] = (q == rank ? b->ar_flags : b->ar_peer_flags[q]) + (uint64_t)j * P + rank;
+        }
+        ActsView a = b->acts->v;
+        a.n_tok = (uint32_t)n;
+        a.k = k;
+        a.have = fmt;
+        const HostJob hj{w, b->ar_buf + slot + rank * stride, e};
+        if (int st = launch_gemv(ctx, a, &hj, 1, 0, (uint32_t)n, &push)) return st;
+        *sum = ArSum{b->ar_buf + slot, b->ar_flags + (uint64_t)j * P, b->ar_epoch, kArUnit, (uint32_t)P,
+                     (uint32_t)stride, ctx->dev_err};
+        return RCU_OK;
+    };
     const float *pend_o = nullptr, *pend_post = nullptr;  // residual not yet added to x
+    ArSum pend_ar{};                                       // (or the ranks' partial rows)
+    uint32_t ar_j = 0;
     int st;
     for (uint32_t il = 0; il < c.n_layer; il++) {
         const LayerW &L = b->layers[il];
         // x comes from k_embed (the launch just before) in layer 0, else from this layer's
         // previous norm (four launches back)
-        if ((st = norm_matmul(n, 0, pend_o, pend_post, L.attn_norm, nullptr, il > 0,
+        if ((st = norm_matmul(n, 0, pend_o, pend_post, L.attn_norm, nullptr, il > 0, pend_ar,
                               {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}})))
             return st;
         const bool swa_rope = L.swa && c.rope_base_swa > 0.0f;
@@ -423,25 +520,24 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
             if (!st) st = launch_quantize(ctx, b->acts->v, b->att, (uint32_t)n, qd, fo);
         }
         if (st) return st;
-        if ((st = matmul(b, (uint32_t)n, qd, fo, {{L.wo, b->o, e}}))) return st;
-        if ((st = all_reduce(b->o, n * e))) return st;
+        ArSum ar_o;
+        if ((st = row_parallel(L.wo, qd, ar_j++, &ar_o))) return st;
         const uint32_t ff = (uint32_t)L.gate->rows;
-        if ((st = norm_matmul(n, 0, b->o, L.post_attn, L.ffn_norm, nullptr, true,
+        if ((st = norm_matmul(n, 0, fused ? nullptr : b->o, L.post_attn, L.ffn_norm, nullptr, true, ar_o,
                               {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
             return st;
         const uint32_t fd = formats({L.down});
         RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((ff + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, ff,
                                    c.act, acts_out(b, fd)));
-        if ((st = matmul(b, (uint32_t)n, ff, fd, {{L.down, b->o, e}}))) return st;
-        if ((st = all_reduce(b->o, n * e))) return st;
-        pend_o = b->o;
+        if ((st = row_parallel(L.down, ff, ar_j++, &pend_ar))) return st;
+        pend_o = fused ? nullptr : b->o;
         pend_post = L.post_ffn;
     }
     const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
     b->hidden_rows = m;
     // vocab-parallel head: each rank computes its rows of the vocabulary, then all-gather
     float *lg = P == 1 ? logits : b->logits_local;
-    if ((st = norm_matmul(m, first, pend_o, pend_post, b->out_norm, b->xn, true, {{b->out, lg, c.n_vocab}})))
+    if ((st = norm_matmul(m, first, pend_o, pend_post, b->out_norm, b->xn, true, pend_ar, {{b->out, lg, c.n_vocab}})))
         return st;
     const uint64_t vocab = (uint64_t)c.n_vocab * P;
     if (P > 1) {
@@ -549,6 +645,78 @@ static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &
             return RCU_OK;
         }
     }
+}
+
+
+// Receive buffer, arrival counters and forward count for the fused all-reduce, exported to
+// the other ranks with CUDA IPC (handles exchanged through the communicator). If peer
+// mappings are not available the backend keeps using NCCL (ar_ok stays false).
+static int setup_fused_all_reduce(rcu_backend *b) {
+    rcu_ctx *ctx = b->ctx;
+    const int P = b->m->tp_world, rank = b->m->tp_rank;
+    // Opt-in (RIE_TP_FUSED=1): at 2 GPUs on the 8B shape it measured no faster than NCCL,
+    // because its one-float remote stores are scattered (see the GEMV push).
+    const char *v = std::getenv("RIE_TP_FUSED");
+    if (P > 8 || !v || std::strcmp(v, "1") != 0) return RCU_OK;
+    const uint64_t stride = b->max_batch * b->cfg.n_embd;
+    const uint64_t nflag = std::max<uint64_t>(2ull * b->cfg.n_layer * P, 64);
+    RCU_CUDA_TRY(ctx, cudaMalloc(&b->ar_buf, 2 * P * stride * sizeof(float)));
+    RCU_CUDA_TRY(ctx, cudaMemset(b->ar_buf, 0, 2 * P * stride * sizeof(float)));
+    RCU_CUDA_TRY(ctx, cudaMalloc(&b->ar_flags, nflag * sizeof(uint32_t)));
+    RCU_CUDA_TRY(ctx, cudaMemset(b->ar_flags, 0, nflag * sizeof(uint32_t)));
+    if (int st = dalloc(b, (void **)&b->ar_epoch, sizeof(uint64_t))) return st;
+    RCU_CUDA_TRY(ctx, cudaMemset(b->ar_epoch, 0, sizeof(uint64_t)));
+    cudaIpcMemHandle_t mine[2];
+    RCU_CUDA_TRY(ctx, cudaIpcGetMemHandle(&mine[0], b->ar_buf));
+    RCU_CUDA_TRY(ctx, cudaIpcGetMemHandle(&mine[1], b->ar_flags));
+    uint8_t *dh = nullptr;
+    const size_t hb = sizeof(mine);
+    if (int st = dalloc(b, (void **)&dh, P * hb)) return st;
+    RCU_CUDA_TRY(ctx, cudaMemcpy(dh + rank * hb, mine, hb, cudaMemcpyHostToDevice));
+    const ncclResult_t r = ncclAllGather(dh + rank * hb, dh, hb, ncclUint8, b->comm, b->stream);
+    if (r != ncclSuccess) return nccl_err(ctx, r, "ncclAllGather(ipc handles)");
+    RCU_CUDA_TRY(ctx, cudaStreamSynchronize(b->stream));
+    std::vector<cudaIpcMemHandle_t> all(2 * P);
+    RCU_CUDA_TRY(ctx, cudaMemcpy(all.data(), dh, P * hb, cudaMemcpyDeviceToHost));
+    bool mapped = true;
+    for (int q = 0; q < P && mapped; q++) {
+        if (q == rank) {
+            b->ar_peer_buf[q] = b->ar_buf;
+            b->ar_peer_flags[q] = b->ar_flags;
+            continue;
+        }
+        void *pb = nullptr, *pf = nullptr;
+        cudaError_t e1 = cudaIpcOpenMemHandle(&pb, all[2 * q], cudaIpcMemLazyEnablePeerAccess);
+        cudaError_t e2 = e1 == cudaSuccess ? cudaIpcOpenMemHandle(&pf, all[2 * q + 1], cudaIpcMemLazyEnablePeerAccess) : e1;
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            cudaGetLastError();
+            if (pb) cudaIpcCloseMemHandle(pb);
+            mapped = false;
+            break;
+        }
+        b->ar_peer_buf[q] = (float *)pb;
+        b->ar_peer_flags[q] = (uint32_t *)pf;
+    }
+    if (!mapped) {  // no peer mapping here: this backend keeps NCCL (and so do the others)
+        for (int q = 0; q < P; q++)
+            if (q != rank && b->ar_peer_buf[q]) {
+                cudaIpcCloseMemHandle(b->ar_peer_buf[q]);
+                cudaIpcCloseMemHandle(b->ar_peer_flags[q]);
+            }
+        std::fill(b->ar_peer_buf, b->ar_peer_buf + 8, nullptr);
+        std::fill(b->ar_peer_flags, b->ar_peer_flags + 8, nullptr);
+    }
+    // every rank must agree: a rank without mappings would skip the pushes the others wait for
+    int ok_here = mapped ? 1 : 0, *dok = nullptr;
+    if (int st = dalloc(b, (void **)&dok, sizeof(int))) return st;
+    RCU_CUDA_TRY(ctx, cudaMemcpy(dok, &ok_here, sizeof(int), cudaMemcpyHostToDevice));
+    const ncclResult_t r2 = ncclAllReduce(dok, dok, 1, ncclInt32, ncclMin, b->comm, b->stream);
+    if (r2 != ncclSuccess) return nccl_err(ctx, r2, "ncclAllReduce(fused all-reduce agreement)");
+    RCU_CUDA_TRY(ctx, cudaStreamSynchronize(b->stream));
+    int ok_all = 0;
+    RCU_CUDA_TRY(ctx, cudaMemcpy(&ok_all, dok, sizeof(int), cudaMemcpyDeviceToHost));
+    b->ar_ok = ok_all == 1;
+    return RCU_OK;
 }
 
 }  // namespace rcu
@@ -829,6 +997,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
         RCU_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
         const ncclResult_t r = ncclCommInitRank(&b->comm, P, id, m->tp_rank);
         if (r != ncclSuccess) return fail(nccl_err(ctx, r, "ncclCommInitRank"));
+        if (int st = setup_fused_all_reduce(b)) return fail(st);
     }
     *out = b;
     return RCU_OK;
@@ -846,6 +1015,14 @@ void rcu_backend_free(rcu_backend *b) {
     if (b->stream) cudaStreamSynchronize(b->stream);
     if (b->graph_exec) cudaGraphExecDestroy(b->graph_exec);
     if (b->graph) cudaGraphDestroy(b->graph);
+    for (int q = 0; q < 8; q++)
+        if (b->ar_peer_buf[q] && b->ar_peer_buf[q] != b->ar_buf) {
+            cudaIpcCloseMemHandle(b->ar_peer_buf[q]);
+            cudaIpcCloseMemHandle(b->ar_peer_flags[q]);
+        }
+    // b->ar_buf / b->ar_flags stay allocated until the process exits: memory exported over
+    // IPC may only be released after every importing rank has closed it, and free() cannot
+    // synchronise with the other ranks.
     if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its collectives
     if (b->ev_in) cudaEventDestroy(b->ev_in);
     if (b->ev_out) cudaEventDestroy(b->ev_out);
@@ -892,7 +1069,9 @@ static int32_t run_forward(rcu_backend *b, const uint32_t *tokens, bool tokens_o
     } restore{ctx, caller};
     const cudaMemcpyKind kind = tokens_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
     if (tokens != b->tokens) RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->tokens, tokens, n * 4, kind, b->stream));
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_set_pos), dim3(1), dim3(1), 0, b->pos_dev, pos));  // by value: no host buffer to keep alive
+    const bool fused_ar = b->m->tp_world > 1 && b->ar_ok && n <= 8;  // must match forward_dev's choice
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_set_pos), dim3(1), dim3(1), 0, b->pos_dev, pos,
+                               fused_ar ? b->ar_epoch : (uint64_t *)nullptr));  // by value: no host buffer to keep alive
     const bool decode = n == 1 && !all_logits && logits == b->logits;
     if (decode && b->use_graphs && b->graph_exec) {
         RCU_CUDA_TRY(ctx, cudaGraphLaunch(b->graph_exec, b->stream));

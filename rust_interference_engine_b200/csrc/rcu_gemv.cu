@@ -30,6 +30,7 @@ constexpr int kMaxTok = 8;
 constexpr int kMaxStages = 8;
 constexpr int kMaxRw = 2;  // weight rows per warp per tile
 constexpr uint32_t kHdrBytes = 6144;  // barriers + reduction scratch
+constexpr int kMaxPeers = 8;
 
 struct GemvJobDev {
     const uint8_t *w;
@@ -50,6 +51,12 @@ struct GemvParams {
     uint32_t o_q0, o_d0, o_s0, o_sum0, o_qk, o_dk, o_bsk;
     ActsView acts;
     uint32_t *err;
+    // Fused all-reduce push (tensor parallel, one job): every output value is also stored
+    // to ar_dst[q][t * ld + row] (peer GPUs' receive buffers, NVLink), and each CTA adds to
+    // ar_flag[q] (every rank, itself included) once its rows are written, kArUnit per launch.
+    float *ar_dst[kMaxPeers];
+    uint32_t *ar_flag[kMaxPeers];
+    uint32_t ar_ndst, ar_nflag;
 };
 
 struct SmemHdr {
@@ -66,18 +73,27 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Output store of token t, row `row`: the job's own buffer, plus the peers' receive
+// buffers when the launch pushes an all-reduce.
+__device__ __forceinline__ void store_out(const GemvParams &p, const GemvJobDev &jb, uint32_t t, uint32_t row,
+                                          float v) {
+    const uint64_t at = (uint64_t)t * jb.ld + row;
+    jb.out[at] = v;
+    for (uint32_t q = 0; q < p.ar_ndst; q++) p.ar_dst[q][at] = v;
+}
+
 // Publish one warp's finished row sums v[t] (valid in every lane). With wpr > 1 the last
 // of the row's warps to arrive adds the parts in order 0..wpr-1 and stores the row.
 template <int T>
-__device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb, uint32_t row, int row_in_tile,
-                                         int part, const float (&v)[T], int lane) {
+__device__ __forceinline__ void emit_row(const GemvParams &p, SmemHdr *h, int s, const GemvJobDev &jb, uint32_t row,
+                                         int row_in_tile, int part, const float (&v)[T], int lane) {
     if (jb.wpr == 1) {
         if (lane < T) {
             float x = v[0];
 #pragma unroll
             for (int t = 1; t < T; t++)
                 if (lane == t) x = v[t];
-            jb.out[(uint64_t)lane * jb.ld + row] = x;
+            store_out(p, jb, lane, row, x);
         }
         return;
     }
@@ -98,7 +114,7 @@ __device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb
         if (lane < T) {
             float acc = 0.0f;
             for (uint32_t q = 0; q < jb.wpr; q++) acc += *((volatile float *)&h->red[s][row_in_tile * jb.wpr + q][lane]);
-            jb.out[(uint64_t)lane * jb.ld + row] = acc;
+            store_out(p, jb, lane, row, acc);
         }
         __syncwarp();
         if (lane == 0) h->cnt[s][row_in_tile] = 0;
@@ -108,8 +124,9 @@ __device__ __forceinline__ void emit_row(SmemHdr *h, int s, const GemvJobDev &jb
 // Reduce each row's per-lane partials over the warp and store the rows. Two rows share the
 // first butterfly stage (lanes 0-15 end with row 0, lanes 16-31 with row 1).
 template <int T>
-__device__ __forceinline__ void finish_rows(SmemHdr *h, int s, const GemvJobDev &jb, uint32_t r0, uint32_t row_first,
-                                            uint32_t nr, int part, float (&acc)[kMaxRw][T], int lane) {
+__device__ __forceinline__ void finish_rows(const GemvParams &p, SmemHdr *h, int s, const GemvJobDev &jb, uint32_t r0,
+                                            uint32_t row_first, uint32_t nr, int part, float (&acc)[kMaxRw][T],
+                                            int lane) {
     if (kMaxRw == 2 && nr == 2 && jb.wpr == 1) {
         const bool up = lane & 16;
         float v[T];
@@ -128,7 +145,7 @@ __device__ __forceinline__ void finish_rows(SmemHdr *h, int s, const GemvJobDev 
 #pragma unroll
             for (int t = 1; t < T; t++)
                 if (tl == t) x = v[t];
-            jb.out[(uint64_t)tl * jb.ld + r0 + row_first + (up ? 1 : 0)] = x;
+            store_out(p, jb, tl, r0 + row_first + (up ? 1 : 0), x);
         }
         return;
     }
@@ -138,7 +155,7 @@ __device__ __forceinline__ void finish_rows(SmemHdr *h, int s, const GemvJobDev 
             float v[T];
 #pragma unroll
             for (int t = 0; t < T; t++) v[t] = warp_sum(acc[r][t]);
-            emit_row<T>(h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
+            emit_row<T>(p, h, s, jb, r0 + row_first + r, row_first + r, part, v, lane);
         }
     }
 }
@@ -204,7 +221,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
             }
         }
     }
-    finish_rows<T>(h, s, jb, r0, row_first, nr, part, acc, lane);
+    finish_rows<T>(p, h, s, jb, r0, row_first, nr, part, acc, lane);
 }
 
 // ---- 256-value superblock types: 4 groups of 8 lanes per warp, a superblock per group -----
@@ -300,7 +317,7 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
             }
         }
     }
-    finish_rows<T>(h, s, jb, r0, row_first, nr, part, acc, lane);
+    finish_rows<T>(p, h, s, jb, r0, row_first, nr, part, acc, lane);
 }
 
 template <int T, int NW>
@@ -409,6 +426,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
             ph ^= 1u;
         }
     }
+    if (p.ar_nflag) {  // this CTA's rows are in every receive buffer: count it in
+        __threadfence_system();
+        named_bar_sync(1, NW * 32);
+        // every launch adds exactly kArUnit to each counter, whatever its grid: CTA 0 adds
+        // kArUnit - (grid - 1), the others 1
+        const uint32_t add = blockIdx.x == 0 ? kArUnit - (gridDim.x - 1) : 1u;
+        if (threadIdx.x == 0)
+            for (uint32_t q = 0; q < p.ar_nflag; q++) atomicAdd_system(p.ar_flag[q], add);
+    }
 }
 
 // ---- exact per-block integer sums of one (row, token) pair (validation path) ----------
@@ -508,10 +534,19 @@ static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t g
     return RCU_OK;
 }
 
-int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok) {
+int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok,
+                const ArPush *push) {
     if (n_jobs < 1 || n_jobs > kMaxJobs) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..96 jobs per launch");
     if (n_tok < 1 || n_tok > kMaxTok) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..8 tokens per launch");
     GemvParams p{};
+    if (push) {
+        if (n_jobs != 1 || tok0 != 0 || push->n_dst > kMaxPeers || push->n_flag > kMaxPeers)
+            return set_err(ctx, RCU_ERR_INVALID, "gemv: all-reduce push needs one job, one launch, <= 8 ranks");
+        p.ar_ndst = push->n_dst;
+        p.ar_nflag = push->n_flag;
+        for (uint32_t q = 0; q < push->n_dst; q++) p.ar_dst[q] = push->dst[q];
+        for (uint32_t q = 0; q < push->n_flag; q++) p.ar_flag[q] = push->flag[q];
+    }
     p.n_jobs = n_jobs;
     p.k = a.k;
     p.n_tok = n_tok;
@@ -576,6 +611,7 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     p.stages = std::min<uint32_t>(kMaxStages, (budget - p.stage_off) / stage_bytes);
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
+    if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
     switch (n_tok) {
         case 1: return launch_t<1, 16>(ctx, p, smem_bytes, grid);
         case 2: return launch_t<2, 16>(ctx, p, smem_bytes, grid);

@@ -58,7 +58,13 @@ inline bool gemv_supported(int t) {
 }
 
 // Device-side error bits (written with atomicOr into rcu_ctx::dev_err).
-enum : uint32_t { ERR_TIMEOUT_FULL = 1u, ERR_TIMEOUT_EMPTY = 2u, ERR_TIMEOUT_DRAIN = 4u, ERR_BAD_ARG = 8u };
+enum : uint32_t {
+    ERR_TIMEOUT_FULL = 1u,
+    ERR_TIMEOUT_EMPTY = 2u,
+    ERR_TIMEOUT_DRAIN = 4u,
+    ERR_BAD_ARG = 8u,
+    ERR_TIMEOUT_PEER = 16u  // a tensor-parallel peer's partial rows did not arrive in time
+};
 
 // Quantized activations in HBM, structure-of-arrays (the reference's BlockQ8_0 /
 // BlockQ8K hold the same fields per block; rcu_acts_export writes that layout).

@@ -13,7 +13,17 @@ struct HostJob {
 };
 // Decode GEMV over up to kGemvMaxJobs jobs sharing one activation batch (n_tok <= 8).
 constexpr int kGemvMaxJobs = 96;
-int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok);
+// Fused all-reduce push of a one-job GEMV (tensor parallel): outputs also go to dst[q] (the
+// peers' receive buffers, same [t][ld] layout) and, once all its CTAs have written their
+// rows, the launch has added exactly kArUnit to each flag[q].
+constexpr uint32_t kArUnit = 4096;
+struct ArPush {
+    float *dst[8];
+    uint32_t *flag[8];
+    uint32_t n_dst, n_flag;
+};
+int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok,
+                const ArPush *push = nullptr);
 // Int8 tensor-core GEMM (n_tok > 8). Returns RCU_ERR_UNSUPPORTED for types it lacks.
 int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs);
 // Exact per-block integer sums of one (row, token) pair.

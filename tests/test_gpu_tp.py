@@ -34,7 +34,9 @@ def _tensors(spec):
 PROMPT = [5, 17, 200, 3, 99, 42]
 
 
-def _rank(rank, world, q_uid, q_out, kv_type):
+def _rank(rank, world, q_uid, q_out, kv_type, fused):
+    import os
+    os.environ["RIE_TP_FUSED"] = "1" if fused else "0"
     import torch
     torch.cuda.set_device(rank)
     import rust_interference_engine_b200 as rie
@@ -61,20 +63,26 @@ def _rank(rank, world, q_uid, q_out, kv_type):
     m.free()
 
 
-@pytest.mark.parametrize("kv_type", [0, 2])
-def test_tp2_forward_matches_oracle(kv_type):
+@pytest.mark.parametrize("kv_type,fused", [(0, False), (2, False), (0, True)])
+def test_tp2_forward_matches_oracle(kv_type, fused):
+    """fused: the all-reduce pushed over NVLink by the GEMVs instead of NCCL."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q_uid, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, q_uid, q_out, kv_type)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, q_uid, q_out, kv_type, fused)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q_out.get(timeout=600) for _ in procs)
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        res = dict(q_out.get(timeout=300) for _ in procs)
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
     spec = _spec()
     cfg = spec.config()
     om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(cfg)))
