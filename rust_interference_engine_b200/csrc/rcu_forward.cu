@@ -29,6 +29,11 @@ struct LayerW {
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
     const float *bq = nullptr, *bk = nullptr, *bv = nullptr, *post_attn = nullptr, *post_ffn = nullptr;
     bool swa = false;
+    // mixture of experts (model/mod.rs:147-180): F32 router [n_expert][n_embd], experts
+    // stacked [expert][rows][cols], optional shared expert with an F32 gate vector
+    const rcu_weight *router = nullptr, *gate_exps = nullptr, *up_exps = nullptr, *down_exps = nullptr;
+    const rcu_weight *gate_sh = nullptr, *up_sh = nullptr, *down_sh = nullptr;
+    const float *sh_gate = nullptr;
 };
 
 }  // namespace rcu
@@ -51,6 +56,12 @@ struct rcu_backend {
     // fused all-reduce over NVLink (tensor parallel, batches of <= 8 tokens): receive buffer
     // [2 slots][P ranks][max_batch][n_embd], arrival counters [2 per layer][P], the forward
     // count, and the peers' buffers / counters mapped into this process (CUDA IPC)
+    // mixture-of-experts scratch: router logits, shared-expert gates, chosen experts and
+    // their weights per token, expert hidden rows and outputs, second activation batch
+    float *moe_logits = nullptr, *moe_sgate = nullptr, *moe_w = nullptr, *moe_g = nullptr, *moe_u = nullptr;
+    float *moe_y = nullptr, *moe_ys = nullptr;
+    uint32_t *moe_sel = nullptr;
+    rcu_acts *acts2 = nullptr;
     bool ar_ok = false;
     float *ar_buf = nullptr;
     uint32_t *ar_flags = nullptr;
@@ -359,6 +370,120 @@ __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, con
     }
 }
 
+// ---- mixture of experts (model/cpu.rs:469-524) ---------------------------------------------
+// Router logits l[t][x] = R[x] . xn[t] over the f32 normed rows (F32 router, dot in f32), and
+// the shared expert's gate sigmoid(g . xn[t]) as an extra row. One warp per (token, row).
+__global__ void k_router(const float *__restrict__ R, const float *__restrict__ gs, const float *__restrict__ xn,
+                         uint32_t n, uint32_t ne, uint32_t e, float *__restrict__ logits, float *__restrict__ sgate) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t per = ne + (gs ? 1 : 0), lane = threadIdx.x & 31;
+    const uint64_t item = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (item >= (uint64_t)n * per) return;
+    const uint32_t t = (uint32_t)(item / per), x = (uint32_t)(item % per);
+    const float *row = x < ne ? R + (uint64_t)x * e : gs, *v = xn + (uint64_t)t * e;
+    float acc = 0.0f;
+    for (uint32_t i = lane; i < e; i += 32) acc = fmaf(row[i], v[i], acc);
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+        if (x < ne)
+            logits[(uint64_t)t * ne + x] = acc;
+        else
+            sgate[t] = 1.0f / (1.0f + expf(-acc));
+    }
+}
+
+// Softmax over the router logits, top-k by (probability desc, index asc), weights
+// p / sum(top-k p) (norm_topk), p, or 1 (unit weights). The k choices are written in
+// increasing expert id, the order in which the reference adds the experts' outputs.
+// One warp per token; ne <= 256.
+__global__ void k_moe_route(const float *__restrict__ logits, uint32_t n, uint32_t ne, uint32_t k, int norm_topk,
+                            int unit, uint32_t *__restrict__ sel, float *__restrict__ wsel) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t t = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (t >= n) return;
+    const float *l = logits + t * ne;
+    float p[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const uint32_t i = lane + 32 * j;
+        p[j] = i < ne ? l[i] : -INFINITY;
+        mx = fmaxf(mx, p[j]);
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        p[j] = p[j] == -INFINITY ? 0.0f : expf(p[j] - mx);
+        sum += p[j];
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int j = 0; j < 8; j++) p[j] *= inv;
+    uint32_t ids[16];
+    float ps[16];
+    float norm = 0.0f;
+    for (uint32_t r = 0; r < k; r++) {
+        unsigned long long key = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t i = lane + 32 * j;
+            if (i < ne && p[j] >= 0.0f) {
+                const unsigned long long kk = ((unsigned long long)__float_as_uint(p[j]) << 32) | (0xffffffffu - i);
+                key = kk > key ? kk : key;
+            }
+        }
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other > key ? other : key;
+        }
+        const uint32_t win = 0xffffffffu - (uint32_t)(key & 0xffffffffu);
+        const float pw = __uint_as_float((uint32_t)(key >> 32));
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (lane + 32 * j == win) p[j] = -1.0f;  // taken
+        ids[r] = win;
+        ps[r] = pw;
+        norm += pw;  // in probability order, as the reference sums the sorted top-k
+    }
+    if (lane == 0) {
+        if (!norm_topk) norm = 1.0f;
+        // insertion order by expert id
+        for (uint32_t r = 0; r < k; r++) {
+            uint32_t best = r;
+            for (uint32_t q = r + 1; q < k; q++)
+                if (ids[q] < ids[best]) best = q;
+            const uint32_t ti = ids[r];
+            ids[r] = ids[best];
+            ids[best] = ti;
+            const float tp = ps[r];
+            ps[r] = ps[best];
+            ps[best] = tp;
+            sel[t * k + r] = ids[r];
+            wsel[t * k + r] = unit ? 1.0f : ps[r] / norm;
+        }
+    }
+}
+
+// out[t] = sum_j w[t][j] * y[t*k + j] (experts in id order) [+ sgate[t] * ys[t]].
+__global__ void k_moe_combine(const float *__restrict__ y, const float *__restrict__ wsel, const float *__restrict__ ys,
+                              const float *__restrict__ sgate, uint32_t n, uint32_t k, uint32_t e,
+                              float *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n * e) return;
+    const uint64_t t = i / e, c = i % e;
+    float o = 0.0f;
+    for (uint32_t j = 0; j < k; j++) o += wsel[t * k + j] * y[(t * k + j) * e + c];
+    if (ys) o += (sgate ? sgate[t] : 1.0f) * ys[t * e + c];
+    out[i] = o;
+}
+
 __global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos, uint64_t *epoch) {
     pdl_wait();
     pdl_trigger();
@@ -435,6 +560,82 @@ __global__ void k_unshard_cols(const float *__restrict__ src, float *__restrict_
         const uint64_t c = i % cols, r = (i / cols) % rows, p = i / ((uint64_t)cols * rows);
         dst[r * (uint64_t)P * cols + p * cols + c] = src[i];
     }
+}
+
+// Mixture-of-experts FFN of one layer (model/cpu.rs:469-524) for n tokens: residual + norm
+// (f32 rows for the router and quantized rows for the experts), router logits, softmax /
+// top-k on the device, the shared expert, then the chosen experts as GEMVs whose weights
+// and activation rows come from the routing (graph-capturable), 8 tokens at a time; the
+// weighted sum lands in b->o.
+static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_attn, const ArSum &ar_o) {
+    rcu_ctx *ctx = b->ctx;
+    const rcu_model_config &c = b->cfg;
+    const uint32_t e = c.n_embd, ne = (uint32_t)L.router->rows, fx = c.n_ff_exp;
+    const uint32_t k = std::min<uint32_t>(std::max<uint32_t>(c.n_expert_used, 1), ne);
+    const uint32_t fx_in = formats({L.gate_exps, L.up_exps}) | (L.gate_sh ? formats({L.gate_sh, L.up_sh}) : 0);
+    if (int st = norm_q(b, n, b->x, o_attn, L.post_attn, L.ffn_norm, b->xn, fx_in, true, ar_o)) return st;
+    const uint32_t per = ne + (L.sh_gate ? 1 : 0);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_router), dim3((uint32_t)((n * per + 7) / 8)), dim3(256), 0,
+                               (const float *)L.router->data, L.sh_gate, (const float *)b->xn, (uint32_t)n, ne, e,
+                               b->moe_logits, b->moe_sgate));
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_route), dim3((uint32_t)((n + 7) / 8)), dim3(256), 0,
+                               (const float *)b->moe_logits, (uint32_t)n, ne, k, c.expert_norm_topk,
+                               c.expert_unit_weights, b->moe_sel, b->moe_w));
+    auto view = [&](rcu_acts *a, uint32_t rows, uint32_t kk, uint32_t fmt) {
+        ActsView v = a->v;
+        v.n_tok = rows;
+        v.k = kk;
+        v.have = fmt;
+        return v;
+    };
+    // shared expert first: it reads the norm's activations, its GLU goes to the second batch
+    if (L.gate_sh) {
+        const uint32_t fs = (uint32_t)L.gate_sh->rows, fsd = formats({L.down_sh});
+        if (int st = matmul(b, (uint32_t)n, e, fx_in, {{L.gate_sh, b->g, fs}, {L.up_sh, b->u, fs}})) return st;
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fs + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, fs,
+                                   c.act, act_out(b->acts2->v, fsd, ctx->rounding)));
+        const HostJob dj{L.down_sh, b->moe_ys, e};
+        for (uint32_t t0 = 0; t0 < n; t0 += 8)
+            if (int st = launch_gemv(ctx, view(b->acts2, (uint32_t)n, fs, fsd), &dj, 1, t0,
+                                     std::min<uint32_t>(8, (uint32_t)n - t0)))
+                return st;
+    }
+    const uint64_t rb_g = L.gate_exps->row_bytes, rb_u = L.up_exps->row_bytes, rb_d = L.down_exps->row_bytes;
+    const uint32_t fdn = formats({L.down_exps});
+    for (uint32_t c0 = 0; c0 < n; c0 += 8) {
+        const uint32_t nt = std::min<uint32_t>(8, (uint32_t)n - c0);
+        std::vector<HostJob> gu, dn;
+        for (uint32_t t = 0; t < nt; t++)
+            for (uint32_t j = 0; j < k; j++) {
+                const uint32_t idx = (c0 + t) * k + j;
+                HostJob g{L.gate_exps, b->moe_g + (uint64_t)idx * fx, fx};
+                g.sel = b->moe_sel + idx, g.w_stride = (uint64_t)fx * rb_g, g.rows = fx, g.tok = t;
+                HostJob u{L.up_exps, b->moe_u + (uint64_t)idx * fx, fx};
+                u.sel = b->moe_sel + idx, u.w_stride = (uint64_t)fx * rb_u, u.rows = fx, u.tok = t;
+                gu.push_back(g);
+                gu.push_back(u);
+                HostJob d{L.down_exps, b->moe_y + (uint64_t)idx * e, e};
+                d.sel = b->moe_sel + idx, d.w_stride = (uint64_t)e * rb_d, d.rows = e, d.tok = t * k + j;
+                dn.push_back(d);
+            }
+        for (size_t j0 = 0; j0 < gu.size(); j0 += kGemvMaxJobs)
+            if (int st = launch_gemv(ctx, view(b->acts, (uint32_t)n, e, fx_in), gu.data() + j0,
+                                     (int)std::min<size_t>(kGemvMaxJobs, gu.size() - j0), c0, 1))
+                return st;
+        const uint64_t r0 = (uint64_t)c0 * k;
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, nt * k), dim3(1024), 0, b->moe_g + r0 * fx,
+                                   b->moe_u + r0 * fx, fx, c.act, act_out(b->acts2->v, fdn, ctx->rounding)));
+        for (size_t j0 = 0; j0 < dn.size(); j0 += kGemvMaxJobs)
+            if (int st = launch_gemv(ctx, view(b->acts2, nt * k, fx, fdn), dn.data() + j0,
+                                     (int)std::min<size_t>(kGemvMaxJobs, dn.size() - j0), 0, 1))
+                return st;
+    }
+    const uint64_t tot = n * e;
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_combine), dim3((uint32_t)((tot + 255) / 256)), dim3(256), 0,
+                               (const float *)b->moe_y, (const float *)b->moe_w,
+                               L.gate_sh ? (const float *)b->moe_ys : (const float *)nullptr,
+                               L.sh_gate ? (const float *)b->moe_sgate : (const float *)nullptr, (uint32_t)n, k, e, b->o));
+    return RCU_OK;
 }
 
 static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
@@ -522,6 +723,13 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         if (st) return st;
         ArSum ar_o;
         if ((st = row_parallel(L.wo, qd, ar_j++, &ar_o))) return st;
+        if (L.router) {
+            if ((st = moe_ffn(b, L, n, fused ? nullptr : b->o, ar_o))) return st;
+            pend_o = b->o;
+            pend_ar = ArSum{};
+            pend_post = L.post_ffn;
+            continue;
+        }
         const uint32_t ff = (uint32_t)L.gate->rows;
         if ((st = norm_matmul(n, 0, fused ? nullptr : b->o, L.post_attn, L.ffn_norm, nullptr, true, ar_o,
                               {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
@@ -739,7 +947,6 @@ int32_t rcu_model_create_tp(rcu_ctx *ctx, const rcu_model_config *cfg, int32_t r
     if (c.n_head % c.n_head_kv) return set_err(ctx, RCU_ERR_INVALID, "n_head not divisible by n_head_kv");
     if (c.rope_dim > c.head_dim || c.rope_dim % 2) return set_err(ctx, RCU_ERR_INVALID, "invalid rope dimension");
     if (c.head_dim > 256 || c.head_dim % 32) return set_err(ctx, RCU_ERR_UNSUPPORTED, "head_dim must be a multiple of 32, <= 256");
-    if (c.n_expert) return set_err(ctx, RCU_ERR_UNSUPPORTED, "mixture-of-experts layers are not supported by this backend yet");
     rcu_model *m = new (std::nothrow) rcu_model();
     if (!m) return RCU_ERR_OOM;
     m->ctx = ctx;
@@ -920,10 +1127,11 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
             L.wq = W(p + "attn_q.weight"), L.wk = W(p + "attn_k.weight"), L.wv = W(p + "attn_v.weight");
         }
         L.wo = W(p + "attn_output.weight");
+        L.router = W(p + "ffn_gate_inp.weight");
         L.gate = W(p + "ffn_gate.weight");
         L.up = W(p + "ffn_up.weight");
         L.down = W(p + "ffn_down.weight");
-        if (!L.gate && L.up && L.up->rows == 2ull * c.n_ff) {
+        if (!L.router && !L.gate && L.up && L.up->rows == 2ull * c.n_ff) {
             rcu_weight *g = nullptr, *u = nullptr;
             if (int st = rcu_weight_slice_rows(L.up, 0, c.n_ff, &g)) return fail(st);
             m->slices.push_back(g);
@@ -931,10 +1139,37 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
             m->slices.push_back(u);
             L.gate = g, L.up = u;
         }
+        if (L.router) {  // mixture of experts (model/mod.rs:147-180)
+            const uint64_t ne = c.n_expert, fx = c.n_ff_exp;
+            if (P > 1) return fail(set_err(ctx, RCU_ERR_UNSUPPORTED, "mixture-of-experts layers with tensor parallelism"));
+            if (int st = need(L.router->type == T_F32 && L.router->rows == ne && L.router->cols == e && ne <= 256 &&
+                                  c.n_expert_used <= 16 && fx > 0,
+                              p + "ffn_gate_inp.weight"))
+                return fail(st);
+            L.gate_exps = W(p + "ffn_gate_exps.weight"), L.up_exps = W(p + "ffn_up_exps.weight");
+            L.down_exps = W(p + "ffn_down_exps.weight");
+            const rcu_weight *ex[3] = {L.gate_exps, L.up_exps, L.down_exps};
+            const uint64_t exs[3][2] = {{ne * fx, e}, {ne * fx, e}, {ne * e, fx}};
+            for (int i = 0; i < 3; i++)
+                if (int st = need(ex[i] && ex[i]->rows == exs[i][0] && ex[i]->cols == exs[i][1] && gemv_supported(ex[i]->type),
+                                  p + "ffn_*_exps.weight"))
+                    return fail(st);
+            L.gate_sh = W(p + "ffn_gate_shexp.weight");
+            if (L.gate_sh) {
+                L.up_sh = W(p + "ffn_up_shexp.weight"), L.down_sh = W(p + "ffn_down_shexp.weight");
+                if (int st = need(L.up_sh && L.down_sh && L.gate_sh->cols == e && L.up_sh->rows == L.gate_sh->rows &&
+                                      L.down_sh->rows == e && L.down_sh->cols == L.gate_sh->rows,
+                                  p + "ffn_*_shexp.weight"))
+                    return fail(st);
+                L.sh_gate = V(p + "ffn_gate_inp_shexp.weight");
+                b->ff_max = std::max<uint32_t>(b->ff_max, (uint32_t)L.gate_sh->rows);
+            }
+            L.gate = L.up = L.down = nullptr;
+        }
         const rcu_weight *mats[7] = {L.wq, L.wk, L.wv, L.wo, L.gate, L.up, L.down};
         const uint64_t shp[7][2] = {{qd, e}, {kvd, e}, {kvd, e}, {e, qd}, {c.n_ff, e}, {c.n_ff, e}, {e, c.n_ff}};
         const char *names[7] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
-        for (int i = 0; i < 7; i++)
+        for (int i = 0; i < (L.router ? 4 : 7); i++)
             if (int st = need(mats[i] && mats[i]->rows == shp[i][0] && mats[i]->cols == shp[i][1] && gemv_supported(mats[i]->type),
                               p + names[i]))
                 return fail(st);
@@ -945,7 +1180,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
         L.bq = V(p + "attn_q.bias"), L.bk = V(p + "attn_k.bias"), L.bv = V(p + "attn_v.bias");
         L.post_attn = V(p + "post_attention_norm.weight"), L.post_ffn = V(p + "post_ffw_norm.weight");
         L.swa = c.swa_window > 0 && c.swa_pattern > 0 && (il % c.swa_pattern) < c.swa_pattern - 1;
-        b->ff_max = std::max<uint32_t>(b->ff_max, (uint32_t)L.gate->rows);
+        if (L.gate) b->ff_max = std::max<uint32_t>(b->ff_max, (uint32_t)L.gate->rows);
         b->layers.push_back(L);
         const uint64_t slots = L.swa ? std::min<uint64_t>(c.swa_window + b->max_batch, n_ctx) : n_ctx;
         rcu_kv *kv = nullptr;
@@ -955,6 +1190,24 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     const uint64_t T = b->max_batch;
     const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(e, qd), b->ff_max);
     if (int st = rcu_acts_create(ctx, T, kmax, &b->acts)) return fail(st);
+    bool moe = false;
+    for (auto &L : b->layers) moe = moe || L.router;
+    if (moe) {  // mixture-of-experts scratch (sizes for the largest batch)
+        const uint64_t ne = c.n_expert, kk = std::min<uint64_t>(std::max<uint32_t>(c.n_expert_used, 1), ne);
+        const uint64_t fx = c.n_ff_exp;
+        struct {
+            void **p;
+            uint64_t bytes;
+        } mb[] = {{(void **)&b->moe_logits, T * ne * 4}, {(void **)&b->moe_sgate, T * 4}, {(void **)&b->moe_w, T * kk * 4},
+                  {(void **)&b->moe_sel, T * kk * 4},   {(void **)&b->moe_g, T * kk * fx * 4},
+                  {(void **)&b->moe_u, T * kk * fx * 4}, {(void **)&b->moe_y, T * kk * e * 4},
+                  {(void **)&b->moe_ys, T * e * 4}};
+        for (auto &x : mb)
+            if (int st = dalloc(b, x.p, x.bytes)) return fail(st);
+        if (8 * kk > 64) return fail(set_err(ctx, RCU_ERR_UNSUPPORTED, "more than 8 experts per token"));
+        if (int st = rcu_acts_create(ctx, std::max<uint64_t>(T, 8 * kk), std::max<uint64_t>(fx, b->ff_max), &b->acts2))
+            return fail(st);
+    }
     struct {
         float **p;
         uint64_t n;
@@ -1029,6 +1282,7 @@ void rcu_backend_free(rcu_backend *b) {
     if (b->stream) cudaStreamDestroy(b->stream);
     for (auto *kv : b->kv) rcu_kv_free(kv);
     rcu_acts_free(b->acts);
+    rcu_acts_free(b->acts2);
     cudaSetDevice(b->ctx->device);
     for (void *p : b->allocs) cudaFree(p);
     delete b;

@@ -31,6 +31,7 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxRw = 2;  // weight rows per warp per tile
 constexpr uint32_t kHdrBytes = 6144;  // barriers + reduction scratch
 constexpr int kMaxPeers = 8;
+constexpr uint32_t kMaxStageRows = 64;
 
 struct GemvJobDev {
     const uint8_t *w;
@@ -39,6 +40,11 @@ struct GemvJobDev {
     uint32_t rows, row_bytes;
     int32_t type;
     uint32_t rows_per_tile, tile_begin, wpr, rw;
+    // indirect (mixture-of-experts) jobs: the weight is w + (*sel) * w_stride, chosen on
+    // the device by the router; the job's activations start at staged row `tok`
+    const uint32_t *sel;
+    uint64_t w_stride;
+    uint32_t tok;
 };
 
 struct GemvParams {
@@ -46,6 +52,7 @@ struct GemvParams {
     int32_t n_jobs;
     uint32_t total_tiles, stages, stage_bytes, stage_off;
     uint32_t k, n_tok, tok0, formats;
+    uint32_t n_stage;  // activation rows staged in shared memory (>= n_tok + every job's tok)
     uint32_t early_weights;  // producer may load weights before the previous kernel ends
     // shared-memory offsets of the staged activations
     uint32_t o_q0, o_d0, o_s0, o_sum0, o_qk, o_dk, o_bsk;
@@ -182,10 +189,10 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
     }
     if (row_first >= nrows) return;
     if (row_first + nr > nrows) nr = nrows - row_first;
-    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_q0);
-    const float *ad = reinterpret_cast<const float *>(sm + p.o_d0);
-    const float *as = reinterpret_cast<const float *>(sm + p.o_s0);
-    const int32_t *asm_ = reinterpret_cast<const int32_t *>(sm + p.o_sum0);
+    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_q0) + (size_t)jb.tok * p.k;
+    const float *ad = reinterpret_cast<const float *>(sm + p.o_d0) + (size_t)jb.tok * nb;
+    const float *as = reinterpret_cast<const float *>(sm + p.o_s0) + (size_t)jb.tok * nb;
+    const int32_t *asm_ = reinterpret_cast<const int32_t *>(sm + p.o_sum0) + (size_t)jb.tok * nb;
     const uint32_t rb = jb.row_bytes, wrow0 = row_first * rb;
     float acc[kMaxRw][T];
 #pragma unroll
@@ -250,9 +257,9 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
     if (row_first >= nrows) return;
     if (row_first + nr > nrows) nr = nrows - row_first;
     const uint32_t g = lane >> 3, sub = lane & 7;
-    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_qk);
-    const float *adk = reinterpret_cast<const float *>(sm + p.o_dk);
-    const uint32_t *abs2 = reinterpret_cast<const uint32_t *>(sm + p.o_bsk);  // bsums pairs
+    const int8_t *aq = reinterpret_cast<const int8_t *>(sm + p.o_qk) + (size_t)jb.tok * p.k;
+    const float *adk = reinterpret_cast<const float *>(sm + p.o_dk) + (size_t)jb.tok * nsb;
+    const uint32_t *abs2 = reinterpret_cast<const uint32_t *>(sm + p.o_bsk) + (size_t)jb.tok * (p.k / 32);  // bsums pairs
     const uint32_t rb = jb.row_bytes, wrow0 = row_first * rb;
     float acc[kMaxRw][T];
 #pragma unroll
@@ -352,7 +359,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
                 const uint32_t bytes = (nrows * jb.row_bytes + 15u) & ~15u;
                 uint8_t *dst = smem + p.stage_off + s * p.stage_bytes;
                 mbar_arrive_expect_tx(&h->full[s], bytes);
-                bulk_g2s(dst, jb.w + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s], pol);
+                const uint8_t *wbase = jb.sel ? jb.w + (uint64_t)(*jb.sel) * jb.w_stride : jb.w;
+                bulk_g2s(dst, wbase + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s], pol);
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
@@ -373,7 +381,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
     // everything else waits for it)
     pdl_wait();
     {
-        const uint32_t nt = p.n_tok, k = p.k, tid = threadIdx.x, nthr = NW * 32;
+        const uint32_t nt = p.n_stage, k = p.k, tid = threadIdx.x, nthr = NW * 32;
         const ActsView &A = p.acts;
         if (p.formats & RCU_ACT_Q8_0) {
             const uint32_t nb = k / QK;
@@ -559,9 +567,14 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
         const rcu_weight *w = jobs[i].w;
         GemvJobDev &jd = p.jobs[i];
         jd.w = w->data;
-        jd.out = jobs[i].out + (uint64_t)tok0 * jobs[i].ld;
+        jd.out = jobs[i].out + (jobs[i].sel ? 0 : (uint64_t)tok0 * jobs[i].ld);  // indirect jobs: own rows
         jd.ld = jobs[i].ld;
-        jd.rows = (uint32_t)w->rows;
+        jd.rows = jobs[i].rows ? jobs[i].rows : (uint32_t)w->rows;
+        jd.sel = jobs[i].sel;
+        jd.w_stride = jobs[i].w_stride;
+        jd.tok = jobs[i].tok;
+        if (jd.sel) p.early_weights = 0;  // the producer reads the router's choice: wait first
+        p.n_stage = std::max(p.n_stage, jd.tok + n_tok);
         jd.row_bytes = (uint32_t)w->row_bytes;
         jd.type = w->type;
         p.formats |= act_format(w->type);
@@ -589,20 +602,22 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
-    // activations staged in shared memory
+    // activations staged in shared memory (n_stage rows from tok0)
+    if (p.n_stage > kMaxStageRows) return set_err(ctx, RCU_ERR_INVALID, "gemv: more than 64 activation rows");
+    const uint32_t n_rows = p.n_stage;
     uint32_t off = kHdrBytes;
     const uint32_t k = a.k;
     if (p.formats & RCU_ACT_Q8_0) {
         const uint32_t nb = k / QK;
-        p.o_q0 = off; off = round_up(off + n_tok * k, 16);
-        p.o_d0 = off; off = round_up(off + n_tok * nb * 4, 16);
-        p.o_s0 = off; off = round_up(off + n_tok * nb * 4, 16);
-        p.o_sum0 = off; off = round_up(off + n_tok * nb * 4, 16);
+        p.o_q0 = off; off = round_up(off + n_rows * k, 16);
+        p.o_d0 = off; off = round_up(off + n_rows * nb * 4, 16);
+        p.o_s0 = off; off = round_up(off + n_rows * nb * 4, 16);
+        p.o_sum0 = off; off = round_up(off + n_rows * nb * 4, 16);
     }
     if (p.formats & RCU_ACT_Q8K) {
-        p.o_qk = off; off = round_up(off + n_tok * k, 16);
-        p.o_dk = off; off = round_up(off + n_tok * (k / QK_K) * 4, 16);
-        p.o_bsk = off; off = round_up(off + n_tok * (k / 16) * 2, 16);
+        p.o_qk = off; off = round_up(off + n_rows * k, 16);
+        p.o_dk = off; off = round_up(off + n_rows * (k / QK_K) * 4, 16);
+        p.o_bsk = off; off = round_up(off + n_rows * (k / 16) * 2, 16);
     }
     p.stage_off = round_up(off, 128);
     const uint32_t budget = (uint32_t)ctx->max_smem_optin;

@@ -10,6 +10,12 @@ struct HostJob {
     const rcu_weight *w;
     float *out;
     uint64_t ld;
+    // indirect job (mixture of experts): weight = w + (*sel) * w_stride bytes with `rows`
+    // rows (0: all of w), the expert id written on the device; activations from row `tok`
+    const uint32_t *sel = nullptr;
+    uint64_t w_stride = 0;
+    uint32_t rows = 0;
+    uint32_t tok = 0;
 };
 // Decode GEMV over up to kGemvMaxJobs jobs sharing one activation batch (n_tok <= 8).
 constexpr int kGemvMaxJobs = 96;

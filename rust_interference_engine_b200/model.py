@@ -55,13 +55,19 @@ class SyntheticSpec:
     rope_base: float = 10000.0
     rms_eps: float = 1e-6
     type_overrides: dict = field(default_factory=dict)  # per-tensor-suffix ggml type (Q4_K_M style mixes)
+    n_expert: int = 0        # mixture of experts (testing.rs:115-120): 0 = dense
+    n_expert_used: int = 2
+    n_ff_exp: int = 256
+    n_ff_shexp: int = 0      # always-on shared expert (qwen2moe)
 
     @classmethod
     def tiny(cls, arch: str, wtype: int) -> "SyntheticSpec":  # testing.rs:127-154
         return cls(arch=arch, wtype=wtype, embd_type=GgmlType.Q8_0 if GgmlType(wtype).block_size > 1 else wtype,
                    qkv_bias=arch == "qwen2", qk_norm=arch in ("qwen3", "gemma3"),
                    post_norms=arch in ("gemma2", "gemma3"), fused=arch == "phi3",
-                   swa_window=5 if arch in ("gemma2", "gemma3") else 0)
+                   swa_window=5 if arch in ("gemma2", "gemma3") else 0,
+                   n_expert=8 if arch in ("qwen3moe", "qwen2moe") else 0,
+                   n_ff_shexp=256 if arch == "qwen2moe" else 0)
 
     def config(self) -> ModelConfig:
         """ModelConfig::from_gguf rules for the synthetic metadata (model/config.rs:106-247)."""
@@ -84,6 +90,9 @@ class SyntheticSpec:
         c.swa_pattern = 2 if self.arch == "gemma2" else (6 if self.arch == "gemma3" else 0)
         c.rope_base_swa = 10000.0 if self.arch == "gemma3" else 0.0
         c.act = 1 if gemma else 0
+        c.n_expert, c.n_expert_used, c.n_ff_exp = self.n_expert, self.n_expert_used, self.n_ff_exp
+        c.expert_norm_topk = int(self.arch != "qwen2moe")  # expert_weights_norm default (config.rs:167)
+        c.expert_unit_weights = 0
         return c
 
     def type_of(self, name: str) -> int:
@@ -126,7 +135,19 @@ def synthetic_tensors(spec: SyntheticSpec, weight, vec_f32, norm):
             yield p + "post_attention_norm.weight", GgmlType.F32, 1, e, norm(e)
             yield p + "post_ffw_norm.weight", GgmlType.F32, 1, e, norm(e)
         yield p + "ffn_norm.weight", GgmlType.F32, 1, e, norm(e)
-        if spec.fused:
+        if spec.n_expert:  # testing.rs:358-372 (router F32, experts stacked [expert][rows][cols])
+            ne, fx, t = spec.n_expert, spec.n_ff_exp, spec.wtype
+            yield p + "ffn_gate_inp.weight", GgmlType.F32, ne, e, vec_f32(ne * e, 0.5)
+            yield p + "ffn_gate_exps.weight", t, fx * ne, e, weight(t, fx * ne, e)
+            yield p + "ffn_up_exps.weight", t, fx * ne, e, weight(t, fx * ne, e)
+            yield p + "ffn_down_exps.weight", t, e * ne, fx, weight(t, e * ne, fx)
+            if spec.n_ff_shexp:
+                fs = spec.n_ff_shexp
+                yield p + "ffn_gate_shexp.weight", t, fs, e, weight(t, fs, e)
+                yield p + "ffn_up_shexp.weight", t, fs, e, weight(t, fs, e)
+                yield p + "ffn_down_shexp.weight", t, e, fs, weight(t, e, fs)
+                yield p + "ffn_gate_inp_shexp.weight", GgmlType.F32, 1, e, vec_f32(e, 0.3)
+        elif spec.fused:
             t = spec.type_of("ffn_up.weight")
             yield p + "ffn_up.weight", t, 2 * ff, e, weight(t, 2 * ff, e)
             t = spec.type_of("ffn_down.weight")

@@ -139,3 +139,24 @@ def test_long_decode_replays_graph(env):
     # a batch in between leaves the graph valid
     close(gb.forward(toks[:8], 40), ob.forward(toks[:8], 40))
     close(gb.forward(toks[8:9], 48), ob.forward(toks[8:9], 48))
+
+
+@pytest.mark.parametrize("arch,wtype", [("qwen3moe", O.Q4_K), ("qwen3moe", O.Q4_0), ("qwen2moe", O.Q8_0)],
+                         ids=["qwen3moe-q4_k", "qwen3moe-q4_0", "qwen2moe-q8_0"])
+def test_moe_forward_matches_oracle(env, arch, wtype):
+    """moe_ffn (model/cpu.rs:469-524): F32 router, softmax top-k on the device, experts as
+    GEMVs selected by the routing, shared expert (qwen2moe); prompt of 7 then decode steps
+    (graph replay)."""
+    from rust_interference_engine_b200 import model as M
+    run_compare(env, M.SyntheticSpec.tiny(arch, wtype), O.KV_F16)
+
+
+def test_moe_batch_above_eight_tokens(env):
+    # experts run 8 tokens at a time; a 13-token batch crosses a chunk
+    from rust_interference_engine_b200 import model as M
+    gb, ob, keep = build_pair(env, M.SyntheticSpec.tiny("qwen3moe", O.Q4_K), O.KV_F16)
+    toks = np.random.default_rng(9).integers(0, 384, 13).astype(np.uint32)
+    g = gb.forward(toks, 0, all_logits=True)
+    o = ob.forward(toks, 0, all_logits=True)
+    close(g, o, what="13-token MoE batch")
+    same_greedy(g, o)
