@@ -597,6 +597,164 @@ def run_decode(args, world, rank, local):
     }
 
 
+# ---- workload: config 4 MoE decode (Qwen3-30B-A3B shape) --------------------------------
+QWEN3_30B_A3B = dict(arch="qwen3moe", n_vocab=151936, n_embd=2048, n_layer=48, n_head=32, n_head_kv=4, head_dim=128,
+                     n_ff=6144, rope_dim=128, rope_base=1_000_000.0, rms_eps=1e-6, n_expert=128, n_expert_used=8,
+                     n_ff_exp=768, n_ff_shexp=0)
+MOE_PROMPT = 64
+
+
+def qwen3_moe_spec():
+    from rust_interference_engine_b200 import GgmlType as G
+    from rust_interference_engine_b200.model import SyntheticSpec
+    return SyntheticSpec(wtype=G.Q4_K, embd_type=G.Q4_K, qk_norm=True, **QWEN3_30B_A3B)
+
+
+def moe_bytes_per_token(spec):
+    """Weight bytes one decoded token reads: attention, router (f32), 8 experts, head."""
+    from rust_interference_engine_b200 import GgmlType as G
+    rb = lambda cols: G.Q4_K.row_bytes(cols)
+    e, qd, kvd = spec.n_embd, spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim
+    attn = (qd + 2 * kvd) * rb(e) + e * rb(qd)
+    experts = spec.n_expert_used * (2 * spec.n_ff_exp * rb(e) + e * rb(spec.n_ff_exp))
+    router = spec.n_expert * e * 4
+    return spec.n_layer * (attn + experts + router) + spec.n_vocab * rb(e)
+
+
+def run_moe(args, world, rank, local):
+    import torch
+
+    import rust_interference_engine_b200 as rie
+    from rust_interference_engine_b200 import model as M
+    if world > 1:
+        raise SystemExit("the MoE workload runs on one GPU (expert parallelism is not built)")
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    spec = qwen3_moe_spec()
+    gen = RandomBlocks(4)
+    model = M.Model(ctx, spec.config())
+    t_build = time.perf_counter()
+    for name, t, rows, cols, data in M.synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
+        model.set_tensor(name, int(t), rows, cols, data)
+    t_build = time.perf_counter() - t_build
+    n_gen = max(args.warmup, 3) + args.steps
+    be = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16)
+    prompt = torch.from_numpy(np.random.default_rng(4).integers(0, spec.n_vocab, MOE_PROMPT).astype(np.int32)).cuda()
+    gen_tokens = torch.from_numpy(np.random.default_rng(5).integers(0, spec.n_vocab, n_gen).astype(np.int32)).cuda()
+    logits = torch.zeros(spec.n_vocab, device="cuda")
+    be.forward_device(prompt, MOE_PROMPT, 0, logits)
+    pos = MOE_PROMPT
+    for i in range(max(args.warmup, 3)):
+        be.forward_device(gen_tokens[i:], 1, pos, logits)
+        pos += 1
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            be.forward_device(gen_tokens[max(args.warmup, 3) + i:], 1, pos + i, logits)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    finite = bool(torch.isfinite(logits).all())
+    # e2e: host tokens in, host logits out (Backend::forward)
+    be2 = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16)
+    be2.forward(prompt.cpu().numpy().astype(np.uint32), 0)
+    tok, p2 = np.array([1], dtype=np.uint32), MOE_PROMPT
+    for i in range(max(args.warmup, 3)):
+        be2.forward(tok, p2)
+        p2 += 1
+    e0 = time.perf_counter()
+    for i in range(args.steps):
+        out = be2.forward(tok, p2)
+        tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
+        p2 += 1
+    e2e_tps = args.steps / (time.perf_counter() - e0)
+    be2.free()
+    # batch of 256 tokens in one forward (config 4's large batch)
+    be3 = M.CudaBackend(model, 512, 256, rie.KvType.F16)
+    big = torch.from_numpy(np.random.default_rng(6).integers(0, spec.n_vocab, 256).astype(np.int32)).cuda()
+    be3.forward_device(big, 256, 0, logits)
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    be3.forward_device(big, 256, 256, logits)
+    b1.record(stream)
+    torch.cuda.synchronize()
+    b256_tps = 256 / (b0.elapsed_time(b1) * 1e-3)
+    be3.free()
+    # dominant kernel: the expert gate+up GEMV of one token (16 x 768 x 2048 Q4_K), timed alone
+    # over distinct copies (> L2)
+    ws = [rie.Weight.upload(ctx, rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd,
+                            gen.weight(rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd)) for _ in range(16 * 12)]
+    xg = torch.randn(1, spec.n_embd, device="cuda")
+    acts = rie.QuantActs(ctx, 1, spec.n_embd)
+    acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
+    og = torch.zeros(16, spec.n_ff_exp, device="cuda")
+    jobs = [[rie.MatmulJob(ws[16 * g + j], og[j]) for j in range(16)] for g in range(12)]
+    for j in jobs:
+        rie.matmul_multi(ctx, acts, j)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 48
+    g0.record(stream)
+    for r in range(reps):
+        rie.matmul_multi(ctx, acts, jobs[r % 12])
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gemv_ms = g0.elapsed_time(g1) / reps
+    gemv_bytes = 16 * rie.GgmlType.Q4_K.row_bytes(spec.n_embd) * spec.n_ff_exp
+    peak, peak_kind = peaks()
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    wb = moe_bytes_per_token(spec)
+    return {
+        "metric": META["moe"]["metric"], "value": 1000.0 / ms, "unit": "tok/s", "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "dtype": META["moe"]["dtype"],
+        "config": {"workload": META["moe"]["workload"], "layers": spec.n_layer, "hidden": spec.n_embd,
+                   "experts": f"{spec.n_expert} x ffn {spec.n_ff_exp}, top-{spec.n_expert_used} softmax",
+                   "heads": f"{spec.n_head}/{spec.n_head_kv}x{spec.head_dim}", "vocab": spec.n_vocab,
+                   "prompt": MOE_PROMPT, "weight_bytes_per_token": wb, "b256_tok_s": b256_tps, "batch": 1,
+                   "l2": "inputs larger than L2 (expert weights streamed per token)", "parallelism": "replicas x1",
+                   "decode": "CUDA graph replay per token", "model_build_s": t_build},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_moe_experts"),
+                     "kernel": "k_gemv<1,16> (8 experts' gate+up, 16 x 768 x 2048 Q4_K)",
+                     "bytes_per_launch": gemv_bytes, "launch_ms": gemv_ms,
+                     "whole_step_weight_gb_s": wb / (ms * 1e-3) / 1e9},
+        "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.n_vocab * 4,
+                "api": "CudaBackend.forward (rcu_backend_forward, host tokens/logits, greedy)"},
+        "gpu_launches": args.steps * (spec.n_layer * 14 + 4),
+        "clocks": clk.summary(),
+        "check": {"logits_finite": finite},
+    }
+
+
+def cpu_moe_sample(seconds: float, threads: int):
+    """The oracle's restated CPU forward (moe_ffn, AVX2 tier, all host threads) decoding the
+    same MoE shape after a 16-token prompt."""
+    import oracle as O
+    from rust_interference_engine_b200.model import synthetic_tensors
+    spec = qwen3_moe_spec()
+    gen = RandomBlocks(4)
+    om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(spec.config())))
+    for name, t, rows, cols, data in synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
+        om.set_tensor(name, int(t), rows, cols, data)
+    ob = O.OracleBackend(om, 256, 16, kv_type=O.KV_F16, n_threads=threads)
+    ob.forward(np.arange(16, dtype=np.uint32), 0)
+    n, pos, t0 = 0, 16, time.perf_counter()
+    tok = np.array([1], dtype=np.uint32)
+    while True:
+        out = ob.forward(tok, pos)
+        tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
+        n, pos = n + 1, pos + 1
+        el = time.perf_counter() - t0
+        if el >= seconds or pos >= 255:
+            break
+    return {"value": n / el, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of the 48-layer Qwen3-30B-A3B-shape MoE at context 16-{pos}, {el:.1f} s",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
 def cpu_decode_sample(seconds: float, threads: int):
     """The oracle's restated CPU forward (AVX2 tier, all host threads) decoding on the same
     model shape: a 16-token prompt, then single-token steps until `seconds` elapse."""
@@ -644,8 +802,11 @@ def cpu_prefill_sample(seconds: float, threads: int):
 
 
 WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample),
-             "decode": (run_decode, cpu_decode_sample)}
+             "decode": (run_decode, cpu_decode_sample), "moe": (run_moe, cpu_moe_sample)}
 META = {  # metric / unit / config of each workload, shared by both arms
+    "moe": {"metric": "Qwen3-30B-A3B-shape MoE decode tg tok/s (config 4, batch 1)", "unit": "tok/s",
+            "dtype": "int8 x Q4_K blocks (Q8_K activations), f32 router / glue, f16 KV",
+            "workload": "qwen3_30b_a3b_moe_decode_config4"},
     "decode": {"metric": "Qwen3-8B-shape Q4_K_M decode tg tok/s (config 3, batch 1)", "unit": "tok/s",
                "dtype": "int8 x Q4_K/Q6_K blocks (Q8_K activations), f32 glue, f16 KV",
                "workload": "qwen3_8b_q4_k_m_decode_config3"},
