@@ -755,6 +755,133 @@ def cpu_moe_sample(seconds: float, threads: int):
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
+# ---- workload: config 5 turbo4 attention (Llama-3.1-70B shape, context 32768) ------------
+T5 = dict(n_layer=80, n_head=64, n_head_kv=8, head_dim=128, ctx=32768)
+
+
+def run_turbo(args, world, rank, local):
+    """One decode token's attention over all 80 layers' turbo4 caches at context 32768. With
+    N > 1 every rank holds 8/N KV heads (and their 64/N query heads) of every layer, as the
+    tensor-parallel forward does: each rank reads 1/N of the KV bytes, no exchange."""
+    import torch
+
+    import oracle as O
+    import rust_interference_engine_b200 as rie
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    L, H, KV, hd, S = T5["n_layer"], T5["n_head"], T5["n_head_kv"], T5["head_dim"], T5["ctx"]
+    if KV % world:
+        raise SystemExit("KV heads must divide by the GPU count")
+    kvl, hl = KV // world, H // world
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    caches = []
+    t_fill = time.perf_counter()
+    chunk = 4096
+    for _ in range(L):  # K, V ~ N(0, 1), encoded by the library's turbo4 append (rotate + 4-bit codes)
+        c = rie.LayerCache(ctx, rie.KvType.Turbo4, kvl, hd, S)
+        for p0 in range(0, S, chunk):
+            k = torch.randn(chunk, kvl * hd, device="cuda", generator=gen)
+            v = torch.randn(chunk, kvl * hd, device="cuda", generator=gen)
+            c.store(k, v, chunk, p0)
+        caches.append(c)
+    torch.cuda.synchronize()
+    t_fill = time.perf_counter() - t_fill
+    q = torch.randn(L, hl * hd, device="cuda", generator=gen)
+    out = torch.zeros(L, hl * hd, device="cuda")
+    pos = S - 1  # the last position: the whole window is read
+
+    def step():
+        for il in range(L):
+            rie.attention(ctx, caches[il], q[il], 1, hl, pos, out[il])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # parity spot check of layer 0 against the oracle's turbo4 attention on the same cache bytes
+    kc, vc = caches[0].export()
+    want = O.attention(q[0].cpu().numpy(), kc, vc, hl, kvl, hd, pos, S, O.KV_TURBO4, n_threads=16)
+    got = out[0].cpu().numpy()
+    max_rel = float(np.max(np.abs(got - want.reshape(-1))) / max(float(np.max(np.abs(want))), 1e-6))
+    kern = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            kern[i][0].record(stream)
+            step()
+            kern[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = dist_max(t0.elapsed_time(t1) / args.steps, world)
+    row = rie.turbo.row_bytes_4(hd)
+    kv_bytes = L * 2 * kvl * S * row  # per rank per step
+    # e2e through the public API: query from pinned host memory, output back to the host
+    qh = q.cpu().pin_memory()
+    oh = torch.empty_like(out, device="cpu").pin_memory()
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            torch.cuda.synchronize()
+            e0 = time.perf_counter()
+        q.copy_(qh, non_blocking=True)
+        step()
+        oh.copy_(out, non_blocking=True)
+        stream.synchronize()
+    e2e_s = (time.perf_counter() - e0) / args.steps
+    e2e_s = dist_max(e2e_s, world)
+    peak, peak_kind = peaks()
+    achieved = kv_bytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": META["turbo"]["metric"], "value": world * kv_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "dtype": META["turbo"]["dtype"],
+        "config": {"workload": META["turbo"]["workload"], "layers": L, "heads": f"{H}/{KV}x{hd}", "context": S,
+                   "kv_bytes_per_step": world * kv_bytes, "row_bytes": row, "tok_s": 1000.0 / ms,
+                   "l2": f"inputs larger than L2 ({world * kv_bytes / 1e9:.2f} GB of turbo4 KV per step)",
+                   "parallelism": f"tp{world} (KV heads split, no exchange)", "kv_fill_s": t_fill},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": profile_traffic("attn_turbo4_70b_ctx32k"),
+                     "kernel": "k_attn<turbo4, G=8> (80 launches per step)", "bytes_per_launch": kv_bytes // L,
+                     "launch_ms": float(np.mean([a.elapsed_time(b) for a, b in kern])) / L},
+        "e2e": {"value": world * kv_bytes / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(q.numel() * 4),
+                "d2h_bytes_per_step": int(out.numel() * 4), "ms_per_step": e2e_s * 1e3},
+        "gpu_launches": args.steps * L,
+        "clocks": clk.summary(),
+        "check": {"max_rel_err_vs_oracle": max_rel, "tolerance": 2e-3},
+    }
+
+
+def cpu_turbo_sample(seconds: float, threads: int):
+    """The oracle's turbo4 attention (turbo.rs score/axpy, AVX2 tier, all host threads) over
+    one layer's 8 KV heads at context 32768; GB/s of KV read."""
+    import oracle as O
+    H, KV, hd, S = T5["n_head"], T5["n_head_kv"], T5["head_dim"], T5["ctx"]
+    rng = np.random.default_rng(7)
+    row = O.kv_row_bytes(O.KV_TURBO4, hd)
+    # random valid rows (f16 scale + codes), same bytes / work as encoded N(0, 1) rows
+    kc = rng.integers(0, 256, (KV * S, row), dtype=np.uint8)
+    vc = rng.integers(0, 256, (KV * S, row), dtype=np.uint8)
+    sc = np.frombuffer(np.float16(0.02).tobytes(), dtype=np.uint8)
+    for b in range((row - hd // 2) // 2):  # one f16 scale per rotation block, then the codes
+        kc[:, 2 * b:2 * b + 2] = sc
+        vc[:, 2 * b:2 * b + 2] = sc
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    O.attention(q, kc, vc, H, KV, hd, S - 1, S, O.KV_TURBO4, n_threads=threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.attention(q, kc, vc, H, KV, hd, S - 1, S, O.KV_TURBO4, n_threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": n * 2 * KV * S * row / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} single-layer turbo4 attentions (64/8 heads x 128, context {S}), {el:.1f} s",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
 def cpu_decode_sample(seconds: float, threads: int):
     """The oracle's restated CPU forward (AVX2 tier, all host threads) decoding on the same
     model shape: a 16-token prompt, then single-token steps until `seconds` elapse."""
@@ -802,8 +929,12 @@ def cpu_prefill_sample(seconds: float, threads: int):
 
 
 WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample),
-             "decode": (run_decode, cpu_decode_sample), "moe": (run_moe, cpu_moe_sample)}
+             "decode": (run_decode, cpu_decode_sample), "moe": (run_moe, cpu_moe_sample),
+             "turbo": (run_turbo, cpu_turbo_sample)}
 META = {  # metric / unit / config of each workload, shared by both arms
+    "turbo": {"metric": "turbo4 KV attention HBM GB/s (config 5, Llama-3.1-70B shape, context 32768)", "unit": "GB/s",
+              "dtype": "u4 codes x int8 query (rotated domain, byte-shuffle lookup), f32 softmax",
+              "workload": "turbo4_attention_70b_ctx32768_config5"},
     "moe": {"metric": "Qwen3-30B-A3B-shape MoE decode tg tok/s (config 4, batch 1)", "unit": "tok/s",
             "dtype": "int8 x Q4_K blocks (Q8_K activations), f32 router / glue, f16 KV",
             "workload": "qwen3_30b_a3b_moe_decode_config4"},

@@ -343,9 +343,8 @@ __device__ __forceinline__ StagedRows stage_rows(const uint8_t *cache, uint64_t 
 // partial output. The last CTA of (t, g) to finish merges the splits (cpu.rs:590-634 softmax
 // and weighted sum), applies the inverse rotation (turbo) and writes the f32 output and/or
 // the quantized activations of the Wo matmul.
-template <int KV, int G>
+template <int KV, int G, int DPL>  // DPL: values per lane in the V sum (head_dim / 32, at most)
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnParams p) {
-    constexpr int DPL = kMaxAttnHd / 32;
     extern __shared__ __align__(16) uint8_t dsm[];
     __shared__ __align__(16) float qf[G][kMaxAttnHd];  // f32 query (f16 cache) / rotation scratch
     __shared__ __align__(16) int8_t qi[G][kMaxAttnHd];
@@ -425,6 +424,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
 #pragma unroll
             for (int e = 0; e < DPL; e++) acc[hh][e] = 0.0f;
         const uint32_t d0 = lane * dpl;
+        // V-row byte offsets of this lane's codes and scale (turbo4: f16 scale per rotation
+        // block, then Q4_0-ordered nibbles; Q8_0: 34-byte blocks)
+        const uint32_t tbk = turbo_block(hd), tnb = hd / tbk;
+        const bool v_hi = (d0 % 32) >= 16;
+        const uint32_t v_code_off = KV == RCU_KV_TURBO4 ? 2 * tnb + 16 * (d0 / 32) + ((d0 % 32) & 15)
+                                                         : 34 * (d0 / 32) + 2 + d0 % 32;
+        const uint32_t v_scale_off = KV == RCU_KV_TURBO4 ? 2 * (d0 / tbk) : 34 * (d0 / 32);
 
         uint32_t sub = 0;
         for (uint32_t s0 = c0; s0 < c1; s0 += kSub, sub++) {
@@ -457,13 +463,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
                 if (s0 + r < s1) {
                     const uint32_t ro = krc.off(r, rb);
                     if (KV == RCU_KV_TURBO4) {
-                        const uint32_t b = turbo_block(hd), nb = hd / b;
                         for (uint32_t cc = qq; cc < hd / 32; cc += 4) {
-                            uint32_t sw[1];
-                            ld_words<1>(kbuf, ro + 2 * ((cc * 32) / b), sw);
-                            const float scale = f16_bits_to_f32(sw[0]);
+                            const float scale =
+                                f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(kbuf + ro + 2 * ((cc * 32) / tbk)));
                             uint32_t w[4];
-                            ld_words<4>(kbuf, ro + 2 * nb + 16 * cc, w);
+                            ld_words<4>(kbuf, ro + 2 * tnb + 16 * cc, w);
                             uint32_t lv[8];
 #pragma unroll
                             for (int i2 = 0; i2 < 4; i2++) {
@@ -564,25 +568,28 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
                         for (int e = 0; e < DPL; e++)
                             if ((uint32_t)e < dpl) val[e] = __half2float(reinterpret_cast<const __half *>(vbuf + ro)[d0 + e]);
                     }
+                } else if (KV == RCU_KV_TURBO4 || KV == RCU_KV_Q8_0) {
+                    // the lane's dpl values are consecutive codes of one 32-value chunk: one or
+                    // two words, one f16 scale per row
+                    uint32_t cw[2] = {0u, 0u};
+                    if (dpl > 4)
+                        ld_words<2>(vbuf, ro + v_code_off, cw);
+                    else
+                        ld_words<1>(vbuf, ro + v_code_off, *reinterpret_cast<uint32_t(*)[1]>(cw));
+                    const float scale = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(vbuf + ro + v_scale_off)) *
+                                        (KV == RCU_KV_TURBO4 ? inv46 : 1.0f);
+                    if (KV == RCU_KV_TURBO4) {  // nibbles -> int8 levels (byte-shuffle lookup)
+#pragma unroll
+                        for (int w = 0; w < 2; w++)
+                            cw[w] = lut16(v_hi ? (cw[w] >> 4) & 0x0F0F0F0Fu : cw[w] & 0x0F0F0F0Fu, tb[0], tb[1], tb[2], tb[3]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < DPL; e++)
+                        if ((uint32_t)e < dpl) val[e] = scale * (float)sbyte(cw[e >> 2], e & 3);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < DPL; e++) {
-                        if ((uint32_t)e >= dpl) break;
-                        const uint32_t dd = d0 + e;
-                        if (KV == RCU_KV_TURBO4) {
-                            const uint32_t b = turbo_block(hd), nb = hd / b, c = dd / 32, m2 = dd % 32;
-                            const uint32_t byte = vbuf[ro + 2 * nb + 16 * c + (m2 & 15)];
-                            const uint32_t code = m2 < 16 ? (byte & 15) : (byte >> 4);
-                            const uint32_t sbits = *reinterpret_cast<const uint16_t *>(vbuf + ro + 2 * (dd / b));
-                            val[e] = f16_bits_to_f32(sbits) * inv46 * (float)c_levels[code];
-                        } else if (KV == RCU_KV_Q8_0) {
-                            const uint32_t bi = dd / 32;
-                            const uint32_t sbits = *reinterpret_cast<const uint16_t *>(vbuf + ro + bi * 34);
-                            val[e] = f16_bits_to_f32(sbits) * (float)(int8_t)vbuf[ro + bi * 34 + 2 + dd % 32];
-                        } else {
-                            val[e] = __half2float(reinterpret_cast<const __half *>(vbuf + ro)[dd]);
-                        }
-                    }
+                    for (int e = 0; e < DPL; e++)
+                        if ((uint32_t)e < dpl) val[e] = __half2float(reinterpret_cast<const __half *>(vbuf + ro)[d0 + e]);
                 }
 #pragma unroll
                 for (int hh = 0; hh < G; hh++) {
@@ -765,30 +772,31 @@ bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint3
     return (fmt & RCU_ACT_Q8K) ? gv % QK_K == 0 : gv % QK == 0;
 }
 
-template <int KV, int G>
+template <int KV, int G, int DPL>
 static int launch_group(rcu_ctx *ctx, const AttnParams &p, dim3 grid, uint32_t dyn) {
     static int max_dyn[64] = {};  // per device: opt-in limit minus the kernel's static shared memory
     int &md = max_dyn[ctx->device & 63];
     if (!md) {
         cudaFuncAttributes fa;
-        RCU_CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, k_attn<KV, G>));
+        RCU_CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, k_attn<KV, G, DPL>));
         const int lim = (int)ctx->max_smem_optin - (int)fa.sharedSizeBytes;
-        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_attn<KV, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_attn<KV, G, DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
         md = lim;
     }
     if ((int)dyn > md) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: cache rows too long for shared memory");
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn<KV, G>), grid, dim3(kAttnThreads), dyn, p));
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_attn<KV, G, DPL>), grid, dim3(kAttnThreads), dyn, p));
     return RCU_OK;
 }
 
 template <int KV>
 static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 grid, uint32_t dyn) {
+    const bool wide = p.hd > 128;
     switch (group) {
-        case 1: return launch_group<KV, 1>(ctx, p, grid, dyn);
-        case 2: return launch_group<KV, 2>(ctx, p, grid, dyn);
-        case 4: return launch_group<KV, 4>(ctx, p, grid, dyn);
-        case 8: return launch_group<KV, 8>(ctx, p, grid, dyn);
-        case 16: return launch_group<KV, 16>(ctx, p, grid, dyn);
+        case 1: return wide ? launch_group<KV, 1, 8>(ctx, p, grid, dyn) : launch_group<KV, 1, 4>(ctx, p, grid, dyn);
+        case 2: return wide ? launch_group<KV, 2, 8>(ctx, p, grid, dyn) : launch_group<KV, 2, 4>(ctx, p, grid, dyn);
+        case 4: return wide ? launch_group<KV, 4, 8>(ctx, p, grid, dyn) : launch_group<KV, 4, 4>(ctx, p, grid, dyn);
+        case 8: return wide ? launch_group<KV, 8, 8>(ctx, p, grid, dyn) : launch_group<KV, 8, 4>(ctx, p, grid, dyn);
+        case 16: return wide ? launch_group<KV, 16, 8>(ctx, p, grid, dyn) : launch_group<KV, 16, 4>(ctx, p, grid, dyn);
         default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4, 8 or 16");
     }
 }
