@@ -38,6 +38,18 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def bf16_peak():
+    """Dense bf16 (= f16) tensor throughput: MEASURED_PEAKS.json burst figure, else fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16 8192^3 burst)"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
 def profile_traffic(name: str):
     """Per-launch DRAM bytes recorded from an ncu capture (profiles/traffic.json)."""
     try:
@@ -332,6 +344,8 @@ def run_prefill(args, world, rank, local):
     torch.cuda.set_device(local)
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
+    i8 = args.gemm == "i8"
+    ctx.set_prefill_gemm(rie.PrefillGemm.I8 if i8 else rie.PrefillGemm.F16)
     rng = np.random.default_rng(2)
     x = rng.standard_normal((PF_M, PF_K)).astype(np.float32)
     mats = [O.quantize_weight(O.Q4_0, rng.normal(0.0, 0.02, (n, PF_K)).astype(np.float32)) for n in PF_N]
@@ -385,8 +399,17 @@ def run_prefill(args, world, rank, local):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = dist_max(e0.elapsed_time(e1) / args.steps, world)
-    peak, peak_kind = measured_int8_peak(torch)
+    i8_peak, i8_kind = measured_int8_peak(torch)
     achieved = flops / (kern_ms * 1e-3) / 1e12
+    if i8:
+        peak, peak_kind, kernel = i8_peak, i8_kind, "k_gemm<Q4_0> (tcgen05 kind::i8)"
+        dtype = "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, exact block sums, f32 block-scale epilogue)"
+        launches = 1 + len(PF_N)
+    else:
+        peak, peak_kind = bf16_peak()
+        kernel = "k_acts_f16 + k_gemm_f16<Q4_0> (tcgen05 kind::f16, both weights in one launch)"
+        dtype = "f16 MMA on dequantized Q4_0 weights x Q8_0 activations (d*q), f32 accumulate"
+        launches = 3
     return {
         "metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)",
         "value": world * flops / (ms * 1e-3) / 1e12,
@@ -394,17 +417,20 @@ def run_prefill(args, world, rank, local):
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
-        "dtype": "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, f32 block-scale epilogue)",
+        "dtype": dtype,
         "config": {"workload": "prefill_q4_0_m512_k4096_config2", "m": PF_M, "k": PF_K, "n": list(PF_N),
                    "ops_per_step": flops, "l2": "weights 42 MB + activations (L2-resident re-use by design)",
-                   "parallelism": f"replicas x{world}"},
+                   "parallelism": f"replicas x{world}", "gemm": args.gemm,
+                   "int8_peak_tops": i8_peak, "frac_of_int8_peak": achieved / i8_peak},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": profile_traffic("gemm_q4_0_config2"),
-                     "kernel": "k_gemm<Q4_0>", "launch_ms": kern_ms},
+                     "peak_source": peak_kind,
+                     "traffic": profile_traffic("gemm_q4_0_config2" if i8 else "gemm_f16_q4_0_config2"),
+                     "kernel": kernel, "launch_ms": kern_ms,
+                     "note": "achieved = 2*M*K*N over the matmul_multi call (activation f16 prep + GEMM)"},
         "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                 "h2d_bytes_per_step": PF_M * PF_K * 4, "d2h_bytes_per_step": sum(PF_M * n * 4 for n in PF_N),
                 "ms_per_step": e2e_ms},
-        "gpu_launches": (1 + len(PF_N)) * args.steps,
+        "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
         "check": {"max_rel_err_vs_oracle": max_rel, "tolerance": 1e-3},
     }
@@ -959,6 +985,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--wtype", default="Q4_0", choices=sorted(BLOCK),
                     help="GGUF type of the gemv workload (config 1 is Q4_0)")
+    ap.add_argument("--gemm", default="f16", choices=["f16", "i8"],
+                    help="prefill workload: tensor-core GEMM kind (f16 dequantized operands, or exact int8 for Q4_0)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt length of the decode workload (config 3: 512)")
     ap.add_argument("--shape", default=None, help="gemv workload: ROWSxK weights, one launch each (e.g. 24576x4096)")
     args = ap.parse_args()

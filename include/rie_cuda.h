@@ -64,6 +64,14 @@ RCU_API int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char
 RCU_API void rcu_ctx_destroy(rcu_ctx *ctx);
 RCU_API int32_t rcu_set_stream(rcu_ctx *ctx, void *stream);
 RCU_API int32_t rcu_set_rounding(rcu_ctx *ctx, int32_t mode);
+/* Prefill matmul kernel (batches above 8 tokens; replaces the 4-token / SMMLA tiles of
+ * kernels/mod.rs:234-320 and matmul.rs:178-241). RCU_GEMM_F16 (default): every weight type,
+ * weights dequantized as reference.rs:53-207 defines and activations as d * q of their Q8_0 /
+ * Q8_K blocks, both rounded once to f16, f32 accumulation on the tensor cores. RCU_GEMM_I8:
+ * Q4_0 weights through int8 MMA with the exact per-block int32 sums of reference.rs:221-233
+ * (other types keep the f16 kernel). Both stay within the matmul tolerance of the reference. */
+enum rcu_gemm_kind { RCU_GEMM_F16 = 0, RCU_GEMM_I8 = 1 };
+RCU_API int32_t rcu_set_prefill_gemm(rcu_ctx *ctx, int32_t kind);
 /* Last error message of this context ("" if none). Valid until the next call. */
 RCU_API const char *rcu_last_error(const rcu_ctx *ctx);
 /* Waits for all work on the context stream; returns RCU_ERR_TIMEOUT if any bounded

@@ -27,7 +27,7 @@ from typing import Iterable, Sequence
 from . import _lib
 from ._lib import RcuError, RcuJob
 
-__all__ = ["GgmlType", "ActFormat", "KvType", "Rounding", "Context", "Weight", "QuantActs", "MatmulJob",
+__all__ = ["GgmlType", "ActFormat", "KvType", "Rounding", "PrefillGemm", "Context", "Weight", "QuantActs", "MatmulJob",
            "matmul", "matmul_multi", "matmul_f32_static", "formats_for", "block_sums", "LayerCache", "attention", "turbo", "RcuError"]
 
 
@@ -85,6 +85,11 @@ class Rounding(enum.IntEnum):
     HALF_AWAY = 1     # scalar tier (RIE_DISABLE=simd)
 
 
+class PrefillGemm(enum.IntEnum):
+    F16 = 0  # every weight type: f16-dequantized operands on the tensor cores (default)
+    I8 = 1   # Q4_0: int8 MMA with the exact per-block int32 sums
+
+
 def _check(ctx_ptr, status: int):
     if status != 0:
         msg = _lib.load().rcu_last_error(ctx_ptr) if ctx_ptr else b""
@@ -125,6 +130,9 @@ class Context:
 
     def set_rounding(self, mode: Rounding) -> None:
         _check(self.ptr, self._lib.rcu_set_rounding(self.ptr, int(mode)))
+
+    def set_prefill_gemm(self, kind: "PrefillGemm") -> None:
+        _check(self.ptr, self._lib.rcu_set_prefill_gemm(self.ptr, int(kind)))
 
     def sync(self) -> None:
         _check(self.ptr, self._lib.rcu_sync(self.ptr))

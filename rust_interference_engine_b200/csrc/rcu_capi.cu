@@ -105,6 +105,7 @@ void rcu_ctx_destroy(rcu_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->h_act) cudaFree(ctx->h_act);
     delete ctx;
 }
 
@@ -119,6 +120,13 @@ int32_t rcu_set_rounding(rcu_ctx *ctx, int32_t mode) {
     if (mode != RCU_ROUND_NEAREST_EVEN && mode != RCU_ROUND_HALF_AWAY)
         return set_err(ctx, RCU_ERR_INVALID, "unknown rounding mode");
     ctx->rounding = mode;
+    return RCU_OK;
+}
+
+int32_t rcu_set_prefill_gemm(rcu_ctx *ctx, int32_t kind) {
+    if (!ctx) return RCU_ERR_INVALID;
+    if (kind != RCU_GEMM_F16 && kind != RCU_GEMM_I8) return set_err(ctx, RCU_ERR_INVALID, "unknown prefill GEMM kind");
+    ctx->gemm_i8 = kind == RCU_GEMM_I8;
     return RCU_OK;
 }
 

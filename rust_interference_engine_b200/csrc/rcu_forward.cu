@@ -1190,6 +1190,8 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     const uint64_t T = b->max_batch;
     const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(e, qd), b->ff_max);
     if (int st = rcu_acts_create(ctx, T, kmax, &b->acts)) return fail(st);
+    if (T >= 32)  // prefill batches take the tensor-core GEMM: size its f16 activations now
+        if (int st = gemm_f16_reserve(ctx, T, kmax)) return fail(st);
     bool moe = false;
     for (auto &L : b->layers) moe = moe || L.router;
     if (moe) {  // mixture-of-experts scratch (sizes for the largest batch)

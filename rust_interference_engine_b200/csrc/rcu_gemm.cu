@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "rcu_kernels.h"
+#include "rcu_tc.cuh"
 
 namespace rcu {
 
@@ -57,29 +58,6 @@ struct GemmParams {
     uint32_t *err;
 };
 
-// ---- PTX wrappers (tcgen05 / TMA) ------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(const void *p) {
-    const uint64_t addr = smem_u32(p);
-    uint64_t d = 0;
-    d |= (addr >> 4) & 0x3fffull;        // start address
-    d |= (uint64_t)1 << 16;              // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
-    d |= (uint64_t)1 << 46;              // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;              // SWIZZLE_128B
-    return d;
-}
 // Instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileM >> 3) << 17) |
                             ((uint32_t)(kTileN >> 4) << 24);
@@ -91,30 +69,6 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b) 
         "l"(a), "l"(b), "r"(kIdesc)
         : "memory");
 }
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     uint64_t r;
     asm("fma.rn.f32x2 %0, %1, %2, %3;"
@@ -360,16 +314,14 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-static int make_map_2d(rcu_ctx *ctx, CUtensorMap *m, CUtensorMapDataType dt, uint32_t esize, const void *base,
-                       uint64_t inner, uint64_t outer, uint64_t stride_bytes, uint32_t box_in, uint32_t box_out,
-                       CUtensorMapSwizzle sw) {
+int make_map_2d(rcu_ctx *ctx, CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                uint64_t outer, uint64_t stride_bytes, uint32_t box_in, uint32_t box_out, CUtensorMapSwizzle sw) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return set_err(ctx, RCU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {stride_bytes};
     const cuuint32_t box[2] = {box_in, box_out};
     const cuuint32_t estr[2] = {1, 1};
-    (void)esize;
     const CUresult r = fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_err(ctx, RCU_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -391,13 +343,13 @@ static int launch_type(rcu_ctx *ctx, const ActsView &a, const HostJob &j) {
     p.raw_box = kStageBlocks * BB;  // 144 (Q4_0) or 272 (Q8_0) bytes per row per stage
     p.err = ctx->dev_err;
     CUtensorMap mw, ma, mda;
-    int st = make_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->data, w->row_bytes, w->rows, w->row_bytes,
+    int st = make_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->row_bytes, w->rows, w->row_bytes,
                          p.raw_box, kTileN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.q0, a.k, a.n_tok, a.k, 128, kTileM,
+    st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.q0, a.k, a.n_tok, a.k, 128, kTileM,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = make_map_2d(ctx, &mda, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.d0, a.k / QK, a.n_tok, (uint64_t)(a.k / QK) * 4,
+    st = make_map_2d(ctx, &mda, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.d0, a.k / QK, a.n_tok, (uint64_t)(a.k / QK) * 4,
                      kStageBlocks, kTileM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
     const size_t smem = sizeof(GemmSmem) + 1024;
@@ -419,7 +371,7 @@ static bool gemm_ok(const ActsView &a, const HostJob &j) {
     return a.n_tok >= kGemmMinTok;
 }
 
-int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
+static int launch_gemm_i8(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     if (sizeof(GemmSmem) + 1024 > ctx->max_smem_optin) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: smem");
     for (int i = 0; i < n_jobs; i++)
         if (!gemm_ok(a, jobs[i])) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: type or shape not supported");
@@ -428,6 +380,17 @@ int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
         if (st) return st;
     }
     return RCU_OK;
+}
+
+// Prefill matmul: the f16 tensor-core GEMM (every weight type) by default; the int8 GEMM with
+// exact per-block sums for Q4_0 weights when the context asks for it (rcu_set_prefill_gemm).
+int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
+    if (ctx->gemm_i8) {
+        bool all = true;
+        for (int i = 0; i < n_jobs; i++) all &= gemm_ok(a, jobs[i]);
+        if (all) return launch_gemm_i8(ctx, a, jobs, n_jobs);
+    }
+    return launch_gemm_f16(ctx, a, jobs, n_jobs);
 }
 
 }  // namespace rcu

@@ -30,8 +30,14 @@ struct ArPush {
 };
 int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0, uint32_t n_tok,
                 const ArPush *push = nullptr);
-// Int8 tensor-core GEMM (n_tok > 8). Returns RCU_ERR_UNSUPPORTED for types it lacks.
+// Prefill GEMM on the tensor cores (n_tok > 8). Returns RCU_ERR_UNSUPPORTED for shapes it
+// lacks (the caller then runs GEMV slices). launch_gemm_f16: every weight type, operands
+// dequantized to f16; the int8 kernel (exact per-block sums, Q4_0) when ctx->gemm_i8.
 int launch_gemm(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs);
+int launch_gemm_f16(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs);
+bool gemm_f16_ok(const ActsView &a, const HostJob &j);
+// Sizes the f16 activation scratch for n_tok x k (so a forward never allocates mid-stream).
+int gemm_f16_reserve(rcu_ctx *ctx, uint64_t n_tok, uint64_t k);
 // Exact per-block integer sums of one (row, token) pair.
 int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint64_t row, uint64_t tok,
                       int32_t *out);

@@ -160,3 +160,43 @@ def test_moe_batch_above_eight_tokens(env):
     o = ob.forward(toks, 0, all_logits=True)
     close(g, o, what="13-token MoE batch")
     same_greedy(g, o)
+
+
+# The reference compares two implementations of a quantized forward at 0.03 (tests/model.rs:
+# 302-364): an output that differs in its last bits moves some int8 activation codes of the next
+# layer across a rounding boundary, and through attention one such flip reaches every later
+# token. The f16 tensor-core GEMM rounds its operands (at most 2^-11 relative each, 3e-4 of max
+# |y| on the config-2 GEMM), which flips more codes than f32 summation order does.
+RTOL_GEMM = 0.03
+
+
+@pytest.mark.parametrize("wtype", [O.Q4_K, O.Q4_0, O.Q6_K], ids=["q4_k", "q4_0", "q6_k"])
+def test_prefill_batch_takes_the_gemm(env, wtype):
+    # a 40-token prompt runs its matmuls through the tensor-core GEMM (n_tok >= 32)
+    from rust_interference_engine_b200 import model as M
+    spec = M.SyntheticSpec.tiny("qwen3", wtype)
+    gb, ob, keep = build_pair(env, spec, O.KV_F16, n_ctx=96, max_batch=64)
+    toks = np.random.default_rng(11).integers(0, spec.n_vocab, 40).astype(np.uint32)
+    g = gb.forward(toks, 0, all_logits=True)
+    o = ob.forward(toks, 0, all_logits=True)
+    close(g, o, RTOL_GEMM, "40-token prompt")
+    same_greedy(g, o, RTOL_GEMM)
+    tok = np.array([int(np.argmax(o[-1]))], dtype=np.uint32)
+    close(gb.forward(tok, 40), ob.forward(tok, 40), RTOL_GEMM, "decode after the prompt")
+
+
+def test_prefill_batch_int8_gemm_is_exact(env):
+    # the int8 GEMM keeps the reference's exact per-block sums: the 40-token Q4_0 prompt stays
+    # within the bound of the GEMV path
+    torch, rie, M, ctx = env
+    spec = M.SyntheticSpec.tiny("qwen3", O.Q4_0)
+    ctx.set_prefill_gemm(rie.PrefillGemm.I8)
+    try:
+        gb, ob, keep = build_pair(env, spec, O.KV_F16, n_ctx=96, max_batch=64)
+        toks = np.random.default_rng(11).integers(0, spec.n_vocab, 40).astype(np.uint32)
+        g = gb.forward(toks, 0, all_logits=True)
+    finally:
+        ctx.set_prefill_gemm(rie.PrefillGemm.F16)
+    o = ob.forward(toks, 0, all_logits=True)
+    close(g, o, 2e-3, "40-token prompt, int8 GEMM")
+    same_greedy(g, o)

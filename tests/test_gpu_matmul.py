@@ -182,6 +182,51 @@ def test_prefill_gemm_q4_0(env, n_tok, rows, k):
     close(got, want)
 
 
+ALL_TYPES = [O.Q4_0, O.Q4_1, O.Q5_0, O.Q5_1, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K]
+
+
+@pytest.mark.parametrize("t", ALL_TYPES, ids=[O.TYPE_NAMES[t] for t in ALL_TYPES])
+@pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 2048), (65, 333, 4096), (130, 1000, 2048), (300, 129, 4096)])
+def test_prefill_gemm_f16_all_types(env, t, n_tok, rows, k):
+    # f16 tensor-core GEMM (n_tok >= 32): ragged row and token tiles (64/128/192/256 tokens
+    # per CTA), every weight type dequantized in shared memory
+    rng = O.Rng(2000 + 7 * t + n_tok + rows)
+    w = rng.weight(t, rows, k)
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    got = gpu_matmul(env, [(t, w, k)], x)[0][0]
+    want = O.matmul_multi(x, [(t, w, k)], n_threads=8)[0]
+    close(got, want)
+
+
+def test_prefill_gemm_f16_jobs_share_a_launch(env):
+    # q/k/v-like jobs of one type share a launch; a second type and format follow
+    rng = O.Rng(77)
+    k, n_tok = 4096, 96
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    ws = [(O.Q4_K, rng.weight(O.Q4_K, r, k), k) for r in (512, 128, 128)]
+    ws += [(O.Q6_K, rng.weight(O.Q6_K, 256, k), k), (O.Q8_0, rng.weight(O.Q8_0, 200, k), k)]
+    got = gpu_matmul(env, ws, x)[0]
+    want = O.matmul_multi(x, ws, n_threads=8)
+    for g, wv in zip(got, want):
+        close(g, wv)
+
+
+@pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 512), (128, 256, 4096)])
+def test_prefill_gemm_q4_0_int8_kind(env, n_tok, rows, k):
+    # the int8 GEMM (exact per-block sums) stays selectable for Q4_0
+    torch, rie, ctx = env
+    rng = O.Rng(3000 + n_tok + rows)
+    w = rng.weight(O.Q4_0, rows, k)
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    ctx.set_prefill_gemm(rie.PrefillGemm.I8)
+    try:
+        got = gpu_matmul(env, [(O.Q4_0, w, k)], x)[0][0]
+    finally:
+        ctx.set_prefill_gemm(rie.PrefillGemm.F16)
+    want = O.matmul_multi(x, [(O.Q4_0, w, k)], n_threads=8)[0]
+    close(got, want)
+
+
 def test_prefill_gemm_config2(env):
     # M = 512 tokens x K = 4096, N = 4096 and 14336, W ~ N(0, 0.02) -> Q4_0
     rng = np.random.default_rng(2)
