@@ -440,6 +440,7 @@ def run_prefill(args, world, rank, local):
 QWEN3_8B = dict(arch="qwen3", n_vocab=151936, n_embd=4096, n_layer=36, n_head=32, n_head_kv=8, head_dim=128,
                 n_ff=12288, rope_dim=128, rope_base=1_000_000.0, rms_eps=1e-6)
 DEC_PROMPT = 512  # config 3: 512-token prompt (--prompt changes it, e.g. for a short profile)
+DEC_BATCH = 512   # prompt tokens per forward (the reference's --batch / n_batch; its CLI default is 64)
 
 
 def qwen3_8b_spec(n_layer=None):
@@ -514,15 +515,16 @@ def run_decode(args, world, rank, local):
     t_build = time.perf_counter() - t_build
     n_gen = max(args.warmup, 3) + args.steps
     n_ctx = DEC_PROMPT + n_gen + 1
-    be = M.CudaBackend(model, n_ctx, 64, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
+    nb = DEC_BATCH
+    be = M.CudaBackend(model, n_ctx, nb, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
     prompt = np.random.default_rng(4).integers(0, spec.n_vocab, DEC_PROMPT).astype(np.uint32)
     gen_tokens = torch.from_numpy(np.random.default_rng(5).integers(0, spec.n_vocab, n_gen).astype(np.int32)).cuda()
     logits = torch.zeros(spec.n_vocab, device="cuda")
     prompt_d = torch.from_numpy(prompt.astype(np.int32)).cuda()
 
     def prefill():
-        for p0 in range(0, DEC_PROMPT, 64):  # Engine::eval_tokens chunks at n_batch (engine.rs:263-269)
-            be.forward_device(prompt_d[p0:], min(64, DEC_PROMPT - p0), p0, logits)
+        for p0 in range(0, DEC_PROMPT, nb):  # Engine::eval_tokens chunks at n_batch (engine.rs:263-269)
+            be.forward_device(prompt_d[p0:], min(nb, DEC_PROMPT - p0), p0, logits)
 
     prefill()  # warm: kernel attributes, L2
     torch.cuda.synchronize()
@@ -553,9 +555,9 @@ def run_decode(args, world, rank, local):
     finite = bool(torch.isfinite(logits).all())
 
     # e2e: the host API (Backend::forward), token in and logits out through host memory
-    be2 = M.CudaBackend(model, n_ctx, 64, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
-    for p0_ in range(0, DEC_PROMPT, 64):
-        be2.forward(prompt[p0_:p0_ + 64], p0_, False)
+    be2 = M.CudaBackend(model, n_ctx, nb, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
+    for p0_ in range(0, DEC_PROMPT, nb):
+        be2.forward(prompt[p0_:p0_ + nb], p0_, False)
     pos2, tok = DEC_PROMPT, np.array([1], dtype=np.uint32)
     for i in range(max(args.warmup, 3)):
         be2.forward(tok, pos2)
@@ -608,7 +610,7 @@ def run_decode(args, world, rank, local):
                    "l2": "inputs larger than L2 (4.9 GB of weights streamed per token)",
                    "parallelism": f"tp{world} (NCCL all-reduce of Wo/down, all-gather of logits)" if world > 1
                    else "tp1", "decode": "CUDA graph replay per token",
-                   "pp_tok_s": pp_tps, "model_build_s": t_build},
+                   "pp_tok_s": pp_tps, "prefill_batch": nb, "model_build_s": t_build},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_gate_up"),
                      "kernel": "k_gemv<1,16> (gate+up, 2 x 12288 x 4096 Q4_K)", "bytes_per_launch": gemv_bytes,
@@ -987,10 +989,11 @@ def main():
                     help="GGUF type of the gemv workload (config 1 is Q4_0)")
     ap.add_argument("--gemm", default="f16", choices=["f16", "i8"],
                     help="prefill workload: tensor-core GEMM kind (f16 dequantized operands, or exact int8 for Q4_0)")
+    ap.add_argument("--batch", type=int, default=512, help="decode workload: prompt tokens per forward (n_batch)")
     ap.add_argument("--prompt", type=int, default=512, help="prompt length of the decode workload (config 3: 512)")
     ap.add_argument("--shape", default=None, help="gemv workload: ROWSxK weights, one launch each (e.g. 24576x4096)")
     args = ap.parse_args()
-    global GEMV_TYPE, DEC_PROMPT, GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_EACH, GEMV_DISTINCT
+    global GEMV_TYPE, DEC_PROMPT, DEC_BATCH, GEMV_ROWS, GEMV_K, GEMV_COPIES, GEMV_EACH, GEMV_DISTINCT
     GEMV_TYPE = args.wtype
     if args.shape:
         GEMV_ROWS, GEMV_K = (int(v) for v in args.shape.lower().split("x"))
@@ -999,6 +1002,7 @@ def main():
         GEMV_DISTINCT = max(1, min(GEMV_DISTINCT, 800_000_000 // (GEMV_ROWS * GEMV_K * 4)))  # host f32 draft
         GEMV_EACH = True
     DEC_PROMPT = args.prompt
+    DEC_BATCH = args.batch
     META["gemv"] = gemv_meta()
     world, rank, local = dist_init()
 

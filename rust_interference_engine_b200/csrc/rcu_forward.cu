@@ -1226,8 +1226,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
         b->fused_merge = b->fused_merge &&
                          attention_fused_merge_ok(c.n_head, c.n_head_kv, c.head_dim, act_format(b->layers[il].wo->type));
         const uint64_t window = b->layers[il].swa ? c.swa_window : 0;
-        scratch = std::max<uint64_t>(scratch, attention_scratch_bytes(b->kv[il], T, c.n_head,
-                                                                      attention_max_splits(b->kv[il], window)));
+        scratch = std::max<uint64_t>(scratch, attention_scratch_bytes_upto(ctx, b->kv[il], T, c.n_head, window));
     }
     if (int st = dalloc(b, (void **)&b->attn_scratch, scratch)) return fail(st);
     RCU_CUDA_TRY(ctx, cudaMemset(b->attn_scratch, 0, scratch));  // attention completion counters

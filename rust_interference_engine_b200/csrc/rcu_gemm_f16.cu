@@ -17,16 +17,19 @@
 //               map over [rows][row_bytes] in 16-bit elements), and f16 activation tiles of K 64
 //               (128B-swizzled, K-major) per operand stage;
 //   * warp 1    TMEM owner and MMA issuer: 4 x tcgen05.mma.kind::f16 (M = 128, N = NT, K = 16)
-//               per operand stage into one f32 accumulator of NT columns;
-//   * warps 2-9 dequantize: two threads per weight row, 32 values each per operand stage,
-//               written as f16 into the canonical 128B-swizzled K-major layout; after the last
-//               stage the same warps read the accumulator (tcgen05.ld) and store Y.
+//               per operand stage, weights (A) read from tensor memory, activations (B) from
+//               shared memory, into one f32 accumulator of NT TMEM columns;
+//   * warps 2-17 dequantize: four threads per weight row, 16 values each per operand stage,
+//               stored as packed f16 pairs into the stage's TMEM columns (tcgen05.st, lane =
+//               weight row), which keeps the weight operand off the shared-memory port; after
+//               the last stage the same warps read the accumulator (tcgen05.ld) and store Y.
 // Up to kF16MaxJobs weights sharing the activations (q/k/v, gate/up) run in one launch: the
 // grid's x dimension walks the row tiles of each job in turn.
 // All waits are bounded; TMEM is freed on every exit path.
 #include <cuda.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
@@ -36,16 +39,17 @@ namespace rcu {
 
 constexpr int kHRows = 128;        // weight rows per CTA (MMA M)
 constexpr int kHMaxTok = 256;      // tokens per CTA at most (MMA N)
-constexpr int kHStages = 3;        // operand stages (K 64 each)
+constexpr int kHStages = 4;        // operand stages (K 64 each)
+constexpr int kHAccCols = 256;     // TMEM columns of the f32 accumulator (one per token)
+constexpr int kHTmemCols = 512;    // accumulator + kHStages weight stages of 32 columns
 constexpr int kHRawStages = 2;     // raw GGUF stages (K 256 each)
 constexpr int kHRawMax = 272;      // raw bytes per row per stage at most (Q8_0: 8 x 34)
-constexpr int kHUnpackWarps = 8;
+constexpr int kHUnpackWarps = 16;  // 4 threads per weight row, 16 values each per stage
 constexpr int kHThreads = (2 + kHUnpackWarps) * 32;
 constexpr int kF16MaxJobs = 4;
 constexpr uint32_t kF16MinTok = 32;  // below this the 8-token GEMV slices are used
 
 struct HSmem {
-    uint8_t a[kHStages][kHRows * 128];      // f16 weights, 8 rows x 128 B swizzle atoms
     uint8_t b[kHStages][kHMaxTok * 128];    // f16 activations (TMA, 128B swizzle)
     uint8_t raw[kHRawStages][kHRows * kHRawMax];
     uint64_t raw_full[kHRawStages], raw_empty[kHRawStages];
@@ -64,6 +68,7 @@ struct HMaps {
 };
 struct HParams {
     HJob job[kF16MaxJobs];
+    const float *tok_scale;  // [n_tok] power of two that undoes the activation row's f16 scaling
     uint32_t n_jobs, k, n_tok, nt, idesc;
     int early;  // weights may be loaded before the grid dependency wait
     uint32_t *err;
@@ -74,96 +79,199 @@ template <int TYPE>
 constexpr uint32_t unit_bytes_c() {  // bytes of 256 values of K
     return TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : TYPE == T_Q6_K ? 210 : 8 * blk_bytes_c<TYPE>();
 }
-// Raw stage box per row: Q6_K superblocks (210 B) start on even, not 16-byte, offsets, so its
+// Raw stage box per row. Q6_K superblocks (210 B) start on even, not 16-byte, offsets, so its
 // box starts at the 16-byte boundary below and is wide enough for any start within 16 bytes.
+// Every box is an odd number of 16-byte chunks (Q4_1 and Q5_1 rows carry one spare chunk):
+// 8 consecutive rows then start in 8 different bank groups, so the 16-byte reads of a warp's
+// 8-lane phases are conflict-free.
 template <int TYPE>
 constexpr uint32_t raw_box_c() {
-    return TYPE == T_Q6_K ? 240 : unit_bytes_c<TYPE>();
+    return TYPE == T_Q6_K ? 240 : TYPE == T_Q4_1 ? 176 : TYPE == T_Q5_1 ? 208 : unit_bytes_c<TYPE>();
 }
+static_assert(raw_box_c<T_Q4_0>() % 32 == 16 && raw_box_c<T_Q4_1>() % 32 == 16 && raw_box_c<T_Q5_0>() % 32 == 16 &&
+                  raw_box_c<T_Q5_1>() % 32 == 16 && raw_box_c<T_Q8_0>() % 32 == 16 &&
+                  raw_box_c<T_Q4_K>() % 32 == 16 && raw_box_c<T_Q5_K>() % 32 == 16 && raw_box_c<T_Q6_K>() % 32 == 16,
+              "raw rows must be an odd number of 16-byte chunks");
 
-// Byte b of w as the exact float (byte - bias): the byte is placed in the mantissa of 2^23.
-__device__ __forceinline__ float bytef(uint32_t w, uint32_t b, float c0) {
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | b)) - c0;
+// ---- 16 values of one row as 8 packed f16 pairs ---------------------------------------------
+// 32-value block types: each code byte becomes the f16 1024 + code (byte placed in the mantissa
+// of 0x6400), one subtraction makes the code exact, one f16 multiply (or fma with the min) by the
+// f16 block scale rounds once: the same value as the f32 product rounded to f16.
+// K-quants: the code becomes the f32 2^23 + code, an f32x2 add makes it exact, an f32x2 fma with
+// d*sc (exact in f32) and -dmin*m rounds once in f32, and the pair is rounded to f16.
+__device__ __forceinline__ uint32_t h2_pair(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, __half2 b) {
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&a), b);
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, __half2 b) {
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a), b);
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, __half2 b, __half2 c) {
+    const __half2 r = __hfma2(*reinterpret_cast<const __half2 *>(&a), b, c);
+    return *reinterpret_cast<const uint32_t *>(&r);
 }
 __device__ __forceinline__ uint32_t h2u(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t *>(&h);
 }
-
-// Values [32 j, 32 j + 32) of the 256-value unit that starts `ofs` bytes into `row` (a 16-byte
-// aligned row of a raw stage), dequantized as reference.rs:53-207 defines them.
-template <int TYPE>
-__device__ __forceinline__ void dq32(const uint8_t *row, uint32_t ofs, uint32_t j, float (&v)[32]) {
-    if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1 || TYPE == T_Q5_0 || TYPE == T_Q5_1 || TYPE == T_Q8_0) {
-        BlkW b;
-        dec_blk<TYPE>(row, j * blk_bytes_c<TYPE>(), b);
-        constexpr float bias = TYPE == T_Q4_0 ? 8.0f : TYPE == T_Q5_0 ? 16.0f : TYPE == T_Q8_0 ? 128.0f : 0.0f;
-        constexpr float c0 = 8388608.0f + bias;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            uint32_t w = b.v[i];
-            if ((TYPE == T_Q4_0 || TYPE == T_Q4_1) && i >= 4) w >>= 4;  // 16 x high nibble -> nibble
-            if (TYPE == T_Q8_0) w ^= 0x80808080u;                        // int8 -> q + 128
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float q = bytef(w, e, c0);
-                v[4 * i + e] = (TYPE == T_Q4_1 || TYPE == T_Q5_1) ? fmaf(q, b.d, b.m) : q * b.d;
-            }
-        }
-    } else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        // d, dmin, 12 scale bytes, [Q5_K: qh 32 B], qs 128 B (reference.rs:153-189)
-        const uint32_t *w = reinterpret_cast<const uint32_t *>(row);
-        const uint32_t h0 = w[0];
-        // get_scale_min_k4 (reference.rs:8-14) with a runtime j and no indexed array
-        const uint32_t sh = 8 * (j & 3);
-        const uint32_t b0 = (w[1] >> sh) & 0xffu, b1 = (w[2] >> sh) & 0xffu, b2 = (w[3] >> sh) & 0xffu;
-        const uint32_t sc = j < 4 ? b0 & 63u : (b2 & 0xFu) | ((b0 >> 6) << 4);
-        const uint32_t mn = j < 4 ? b1 & 63u : (b2 >> 4) | ((b1 >> 6) << 4);
-        const float ds = f16_bits_to_f32(h0) * (float)sc, dm = f16_bits_to_f32(h0 >> 16) * (float)mn;
-        constexpr uint32_t qs_word = TYPE == T_Q4_K ? 4 : 12;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t qw = w[qs_word + 8 * (j >> 1) + i];
-            uint32_t q = (j & 1) ? (qw >> 4) & 0x0F0F0F0Fu : qw & 0x0F0F0F0Fu;
-            if (TYPE == T_Q5_K) q |= ((w[4 + i] >> j) & 0x01010101u) << 4;  // bit j of qh[l]
-#pragma unroll
-            for (int e = 0; e < 4; e++) v[4 * i + e] = fmaf(bytef(q, e, 8388608.0f), ds, -dm);
-        }
-    } else {  // Q6_K: ql 128 B, qh 64 B, 16 int8 scales, d (reference.rs:190-207)
-        const uint32_t n = j >> 2, jj = j & 3;
-        uint32_t ql[8], qh[8];
-        ld_words<8>(row, ofs + 64 * n + 32 * (jj & 1), ql);
-        ld_words<8>(row, ofs + 128 + 32 * n, qh);
-        const float d = __half2float(*reinterpret_cast<const __half *>(row + ofs + 208));
-        const float ds0 = d * (float)(int8_t)row[ofs + 192 + 8 * n + 2 * jj];
-        const float ds1 = d * (float)(int8_t)row[ofs + 193 + 8 * n + 2 * jj];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t lo = jj < 2 ? ql[i] & 0x0F0F0F0Fu : (ql[i] >> 4) & 0x0F0F0F0Fu;
-            const uint32_t q = lo | (((qh[i] >> (2 * jj)) & 0x03030303u) << 4);
-#pragma unroll
-            for (int e = 0; e < 4; e++) v[4 * i + e] = bytef(q, e, 8388608.0f + 32.0f) * (i < 4 ? ds0 : ds1);
-        }
-    }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&r);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)),
+          "l"(*reinterpret_cast<uint64_t *>(&c)));
+    return *reinterpret_cast<float2 *>(&r);
+}
+// Bytes (e, e+1) of w (codes 0..255) as the f32 pair 2^23 + code.
+__device__ __forceinline__ float2 magic2(uint32_t w, uint32_t e) {
+    return make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | e)),
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (e + 1))));
 }
 
-// 32 f16 values of row r as 16-byte chunks c0..c0+3 of a 128B-swizzled K-major tile.
-__device__ __forceinline__ void store_chunks(uint8_t *tile, uint32_t r, uint32_t c0, const float (&v)[32]) {
-    uint8_t *rowp = tile + r * 128;
+// 4 code words (16 codes, byte order = value order) -> 8 f16 pairs, w = (code - bias) * d [+ m].
+template <bool MIN>
+__device__ __forceinline__ void codes_f16(const uint32_t (&c)[4], float bias, float d, float m, uint32_t (&o)[8]) {
+    const __half2 b2 = __float2half2_rn(1024.0f + bias), d2 = __float2half2_rn(d), m2 = __float2half2_rn(m);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint4 q = make_uint4(h2u(v[8 * i], v[8 * i + 1]), h2u(v[8 * i + 2], v[8 * i + 3]),
-                                   h2u(v[8 * i + 4], v[8 * i + 5]), h2u(v[8 * i + 6], v[8 * i + 7]));
-        *reinterpret_cast<uint4 *>(rowp + (((c0 + i) ^ (r & 7)) << 4)) = q;
+        const uint32_t lo = h2_sub(h2_pair(c[i], 0x5140u), b2), hi = h2_sub(h2_pair(c[i], 0x7362u), b2);
+        o[2 * i] = MIN ? h2_fma(lo, d2, m2) : h2_mul(lo, d2);
+        o[2 * i + 1] = MIN ? h2_fma(hi, d2, m2) : h2_mul(hi, d2);
+    }
+}
+// 4 code words -> 8 f16 pairs, w = fma(code - bias, ds, -dm) in f32 (K-quants).
+__device__ __forceinline__ void codes_f32(const uint32_t (&c)[4], float bias, float ds, float dm, uint32_t (&o)[8]) {
+    const float2 nb = make_float2(-8388608.0f - bias, -8388608.0f - bias), s2 = make_float2(ds, ds),
+                 m2 = make_float2(-dm, -dm);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 a = fma2(add2(magic2(c[i], 0), nb), s2, m2), b = fma2(add2(magic2(c[i], 2), nb), s2, m2);
+        o[2 * i] = h2u(a.x, a.y);
+        o[2 * i + 1] = h2u(b.x, b.y);
     }
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+// N words starting at the even byte offset `off` of a 16-byte aligned shared-memory row, read as
+// the 16-byte chunks around them. With `off` known at compile time the selects fold away.
+template <int N>
+__device__ __forceinline__ void ldw16(const uint8_t *row, uint32_t off, uint32_t (&out)[N]) {
+    constexpr int M = (4 * N + 14 + 15) / 16;  // chunks covering any even start within a chunk
+    static_assert(4 * M >= N + 4, "chunk window");
+    const uint4 *p = reinterpret_cast<const uint4 *>(row + (off & ~15u));
+    uint32_t r[4 * M];
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        const uint4 v = p[m];
+        r[4 * m] = v.x, r[4 * m + 1] = v.y, r[4 * m + 2] = v.z, r[4 * m + 3] = v.w;
+    }
+    const uint32_t k = (off >> 2) & 3u, sh = (off & 3u) * 8u;
+    uint32_t t[N + 1];
+#pragma unroll
+    for (int i = 0; i <= N; i++) {
+        const uint32_t a = (k & 2u) ? r[i + 2] : r[i], b = (k & 2u) ? r[i + 3] : r[i + 1];
+        t[i] = (k & 1u) ? b : a;
+    }
+#pragma unroll
+    for (int i = 0; i < N; i++) out[i] = __funnelshift_r(t[i], t[i + 1], sh);
+}
+
+// Values [32 J + 16 h, +16) of the 256-value unit that starts `ofs` bytes into `row` (a 16-byte
+// aligned row of a raw stage), dequantized as reference.rs:53-207 defines them, as f16 pairs.
+template <int TYPE, int J>
+__device__ __forceinline__ void dq16(const uint8_t *row, uint32_t ofs, uint32_t h, uint32_t (&o)[8]) {
+    uint32_t c[4];
+    if constexpr (TYPE == T_Q4_0) {  // d, qs[16]: low nibbles = values 0..15, high = 16..31
+        uint32_t w[5];
+        ldw16<5>(row, J * 18, w);
+#pragma unroll
+        for (int i = 0; i < 4; i++) c[i] = (__funnelshift_r(w[i], w[i + 1], 16) >> (4 * h)) & 0x0F0F0F0Fu;
+        codes_f16<false>(c, 8.0f, f16_bits_to_f32(w[0]), 0.0f, o);
+    } else if constexpr (TYPE == T_Q8_0) {  // d, qs[32] int8
+        uint32_t d[1];
+        ldw16<1>(row, J * 34, d);
+        ldw16<4>(row, J * 34 + 2 + 16 * h, c);
+#pragma unroll
+        for (int i = 0; i < 4; i++) c[i] ^= 0x80808080u;
+        codes_f16<false>(c, 128.0f, f16_bits_to_f32(d[0]), 0.0f, o);
+    } else if constexpr (TYPE == T_Q5_0) {  // d, qh (u32), qs[16]; bit l of qh is the 5th bit of value l
+        uint32_t w[6];
+        ldw16<6>(row, J * 22, w);
+        const uint32_t qh = __funnelshift_r(w[0], w[1], 16);
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            c[i] = ((__funnelshift_r(w[1 + i], w[2 + i], 16) >> (4 * h)) & 0x0F0F0F0Fu) |
+                   spread4_bit4(qh >> (16 * h + 4 * i));
+        codes_f16<false>(c, 16.0f, f16_bits_to_f32(w[0]), 0.0f, o);
+    } else if constexpr (TYPE == T_Q4_1 || TYPE == T_Q5_1) {  // d, m, [qh], qs[16]
+        constexpr int Q = TYPE == T_Q4_1 ? 1 : 2;
+        uint32_t w[4 + Q];
+        ldw16<4 + Q>(row, J * blk_bytes_c<TYPE>(), w);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            c[i] = (w[Q + i] >> (4 * h)) & 0x0F0F0F0Fu;
+            if (TYPE == T_Q5_1) c[i] |= spread4_bit4(w[1] >> (16 * h + 4 * i));
+        }
+        codes_f16<true>(c, 0.0f, f16_bits_to_f32(w[0]), f16_bits_to_f32(w[0] >> 16), o);
+    } else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        // d, dmin, 12 scale bytes, [Q5_K: qh 32 B], qs 128 B (reference.rs:153-189); sub-block J
+        const uint4 hd = *reinterpret_cast<const uint4 *>(row);
+        // get_scale_min_k4 (reference.rs:8-14)
+        constexpr uint32_t sh = 8 * (J & 3);
+        const uint32_t b0 = (hd.y >> sh) & 0xffu, b1 = (hd.z >> sh) & 0xffu, b2 = (hd.w >> sh) & 0xffu;
+        const uint32_t sc = J < 4 ? b0 & 63u : (b2 & 0xFu) | ((b0 >> 6) << 4);
+        const uint32_t mn = J < 4 ? b1 & 63u : (b2 >> 4) | ((b1 >> 6) << 4);
+        const float ds = f16_bits_to_f32(hd.x) * (float)sc, dm = f16_bits_to_f32(hd.x >> 16) * (float)mn;
+        constexpr uint32_t qs_off = TYPE == T_Q4_K ? 16 : 48;
+        const uint4 q = *reinterpret_cast<const uint4 *>(row + qs_off + 32 * (J >> 1) + 16 * h);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        uint4 hb = make_uint4(0, 0, 0, 0);
+        if (TYPE == T_Q5_K) hb = *reinterpret_cast<const uint4 *>(row + 16 + 16 * h);  // qh[16h..16h+16)
+        const uint32_t hw[4] = {hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            c[i] = ((J & 1) ? qw[i] >> 4 : qw[i]) & 0x0F0F0F0Fu;
+            if (TYPE == T_Q5_K) c[i] |= ((hw[i] >> J) & 0x01010101u) << 4;  // bit J of qh[l]
+        }
+        codes_f32(c, 0.0f, ds, dm, o);
+    } else {  // Q6_K: ql 128 B, qh 64 B, 16 int8 scales, d (reference.rs:190-207); group J
+        constexpr uint32_t n = J >> 2, jj = J & 3;
+        uint32_t ql[4], qh[4], sd[5];
+        ldw16<4>(row, ofs + 64 * n + 32 * (jj & 1) + 16 * h, ql);
+        ldw16<4>(row, ofs + 128 + 32 * n + 16 * h, qh);
+        ldw16<5>(row, ofs + 192, sd);  // scales[16], d
+        const uint32_t si = 8 * n + 2 * jj;  // scale of values l < 16; l >= 16 uses si + 1
+        const int sc = (int)(int8_t)(__funnelshift_r(sd[si >> 2], sd[(si >> 2) + 1], 8 * (si & 3) + 8 * h) & 0xffu);
+        const float ds = f16_bits_to_f32(sd[4]) * (float)sc;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            c[i] = (jj < 2 ? ql[i] & 0x0F0F0F0Fu : (ql[i] >> 4) & 0x0F0F0F0Fu) |
+                   (((qh[i] >> (2 * jj)) & 0x03030303u) << 4);
+        codes_f32(c, 32.0f, ds, 0.0f, o);
+    }
+}
+
+// D[tmem] (+)= A[tmem] * B[smem descriptor]^T: the weights come from tensor memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, bool acc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc)
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"((uint32_t)acc)
         : "memory");
+}
+// 8 columns of this warp's 32 TMEM lanes, one 32-bit register per column and thread.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 // Every lane of the warp waits; the warp gives up together if any lane timed out.
@@ -199,7 +307,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
         mbar_init(&S.acc_full, 1);
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc<kHMaxTok>(&S.tmem_base);
+    if (warp == 1) tmem_alloc<kHTmemCols>(&S.tmem_base);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -254,48 +362,66 @@ __global__ void __launch_bounds__(kHThreads, 1)
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++)
-                    mma_f16(tmem, sw128_desc(S.a[s] + 32 * kk), sw128_desc(S.b[s] + 32 * kk), p.idesc, (it | kk) != 0);
+                    mma_f16_ts(tmem, tmem + kHAccCols + 32 * s + 8 * kk, sw128_desc(S.b[s] + 32 * kk), p.idesc,
+                               (it | kk) != 0);
                 mma_commit(&S.ab_empty[s]);
             }
             mma_commit(&S.acc_full);  // also on an early exit: tracks every MMA issued
         }
-    } else {  // ---- dequantize, then epilogue (warps 2-9) ----
-        const uint32_t ut = threadIdx.x - 64, r = ut & (kHRows - 1), h = ut / kHRows;
+    } else {  // ---- dequantize, then epilogue (warps 2-17) ----
+        // a warp may only reach TMEM lanes 32 (warp % 4) .. +31: warp (q, part) dequantizes rows
+        // 32 q .. 32 q + 31, values [16 part, +16) of every operand stage
+        const uint32_t q = warp & 3, part = (warp - 2) >> 2, r = 32 * q + lane;
+        static_assert(kHStages == 4, "one unit of K 256 = kHStages operand stages");
+        const uint32_t rh = part & 1;  // which half of its 32-value group this thread dequantizes
         bool ok = true;
-        for (uint32_t it = 0; it < n_it; it++) {
-            const uint32_t u = it >> 2, g = it & 3, rs = u % kHRawStages, s = it % kHStages;
-            if (g == 0 && !warp_wait(&S.raw_full[rs], (u / kHRawStages) & 1, p.err, ERR_TIMEOUT_FULL)) {
+        for (uint32_t u = 0; u < n_unit && ok; u++) {
+            const uint32_t rs = u % kHRawStages, ofs = (u * UB) & 15u;
+            if (!warp_wait(&S.raw_full[rs], (u / kHRawStages) & 1, p.err, ERR_TIMEOUT_FULL)) {
                 ok = false;
                 break;
             }
-            if (it >= kHStages && !warp_wait(&S.ab_empty[s], ((it / kHStages) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-                ok = false;
-                break;
-            }
-            float v[32];
-            dq32<TYPE>(S.raw[rs] + r * BOX, (u * UB) & 15u, 2 * g + h, v);
-            store_chunks(S.a[s], r, 4 * h, v);
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&S.a_full[s]);
-                if (g == 3) mbar_arrive(&S.raw_empty[rs]);
-            }
+            const uint8_t *rrow = S.raw[rs] + r * BOX;
+            // operand stage G of this unit (values [64 G, +64)); G is a compile-time constant so
+            // that the 32-value group index and its byte offsets are too
+            auto stage = [&](auto gc) -> bool {
+                constexpr int G = decltype(gc)::value;
+                if (u > 0 && !warp_wait(&S.ab_empty[G], (u - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) return false;
+                tc_fence_after();  // the MMA that read this weight stage has completed
+                uint32_t o[8];
+                if (part >> 1)  // warp-uniform
+                    dq16<TYPE, 2 * G + 1>(rrow, ofs, rh, o);
+                else
+                    dq16<TYPE, 2 * G>(rrow, ofs, rh, o);
+                // K values [16 part, +16) of this stage: 8 columns of packed f16 pairs, lane = row
+                tmem_st8(tmem + ((32 * q) << 16) + kHAccCols + 32 * G + 8 * part, o);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&S.a_full[G]);
+                    if (G == 3) mbar_arrive(&S.raw_empty[rs]);
+                }
+                return true;
+            };
+            ok = stage(std::integral_constant<int, 0>{}) && stage(std::integral_constant<int, 1>{}) &&
+                 stage(std::integral_constant<int, 2>{}) && stage(std::integral_constant<int, 3>{});
         }
         pdl_wait();  // the output may still be read by the kernel before this one
         if (ok && warp_wait(&S.acc_full, 0, p.err, ERR_TIMEOUT_FULL)) {
             tc_fence_after();
-            const uint32_t q = warp & 3, hh = (warp - 2) >> 2, half = p.nt / 2;
-            const uint32_t n = n0 + 32 * q + lane;
-            for (uint32_t c = hh * half; c < (hh + 1) * half; c += 32) {
-                uint32_t x[32];
-                tmem_ld32(tmem + ((32 * q) << 16) + c, x);
+            // the four warps of a lane quarter split the accumulator columns
+            const uint32_t span = p.nt / (kHUnpackWarps / 4);
+            const uint32_t n = n0 + r;
+            for (uint32_t c = part * span; c < (part + 1) * span; c += 16) {
+                uint32_t x[16];
+                tmem_ld16(tmem + ((32 * q) << 16) + c, x);
                 tmem_wait_ld();
                 if (n < jb.rows) {
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
+                    for (int e = 0; e < 16; e++) {
                         const uint32_t m = m0 + c + e;
-                        if (m < p.n_tok) jb.out[(uint64_t)m * jb.ld + n] = __uint_as_float(x[e]);
+                        if (m < p.n_tok) jb.out[(uint64_t)m * jb.ld + n] = __uint_as_float(x[e]) * p.tok_scale[m];
                     }
                 }
             }
@@ -310,27 +436,52 @@ __global__ void __launch_bounds__(kHThreads, 1)
         if (lane == 0) mbar_wait_bounded(&S.acc_full, 0, p.err, ERR_TIMEOUT_DRAIN);
         __syncwarp();
         tc_fence_after();
-        tmem_free<kHMaxTok>(tmem);
+        tmem_free<kHTmemCols>(tmem);
     }
 }
 
-// A[t][k] = f16(d_a * q_a) of the prepared Q8_0 or Q8_K activations (8 values per thread).
-__global__ void k_acts_f16(const ActsView a, uint32_t fmt, __half *__restrict__ out) {
+// A[t][k] = f16(d_a * q_a * 2^-e_t) of the prepared Q8_0 or Q8_K activations, one CTA per token
+// row. e_t >= 0 is the smallest power that keeps the row's largest value (127 * max |d_a|) within
+// 2^15, so that no value overflows f16 (activations of some models reach 1e5); tok_scale[t] = 2^e_t
+// is multiplied back, exactly, in the GEMM epilogue. Rows already in range are unchanged.
+constexpr int kActsF16Threads = 256;
+__global__ void __launch_bounds__(kActsF16Threads) k_acts_f16(const ActsView a, uint32_t fmt, __half *__restrict__ out,
+                                                              float *__restrict__ tok_scale) {
     pdl_wait();
     pdl_trigger();
-    const uint64_t n8 = (uint64_t)a.n_tok * a.k / 8;
-    const int8_t *qs = fmt == RCU_ACT_Q8_0 ? a.q0 : a.qk;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t e0 = i * 8, t = e0 / a.k;
-        const uint32_t kk = (uint32_t)(e0 - t * a.k);
-        const uint2 c = *reinterpret_cast<const uint2 *>(qs + e0);
-        const float d = fmt == RCU_ACT_Q8_0 ? a.d0[t * (a.k / QK) + kk / QK] : a.dk[t * (a.k / QK_K) + kk / QK_K];
+    __shared__ float red[kActsF16Threads / 32];
+    const uint32_t t = blockIdx.x, tid = threadIdx.x;
+    const bool q0 = fmt == RCU_ACT_Q8_0;
+    const uint32_t bs = q0 ? QK : QK_K, nb = a.k / bs;
+    const float *dr = (q0 ? a.d0 : a.dk) + (uint64_t)t * nb;
+    float mx = 0.0f;
+    for (uint32_t b = tid; b < nb; b += kActsF16Threads) mx = fmaxf(mx, fabsf(dr[b]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kActsF16Threads / 32; w++) mx = fmaxf(mx, red[w]);
+    // e = max(0, ceil(log2(127 * mx / 2^15))), from the exponent of the (finite) bound
+    const float amax = 127.0f * mx;
+    int e = 0;
+    if (amax > 32768.0f) {
+        const int ex = (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127;  // amax in [2^ex, 2^(ex+1))
+        e = ex - 14;                                                         // amax / 2^e < 2^15
+    }
+    const float down = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e (e <= 113 for finite input)
+    if (tid == 0) tok_scale[t] = __uint_as_float((uint32_t)(127 + e) << 23);
+    const int8_t *qs = (q0 ? a.q0 : a.qk) + (uint64_t)t * a.k;
+    __half *orow = out + (uint64_t)t * a.k;
+    for (uint32_t i = tid * 8; i < a.k; i += kActsF16Threads * 8) {
+        const uint2 c = *reinterpret_cast<const uint2 *>(qs + i);
+        const float d = dr[i / bs] * down;  // exact: a power-of-two scaling
         uint4 o;
         o.x = h2u((float)sbyte(c.x, 0) * d, (float)sbyte(c.x, 1) * d);
         o.y = h2u((float)sbyte(c.x, 2) * d, (float)sbyte(c.x, 3) * d);
         o.z = h2u((float)sbyte(c.y, 0) * d, (float)sbyte(c.y, 1) * d);
         o.w = h2u((float)sbyte(c.y, 2) * d, (float)sbyte(c.y, 3) * d);
-        *reinterpret_cast<uint4 *>(out + e0) = o;
+        *reinterpret_cast<uint4 *>(orow + i) = o;
     }
 }
 
@@ -376,10 +527,15 @@ static int ensure_f16_scratch(rcu_ctx *ctx, size_t bytes) {
     return RCU_OK;
 }
 
-int gemm_f16_reserve(rcu_ctx *ctx, uint64_t n_tok, uint64_t k) { return ensure_f16_scratch(ctx, n_tok * k * 2); }
+// f16 activations [n_tok][k], then the per-token scales [n_tok]
+static size_t f16_scratch_bytes(uint64_t n_tok, uint64_t k) { return ((n_tok * k * 2 + 255) & ~(size_t)255) + n_tok * 4; }
+int gemm_f16_reserve(rcu_ctx *ctx, uint64_t n_tok, uint64_t k) {
+    return ensure_f16_scratch(ctx, f16_scratch_bytes(n_tok, k));
+}
 
 template <int TYPE>
-static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const ActsView &a, const HostJob *jobs, int n_jobs) {
+static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const float *tok_scale, const ActsView &a,
+                           const HostJob *jobs, int n_jobs) {
     constexpr uint32_t BOX = raw_box_c<TYPE>();
     HParams p{};
     HMaps maps{};
@@ -395,6 +551,7 @@ static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const ActsView &a, 
     if (tiles >= (1u << 31)) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: too many row tiles");
     const uint32_t nt = pick_nt(tiles, a.n_tok, ctx->num_sms);
     p.n_jobs = (uint32_t)n_jobs;
+    p.tok_scale = tok_scale;
     p.k = a.k;
     p.n_tok = a.n_tok;
     p.nt = nt;
@@ -413,16 +570,17 @@ static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const ActsView &a, 
     return RCU_OK;
 }
 
-static int launch_f16_group(rcu_ctx *ctx, const __half *bact, const ActsView &a, const HostJob *jobs, int n) {
+static int launch_f16_group(rcu_ctx *ctx, const __half *bact, const float *ts, const ActsView &a, const HostJob *jobs,
+                            int n) {
     switch (jobs[0].w->type) {
-        case T_Q4_0: return launch_f16_type<T_Q4_0>(ctx, bact, a, jobs, n);
-        case T_Q4_1: return launch_f16_type<T_Q4_1>(ctx, bact, a, jobs, n);
-        case T_Q5_0: return launch_f16_type<T_Q5_0>(ctx, bact, a, jobs, n);
-        case T_Q5_1: return launch_f16_type<T_Q5_1>(ctx, bact, a, jobs, n);
-        case T_Q8_0: return launch_f16_type<T_Q8_0>(ctx, bact, a, jobs, n);
-        case T_Q4_K: return launch_f16_type<T_Q4_K>(ctx, bact, a, jobs, n);
-        case T_Q5_K: return launch_f16_type<T_Q5_K>(ctx, bact, a, jobs, n);
-        case T_Q6_K: return launch_f16_type<T_Q6_K>(ctx, bact, a, jobs, n);
+        case T_Q4_0: return launch_f16_type<T_Q4_0>(ctx, bact, ts, a, jobs, n);
+        case T_Q4_1: return launch_f16_type<T_Q4_1>(ctx, bact, ts, a, jobs, n);
+        case T_Q5_0: return launch_f16_type<T_Q5_0>(ctx, bact, ts, a, jobs, n);
+        case T_Q5_1: return launch_f16_type<T_Q5_1>(ctx, bact, ts, a, jobs, n);
+        case T_Q8_0: return launch_f16_type<T_Q8_0>(ctx, bact, ts, a, jobs, n);
+        case T_Q4_K: return launch_f16_type<T_Q4_K>(ctx, bact, ts, a, jobs, n);
+        case T_Q5_K: return launch_f16_type<T_Q5_K>(ctx, bact, ts, a, jobs, n);
+        case T_Q6_K: return launch_f16_type<T_Q6_K>(ctx, bact, ts, a, jobs, n);
         default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: type");
     }
 }
@@ -431,20 +589,20 @@ int launch_gemm_f16(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_
     if (sizeof(HSmem) + 1024 > ctx->max_smem_optin) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: smem");
     for (int i = 0; i < n_jobs; i++)
         if (!gemm_f16_ok(a, jobs[i])) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: type or shape not supported");
-    if (int st = ensure_f16_scratch(ctx, (size_t)a.n_tok * a.k * 2)) return st;
+    if (int st = ensure_f16_scratch(ctx, f16_scratch_bytes(a.n_tok, a.k))) return st;
     __half *bact = reinterpret_cast<__half *>(ctx->h_act);
-    const uint64_t n8 = (uint64_t)a.n_tok * a.k / 8;
-    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n8 + 255) / 256, (uint64_t)ctx->num_sms * 8);
+    float *ts = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ctx->h_act) +
+                                          (f16_scratch_bytes(a.n_tok, a.k) - (size_t)a.n_tok * 4));
     uint32_t done_fmt = 0;
     for (int i = 0; i < n_jobs;) {
         const uint32_t fmt = act_format(jobs[i].w->type);
         if (fmt != done_fmt) {  // jobs of one format share the f16 activations
-            RCU_CUDA_TRY(ctx, launch_k(ctx, k_acts_f16, dim3(blocks), dim3(256), 0, a, fmt, bact));
+            RCU_CUDA_TRY(ctx, launch_k(ctx, k_acts_f16, dim3(a.n_tok), dim3(kActsF16Threads), 0, a, fmt, bact, ts));
             done_fmt = fmt;
         }
         int n = 1;  // consecutive jobs of the same type share a launch
         while (i + n < n_jobs && n < kF16MaxJobs && jobs[i + n].w->type == jobs[i].w->type) n++;
-        if (int st = launch_f16_group(ctx, bact, a, jobs + i, n)) return st;
+        if (int st = launch_f16_group(ctx, bact, ts, a, jobs + i, n)) return st;
         i += n;
     }
     return RCU_OK;

@@ -68,10 +68,19 @@ struct QkvPostParams {
     float eps, attn_scale;
 };
 int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p);
+// Prompt batches of at least kPrefillAttnMinTok tokens over an f16 cache take the tensor-core
+// attention (64 query rows per CTA, key blocks of 64); out is [n_tok][n_head * hd] f32.
+constexpr uint64_t kPrefillAttnMinTok = 16;
+bool attention_prefill_ok(int kv_type, uint64_t hd, uint64_t group, uint64_t n_tok);
+int launch_attention_prefill(rcu_ctx *ctx, const void *kc, const void *vc, uint64_t n_kv, uint64_t hd, uint64_t slots,
+                             const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0, const uint64_t *pos_ptr,
+                             uint64_t window, float softcap, float *out);
 // Whether the merge can quantize in the same kernel for this head shape and act format
 // (a GQA group's output must hold whole activation blocks).
 bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt);
 uint32_t attention_max_splits(const rcu_kv *kv, uint64_t window);
 uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head, uint32_t n_split);
+uint64_t attention_scratch_bytes_upto(const rcu_ctx *ctx, const rcu_kv *kv, uint64_t max_batch, uint64_t n_head,
+                                      uint64_t window);
 
 }  // namespace rcu

@@ -767,6 +767,21 @@ uint64_t attention_scratch_bytes(const rcu_kv *kv, uint64_t n_tok, uint64_t n_he
     return counters_bytes(n_tok, kv->n_kv) + n_tok * n_head * n_split * (kv->hd + 2) * sizeof(float);
 }
 
+// Scratch for every batch of 1..max_batch tokens: a batch of n tokens splits the context into at
+// most min(2 * SMs / (n_kv * n), 256) parts, so n * splits stays near max(max_batch, 2 * SMs / n_kv);
+// single-token steps replayed as a graph use the fixed grid of attention_max_splits.
+uint64_t attention_scratch_bytes_upto(const rcu_ctx *ctx, const rcu_kv *kv, uint64_t max_batch, uint64_t n_head,
+                                      uint64_t window) {
+    const uint64_t max_len = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
+    uint64_t best = attention_scratch_bytes(kv, 1, n_head, attention_max_splits(kv, window));
+    for (uint64_t n = 1; n <= max_batch; n++) {
+        uint32_t ns = 0, rps = 0;
+        split_plan(max_len, n, kv->n_kv, ctx->num_sms, &ns, &rps);
+        best = std::max<uint64_t>(best, attention_scratch_bytes(kv, n, n_head, ns));
+    }
+    return best;
+}
+
 bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt) {
     const uint64_t gv = (n_head / n_kv) * hd;
     return (fmt & RCU_ACT_Q8K) ? gv % QK_K == 0 : gv % QK == 0;
@@ -808,6 +823,31 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
     if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
     if (aq && !attention_fused_merge_ok(n_head, kv->n_kv, kv->hd, aq->fmt))
         return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: group output does not hold whole activation blocks");
+    if (n_split == 0 && attention_prefill_ok(kv->type, kv->hd, group, n_tok)) {
+        // prompt batch: tensor-core kernel into f32 rows (out, else the scratch), then the
+        // quantization for Wo when asked for
+        float *o = out;
+        if (!o) {
+            if (scratch) {
+                o = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(scratch) + counters_bytes(n_tok, kv->n_kv));
+            } else {
+                void *v = nullptr;
+                if (int st = scratch_get(ctx, n_tok * n_head * kv->hd * sizeof(float), &v)) return st;
+                o = reinterpret_cast<float *>(v);
+            }
+        }
+        if (int st = launch_attention_prefill(ctx, kv->k, kv->v, kv->n_kv, kv->hd, kv->slots, q, n_tok, n_head, pos0,
+                                              pos_ptr, window, softcap, o))
+            return st;
+        if (aq && aq->fmt) {
+            ActsView v{};
+            v.q0 = aq->q0, v.d0 = aq->d0, v.s0 = aq->s0, v.sum0 = aq->sum0;
+            v.qk = aq->qk, v.dk = aq->dk, v.bsk = aq->bsk;
+            v.n_tok = (uint32_t)n_tok, v.k = (uint32_t)(n_head * kv->hd), v.have = aq->fmt;
+            return launch_quantize(ctx, v, o, (uint32_t)n_tok, (uint32_t)(n_head * kv->hd), aq->fmt);
+        }
+        return RCU_OK;
+    }
     AttnParams p{};
     p.kc = kv->k;
     p.vc = kv->v;

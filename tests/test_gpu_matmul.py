@@ -211,6 +211,21 @@ def test_prefill_gemm_f16_jobs_share_a_launch(env):
         close(g, wv)
 
 
+@pytest.mark.parametrize("t", [O.Q4_0, O.Q4_K, O.Q6_K], ids=["Q4_0", "Q4_K", "Q6_K"])
+def test_prefill_gemm_f16_large_activations(env, t):
+    # rows whose values pass the f16 range (65504) are scaled by a power of two per token
+    rng = O.Rng(4242 + t)
+    n_tok, rows, k = 64, 300, 2048
+    w = rng.weight(t, rows, k)
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    x *= np.array([10.0 ** (i % 8) for i in range(n_tok)], np.float32)[:, None]  # up to 1e7
+    got = gpu_matmul(env, [(t, w, k)], x)[0][0]
+    want = O.matmul_multi(x, [(t, w, k)], n_threads=8)[0]
+    assert np.all(np.isfinite(got))
+    for i in range(n_tok):  # every token row against its own scale
+        close(got[i], want[i])
+
+
 @pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 512), (128, 256, 4096)])
 def test_prefill_gemm_q4_0_int8_kind(env, n_tok, rows, k):
     # the int8 GEMM (exact per-block sums) stays selectable for Q4_0

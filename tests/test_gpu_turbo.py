@@ -111,6 +111,19 @@ def test_attention_sliding_window_and_softcap(env):
     close(got, want, 2e-3)
 
 
+@pytest.mark.parametrize("case", [(4, 2, 64, 200, 40, 30, 0, 0.0), (8, 8, 128, 300, 100, 0, 0, 0.0),
+                                  (16, 1, 64, 600, 33, 500, 0, 0.0), (32, 8, 128, 700, 256, 400, 0, 0.0),
+                                  (8, 4, 64, 180, 64, 300, 100, 30.0), (8, 2, 128, 90, 17, 5, 0, 0.0)],
+                         ids=["g2", "mha", "g16", "qwen3", "swa_softcap", "ragged"])
+def test_prefill_attention_f16(env, case):
+    # prompt batches (>= 16 tokens) over an f16 cache take the tensor-core kernel: GQA groups of
+    # 1..16, ragged query tiles, a wrapped sliding-window ring with softcap
+    n_head, n_kv, hd, slots, n_tok, pos0, window, softcap = case
+    got, want = _attn_case(env, O.KV_F16, n_head, n_kv, hd, slots, n_tok, pos0, window=window, softcap=softcap,
+                           seed=n_tok + pos0)
+    close(got, want, 1e-3)
+
+
 def test_turbo_attention_equals_attention_over_reconstruction(env):
     # model/cpu.rs:665-718 run on the GPU: turbo cache vs f16 cache of the reconstruction
     torch, rie, ctx = env
