@@ -654,20 +654,19 @@ def run_moe(args, world, rank, local):
 
     import rust_interference_engine_b200 as rie
     from rust_interference_engine_b200 import model as M
-    if world > 1:
-        raise SystemExit("the MoE workload runs on one GPU (expert parallelism is not built)")
     torch.cuda.set_device(local)
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
     spec = qwen3_moe_spec()
-    gen = RandomBlocks(4)
-    model = M.Model(ctx, spec.config())
+    gen = RandomBlocks(4)  # same seed on every rank: every rank sees the same full tensors
+    # N > 1: attention tensor-parallel, experts split across the ranks (expert parallelism)
+    model = M.Model(ctx, spec.config(), rank, world)
     t_build = time.perf_counter()
     for name, t, rows, cols, data in M.synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
         model.set_tensor(name, int(t), rows, cols, data)
     t_build = time.perf_counter() - t_build
     n_gen = max(args.warmup, 3) + args.steps
-    be = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16)
+    be = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
     prompt = torch.from_numpy(np.random.default_rng(4).integers(0, spec.n_vocab, MOE_PROMPT).astype(np.int32)).cuda()
     gen_tokens = torch.from_numpy(np.random.default_rng(5).integers(0, spec.n_vocab, n_gen).astype(np.int32)).cuda()
     logits = torch.zeros(spec.n_vocab, device="cuda")
@@ -678,39 +677,45 @@ def run_moe(args, world, rank, local):
         pos += 1
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
     with Clocks(local) as clk:
         t0.record(stream)
         for i in range(args.steps):
             be.forward_device(gen_tokens[max(args.warmup, 3) + i:], 1, pos + i, logits)
         t1.record(stream)
         torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
+    barrier(world)
+    ms = dist_max(t0.elapsed_time(t1) / args.steps, world)
     finite = bool(torch.isfinite(logits).all())
     # e2e: host tokens in, host logits out (Backend::forward)
-    be2 = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16)
+    be2 = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
     be2.forward(prompt.cpu().numpy().astype(np.uint32), 0)
     tok, p2 = np.array([1], dtype=np.uint32), MOE_PROMPT
     for i in range(max(args.warmup, 3)):
         be2.forward(tok, p2)
         p2 += 1
+    barrier(world)
     e0 = time.perf_counter()
     for i in range(args.steps):
         out = be2.forward(tok, p2)
         tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
         p2 += 1
-    e2e_tps = args.steps / (time.perf_counter() - e0)
+    e2e_tps = args.steps / dist_max(time.perf_counter() - e0, world)
     be2.free()
     # batch of 256 tokens in one forward (config 4's large batch)
-    be3 = M.CudaBackend(model, 512, 256, rie.KvType.F16)
+    be3 = M.CudaBackend(model, 512, 256, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
     big = torch.from_numpy(np.random.default_rng(6).integers(0, spec.n_vocab, 256).astype(np.int32)).cuda()
     be3.forward_device(big, 256, 0, logits)
     torch.cuda.synchronize()
     b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
     b0.record(stream)
     be3.forward_device(big, 256, 256, logits)
     b1.record(stream)
     torch.cuda.synchronize()
-    b256_tps = 256 / (b0.elapsed_time(b1) * 1e-3)
+    b256_tps = 256 / (dist_max(b0.elapsed_time(b1), world) * 1e-3)
     be3.free()
     # dominant kernel: the expert gate+up GEMV of one token (16 x 768 x 2048 Q4_K), timed alone
     # over distinct copies (> L2)
@@ -737,12 +742,13 @@ def run_moe(args, world, rank, local):
     wb = moe_bytes_per_token(spec)
     return {
         "metric": META["moe"]["metric"], "value": 1000.0 / ms, "unit": "tok/s", "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "dtype": META["moe"]["dtype"],
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "dtype": META["moe"]["dtype"],
         "config": {"workload": META["moe"]["workload"], "layers": spec.n_layer, "hidden": spec.n_embd,
                    "experts": f"{spec.n_expert} x ffn {spec.n_ff_exp}, top-{spec.n_expert_used} softmax",
                    "heads": f"{spec.n_head}/{spec.n_head_kv}x{spec.head_dim}", "vocab": spec.n_vocab,
                    "prompt": MOE_PROMPT, "weight_bytes_per_token": wb, "b256_tok_s": b256_tps, "batch": 1,
-                   "l2": "inputs larger than L2 (expert weights streamed per token)", "parallelism": "replicas x1",
+                   "l2": "inputs larger than L2 (expert weights streamed per token)",
+                   "parallelism": f"tp{world} attention, ep{world} experts (NCCL all-reduce)" if world > 1 else "tp1",
                    "decode": "CUDA graph replay per token", "model_build_s": t_build},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_moe_experts"),

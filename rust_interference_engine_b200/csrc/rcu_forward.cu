@@ -61,6 +61,7 @@ struct rcu_backend {
     float *moe_logits = nullptr, *moe_sgate = nullptr, *moe_w = nullptr, *moe_g = nullptr, *moe_u = nullptr;
     float *moe_y = nullptr, *moe_ys = nullptr;
     uint32_t *moe_sel = nullptr;
+    uint32_t ep_e0 = 0, ep_n = 0xffffffffu;  // experts of this rank: [ep_e0, ep_e0 + ep_n)
     rcu_acts *acts2 = nullptr;
     bool ar_ok = false;
     float *ar_buf = nullptr;
@@ -398,7 +399,8 @@ __global__ void k_router(const float *__restrict__ R, const float *__restrict__ 
 // increasing expert id, the order in which the reference adds the experts' outputs.
 // One warp per token; ne <= 256.
 __global__ void k_moe_route(const float *__restrict__ logits, uint32_t n, uint32_t ne, uint32_t k, int norm_topk,
-                            int unit, uint32_t *__restrict__ sel, float *__restrict__ wsel) {
+                            int unit, uint32_t e0, uint32_t n_local, uint32_t *__restrict__ sel,
+                            float *__restrict__ wsel) {
     pdl_wait();
     pdl_trigger();
     const uint32_t lane = threadIdx.x & 31;
@@ -463,23 +465,25 @@ __global__ void k_moe_route(const float *__restrict__ logits, uint32_t n, uint32
             const float tp = ps[r];
             ps[r] = ps[best];
             ps[best] = tp;
-            sel[t * k + r] = ids[r];
+            // expert parallelism: this rank holds experts [e0, e0 + n_local), as local ids
+            sel[t * k + r] = ids[r] - e0 < n_local ? ids[r] - e0 : kNoExpert;
             wsel[t * k + r] = unit ? 1.0f : ps[r] / norm;
         }
     }
 }
 
-// out[t] = sum_j w[t][j] * y[t*k + j] (experts in id order) [+ sgate[t] * ys[t]].
-__global__ void k_moe_combine(const float *__restrict__ y, const float *__restrict__ wsel, const float *__restrict__ ys,
-                              const float *__restrict__ sgate, uint32_t n, uint32_t k, uint32_t e,
-                              float *__restrict__ out) {
+// out[t] = sum_j w[t][j] * y[t*k + j] (experts in id order, those of this rank) [+ sgate[t] * ys[t]].
+__global__ void k_moe_combine(const float *__restrict__ y, const float *__restrict__ wsel, const uint32_t *__restrict__ sel,
+                              const float *__restrict__ ys, const float *__restrict__ sgate, uint32_t n, uint32_t k,
+                              uint32_t e, float *__restrict__ out) {
     pdl_wait();
     pdl_trigger();
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)n * e) return;
     const uint64_t t = i / e, c = i % e;
     float o = 0.0f;
-    for (uint32_t j = 0; j < k; j++) o += wsel[t * k + j] * y[(t * k + j) * e + c];
+    for (uint32_t j = 0; j < k; j++)
+        if (sel[t * k + j] != kNoExpert) o += wsel[t * k + j] * y[(t * k + j) * e + c];
     if (ys) o += (sgate ? sgate[t] : 1.0f) * ys[t * e + c];
     out[i] = o;
 }
@@ -570,6 +574,10 @@ __global__ void k_unshard_cols(const float *__restrict__ src, float *__restrict_
 static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_attn, const ArSum &ar_o) {
     rcu_ctx *ctx = b->ctx;
     const rcu_model_config &c = b->cfg;
+    // expert parallelism: this rank holds experts [e0, e0 + n_local); the shared expert (kept
+    // whole on every rank) is added by rank 0 only, and the ranks' sums are all-reduced below
+    const int P = b->m->tp_world, rank = b->m->tp_rank;
+    const bool shared_here = L.gate_sh && rank == 0;
     const uint32_t e = c.n_embd, ne = (uint32_t)L.router->rows, fx = c.n_ff_exp;
     const uint32_t k = std::min<uint32_t>(std::max<uint32_t>(c.n_expert_used, 1), ne);
     const uint32_t fx_in = formats({L.gate_exps, L.up_exps}) | (L.gate_sh ? formats({L.gate_sh, L.up_sh}) : 0);
@@ -580,7 +588,7 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
                                b->moe_logits, b->moe_sgate));
     RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_route), dim3((uint32_t)((n + 7) / 8)), dim3(256), 0,
                                (const float *)b->moe_logits, (uint32_t)n, ne, k, c.expert_norm_topk,
-                               c.expert_unit_weights, b->moe_sel, b->moe_w));
+                               c.expert_unit_weights, b->ep_e0, b->ep_n, b->moe_sel, b->moe_w));
     auto view = [&](rcu_acts *a, uint32_t rows, uint32_t kk, uint32_t fmt) {
         ActsView v = a->v;
         v.n_tok = rows;
@@ -589,7 +597,7 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
         return v;
     };
     // shared expert first: it reads the norm's activations, its GLU goes to the second batch
-    if (L.gate_sh) {
+    if (shared_here) {
         const uint32_t fs = (uint32_t)L.gate_sh->rows, fsd = formats({L.down_sh});
         if (int st = matmul(b, (uint32_t)n, e, fx_in, {{L.gate_sh, b->g, fs}, {L.up_sh, b->u, fs}})) return st;
         RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fs + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, fs,
@@ -632,9 +640,13 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
     }
     const uint64_t tot = n * e;
     RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_combine), dim3((uint32_t)((tot + 255) / 256)), dim3(256), 0,
-                               (const float *)b->moe_y, (const float *)b->moe_w,
-                               L.gate_sh ? (const float *)b->moe_ys : (const float *)nullptr,
+                               (const float *)b->moe_y, (const float *)b->moe_w, (const uint32_t *)b->moe_sel,
+                               shared_here ? (const float *)b->moe_ys : (const float *)nullptr,
                                L.sh_gate ? (const float *)b->moe_sgate : (const float *)nullptr, (uint32_t)n, k, e, b->o));
+    if (P > 1) {  // the experts of the other ranks
+        const ncclResult_t r = ncclAllReduce(b->o, b->o, tot, ncclFloat32, ncclSum, b->comm, ctx->stream);
+        if (r != ncclSuccess) return nccl_err(ctx, r, "ncclAllReduce (experts)");
+    }
     return RCU_OK;
 }
 
@@ -774,11 +786,16 @@ static bool ends_with(const std::string &s, const char *suf) {
 // Column-parallel (rows split): q/k/v (by head), gate/up, the vocabulary rows of the output
 // head, q/k/v biases. Row-parallel (columns split, whole blocks): attn_output, ffn_down.
 // Everything else (embeddings, norms) is replicated.
-enum TpKind { TP_REPL = 0, TP_ROWS = 1, TP_COLS = 2, TP_QKV = 3, TP_UPGATE = 4 };
+enum TpKind { TP_REPL = 0, TP_ROWS = 1, TP_COLS = 2, TP_QKV = 3, TP_UPGATE = 4, TP_EXPERTS = 5 };
 static int tp_kind(const std::string &n, const rcu_model_config &c, uint64_t rows) {
     if (n == "output.weight") return TP_ROWS;  // (not "blk.N.attn_output.weight")
     if (ends_with(n, ".attn_output.weight") || ends_with(n, ".ffn_down.weight")) return TP_COLS;
     if (ends_with(n, ".attn_qkv.weight")) return TP_QKV;
+    // expert parallelism: stacked expert tensors keep this rank's experts (router and shared
+    // expert stay whole)
+    if (ends_with(n, ".ffn_gate_exps.weight") || ends_with(n, ".ffn_up_exps.weight") ||
+        ends_with(n, ".ffn_down_exps.weight"))
+        return TP_EXPERTS;
     if (ends_with(n, ".ffn_up.weight") && rows == 2ull * c.n_ff) return TP_UPGATE;
     for (const char *suf : {".attn_q.weight", ".attn_k.weight", ".attn_v.weight", ".ffn_gate.weight", ".ffn_up.weight",
                             ".attn_q.bias", ".attn_k.bias", ".attn_v.bias"})
@@ -816,6 +833,15 @@ static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &
             if (name == "output.weight") total = c.n_vocab;  // padded vocab rows are dropped
             if (total % world) return bad("rows not divisible by the tensor-parallel degree");
             const uint64_t n = total / world;
+            *out_rows = n, *out_cols = cols;
+            if (out) out->resize(n * rb);
+            copy_rows(rank * n, n, 0);
+            return RCU_OK;
+        }
+        case TP_EXPERTS: {
+            const uint64_t ne = c.n_expert;
+            if (ne == 0 || rows % ne || ne % world) return bad("experts do not split evenly");
+            const uint64_t per = rows / ne, n = ne / world * per;
             *out_rows = n, *out_cols = cols;
             if (out) out->resize(n * rb);
             copy_rows(rank * n, n, 0);
@@ -1058,8 +1084,9 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     if (P > 1 && !uid) return set_err(ctx, RCU_ERR_INVALID, "tensor-parallel backend needs the communicator id");
     if (n_ctx == 0) return set_err(ctx, RCU_ERR_INVALID, "n_ctx must be positive");
     if (kv_type < RCU_KV_F16 || kv_type > RCU_KV_TURBO4) return set_err(ctx, RCU_ERR_INVALID, "unknown kv type");
-    if (m->cfg.n_head % P || m->cfg.n_head_kv % P || m->cfg.n_ff % P || m->cfg.n_vocab % P)
-        return set_err(ctx, RCU_ERR_INVALID, "heads, KV heads, FFN rows and vocabulary must divide by the tensor-parallel degree");
+    if (m->cfg.n_head % P || m->cfg.n_head_kv % P || m->cfg.n_ff % P || m->cfg.n_vocab % P || m->cfg.n_expert % P)
+        return set_err(ctx, RCU_ERR_INVALID,
+                       "heads, KV heads, FFN rows, vocabulary and experts must divide by the tensor-parallel degree");
     rcu_backend *b = new (std::nothrow) rcu_backend();
     if (!b) return RCU_ERR_OOM;
     b->cfg = m->cfg;
@@ -1067,6 +1094,10 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     b->cfg.n_head_kv /= P;
     b->cfg.n_ff /= P;
     b->cfg.n_vocab /= P;
+    if (m->cfg.n_expert > 0) {  // expert parallelism
+        b->ep_n = m->cfg.n_expert / P;
+        b->ep_e0 = (uint32_t)m->tp_rank * b->ep_n;
+    }
     const rcu_model_config &c = b->cfg;
     b->m = m;
     b->ctx = ctx;
@@ -1140,8 +1171,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
             L.gate = g, L.up = u;
         }
         if (L.router) {  // mixture of experts (model/mod.rs:147-180)
-            const uint64_t ne = c.n_expert, fx = c.n_ff_exp;
-            if (P > 1) return fail(set_err(ctx, RCU_ERR_UNSUPPORTED, "mixture-of-experts layers with tensor parallelism"));
+            const uint64_t ne = c.n_expert, fx = c.n_ff_exp, ne_loc = std::min<uint64_t>(ne, b->ep_n);
             if (int st = need(L.router->type == T_F32 && L.router->rows == ne && L.router->cols == e && ne <= 256 &&
                                   c.n_expert_used <= 16 && fx > 0,
                               p + "ffn_gate_inp.weight"))
@@ -1149,7 +1179,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
             L.gate_exps = W(p + "ffn_gate_exps.weight"), L.up_exps = W(p + "ffn_up_exps.weight");
             L.down_exps = W(p + "ffn_down_exps.weight");
             const rcu_weight *ex[3] = {L.gate_exps, L.up_exps, L.down_exps};
-            const uint64_t exs[3][2] = {{ne * fx, e}, {ne * fx, e}, {ne * e, fx}};
+            const uint64_t exs[3][2] = {{ne_loc * fx, e}, {ne_loc * fx, e}, {ne_loc * e, fx}};
             for (int i = 0; i < 3; i++)
                 if (int st = need(ex[i] && ex[i]->rows == exs[i][0] && ex[i]->cols == exs[i][1] && gemv_supported(ex[i]->type),
                                   p + "ffn_*_exps.weight"))

@@ -358,9 +358,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
                 const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
                 const uint32_t bytes = (nrows * jb.row_bytes + 15u) & ~15u;
                 uint8_t *dst = smem + p.stage_off + s * p.stage_bytes;
-                mbar_arrive_expect_tx(&h->full[s], bytes);
-                const uint8_t *wbase = jb.sel ? jb.w + (uint64_t)(*jb.sel) * jb.w_stride : jb.w;
-                bulk_g2s(dst, wbase + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s], pol);
+                const uint32_t ex = jb.sel ? *jb.sel : 0;
+                if (ex == kNoExpert) {  // routed to an expert of another rank: nothing to load
+                    mbar_arrive(&h->full[s]);
+                } else {
+                    mbar_arrive_expect_tx(&h->full[s], bytes);
+                    bulk_g2s(dst, jb.w + (uint64_t)ex * jb.w_stride + (uint64_t)r0 * jb.row_bytes, bytes, &h->full[s],
+                             pol);
+                }
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
         const uint32_t r0 = (tile - jb.tile_begin) * jb.rows_per_tile;
         const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
         const uint8_t *wsm = smem + p.stage_off + s * p.stage_bytes;
-        switch (jb.type) {
+        switch (jb.sel && *jb.sel == kNoExpert ? -1 : jb.type) {
             case T_Q4_0: tile_q<T_Q4_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
             case T_Q4_1: tile_q<T_Q4_1, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
             case T_Q5_0: tile_q<T_Q5_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;

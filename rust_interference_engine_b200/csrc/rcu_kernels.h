@@ -6,6 +6,9 @@ namespace rcu {
 
 int launch_quantize(rcu_ctx *ctx, const ActsView &a, const float *x, uint32_t n_tok, uint32_t k, uint32_t formats);
 
+// Expert id an indirect job reads when the routed expert lives on another rank (expert
+// parallelism): the GEMV skips the job and the combine leaves its output out.
+constexpr uint32_t kNoExpert = 0xffffffffu;
 struct HostJob {
     const rcu_weight *w;
     float *out;

@@ -17,6 +17,7 @@ from rust_interference_engine_b200 import model as M
 ROWS = (".attn_q.weight", ".attn_k.weight", ".attn_v.weight", ".ffn_gate.weight", ".attn_q.bias", ".attn_k.bias",
         ".attn_v.bias")
 COLS = (".attn_output.weight", ".ffn_down.weight")
+EXPERTS = (".ffn_gate_exps.weight", ".ffn_up_exps.weight", ".ffn_down_exps.weight")
 
 
 def tp_spec(arch, wtype):
@@ -39,7 +40,8 @@ def raw(data):
 
 
 @pytest.mark.parametrize("arch,wtype,world", [("qwen3", GgmlType.Q4_K, 2), ("qwen2", GgmlType.Q8_0, 2),
-                                              ("phi3", GgmlType.Q4_0, 2), ("llama", GgmlType.Q4_0, 4)])
+                                              ("phi3", GgmlType.Q4_0, 2), ("llama", GgmlType.Q4_0, 4),
+                                              ("qwen3moe", GgmlType.Q4_K, 2), ("qwen2moe", GgmlType.Q8_0, 4)])
 def test_shards_reassemble(arch, wtype, world):
     spec = tp_spec(arch, wtype)
     cfg = spec.config()
@@ -47,7 +49,11 @@ def test_shards_reassemble(arch, wtype, world):
     for name, t, rows, cols, data in tensors(spec):
         full = raw(data)
         parts = [M.tp_shard(cfg, name, t, rows, cols, data, r, world) for r in range(world)]
-        if name.endswith(ROWS) or name == "output.weight" or (name.endswith("ffn_up.weight") and rows == spec.n_ff):
+        if name.endswith(EXPERTS):  # expert parallelism: whole experts, rank by rank
+            rb = full.size // rows
+            assert all(p[1] == rows // world for p in parts), name
+            assert np.array_equal(np.concatenate([p[0] for p in parts]), full), name
+        elif name.endswith(ROWS) or name == "output.weight" or (name.endswith("ffn_up.weight") and rows == spec.n_ff):
             total = spec.n_vocab if name == "output.weight" else rows
             rb = full.size // rows
             assert all(p[1] == (total // world if rows > 1 else 1) for p in parts), name
