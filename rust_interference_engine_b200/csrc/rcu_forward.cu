@@ -61,6 +61,10 @@ struct rcu_backend {
     float *moe_logits = nullptr, *moe_sgate = nullptr, *moe_w = nullptr, *moe_g = nullptr, *moe_u = nullptr;
     float *moe_y = nullptr, *moe_ys = nullptr;
     uint32_t *moe_sel = nullptr;
+    // grouped expert GEMMs (batches of kMoeGroupedMinTok tokens or more): slot of every
+    // (token, choice) pair in the expert-sorted order, source token of every slot, expert
+    // offsets on the device and their host copy (pinned)
+    uint32_t *moe_slot = nullptr, *moe_row = nullptr, *moe_off = nullptr, *moe_off_host = nullptr;
     uint32_t ep_e0 = 0, ep_n = 0xffffffffu;  // experts of this rank: [ep_e0, ep_e0 + ep_n)
     rcu_acts *acts2 = nullptr;
     bool ar_ok = false;
@@ -88,7 +92,7 @@ struct rcu_backend {
     // The backend runs on its own stream (stream capture needs a non-default stream) and
     // joins the context stream with events on entry and exit.
     cudaStream_t stream = nullptr;
-    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr, ev_plan = nullptr;
     bool use_graphs = true;
     int decode_calls = 0;
     cudaGraph_t graph = nullptr;
@@ -473,9 +477,11 @@ __global__ void k_moe_route(const float *__restrict__ logits, uint32_t n, uint32
 }
 
 // out[t] = sum_j w[t][j] * y[t*k + j] (experts in id order, those of this rank) [+ sgate[t] * ys[t]].
+// slot != nullptr: the output of pair t*k + j is row slot[t*k + j] of y (grouped GEMMs).
 __global__ void k_moe_combine(const float *__restrict__ y, const float *__restrict__ wsel, const uint32_t *__restrict__ sel,
-                              const float *__restrict__ ys, const float *__restrict__ sgate, uint32_t n, uint32_t k,
-                              uint32_t e, float *__restrict__ out) {
+                              const uint32_t *__restrict__ slot, const float *__restrict__ ys,
+                              const float *__restrict__ sgate, uint32_t n, uint32_t k, uint32_t e,
+                              float *__restrict__ out) {
     pdl_wait();
     pdl_trigger();
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -483,9 +489,49 @@ __global__ void k_moe_combine(const float *__restrict__ y, const float *__restri
     const uint64_t t = i / e, c = i % e;
     float o = 0.0f;
     for (uint32_t j = 0; j < k; j++)
-        if (sel[t * k + j] != kNoExpert) o += wsel[t * k + j] * y[(t * k + j) * e + c];
+        if (sel[t * k + j] != kNoExpert) o += wsel[t * k + j] * y[(slot ? slot[t * k + j] : t * k + j) * (uint64_t)e + c];
     if (ys) o += (sgate ? sgate[t] : 1.0f) * ys[t * e + c];
     out[i] = o;
+}
+
+// Expert-sorted order of the (token, choice) pairs for the grouped GEMMs (one CTA): counts per
+// local expert, their exclusive prefix off[0..n_exp], and for every pair its slot (kNoExpert
+// for another rank's expert) and for every slot its token. Slots of one expert are in no fixed
+// order; every slot is computed on its own, so the results do not depend on it.
+constexpr int kMoePlanThreads = 1024;
+constexpr uint64_t kMoeGroupedMinTok = 32;  // tokens per forward from which experts run as grouped GEMMs
+__global__ void __launch_bounds__(kMoePlanThreads) k_moe_plan(const uint32_t *__restrict__ sel, uint32_t n_pairs,
+                                                              uint32_t k, uint32_t n_exp, uint32_t *__restrict__ off,
+                                                              uint32_t *__restrict__ slot, uint32_t *__restrict__ row) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ uint32_t cnt[256], cur[256];
+    const uint32_t tid = threadIdx.x;
+    for (uint32_t e = tid; e < n_exp; e += kMoePlanThreads) cnt[e] = 0;
+    __syncthreads();
+    for (uint32_t q = tid; q < n_pairs; q += kMoePlanThreads)
+        if (sel[q] != kNoExpert) atomicAdd(&cnt[sel[q]], 1u);
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t acc = 0;
+        for (uint32_t e = 0; e < n_exp; e++) {
+            off[e] = acc;
+            cur[e] = acc;
+            acc += cnt[e];
+        }
+        off[n_exp] = acc;
+    }
+    __syncthreads();
+    for (uint32_t q = tid; q < n_pairs; q += kMoePlanThreads) {
+        const uint32_t e = sel[q];
+        if (e == kNoExpert) {
+            slot[q] = kNoExpert;
+        } else {
+            const uint32_t s = atomicAdd(&cur[e], 1u);
+            slot[q] = s;
+            row[s] = q / k;
+        }
+    }
 }
 
 __global__ void k_set_pos(uint64_t *pos_dev, uint64_t pos, uint64_t *epoch) {
@@ -596,51 +642,86 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
         v.have = fmt;
         return v;
     };
+    // Batches of kMoeGroupedMinTok tokens or more: the (token, choice) pairs sorted by expert
+    // (k_moe_plan), then one grouped tensor-core GEMM per stacked expert tensor, which reads
+    // every expert's weights once; the host needs the expert offsets to size those launches.
+    const uint32_t n_loc = std::min<uint32_t>(ne, b->ep_n);
+    const uint32_t fg = act_format(L.gate_exps->type), fdn = formats({L.down_exps});
+    const bool grouped = n >= kMoeGroupedMinTok && b->moe_slot && L.gate_exps->type == L.up_exps->type &&
+                         gemm_f16_grouped_ok(L.gate_exps, e, n_loc, fx) && gemm_f16_grouped_ok(L.up_exps, e, n_loc, fx) &&
+                         gemm_f16_grouped_ok(L.down_exps, fx, n_loc, e);
+    if (grouped) {
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_plan), dim3(1), dim3(kMoePlanThreads), 0, (const uint32_t *)b->moe_sel,
+                                   (uint32_t)(n * k), k, n_loc, b->moe_off, b->moe_slot, b->moe_row));
+        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->moe_off_host, b->moe_off, (n_loc + 1) * sizeof(uint32_t),
+                                          cudaMemcpyDeviceToHost, ctx->stream));
+        RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_plan, ctx->stream));
+    }
     // shared expert first: it reads the norm's activations, its GLU goes to the second batch
     if (shared_here) {
         const uint32_t fs = (uint32_t)L.gate_sh->rows, fsd = formats({L.down_sh});
         if (int st = matmul(b, (uint32_t)n, e, fx_in, {{L.gate_sh, b->g, fs}, {L.up_sh, b->u, fs}})) return st;
         RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fs + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, fs,
                                    c.act, act_out(b->acts2->v, fsd, ctx->rounding)));
-        const HostJob dj{L.down_sh, b->moe_ys, e};
-        for (uint32_t t0 = 0; t0 < n; t0 += 8)
-            if (int st = launch_gemv(ctx, view(b->acts2, (uint32_t)n, fs, fsd), &dj, 1, t0,
-                                     std::min<uint32_t>(8, (uint32_t)n - t0)))
-                return st;
+        b->acts2->v.n_tok = (uint32_t)n;
+        b->acts2->v.k = fs;
+        b->acts2->v.have = fsd;
+        const rcu_job dj{L.down_sh, b->moe_ys, e};
+        if (int st = rcu_matmul_multi(ctx, b->acts2, &dj, 1)) return st;
     }
-    const uint64_t rb_g = L.gate_exps->row_bytes, rb_u = L.up_exps->row_bytes, rb_d = L.down_exps->row_bytes;
-    const uint32_t fdn = formats({L.down_exps});
-    for (uint32_t c0 = 0; c0 < n; c0 += 8) {
-        const uint32_t nt = std::min<uint32_t>(8, (uint32_t)n - c0);
-        std::vector<HostJob> gu, dn;
-        for (uint32_t t = 0; t < nt; t++)
-            for (uint32_t j = 0; j < k; j++) {
-                const uint32_t idx = (c0 + t) * k + j;
-                HostJob g{L.gate_exps, b->moe_g + (uint64_t)idx * fx, fx};
-                g.sel = b->moe_sel + idx, g.w_stride = (uint64_t)fx * rb_g, g.rows = fx, g.tok = t;
-                HostJob u{L.up_exps, b->moe_u + (uint64_t)idx * fx, fx};
-                u.sel = b->moe_sel + idx, u.w_stride = (uint64_t)fx * rb_u, u.rows = fx, u.tok = t;
-                gu.push_back(g);
-                gu.push_back(u);
-                HostJob d{L.down_exps, b->moe_y + (uint64_t)idx * e, e};
-                d.sel = b->moe_sel + idx, d.w_stride = (uint64_t)e * rb_d, d.rows = e, d.tok = t * k + j;
-                dn.push_back(d);
-            }
-        for (size_t j0 = 0; j0 < gu.size(); j0 += kGemvMaxJobs)
-            if (int st = launch_gemv(ctx, view(b->acts, (uint32_t)n, e, fx_in), gu.data() + j0,
-                                     (int)std::min<size_t>(kGemvMaxJobs, gu.size() - j0), c0, 1))
+    if (grouped) {
+        RCU_CUDA_TRY(ctx, cudaEventSynchronize(b->ev_plan));
+        const uint32_t n_slots = b->moe_off_host[n_loc];
+        if (n_slots > 0) {
+            const __half *act = nullptr;
+            const float *sc = nullptr;
+            if (int st = gemm_f16_gather(ctx, view(b->acts, (uint32_t)n, e, fg), fg, b->moe_row, n_slots, &act, &sc))
                 return st;
-        const uint64_t r0 = (uint64_t)c0 * k;
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, nt * k), dim3(1024), 0, b->moe_g + r0 * fx,
-                                   b->moe_u + r0 * fx, fx, c.act, act_out(b->acts2->v, fdn, ctx->rounding)));
-        for (size_t j0 = 0; j0 < dn.size(); j0 += kGemvMaxJobs)
-            if (int st = launch_gemv(ctx, view(b->acts2, nt * k, fx, fdn), dn.data() + j0,
-                                     (int)std::min<size_t>(kGemvMaxJobs, dn.size() - j0), 0, 1))
+            const HostJob gu[2] = {{L.gate_exps, b->moe_g, fx}, {L.up_exps, b->moe_u, fx}};
+            if (int st = launch_gemm_f16_grouped(ctx, act, sc, n_slots, e, gu, 2, fx, b->moe_off_host, n_loc)) return st;
+            RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, n_slots), dim3(1024), 0, b->moe_g,
+                                       b->moe_u, fx, c.act, act_out(b->acts2->v, fdn, ctx->rounding)));
+            if (int st = gemm_f16_gather(ctx, view(b->acts2, n_slots, fx, fdn), fdn, nullptr, n_slots, &act, &sc))
                 return st;
+            const HostJob dj{L.down_exps, b->moe_y, e};
+            if (int st = launch_gemm_f16_grouped(ctx, act, sc, n_slots, fx, &dj, 1, e, b->moe_off_host, n_loc)) return st;
+        }
+    } else {
+        const uint64_t rb_g = L.gate_exps->row_bytes, rb_u = L.up_exps->row_bytes, rb_d = L.down_exps->row_bytes;
+        for (uint32_t c0 = 0; c0 < n; c0 += 8) {
+            const uint32_t nt = std::min<uint32_t>(8, (uint32_t)n - c0);
+            std::vector<HostJob> gu, dn;
+            for (uint32_t t = 0; t < nt; t++)
+                for (uint32_t j = 0; j < k; j++) {
+                    const uint32_t idx = (c0 + t) * k + j;
+                    HostJob g{L.gate_exps, b->moe_g + (uint64_t)idx * fx, fx};
+                    g.sel = b->moe_sel + idx, g.w_stride = (uint64_t)fx * rb_g, g.rows = fx, g.tok = t;
+                    HostJob u{L.up_exps, b->moe_u + (uint64_t)idx * fx, fx};
+                    u.sel = b->moe_sel + idx, u.w_stride = (uint64_t)fx * rb_u, u.rows = fx, u.tok = t;
+                    gu.push_back(g);
+                    gu.push_back(u);
+                    HostJob d{L.down_exps, b->moe_y + (uint64_t)idx * e, e};
+                    d.sel = b->moe_sel + idx, d.w_stride = (uint64_t)e * rb_d, d.rows = e, d.tok = t * k + j;
+                    dn.push_back(d);
+                }
+            for (size_t j0 = 0; j0 < gu.size(); j0 += kGemvMaxJobs)
+                if (int st = launch_gemv(ctx, view(b->acts, (uint32_t)n, e, fx_in), gu.data() + j0,
+                                         (int)std::min<size_t>(kGemvMaxJobs, gu.size() - j0), c0, 1))
+                    return st;
+            const uint64_t r0 = (uint64_t)c0 * k;
+            RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, nt * k), dim3(1024), 0,
+                                       b->moe_g + r0 * fx, b->moe_u + r0 * fx, fx, c.act,
+                                       act_out(b->acts2->v, fdn, ctx->rounding)));
+            for (size_t j0 = 0; j0 < dn.size(); j0 += kGemvMaxJobs)
+                if (int st = launch_gemv(ctx, view(b->acts2, nt * k, fx, fdn), dn.data() + j0,
+                                         (int)std::min<size_t>(kGemvMaxJobs, dn.size() - j0), 0, 1))
+                    return st;
+        }
     }
     const uint64_t tot = n * e;
     RCU_CUDA_TRY(ctx, launch_k(ctx, (k_moe_combine), dim3((uint32_t)((tot + 255) / 256)), dim3(256), 0,
                                (const float *)b->moe_y, (const float *)b->moe_w, (const uint32_t *)b->moe_sel,
+                               grouped ? (const uint32_t *)b->moe_slot : (const uint32_t *)nullptr,
                                shared_here ? (const float *)b->moe_ys : (const float *)nullptr,
                                L.sh_gate ? (const float *)b->moe_sgate : (const float *)nullptr, (uint32_t)n, k, e, b->o));
     if (P > 1) {  // the experts of the other ranks
@@ -1237,8 +1318,22 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
         for (auto &x : mb)
             if (int st = dalloc(b, x.p, x.bytes)) return fail(st);
         if (8 * kk > 64) return fail(set_err(ctx, RCU_ERR_UNSUPPORTED, "more than 8 experts per token"));
-        if (int st = rcu_acts_create(ctx, std::max<uint64_t>(T, 8 * kk), std::max<uint64_t>(fx, b->ff_max), &b->acts2))
-            return fail(st);
+        // batches of kMoeGroupedMinTok tokens or more run grouped expert GEMMs over T * kk rows
+        const bool grp = T >= kMoeGroupedMinTok && ne <= 256;
+        const uint64_t rows2 = std::max<uint64_t>(grp ? T * kk : T, 8 * kk);
+        if (int st = rcu_acts_create(ctx, rows2, std::max<uint64_t>(fx, b->ff_max), &b->acts2)) return fail(st);
+        if (grp) {
+            struct {
+                void **p;
+                uint64_t bytes;
+            } gb[] = {{(void **)&b->moe_slot, T * kk * 4}, {(void **)&b->moe_row, T * kk * 4},
+                      {(void **)&b->moe_off, (ne + 1) * 4}};
+            for (auto &x : gb)
+                if (int st = dalloc(b, x.p, x.bytes)) return fail(st);
+            RCU_CUDA_TRY(ctx, cudaMallocHost((void **)&b->moe_off_host, (ne + 1) * 4));
+            RCU_CUDA_TRY(ctx, cudaEventCreateWithFlags(&b->ev_plan, cudaEventDisableTiming));
+            if (int st = gemm_f16_reserve(ctx, T * kk, std::max<uint64_t>(e, fx))) return fail(st);
+        }
     }
     struct {
         float **p;
@@ -1310,6 +1405,8 @@ void rcu_backend_free(rcu_backend *b) {
     if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its collectives
     if (b->ev_in) cudaEventDestroy(b->ev_in);
     if (b->ev_out) cudaEventDestroy(b->ev_out);
+    if (b->ev_plan) cudaEventDestroy(b->ev_plan);
+    if (b->moe_off_host) cudaFreeHost(b->moe_off_host);
     if (b->stream) cudaStreamDestroy(b->stream);
     for (auto *kv : b->kv) rcu_kv_free(kv);
     rcu_acts_free(b->acts);

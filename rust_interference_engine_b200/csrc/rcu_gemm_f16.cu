@@ -47,6 +47,8 @@ constexpr int kHRawMax = 272;      // raw bytes per row per stage at most (Q8_0:
 constexpr int kHUnpackWarps = 16;  // 4 threads per weight row, 16 values each per stage
 constexpr int kHThreads = (2 + kHUnpackWarps) * 32;
 constexpr int kF16MaxJobs = 4;
+constexpr int kGrpMaxItems = 512;    // grouped (per-expert) launches: (expert, token tile) items
+constexpr int kGrpMaxExperts = 256;
 constexpr uint32_t kF16MinTok = 32;  // below this the 8-token GEMV slices are used
 
 struct HSmem {
@@ -72,6 +74,13 @@ struct HParams {
     uint32_t n_jobs, k, n_tok, nt, idesc;
     int early;  // weights may be loaded before the grid dependency wait
     uint32_t *err;
+    // grouped mode (grp > 0, mixture of experts): each job is a stacked expert tensor of
+    // grp_rows rows per expert; blockIdx.y is work item i = (expert grp_exp[i], token tile
+    // grp_tile[i]) over the activation rows [grp_off[e], grp_off[e + 1]) of that expert, and
+    // blockIdx.x - tile0 the row tile within the expert. Output row = activation row.
+    uint32_t grp, grp_rows;
+    uint16_t grp_exp[kGrpMaxItems], grp_tile[kGrpMaxItems];
+    uint32_t grp_off[kGrpMaxExperts + 1];
 };
 
 // ---- dequantization of 32 values of one row -----------------------------------------------
@@ -291,7 +300,22 @@ __global__ void __launch_bounds__(kHThreads, 1)
     uint32_t ji = 0;
     while (ji + 1 < p.n_jobs && blockIdx.x >= p.job[ji + 1].tile0) ji++;
     const HJob &jb = p.job[ji];
-    const uint32_t n0 = (blockIdx.x - jb.tile0) * kHRows, m0 = blockIdx.y * p.nt;
+    // tile origin: weight row in the tensor map (wrow0), output column (col0, valid below
+    // col_lim), first activation / output row (trow0) and its valid count (tcount)
+    uint32_t wrow0, col0, col_lim, trow0, tcount;
+    if (p.grp) {
+        const uint32_t ex = p.grp_exp[blockIdx.y], t0 = p.grp_tile[blockIdx.y] * p.nt;
+        col0 = (blockIdx.x - jb.tile0) * kHRows;
+        wrow0 = ex * p.grp_rows + col0;
+        col_lim = p.grp_rows;
+        trow0 = p.grp_off[ex] + t0;
+        tcount = p.grp_off[ex + 1] - p.grp_off[ex] - t0;
+    } else {
+        col0 = wrow0 = (blockIdx.x - jb.tile0) * kHRows;
+        col_lim = jb.rows;
+        trow0 = blockIdx.y * p.nt;
+        tcount = p.n_tok - trow0;
+    }
     const uint32_t n_unit = p.k / QK_K, n_it = n_unit * 4;
 
     if (threadIdx.x == 0) {
@@ -324,7 +348,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
                     !mbar_wait_bounded(&S.raw_empty[rs], ((u / kHRawStages) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
                     return false;
                 mbar_arrive_expect_tx(&S.raw_full[rs], BOX * kHRows);
-                tma_load_2d(S.raw[rs], mw, (int)(((u * UB) & ~15u) >> 1), (int)n0, &S.raw_full[rs]);
+                tma_load_2d(S.raw[rs], mw, (int)(((u * UB) & ~15u) >> 1), (int)wrow0, &S.raw_full[rs]);
                 units = u + 1;
                 return true;
             };
@@ -342,7 +366,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&S.b_full[s], p.nt * 128);
-                tma_load_2d(S.b[s], &map_b, (int)(it * 64), (int)m0, &S.b_full[s]);
+                tma_load_2d(S.b[s], &map_b, (int)(it * 64), (int)trow0, &S.b_full[s]);
                 its = it + 1;
             }
             // drain: the last copy issued into each stage has landed (already true unless a
@@ -412,16 +436,16 @@ __global__ void __launch_bounds__(kHThreads, 1)
             tc_fence_after();
             // the four warps of a lane quarter split the accumulator columns
             const uint32_t span = p.nt / (kHUnpackWarps / 4);
-            const uint32_t n = n0 + r;
+            const uint32_t n = col0 + r;
             for (uint32_t c = part * span; c < (part + 1) * span; c += 16) {
                 uint32_t x[16];
                 tmem_ld16(tmem + ((32 * q) << 16) + c, x);
                 tmem_wait_ld();
-                if (n < jb.rows) {
+                if (n < col_lim) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
-                        const uint32_t m = m0 + c + e;
-                        if (m < p.n_tok) jb.out[(uint64_t)m * jb.ld + n] = __uint_as_float(x[e]) * p.tok_scale[m];
+                        const uint32_t m = trow0 + c + e;
+                        if (c + e < tcount) jb.out[(uint64_t)m * jb.ld + n] = __uint_as_float(x[e]) * p.tok_scale[m];
                     }
                 }
             }
@@ -445,12 +469,14 @@ __global__ void __launch_bounds__(kHThreads, 1)
 // 2^15, so that no value overflows f16 (activations of some models reach 1e5); tok_scale[t] = 2^e_t
 // is multiplied back, exactly, in the GEMM epilogue. Rows already in range are unchanged.
 constexpr int kActsF16Threads = 256;
+// src_rows != nullptr gathers: output row i is activation row src_rows[i] (grouped GEMM).
 __global__ void __launch_bounds__(kActsF16Threads) k_acts_f16(const ActsView a, uint32_t fmt, __half *__restrict__ out,
-                                                              float *__restrict__ tok_scale) {
+                                                              float *__restrict__ tok_scale,
+                                                              const uint32_t *__restrict__ src_rows) {
     pdl_wait();
     pdl_trigger();
     __shared__ float red[kActsF16Threads / 32];
-    const uint32_t t = blockIdx.x, tid = threadIdx.x;
+    const uint32_t row = blockIdx.x, t = src_rows ? src_rows[row] : row, tid = threadIdx.x;
     const bool q0 = fmt == RCU_ACT_Q8_0;
     const uint32_t bs = q0 ? QK : QK_K, nb = a.k / bs;
     const float *dr = (q0 ? a.d0 : a.dk) + (uint64_t)t * nb;
@@ -470,9 +496,9 @@ __global__ void __launch_bounds__(kActsF16Threads) k_acts_f16(const ActsView a, 
         e = ex - 14;                                                         // amax / 2^e < 2^15
     }
     const float down = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e (e <= 113 for finite input)
-    if (tid == 0) tok_scale[t] = __uint_as_float((uint32_t)(127 + e) << 23);
+    if (tid == 0) tok_scale[row] = __uint_as_float((uint32_t)(127 + e) << 23);
     const int8_t *qs = (q0 ? a.q0 : a.qk) + (uint64_t)t * a.k;
-    __half *orow = out + (uint64_t)t * a.k;
+    __half *orow = out + (uint64_t)row * a.k;
     for (uint32_t i = tid * 8; i < a.k; i += kActsF16Threads * 8) {
         const uint2 c = *reinterpret_cast<const uint2 *>(qs + i);
         const float d = dr[i / bs] * down;  // exact: a power-of-two scaling
@@ -597,7 +623,8 @@ int launch_gemm_f16(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_
     for (int i = 0; i < n_jobs;) {
         const uint32_t fmt = act_format(jobs[i].w->type);
         if (fmt != done_fmt) {  // jobs of one format share the f16 activations
-            RCU_CUDA_TRY(ctx, launch_k(ctx, k_acts_f16, dim3(a.n_tok), dim3(kActsF16Threads), 0, a, fmt, bact, ts));
+            RCU_CUDA_TRY(ctx, launch_k(ctx, k_acts_f16, dim3(a.n_tok), dim3(kActsF16Threads), 0, a, fmt, bact, ts,
+                                       (const uint32_t *)nullptr));
             done_fmt = fmt;
         }
         int n = 1;  // consecutive jobs of the same type share a launch
@@ -606,6 +633,99 @@ int launch_gemm_f16(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_
         i += n;
     }
     return RCU_OK;
+}
+
+// ---- grouped launches (mixture of experts) --------------------------------------------------
+bool gemm_f16_grouped_ok(const rcu_weight *w, uint32_t k, uint32_t n_exp, uint32_t grp_rows) {
+    return gemv_supported(w->type) && k % QK_K == 0 && (w->row_bytes & 15) == 0 && (((uintptr_t)w->data) & 15) == 0 &&
+           n_exp >= 1 && n_exp <= kGrpMaxExperts && w->rows == (uint64_t)n_exp * grp_rows && w->cols == k;
+}
+
+int gemm_f16_gather(rcu_ctx *ctx, const ActsView &a, uint32_t fmt, const uint32_t *src_rows, uint32_t n_rows,
+                    const __half **act, const float **scale) {
+    if (int st = ensure_f16_scratch(ctx, f16_scratch_bytes(n_rows, a.k))) return st;
+    __half *bact = reinterpret_cast<__half *>(ctx->h_act);
+    float *ts = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ctx->h_act) +
+                                          (f16_scratch_bytes(n_rows, a.k) - (size_t)n_rows * 4));
+    if (n_rows)
+        RCU_CUDA_TRY(ctx, launch_k(ctx, k_acts_f16, dim3(n_rows), dim3(kActsF16Threads), 0, a, fmt, bact, ts, src_rows));
+    *act = bact;
+    *scale = ts;
+    return RCU_OK;
+}
+
+template <int TYPE>
+static int launch_grouped_type(rcu_ctx *ctx, const __half *act, const float *scale, uint32_t n_rows, uint32_t k,
+                               const HostJob *jobs, int n_jobs, uint32_t grp_rows, const uint32_t *off, uint32_t n_exp) {
+    constexpr uint32_t BOX = raw_box_c<TYPE>();
+    const uint32_t rtiles = (grp_rows + kHRows - 1) / kHRows;
+    // tokens per CTA: the fewest waves over the (expert, token tile) items
+    uint32_t nt = 0, n_items = 0;
+    double best = 1e300;
+    for (uint32_t cand : {64u, 128u, 256u}) {
+        uint64_t items = 0;
+        for (uint32_t e = 0; e < n_exp; e++) items += (off[e + 1] - off[e] + cand - 1) / cand;
+        if (items > (uint64_t)kGrpMaxItems) continue;
+        const uint64_t ctas = items * rtiles * (uint64_t)n_jobs;
+        const double cost = (double)((ctas + ctx->num_sms - 1) / ctx->num_sms) * (cand + 64);
+        if (cost < best) best = cost, nt = cand, n_items = (uint32_t)items;
+    }
+    if (!nt) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: too many expert token tiles");
+    if (n_items == 0) return RCU_OK;
+    HParams p{};
+    HMaps maps{};
+    for (int i = 0; i < n_jobs; i++) {
+        const rcu_weight *w = jobs[i].w;
+        p.job[i] = HJob{jobs[i].out, jobs[i].ld, grp_rows, (uint32_t)(i * rtiles)};
+        if (int st = make_map_2d(ctx, &maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, w->data, w->row_bytes / 2, w->rows,
+                                 w->row_bytes, BOX / 2, kHRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return st;
+    }
+    uint32_t it = 0;
+    for (uint32_t e = 0; e < n_exp; e++)
+        for (uint32_t t0 = 0; t0 < off[e + 1] - off[e]; t0 += nt, it++) {
+            p.grp_exp[it] = (uint16_t)e;
+            p.grp_tile[it] = (uint16_t)(t0 / nt);
+        }
+    for (uint32_t e = 0; e <= n_exp; e++) p.grp_off[e] = off[e];
+    p.grp = n_items;
+    p.grp_rows = grp_rows;
+    p.tok_scale = scale;
+    p.n_jobs = (uint32_t)n_jobs;
+    p.k = k;
+    p.n_tok = n_rows;
+    p.nt = nt;
+    p.idesc = (1u << 4) | ((nt >> 3) << 17) | ((uint32_t)(kHRows >> 4) << 24);
+    p.early = 0;  // the expert choice was made on this pass
+    p.err = ctx->dev_err;
+    CUtensorMap mb;
+    if (int st = make_map_2d(ctx, &mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, k, n_rows, (uint64_t)k * 2, 64, nt,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+        return st;
+    const size_t smem = sizeof(HSmem) + 1024;
+    RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemm_f16<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const dim3 grid(rtiles * (uint32_t)n_jobs, n_items);
+    RCU_CUDA_TRY(ctx, launch_k(ctx, k_gemm_f16<TYPE>, grid, dim3(kHThreads), smem, maps, mb, p));
+    return RCU_OK;
+}
+
+int launch_gemm_f16_grouped(rcu_ctx *ctx, const __half *act, const float *scale, uint32_t n_rows, uint32_t k,
+                            const HostJob *jobs, int n_jobs, uint32_t grp_rows, const uint32_t *off, uint32_t n_exp) {
+    if (n_jobs < 1 || n_jobs > kF16MaxJobs) return set_err(ctx, RCU_ERR_INVALID, "gemm: 1..4 grouped jobs");
+    for (int i = 0; i < n_jobs; i++)
+        if (jobs[i].w->type != jobs[0].w->type || !gemm_f16_grouped_ok(jobs[i].w, k, n_exp, grp_rows))
+            return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: grouped expert shape not supported");
+    switch (jobs[0].w->type) {
+        case T_Q4_0: return launch_grouped_type<T_Q4_0>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q4_1: return launch_grouped_type<T_Q4_1>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q5_0: return launch_grouped_type<T_Q5_0>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q5_1: return launch_grouped_type<T_Q5_1>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q8_0: return launch_grouped_type<T_Q8_0>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q4_K: return launch_grouped_type<T_Q4_K>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q5_K: return launch_grouped_type<T_Q5_K>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        case T_Q6_K: return launch_grouped_type<T_Q6_K>(ctx, act, scale, n_rows, k, jobs, n_jobs, grp_rows, off, n_exp);
+        default: return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: type");
+    }
 }
 
 }  // namespace rcu

@@ -41,6 +41,15 @@ int launch_gemm_f16(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_
 bool gemm_f16_ok(const ActsView &a, const HostJob &j);
 // Sizes the f16 activation scratch for n_tok x k (so a forward never allocates mid-stream).
 int gemm_f16_reserve(rcu_ctx *ctx, uint64_t n_tok, uint64_t k);
+// Grouped GEMM for mixture-of-experts batches: each weight is a stacked expert tensor
+// (n_exp x grp_rows rows); the activation rows [off[e], off[e + 1]) (host copy of the device
+// routing plan) go through expert e. gemm_f16_gather first writes those f16 rows (row i =
+// activation row src_rows[i] of a) into the context scratch.
+bool gemm_f16_grouped_ok(const rcu_weight *w, uint32_t k, uint32_t n_exp, uint32_t grp_rows);
+int gemm_f16_gather(rcu_ctx *ctx, const ActsView &a, uint32_t fmt, const uint32_t *src_rows, uint32_t n_rows,
+                    const __half **act, const float **scale);
+int launch_gemm_f16_grouped(rcu_ctx *ctx, const __half *act, const float *scale, uint32_t n_rows, uint32_t k,
+                            const HostJob *jobs, int n_jobs, uint32_t grp_rows, const uint32_t *off, uint32_t n_exp);
 // Exact per-block integer sums of one (row, token) pair.
 int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint64_t row, uint64_t tok,
                       int32_t *out);

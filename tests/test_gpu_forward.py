@@ -200,3 +200,23 @@ def test_prefill_batch_int8_gemm_is_exact(env):
     o = ob.forward(toks, 0, all_logits=True)
     close(g, o, 2e-3, "40-token prompt, int8 GEMM")
     same_greedy(g, o)
+
+
+@pytest.mark.parametrize("arch,wtype", [("qwen3moe", O.Q4_K), ("qwen2moe", O.Q8_0)], ids=["qwen3moe", "qwen2moe"])
+def test_moe_prompt_grouped_expert_gemms(env, arch, wtype):
+    # 48 tokens: pairs sorted by expert on the device, one grouped tensor-core GEMM per stacked
+    # expert tensor (the shared expert through the plain GEMM), then decode steps on the GEMVs
+    from rust_interference_engine_b200 import model as M
+    spec = M.SyntheticSpec.tiny(arch, wtype)
+    gb, ob, keep = build_pair(env, spec, O.KV_F16, n_ctx=96, max_batch=64)
+    toks = np.random.default_rng(21).integers(0, spec.n_vocab, 48).astype(np.uint32)
+    g = gb.forward(toks, 0, all_logits=True)
+    o = ob.forward(toks, 0, all_logits=True)
+    close(g, o, RTOL_GEMM, "48-token MoE prompt")
+    same_greedy(g, o, RTOL_GEMM)
+    pos = 48
+    for step in range(2):
+        tok = np.array([int(np.argmax(o[-1]))], dtype=np.uint32)
+        g, o = gb.forward(tok, pos), ob.forward(tok, pos)
+        close(g, o, RTOL_GEMM, f"decode step {step}")
+        pos += 1
