@@ -106,6 +106,8 @@ void rcu_ctx_destroy(rcu_ctx *ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->h_act) cudaFree(ctx->h_act);
+    if (ctx->k_part) cudaFree(ctx->k_part);
+    if (ctx->k_cnt) cudaFree(ctx->k_cnt);
     delete ctx;
 }
 

@@ -79,6 +79,12 @@ struct HParams {
     // grp_tile[i]) over the activation rows [grp_off[e], grp_off[e + 1]) of that expert, and
     // blockIdx.x - tile0 the row tile within the expert. Output row = activation row.
     uint32_t grp, grp_rows;
+    // split K (one job, plain mode): blockIdx.z takes units [z * nu / splits, (z + 1) * nu /
+    // splits) of the nu = k / 256; every split writes its scaled tile to part[z] ([n_tok][rows]),
+    // and the last CTA of the output tile (counter cnt[tile], reset by it) adds them in z order
+    uint32_t splits;
+    float *part;
+    uint32_t *cnt;
     uint16_t grp_exp[kGrpMaxItems], grp_tile[kGrpMaxItems];
     uint32_t grp_off[kGrpMaxExperts + 1];
 };
@@ -283,6 +289,17 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                  : "memory");
 }
 
+// AND of v over the nthreads threads (whole warps) that reach named barrier id.
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n barrier.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // Every lane of the warp waits; the warp gives up together if any lane timed out.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
     const bool ok = mbar_wait_bounded(bar, parity, err, code);
@@ -316,7 +333,8 @@ __global__ void __launch_bounds__(kHThreads, 1)
         trow0 = blockIdx.y * p.nt;
         tcount = p.n_tok - trow0;
     }
-    const uint32_t n_unit = p.k / QK_K, n_it = n_unit * 4;
+    const uint32_t nu_all = p.k / QK_K, u_beg = blockIdx.z * nu_all / p.splits;
+    const uint32_t n_unit = (blockIdx.z + 1) * nu_all / p.splits - u_beg, n_it = n_unit * 4;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kHRawStages; s++) {
@@ -348,7 +366,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
                     !mbar_wait_bounded(&S.raw_empty[rs], ((u / kHRawStages) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
                     return false;
                 mbar_arrive_expect_tx(&S.raw_full[rs], BOX * kHRows);
-                tma_load_2d(S.raw[rs], mw, (int)(((u * UB) & ~15u) >> 1), (int)wrow0, &S.raw_full[rs]);
+                tma_load_2d(S.raw[rs], mw, (int)((((u_beg + u) * UB) & ~15u) >> 1), (int)wrow0, &S.raw_full[rs]);
                 units = u + 1;
                 return true;
             };
@@ -366,7 +384,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&S.b_full[s], p.nt * 128);
-                tma_load_2d(S.b[s], &map_b, (int)(it * 64), (int)trow0, &S.b_full[s]);
+                tma_load_2d(S.b[s], &map_b, (int)((u_beg * 4 + it) * 64), (int)trow0, &S.b_full[s]);
                 its = it + 1;
             }
             // drain: the last copy issued into each stage has landed (already true unless a
@@ -400,7 +418,7 @@ __global__ void __launch_bounds__(kHThreads, 1)
         const uint32_t rh = part & 1;  // which half of its 32-value group this thread dequantizes
         bool ok = true;
         for (uint32_t u = 0; u < n_unit && ok; u++) {
-            const uint32_t rs = u % kHRawStages, ofs = (u * UB) & 15u;
+            const uint32_t rs = u % kHRawStages, ofs = ((u_beg + u) * UB) & 15u;
             if (!warp_wait(&S.raw_full[rs], (u / kHRawStages) & 1, p.err, ERR_TIMEOUT_FULL)) {
                 ok = false;
                 break;
@@ -432,11 +450,17 @@ __global__ void __launch_bounds__(kHThreads, 1)
                  stage(std::integral_constant<int, 2>{}) && stage(std::integral_constant<int, 3>{});
         }
         pdl_wait();  // the output may still be read by the kernel before this one
-        if (ok && warp_wait(&S.acc_full, 0, p.err, ERR_TIMEOUT_FULL)) {
+        bool acc_ok = ok && warp_wait(&S.acc_full, 0, p.err, ERR_TIMEOUT_FULL);
+        // the epilogue warps agree, so that its named barriers see all of them or none
+        acc_ok = bar_and(1, kHUnpackWarps * 32, acc_ok);
+        if (acc_ok) {
             tc_fence_after();
             // the four warps of a lane quarter split the accumulator columns
             const uint32_t span = p.nt / (kHUnpackWarps / 4);
             const uint32_t n = col0 + r;
+            // one split: the output; several: this split's slice of the partial sums
+            float *dst = p.splits > 1 ? p.part + (uint64_t)blockIdx.z * p.n_tok * jb.rows : jb.out;
+            const uint64_t ld = p.splits > 1 ? jb.rows : jb.ld;
             for (uint32_t c = part * span; c < (part + 1) * span; c += 16) {
                 uint32_t x[16];
                 tmem_ld16(tmem + ((32 * q) << 16) + c, x);
@@ -445,7 +469,48 @@ __global__ void __launch_bounds__(kHThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
                         const uint32_t m = trow0 + c + e;
-                        if (c + e < tcount) jb.out[(uint64_t)m * jb.ld + n] = __uint_as_float(x[e]) * p.tok_scale[m];
+                        if (c + e < tcount) dst[(uint64_t)m * ld + n] = __uint_as_float(x[e]) * p.tok_scale[m];
+                    }
+                }
+            }
+            if (p.splits > 1) {  // the last split of this output tile adds the partial tiles in order
+                __shared__ uint32_t s_last;
+                __threadfence();
+                named_bar_sync(1, kHUnpackWarps * 32);
+                const uint32_t tile = blockIdx.y * gridDim.x + blockIdx.x;
+                if (warp == 2 && lane == 0) {
+                    const uint32_t done = atomicAdd(p.cnt + tile, 1u);
+                    s_last = done == p.splits - 1;
+                    if (s_last) p.cnt[tile] = 0;  // ready for the next launch
+                }
+                named_bar_sync(1, kHUnpackWarps * 32);
+                if (s_last) {
+                    // this split's values come from TMEM again, the others' from the partial
+                    // tiles (16 independent loads in flight per split), summed in split order
+                    __threadfence();
+                    for (uint32_t c = part * span; c < (part + 1) * span; c += 16) {
+                        uint32_t x[16];
+                        tmem_ld16(tmem + ((32 * q) << 16) + c, x);
+                        tmem_wait_ld();
+                        if (n >= col_lim) continue;
+                        float acc[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) acc[e] = 0.0f;
+                        for (uint32_t z = 0; z < p.splits; z++) {
+                            float v[16];
+#pragma unroll
+                            for (int e = 0; e < 16; e++) {
+                                const uint32_t m = trow0 + c + e;
+                                v[e] = z == blockIdx.z ? __uint_as_float(x[e]) * p.tok_scale[m]
+                                       : c + e < tcount ? __ldcg(p.part + ((uint64_t)z * p.n_tok + m) * jb.rows + n)
+                                                        : 0.0f;
+                            }
+#pragma unroll
+                            for (int e = 0; e < 16; e++) acc[e] += v[e];
+                        }
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            if (c + e < tcount) jb.out[(uint64_t)(trow0 + c + e) * jb.ld + n] = acc[e];
                     }
                 }
             }
@@ -522,20 +587,47 @@ bool gemm_f16_ok(const ActsView &a, const HostJob &j) {
     return a.n_tok >= kF16MinTok;
 }
 
-// Tokens per CTA: the fewest waves of CTAs, a tile of nt tokens costing about nt + 64 (the
-// dequantization of the weight tile is paid once per token tile).
-static uint32_t pick_nt(uint64_t tiles_w, uint32_t n_tok, int sms) {
-    uint32_t best = 64;
-    double best_cost = 1e300;
-    for (uint32_t nt : {256u, 192u, 128u, 64u}) {
-        const uint64_t ctas = tiles_w * ((n_tok + nt - 1) / nt);
-        const double cost = (double)((ctas + sms - 1) / sms) * (nt + 64);
-        if (cost < best_cost) {
-            best_cost = cost;
-            best = nt;
+// Tokens per CTA and K splits: the fewest waves of CTAs, a CTA costing about (nt + 64) per unit
+// of K 256 plus two units of fixed cost (the dequantization of its weight tile is paid once per
+// token tile). A single-weight launch may split K in 2 or 4 (at least 2 units per split,
+// partial sums at most 64 MB), paying for the ordered reduction of the partials. Measured on
+// 512 tokens: ffn_down 4096 x 12288 Q6_K 126 -> 88 us (2 splits), attn_v 1024 x 4096 Q6_K 45 ->
+// 32 us (4); more splits than 4 were slower everywhere.
+static void pick_tiling(uint64_t tiles_w, uint32_t n_tok, uint32_t n_unit, uint64_t split_rows, int sms, uint32_t *nt_out,
+                        uint32_t *splits_out) {
+    double best = 1e300;
+    *nt_out = 64, *splits_out = 1;
+    for (uint32_t nt : {256u, 192u, 128u, 64u})
+        for (uint32_t sp : {1u, 2u, 4u}) {
+            if (sp > 1 && (split_rows == 0 || n_unit / sp < 2 ||
+                           (uint64_t)sp * n_tok * split_rows * 4 > (64ull << 20)))
+                continue;
+            const uint64_t ctas = tiles_w * ((n_tok + nt - 1) / nt) * sp;
+            const double per = ((double)n_unit / sp + 2.0) * (nt + 64) + (sp > 1 ? sp * nt / 2.0 : 0.0);
+            const double cost = (double)((ctas + sms - 1) / sms) * per;
+            if (cost < best) best = cost, *nt_out = nt, *splits_out = sp;
         }
+}
+
+static int ensure_split_scratch(rcu_ctx *ctx, size_t part_bytes, size_t cnt_bytes) {
+    if (ctx->k_part_cap < part_bytes) {
+        RCU_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        if (ctx->k_part) cudaFree(ctx->k_part);
+        ctx->k_part = nullptr;
+        ctx->k_part_cap = 0;
+        RCU_CUDA_TRY(ctx, cudaMalloc(&ctx->k_part, part_bytes));
+        ctx->k_part_cap = part_bytes;
     }
-    return best;
+    if (ctx->k_cnt_cap < cnt_bytes) {  // counters start at zero; each launch leaves them at zero
+        RCU_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        if (ctx->k_cnt) cudaFree(ctx->k_cnt);
+        ctx->k_cnt = nullptr;
+        ctx->k_cnt_cap = 0;
+        RCU_CUDA_TRY(ctx, cudaMalloc((void **)&ctx->k_cnt, cnt_bytes));
+        RCU_CUDA_TRY(ctx, cudaMemset(ctx->k_cnt, 0, cnt_bytes));
+        ctx->k_cnt_cap = cnt_bytes;
+    }
+    return RCU_OK;
 }
 
 static int ensure_f16_scratch(rcu_ctx *ctx, size_t bytes) {
@@ -575,7 +667,16 @@ static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const float *tok_sc
             return st;
     }
     if (tiles >= (1u << 31)) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: too many row tiles");
-    const uint32_t nt = pick_nt(tiles, a.n_tok, ctx->num_sms);
+    uint32_t nt = 0, splits = 1;
+    pick_tiling(tiles, a.n_tok, a.k / QK_K, n_jobs == 1 ? jobs[0].w->rows : 0, ctx->num_sms, &nt, &splits);
+    if (splits > 1) {
+        const size_t part = (size_t)splits * a.n_tok * jobs[0].w->rows * sizeof(float);
+        const size_t cnt = (size_t)tiles * ((a.n_tok + nt - 1) / nt) * sizeof(uint32_t);
+        if (int st = ensure_split_scratch(ctx, part, cnt)) return st;
+        p.part = reinterpret_cast<float *>(ctx->k_part);
+        p.cnt = ctx->k_cnt;
+    }
+    p.splits = splits;
     p.n_jobs = (uint32_t)n_jobs;
     p.tok_scale = tok_scale;
     p.k = a.k;
@@ -591,7 +692,7 @@ static int launch_f16_type(rcu_ctx *ctx, const __half *bact, const float *tok_sc
         return st;
     const size_t smem = sizeof(HSmem) + 1024;
     RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemm_f16<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const dim3 grid((uint32_t)tiles, (a.n_tok + nt - 1) / nt);
+    const dim3 grid((uint32_t)tiles, (a.n_tok + nt - 1) / nt, splits);
     RCU_CUDA_TRY(ctx, launch_k(ctx, k_gemm_f16<TYPE>, grid, dim3(kHThreads), smem, maps, mb, p));
     return RCU_OK;
 }
@@ -690,6 +791,7 @@ static int launch_grouped_type(rcu_ctx *ctx, const __half *act, const float *sca
     for (uint32_t e = 0; e <= n_exp; e++) p.grp_off[e] = off[e];
     p.grp = n_items;
     p.grp_rows = grp_rows;
+    p.splits = 1;
     p.tok_scale = scale;
     p.n_jobs = (uint32_t)n_jobs;
     p.k = k;

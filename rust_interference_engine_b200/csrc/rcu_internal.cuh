@@ -180,6 +180,10 @@ struct rcu_ctx {
     bool gemm_i8 = false;          // prefill: int8 GEMM with exact block sums for Q4_0 weights
     void *h_act = nullptr;         // f16 activations of the prefill GEMM (grown on demand)
     size_t h_act_cap = 0;
+    void *k_part = nullptr;        // split-K partial tiles of the prefill GEMM (grown on demand)
+    size_t k_part_cap = 0;
+    uint32_t *k_cnt = nullptr;     // split-K tile counters (zero between launches)
+    size_t k_cnt_cap = 0;
     std::string last_error;
 };
 

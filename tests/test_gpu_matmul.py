@@ -198,6 +198,20 @@ def test_prefill_gemm_f16_all_types(env, t, n_tok, rows, k):
     close(got, want)
 
 
+def test_prefill_gemm_split_k_is_deterministic(env):
+    # few row tiles: K is split over CTAs and the partial tiles are added in a fixed order by
+    # the last CTA of each tile (counters reset for the next launch): repeated calls agree bit
+    # for bit and with the oracle
+    torch, rie, ctx = env
+    rng = O.Rng(99)
+    n_tok, rows, k = 96, 256, 8192
+    w = rng.weight(O.Q4_K, rows, k)
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    outs = [gpu_matmul(env, [(O.Q4_K, w, k)], x)[0][0] for _ in range(3)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    close(outs[0], O.matmul_multi(x, [(O.Q4_K, w, k)], n_threads=8)[0])
+
+
 def test_prefill_gemm_f16_jobs_share_a_launch(env):
     # q/k/v-like jobs of one type share a launch; a second type and format follow
     rng = O.Rng(77)
