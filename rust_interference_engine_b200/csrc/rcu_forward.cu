@@ -348,6 +348,73 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_q(float *__restrict__ x, 
     }
 }
 
+// k_norm_q with 8 consecutive values per thread (e / 8 threads, whole warps): a warp spans one
+// Q8_K block (or eight Q8_0 blocks), so only the two RMS sums need CTA barriers. Same
+// arithmetic as k_norm_q; rows of whole 256-value blocks, at most 8192 values.
+__device__ __forceinline__ void ld8(const float *p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void st8(float *p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__global__ void __launch_bounds__(1024) k_norm_q8(float *__restrict__ x, const float *__restrict__ o,
+                                                  const float *__restrict__ post_w, float rs,
+                                                  const float *__restrict__ w, uint32_t e, float eps,
+                                                  float *__restrict__ xn_f32, const ActOut ao, int x_ready,
+                                                  const ArSum ar) {
+    __shared__ float red[32];
+    const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, i0 = 8 * tid;
+    float *xr = x + (uint64_t)t * e + i0;
+    float v[8], wv[8], pw[8];
+    ld8(w + i0, wv);
+    if (post_w) ld8(post_w + i0, pw);
+    if (x_ready) ld8(xr, v);
+    pdl_wait();
+    pdl_trigger();
+    if (!x_ready) ld8(xr, v);
+    if (o || ar.P) {
+        float ov[8];
+        if (ar.P) {
+            ar_wait(ar);
+#pragma unroll
+            for (int j = 0; j < 8; j++) ov[j] = 0.0f;
+            for (uint32_t q = 0; q < ar.P; q++) {
+                const float4 *src = reinterpret_cast<const float4 *>(ar.src + (uint64_t)q * ar.stride + (uint64_t)t * e + i0);
+                const float4 a = __ldcg(src), b = __ldcg(src + 1);
+                ov[0] += a.x, ov[1] += a.y, ov[2] += a.z, ov[3] += a.w;
+                ov[4] += b.x, ov[5] += b.y, ov[6] += b.z, ov[7] += b.w;
+            }
+        } else {
+            ld8(o + (uint64_t)t * e + i0, ov);
+        }
+        if (post_w) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; j++) ss += ov[j] * ov[j];
+            ss = block_sum(ss, red);
+            const float scale = 1.0f / sqrtf(ss / (float)e + eps);
+#pragma unroll
+            for (int j = 0; j < 8; j++) ov[j] *= scale * pw[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] += rs == 1.0f ? ov[j] : ov[j] * rs;
+        st8(xr, v);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) ss += v[j] * v[j];
+    ss = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)e + eps);
+    float xn[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) xn[j] = v[j] * scale * wv[j];
+    if (xn_f32) st8(xn_f32 + (uint64_t)t * e + i0, xn);
+    if (ao.fmt & RCU_ACT_Q8_0) q8_0_block8(xn, (uint64_t)t * (e / QK) + i0 / QK, lane, true, ao);
+    if (ao.fmt & RCU_ACT_Q8K) q8_k_block8(xn, (uint64_t)t * (e / QK_K) + i0 / QK_K, lane, ao);
+}
+
 // g = act(g) * u (SwiGLU / GELU-tanh, ops.rs:41-58) quantized for the down matmul; one
 // value per thread, grid (ceil(ff / 1024), tokens).
 __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, const float *__restrict__ u, uint32_t ff,
@@ -373,6 +440,53 @@ __global__ void __launch_bounds__(1024) k_glu_q(const float *__restrict__ g, con
         const uint32_t g0 = blockIdx.x * 1024 + QK_K * (warp / 8);
         q8_k_block(f, tid % QK_K, warp & ~7u, (uint64_t)t * (ff / QK_K) + g0 / QK_K, g0 < ff, ao, sh, 0);
     }
+}
+
+// The same with 8 consecutive values per thread (two float4 loads of g and u): a warp spans one
+// Q8_K block (or eight Q8_0 blocks), so the quantization needs no CTA barrier. 256 threads cover
+// 2048 values; grid (ceil(ff / 2048), tokens). Rows of whole 256-value blocks (Q8_K) or 32-value
+// blocks (Q8_0 only).
+constexpr int kGlu8Threads = 256;
+__global__ void __launch_bounds__(kGlu8Threads) k_glu_q8(const float *__restrict__ g, const float *__restrict__ u,
+                                                         uint32_t ff, int act, const ActOut ao) {
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t t = blockIdx.y, lane = threadIdx.x & 31;
+    const uint32_t i0 = (blockIdx.x * kGlu8Threads + threadIdx.x) * 8;  // first value of this thread
+    const bool in = i0 < ff;
+    float f[8];
+    if (in) {
+        const float4 *gp = reinterpret_cast<const float4 *>(g + (uint64_t)t * ff + i0);
+        const float4 *up = reinterpret_cast<const float4 *>(u + (uint64_t)t * ff + i0);
+        const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float a = gv[i];
+            const float y = act == 1 ? 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a)))
+                                     : a / (1.0f + expf(-a));
+            f[i] = y * uv[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) f[i] = 0.0f;
+    }
+    if (ao.fmt & RCU_ACT_Q8_0) q8_0_block8(f, (uint64_t)t * (ff / QK) + i0 / QK, lane, in, ao);
+    if ((ao.fmt & RCU_ACT_Q8K) && (i0 & ~(QK_K - 1)) < ff) q8_k_block8(f, (uint64_t)t * (ff / QK_K) + i0 / QK_K, lane, ao);
+}
+
+// GLU + quantization of `rows` rows of ff values (k_glu_q8 when the row holds whole blocks).
+static int launch_glu(rcu_ctx *ctx, const float *g, const float *u, uint32_t ff, uint32_t rows, int act,
+                      const ActOut &ao) {
+    if (rows == 0) return RCU_OK;
+    const bool whole = (ao.fmt & RCU_ACT_Q8K) ? ff % QK_K == 0 : ff % QK == 0;
+    if (whole)
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q8), dim3((ff + 8 * kGlu8Threads - 1) / (8 * kGlu8Threads), rows),
+                                   dim3(kGlu8Threads), 0, g, u, ff, act, ao));
+    else
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((ff + 1023) / 1024, rows), dim3(1024), 0, g, u, ff, act, ao));
+    return RCU_OK;
 }
 
 // ---- mixture of experts (model/cpu.rs:469-524) ---------------------------------------------
@@ -583,6 +697,11 @@ static int norm_q(rcu_backend *b, uint64_t n, float *x, const float *o, const fl
     const uint32_t e = c.n_embd, nit = (e + kNormThreads - 1) / kNormThreads;
     const ActOut ao = acts_out(b, fmt);
     const float rs = c.residual_scale, eps = c.rms_eps;
+    if (e % QK_K == 0 && e <= 8192) {
+        RCU_CUDA_TRY(b->ctx, launch_k(b->ctx, k_norm_q8, dim3((uint32_t)n), dim3(e / 8), 0, x, o, post_w, rs, w, e, eps,
+                                      xn_f32, ao, x_ready ? 1 : 0, ar));
+        return RCU_OK;
+    }
     auto kern = nit <= 1 ? k_norm_q<1> : nit <= 2 ? k_norm_q<2> : nit <= 4 ? k_norm_q<4> : nit <= 8 ? k_norm_q<8> : k_norm_q<16>;
     if (nit > 16) return set_err(b->ctx, RCU_ERR_UNSUPPORTED, "n_embd above 16384");
     RCU_CUDA_TRY(b->ctx, launch_k(b->ctx, kern, dim3((uint32_t)n), dim3(kNormThreads), 0, x, o, post_w, rs, w, e, eps,
@@ -661,8 +780,8 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
     if (shared_here) {
         const uint32_t fs = (uint32_t)L.gate_sh->rows, fsd = formats({L.down_sh});
         if (int st = matmul(b, (uint32_t)n, e, fx_in, {{L.gate_sh, b->g, fs}, {L.up_sh, b->u, fs}})) return st;
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fs + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, fs,
-                                   c.act, act_out(b->acts2->v, fsd, ctx->rounding)));
+        if (int st = launch_glu(ctx, b->g, b->u, fs, (uint32_t)n, c.act, act_out(b->acts2->v, fsd, ctx->rounding)))
+            return st;
         b->acts2->v.n_tok = (uint32_t)n;
         b->acts2->v.k = fs;
         b->acts2->v.have = fsd;
@@ -679,8 +798,8 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
                 return st;
             const HostJob gu[2] = {{L.gate_exps, b->moe_g, fx}, {L.up_exps, b->moe_u, fx}};
             if (int st = launch_gemm_f16_grouped(ctx, act, sc, n_slots, e, gu, 2, fx, b->moe_off_host, n_loc)) return st;
-            RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, n_slots), dim3(1024), 0, b->moe_g,
-                                       b->moe_u, fx, c.act, act_out(b->acts2->v, fdn, ctx->rounding)));
+            if (int st = launch_glu(ctx, b->moe_g, b->moe_u, fx, n_slots, c.act, act_out(b->acts2->v, fdn, ctx->rounding)))
+                return st;
             if (int st = gemm_f16_gather(ctx, view(b->acts2, n_slots, fx, fdn), fdn, nullptr, n_slots, &act, &sc))
                 return st;
             const HostJob dj{L.down_exps, b->moe_y, e};
@@ -709,9 +828,9 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
                                          (int)std::min<size_t>(kGemvMaxJobs, gu.size() - j0), c0, 1))
                     return st;
             const uint64_t r0 = (uint64_t)c0 * k;
-            RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((fx + 1023) / 1024, nt * k), dim3(1024), 0,
-                                       b->moe_g + r0 * fx, b->moe_u + r0 * fx, fx, c.act,
-                                       act_out(b->acts2->v, fdn, ctx->rounding)));
+            if (int st = launch_glu(ctx, b->moe_g + r0 * fx, b->moe_u + r0 * fx, fx, nt * k, c.act,
+                                    act_out(b->acts2->v, fdn, ctx->rounding)))
+                return st;
             for (size_t j0 = 0; j0 < dn.size(); j0 += kGemvMaxJobs)
                 if (int st = launch_gemv(ctx, view(b->acts2, nt * k, fx, fdn), dn.data() + j0,
                                          (int)std::min<size_t>(kGemvMaxJobs, dn.size() - j0), 0, 1))
@@ -828,8 +947,7 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
                               {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
             return st;
         const uint32_t fd = formats({L.down});
-        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_glu_q), dim3((ff + 1023) / 1024, (uint32_t)n), dim3(1024), 0, b->g, b->u, ff,
-                                   c.act, acts_out(b, fd)));
+        if ((st = launch_glu(ctx, b->g, b->u, ff, (uint32_t)n, c.act, acts_out(b, fd)))) return st;
         if ((st = row_parallel(L.down, ff, ar_j++, &pend_ar))) return st;
         pend_o = fused ? nullptr : b->o;
         pend_post = L.post_ffn;
