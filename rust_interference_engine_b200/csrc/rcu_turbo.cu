@@ -187,18 +187,32 @@ __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restr
 // RoPE (ops.rs:65-99), then q heads are scaled by attn_scale and written back, while k and v
 // heads go straight into the cache at slot (pos + t) % slots (cpu.rs:280-328).
 // Vectors: [t][0..n_head) = q heads, [t][n_head..n_head+n_kv) = k heads, then v heads.
-__global__ void __launch_bounds__(128) k_qkv_post_store(QkvPostParams p, int type, uint32_t n_kv, uint32_t slots,
-                                                        uint32_t row_bytes, uint8_t *__restrict__ kc,
-                                                        uint8_t *__restrict__ vc) {
+// Grid (tokens, ceil(vectors / 8)); the CTA computes its token's RoPE angles once (the same
+// sincosf of pos * inv_freq[i] for every head) and its 8 warps take one vector each.
+constexpr int kQkvWarps = 8;
+__global__ void __launch_bounds__(kQkvWarps * 32) k_qkv_post_store(QkvPostParams p, int type, uint32_t n_kv,
+                                                                   uint32_t slots, uint32_t row_bytes,
+                                                                   uint8_t *__restrict__ kc, uint8_t *__restrict__ vc) {
     pdl_wait();
     pdl_trigger();
-    __shared__ float buf[4][kMaxHd];
-    __shared__ uint8_t qs[4][kMaxHd];
+    __shared__ float buf[kQkvWarps][kMaxHd];
+    __shared__ uint8_t qs[kQkvWarps][kMaxHd];
+    __shared__ float rope_cs[2][kMaxHd / 2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t hd = p.hd, per_tok = p.n_head + 2 * n_kv;
-    const uint64_t item = (uint64_t)blockIdx.x * 4 + warp;
-    if (item >= (uint64_t)p.n_tok * per_tok) return;
-    const uint32_t t = (uint32_t)(item / per_tok), j = (uint32_t)(item % per_tok);
+    const uint32_t hd = p.hd, per_tok = p.n_head + 2 * n_kv, t = blockIdx.x, half = p.rope_dim / 2;
+    const uint64_t pos = *p.pos_ptr + t;
+    {
+        const float fpos = (float)pos;
+        for (uint32_t i = threadIdx.x; i < half; i += kQkvWarps * 32) {
+            float sn, cs;
+            sincosf(fpos * p.inv_freq[i], &sn, &cs);
+            rope_cs[0][i] = cs;
+            rope_cs[1][i] = sn;
+        }
+    }
+    __syncthreads();
+    const uint32_t j = blockIdx.y * kQkvWarps + warp;
+    if (j >= per_tok) return;
     const float *src, *bias, *norm;
     int kind;  // 0 q, 1 k, 2 v
     uint32_t h;
@@ -223,13 +237,9 @@ __global__ void __launch_bounds__(128) k_qkv_post_store(QkvPostParams p, int typ
         for (uint32_t i = lane; i < hd; i += 32) x[i] *= scale * norm[i];
         __syncwarp();
     }
-    const uint64_t pos = *p.pos_ptr + t;
     if (kind != 2) {
-        const uint32_t half = p.rope_dim / 2;
-        const float fpos = (float)pos;
         for (uint32_t i = lane; i < half; i += 32) {
-            float sn, cs;
-            sincosf(fpos * p.inv_freq[i], &sn, &cs);
+            const float cs = rope_cs[0][i], sn = rope_cs[1][i];
             const uint32_t i0 = p.neox ? i : 2 * i, i1 = p.neox ? i + half : 2 * i + 1;
             const float a = x[i0], b = x[i1];
             x[i0] = a * cs - b * sn;
@@ -729,8 +739,11 @@ int launch_qkv_post_store(rcu_ctx *ctx, rcu_kv *kv, const QkvPostParams &p) {
     if (kv->type == RCU_KV_TURBO4) {
         if (int st = ensure_signs(ctx)) return st;
     }
-    const uint64_t items = (uint64_t)p.n_tok * (p.n_head + 2 * kv->n_kv);
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_qkv_post_store), dim3((uint32_t)((items + 3) / 4)), dim3(128), 0, p, kv->type, (uint32_t)kv->n_kv, (uint32_t)kv->slots, (uint32_t)kv->row_bytes, kv->k, kv->v));
+    if (p.rope_dim > p.hd || p.rope_dim % 2) return set_err(ctx, RCU_ERR_INVALID, "qkv post: rope_dim");
+    const uint32_t per_tok = p.n_head + 2 * (uint32_t)kv->n_kv;
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_qkv_post_store), dim3(p.n_tok, (per_tok + kQkvWarps - 1) / kQkvWarps),
+                               dim3(kQkvWarps * 32), 0, p, kv->type, (uint32_t)kv->n_kv, (uint32_t)kv->slots,
+                               (uint32_t)kv->row_bytes, kv->k, kv->v));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
