@@ -198,6 +198,7 @@ def run_gemv(args, world, rank, local):
     torch.cuda.set_device(local)
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
+    ctx.set_static_weights(True)  # weights are uploaded once: matmuls stream them early (PDL)
     mats, x = gemv_weights()
     ws = [rie.Weight.upload(ctx, getattr(rie.GgmlType, GEMV_TYPE), GEMV_ROWS, GEMV_K, mats[i % GEMV_DISTINCT])
           for i in range(GEMV_COPIES)]
@@ -580,6 +581,7 @@ def run_decode(args, world, rank, local):
     acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
     og = torch.zeros(2, spec.n_ff, device="cuda")
     jobs = [[rie.MatmulJob(gu[2 * i], og[0]), rie.MatmulJob(gu[2 * i + 1], og[1])] for i in range(8)]
+    ctx.set_static_weights(True)  # as inside the forward: weights stream while the previous launch ends
     for j in jobs:
         rie.matmul_multi(ctx, acts, j)
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -724,6 +726,7 @@ def run_moe(args, world, rank, local):
     xg = torch.randn(1, spec.n_embd, device="cuda")
     acts = rie.QuantActs(ctx, 1, spec.n_embd)
     acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
+    ctx.set_static_weights(True)  # as inside the forward: weights stream while the previous launch ends
     og = torch.zeros(16, spec.n_ff_exp, device="cuda")
     jobs = [[rie.MatmulJob(ws[16 * g + j], og[j]) for j in range(16)] for g in range(12)]
     for j in jobs:

@@ -72,6 +72,11 @@ RCU_API int32_t rcu_set_rounding(rcu_ctx *ctx, int32_t mode);
  * (other types keep the f16 kernel). Both stay within the matmul tolerance of the reference. */
 enum rcu_gemm_kind { RCU_GEMM_F16 = 0, RCU_GEMM_I8 = 1 };
 RCU_API int32_t rcu_set_prefill_gemm(rcu_ctx *ctx, int32_t kind);
+/* Caller promise (no counterpart in the reference): the weights of this context are never
+ * written by a kernel after their upload. A matmul may then stream its weights before the
+ * kernel ahead of it in the stream has finished (programmatic dependent launch), as the
+ * forward always does. Off by default. */
+RCU_API int32_t rcu_set_static_weights(rcu_ctx *ctx, int32_t on);
 /* Last error message of this context ("" if none). Valid until the next call. */
 RCU_API const char *rcu_last_error(const rcu_ctx *ctx);
 /* Waits for all work on the context stream; returns RCU_ERR_TIMEOUT if any bounded

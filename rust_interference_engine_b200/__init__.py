@@ -131,6 +131,11 @@ class Context:
     def set_rounding(self, mode: Rounding) -> None:
         _check(self.ptr, self._lib.rcu_set_rounding(self.ptr, int(mode)))
 
+    def set_static_weights(self, on: bool) -> None:
+        """Promise that weights are never written by a kernel after upload (lets matmuls
+        stream them before the previous kernel finishes)."""
+        _check(self.ptr, self._lib.rcu_set_static_weights(self.ptr, int(bool(on))))
+
     def set_prefill_gemm(self, kind: "PrefillGemm") -> None:
         _check(self.ptr, self._lib.rcu_set_prefill_gemm(self.ptr, int(kind)))
 

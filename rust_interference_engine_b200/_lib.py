@@ -23,6 +23,7 @@ SIGNATURES = {
     "rcu_set_stream": (I32, [P, P]),
     "rcu_set_rounding": (I32, [P, I32]),
     "rcu_set_prefill_gemm": (I32, [P, I32]),
+    "rcu_set_static_weights": (I32, [P, I32]),
     "rcu_last_error": (C.c_char_p, [P]),
     "rcu_sync": (I32, [P]),
     "rcu_check_device": (I32, [P, C.POINTER(U32)]),

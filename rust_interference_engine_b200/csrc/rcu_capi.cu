@@ -125,6 +125,13 @@ int32_t rcu_set_rounding(rcu_ctx *ctx, int32_t mode) {
     return RCU_OK;
 }
 
+int32_t rcu_set_static_weights(rcu_ctx *ctx, int32_t on) {
+    if (!ctx) return RCU_ERR_INVALID;
+    ctx->static_weights = on != 0;
+    ctx->early_weights = ctx->static_weights;
+    return RCU_OK;
+}
+
 int32_t rcu_set_prefill_gemm(rcu_ctx *ctx, int32_t kind) {
     if (!ctx) return RCU_ERR_INVALID;
     if (kind != RCU_GEMM_F16 && kind != RCU_GEMM_I8) return set_err(ctx, RCU_ERR_INVALID, "unknown prefill GEMM kind");

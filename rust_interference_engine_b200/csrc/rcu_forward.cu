@@ -1564,7 +1564,7 @@ static int32_t run_forward(rcu_backend *b, const uint32_t *tokens, bool tokens_o
         cudaStream_t s;
         ~Restore() {
             c->stream = s;
-            c->early_weights = false;
+            c->early_weights = c->static_weights;
         }
     } restore{ctx, caller};
     const cudaMemcpyKind kind = tokens_on_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;

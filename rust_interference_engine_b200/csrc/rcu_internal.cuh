@@ -177,6 +177,7 @@ struct rcu_ctx {
     // GEMV weights may be streamed before the previous kernel has finished (set while the
     // forward scheduler runs: its weights are written once, at load time)
     bool early_weights = false;
+    bool static_weights = false;  // caller promise (rcu_set_static_weights): early_weights outside the forward too
     bool gemm_i8 = false;          // prefill: int8 GEMM with exact block sums for Q4_0 weights
     void *h_act = nullptr;         // f16 activations of the prefill GEMM (grown on demand)
     size_t h_act_cap = 0;
