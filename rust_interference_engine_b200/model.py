@@ -90,7 +90,9 @@ class SyntheticSpec:
         c.swa_pattern = 2 if self.arch == "gemma2" else (6 if self.arch == "gemma3" else 0)
         c.rope_base_swa = 10000.0 if self.arch == "gemma3" else 0.0
         c.act = 1 if gemma else 0
-        c.n_expert, c.n_expert_used, c.n_ff_exp = self.n_expert, self.n_expert_used, self.n_ff_exp
+        # expert_feed_forward_length, else feed_forward_length (config.rs:165)
+        c.n_expert, c.n_expert_used = self.n_expert, self.n_expert_used
+        c.n_ff_exp = self.n_ff_exp if self.n_expert else self.n_ff
         c.expert_norm_topk = int(self.arch != "qwen2moe")  # expert_weights_norm default (config.rs:167)
         c.expert_unit_weights = 0
         return c
@@ -202,6 +204,18 @@ class Model:
         lib = _lib.load()
         self.ptr = C.c_void_p()
         _check(ctx.ptr, lib.rcu_model_create_tp(ctx.ptr, C.byref(cfg), rank, world, C.byref(self.ptr)))
+
+    @classmethod
+    def load_gguf(cls, ctx, path_or_file, rank: int = 0, world: int = 1) -> "Model":
+        """A model of a GGUF file (or parsed GgufFile): configuration from its metadata
+        (model/config.rs:106-247), every tensor's GGUF bytes uploaded unchanged; with world > 1
+        each rank keeps its tensor-parallel shard."""
+        from rust_interference_engine_b200 import gguf
+        g = path_or_file if isinstance(path_or_file, gguf.GgufFile) else gguf.GgufFile.open(path_or_file)
+        m = cls(ctx, gguf.config_from_gguf(g), rank, world)
+        for t in g.tensors:
+            m.set_tensor(t.name, t.type, t.n_rows, t.row_len, g.tensor_data(t))
+        return m
 
     def set_tensor(self, name: str, ty: int, rows: int, cols: int, data) -> None:
         a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)

@@ -224,3 +224,27 @@ def test_moe_prompt_grouped_expert_gemms(env, arch, wtype):
         g, o = gb.forward(tok, pos), ob.forward(tok, pos)
         close(g, o, RTOL_GEMM, f"decode step {step}")
         pos += 1
+
+
+@pytest.mark.parametrize("arch,wtype", [("qwen3", O.Q4_K), ("qwen2moe", O.Q8_0)], ids=["qwen3", "qwen2moe"])
+def test_model_from_gguf_file(env, tmp_path, arch, wtype):
+    # a synthetic model written as a GGUF file and loaded through Model.load_gguf (metadata ->
+    # configuration, tensors uploaded unchanged) gives the same logits as the same tensors set
+    # one by one
+    torch, rie, M, ctx = env
+    from rust_interference_engine_b200 import gguf
+    spec = M.SyntheticSpec.tiny(arch, wtype)
+    gb, ob, (gm, om) = build_pair(env, spec, O.KV_F16)
+    rng = O.Rng(1)  # build_pair's seed: the same tensors again
+    weight = lambda t, r, c: rng.weight(int(t), r, c)
+    vec = lambda n, s: rng.vec(n, s)
+    norm = lambda n: (1.0 + 0.1 * rng.vec(n, 1.0)).astype(np.float32)
+    path = tmp_path / "model.gguf"
+    gguf.spec_writer(spec, M.synthetic_tensors(spec, weight, vec, norm)).write(path)
+    fm = M.Model.load_gguf(ctx, path)
+    fb = M.CudaBackend(fm, 64, 16, rie.KvType.F16)
+    toks = np.random.default_rng(3).integers(0, spec.n_vocab, 7).astype(np.uint32)
+    a = fb.forward(toks, 0, all_logits=True)
+    b = gb.forward(toks, 0, all_logits=True)
+    assert np.array_equal(a, b)
+    close(a, ob.forward(toks, 0, all_logits=True), what="GGUF model vs oracle")
