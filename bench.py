@@ -181,6 +181,16 @@ def gemv_bytes_per_step():
     return GEMV_COPIES * (w + GEMV_K * 4 + GEMV_ROWS * 4), w
 
 
+def gemv_kernel_name(wtype: str, launch_bytes: int) -> str:
+    """The batch-1 GEMV kernel the library picks: the tensor-core K-quant kernel for Q4_K /
+    Q5_K / Q6_K launches of at least 8 MiB of weights (default of RIE_GEMV_KQ_MIN_MB), else
+    the lane kernel."""
+    min_mb = int(os.environ.get("RIE_GEMV_KQ_MIN_MB", "8"))
+    if wtype in ("Q4_K", "Q5_K", "Q6_K") and launch_bytes >= (min_mb << 20) and os.environ.get("RIE_GEMV_KQ") != "0":
+        return "k_gemv_kq"
+    return "k_gemv<1,16>"
+
+
 def gemv_meta():
     kq = GEMV_TYPE.endswith("_K")
     tag = "config 1" if GEMV_TYPE == "Q4_0" else "config-1 shape"
@@ -282,7 +292,8 @@ def run_gemv(args, world, rank, local):
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic(gm["workload"]),
-                     "kernel": "k_gemv<1,16>", "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
+                     "kernel": gemv_kernel_name(GEMV_TYPE, step_bytes // (1 if not GEMV_EACH else GEMV_COPIES)),
+                     "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
         "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_COPIES * GEMV_ROWS * 4,
                 "ms_per_step": e2e_ms},
@@ -615,7 +626,8 @@ def run_decode(args, world, rank, local):
                    "pp_tok_s": pp_tps, "prefill_batch": nb, "model_build_s": t_build},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_gate_up"),
-                     "kernel": "k_gemv<1,16> (gate+up, 2 x 12288 x 4096 Q4_K)", "bytes_per_launch": gemv_bytes,
+                     "kernel": gemv_kernel_name("Q4_K", gemv_bytes) + " (gate+up, 2 x 12288 x 4096 Q4_K)",
+                     "bytes_per_launch": gemv_bytes,
                      "launch_ms": gemv_ms,
                      "whole_step_weight_gb_s": (wbytes + kv_bytes) / (ms * 1e-3) / 1e9},
         "e2e": {"value": dist_min(e2e_tps, world), "unit": "tok/s", "h2d_bytes_per_step": 4,

@@ -507,13 +507,21 @@ bool kq_plan(const rcu_weight *w, uint32_t k, bool congruent, KqJob &jd) {
 
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs || !(a.have & RCU_ACT_Q8K)) return false;
+    uint64_t bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
         KqJob jd{};
         if (!kq_plan(jobs[i].w, a.k, ctx->gemv_kq_congruent, jd)) return false;
         if (jobs[i].sel && jobs[i].w_stride % 16 != 0) return false;
         if (jobs[i].tok + 1 > kQMaxStageRows) return false;
+        bytes += (uint64_t)(jobs[i].rows ? jobs[i].rows : jobs[i].w->rows) * jobs[i].w->row_bytes;
     }
-    return true;
+    // Small launches take the lane GEMV: this kernel's start-up (activation staging, the first
+    // tile's latency chain) is longer, and with 1-2 tiles per CTA nothing hides it; K = 768
+    // expert rows also give it few tiles (256-row tiles). Measured on B200: back-to-back launches
+    // of one shape, 7 MB Q4_K 12.4 us here vs 6.0 lane, 9.4 MB 12.6 vs 8.1, 28 MB 12.5 vs 17.0,
+    // 41 MB Q6_K 13.0 vs 21.5, 510 MB Q6_K 131 vs 260; serialized (profiler) 9.4 MB Q4_K 9.4 vs
+    // 10.4 us, and the Qwen3-8B decode step (every launch >= 9.4 MB here) 2.67 ms vs 3.48 ms.
+    return bytes >= ctx->gemv_kq_min_bytes;
 }
 
 int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,

@@ -25,3 +25,26 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(scope="module", params=["kq", "lane"])
+def gemv_ctx(request):
+    """A context whose batch-1 Q4_K / Q5_K / Q6_K matmuls take the tensor-core GEMV at every
+    launch size ("kq") or always the lane GEMV ("lane"); by default the library picks by
+    launch size, so both kernels are exercised on the small test shapes this way. The
+    library reads these settings when the context is created."""
+    import torch
+    import rust_interference_engine_b200 as rie
+    keys = ("RIE_GEMV_KQ", "RIE_GEMV_KQ_MIN_MB")
+    old = {k: os.environ.get(k) for k in keys}
+    os.environ["RIE_GEMV_KQ"] = "1" if request.param == "kq" else "0"
+    os.environ["RIE_GEMV_KQ_MIN_MB"] = "0"
+    try:
+        ctx = rie.Context(0, torch.cuda.current_stream())
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return torch, rie, ctx

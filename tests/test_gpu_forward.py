@@ -23,11 +23,9 @@ def close(a, b, rtol=RTOL, what=""):
 
 
 @pytest.fixture(scope="module")
-def env():
-    import torch
-    import rust_interference_engine_b200 as rie
+def env(gemv_ctx):
     from rust_interference_engine_b200 import model as M
-    ctx = rie.Context(0, torch.cuda.current_stream())
+    torch, rie, ctx = gemv_ctx
     return torch, rie, M, ctx
 
 

@@ -14,11 +14,8 @@ RTOL = 1e-3
 
 
 @pytest.fixture(scope="module")
-def env():
-    import torch
-    import rust_interference_engine_b200 as rie
-    ctx = rie.Context(0, torch.cuda.current_stream())
-    return torch, rie, ctx
+def env(gemv_ctx):
+    return gemv_ctx
 
 
 def close(a, b, rtol=RTOL):
