@@ -633,7 +633,10 @@ def run_decode(args, world, rank, local):
         "e2e": {"value": dist_min(e2e_tps, world), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": spec.n_vocab * 4, "ms_per_step": 1000.0 * e2e_s / args.steps,
                 "api": "CudaBackend.forward (rcu_backend_forward, host tokens/logits, greedy)"},
-        "gpu_launches": args.steps * (17 * spec.n_layer + 5),
+        # per token: 9 per layer (norm, QKV GEMV, q/k post + KV append, attention, Wo GEMV, norm,
+        # gate+up GEMV, GLU, down GEMV) + position, embedding, final norm, head GEMV (NCCL's own
+        # kernels at N > 1 not counted)
+        "gpu_launches": args.steps * (9 * spec.n_layer + 4),
         "clocks": clk.summary(),
         "check": {"logits_finite": finite},
     }
@@ -772,7 +775,10 @@ def run_moe(args, world, rank, local):
                      "whole_step_weight_gb_s": wb / (ms * 1e-3) / 1e9},
         "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.n_vocab * 4,
                 "api": "CudaBackend.forward (rcu_backend_forward, host tokens/logits, greedy)"},
-        "gpu_launches": args.steps * (spec.n_layer * 14 + 4),
+        # per token: 12 per layer (norm, QKV GEMV, q/k post + KV append, attention, Wo GEMV, norm,
+        # router, top-k routing, experts' gate+up GEMV, GLU, experts' down GEMV, weighted combine)
+        # + position, embedding, final norm, head GEMV
+        "gpu_launches": args.steps * (12 * spec.n_layer + 4),
         "clocks": clk.summary(),
         "check": {"logits_finite": finite},
     }
