@@ -123,15 +123,19 @@ def test_matmul_multi_mixed_types(env):
             close(g, w_)
 
 
-@pytest.mark.parametrize("t,k", [(O.Q6_K, 12288), (O.Q4_K, 12288), (O.Q8_0, 14336), (O.Q4_0, 768), (O.Q6_K, 768)])
+@pytest.mark.parametrize("t,k", [(O.Q6_K, 12288), (O.Q4_K, 12288), (O.Q6_K, 6144), (O.Q4_K, 6144), (O.Q8_0, 14336),
+                                 (O.Q4_0, 768), (O.Q6_K, 768)])
 def test_long_and_ragged_rows(env, t, k):
-    # long rows are split over several warps; 768-wide Q6_K rows are not 16-byte multiples
+    # long rows are split over several warps (lane GEMV) or into several k slices per tile
+    # (K-quant GEMV at one token: 16-row tiles x 3 slices at 12288, 32-row tiles x 3 slices at
+    # 6144); 41 rows leave a ragged last tile; 768-wide Q6_K rows are not 16-byte multiples
     rng = O.Rng(3 + k)
     w = rng.weight(t, 41, k)
-    x = rng.vec(2 * k, 1.0).reshape(2, k)
-    got = gpu_matmul(env, [(t, w, k)], x)[0][0]
-    want = O.matmul_multi(x, [(t, w, k)], n_threads=4)[0]
-    close(got, want)
+    for n_tok in (1, 2):
+        x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+        got = gpu_matmul(env, [(t, w, k)], x)[0][0]
+        want = O.matmul_multi(x, [(t, w, k)], n_threads=4)[0]
+        close(got, want)
 
 
 def test_config1_gemv_shape(env):
