@@ -17,6 +17,7 @@
 //     partials in a fixed order (deterministic, no block-wide barrier inside the loop).
 //   * every wait is bounded (2 s) and reports through the context's device error word.
 #include <algorithm>
+#include <atomic>
 
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
@@ -536,11 +537,11 @@ static uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 template <int T, int NW>
 static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t grid) {
-    static bool attr_set[64] = {};
-    if (!attr_set[ctx->device & 63]) {
+    static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
+    if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
         RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)ctx->max_smem_optin));
-        attr_set[ctx->device & 63] = true;
+        attr_set[ctx->device & 63].store(true, std::memory_order_release);
     }
     RCU_CUDA_TRY(ctx, launch_k(ctx, (k_gemv<T, NW>), dim3(grid), dim3((NW + 1) * 32), smem_bytes, p));
     RCU_CUDA_TRY(ctx, cudaGetLastError());

@@ -41,6 +41,7 @@
 // shared buffer and the last warp to arrive (atomic counter, no barrier) adds and stores
 // them. Every wait is bounded (2 s) and reports through the context's error word.
 #include <algorithm>
+#include <atomic>
 
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
@@ -578,11 +579,11 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
     if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
-    static bool attr_set[64] = {};
-    if (!attr_set[ctx->device & 63]) {
+    static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
+    if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
         RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv_kq, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)ctx->max_smem_optin));
-        attr_set[ctx->device & 63] = true;
+        attr_set[ctx->device & 63].store(true, std::memory_order_release);
     }
     RCU_CUDA_TRY(ctx, launch_k(ctx, k_gemv_kq, dim3(grid), dim3(kQThreads), smem_bytes, p));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
