@@ -625,7 +625,10 @@ def run_decode(args, world, rank, local):
                    else "tp1", "decode": "CUDA graph replay per token",
                    "pp_tok_s": pp_tps, "prefill_batch": nb, "model_build_s": t_build},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_gate_up"),
+                     "peak_source": peak_kind,
+                     # ncu figure of this launch for the kernel that runs it (null until captured)
+                     "traffic": profile_traffic("gemv_q4_k_gate_up" if gemv_kernel_name("Q4_K", gemv_bytes) ==
+                                                "k_gemv<1,16>" else "gemv_kq_q4_k_gate_up"),
                      "kernel": gemv_kernel_name("Q4_K", gemv_bytes) + " (gate+up, 2 x 12288 x 4096 Q4_K)",
                      "bytes_per_launch": gemv_bytes,
                      "launch_ms": gemv_ms,
