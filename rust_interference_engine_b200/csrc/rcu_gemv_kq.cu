@@ -504,18 +504,44 @@ bool kq_plan(const rcu_weight *w, uint32_t k, bool congruent, KqJob &jd) {
     return true;
 }
 
+// Shared-memory layout of a launch: header, the staged Q8_K rows (codes, scales, bsums), then
+// the weight stages. Returns false when two stages do not fit next to the staged rows.
+bool kq_smem_layout(const rcu_ctx *ctx, uint32_t k, uint32_t n_rows, uint32_t stage_bytes, KqParams &p) {
+    uint32_t off = kQHdrBytes;
+    p.o_q = off;
+    off = round_up_u(off + n_rows * k, 16);
+    p.o_d = off;
+    off = round_up_u(off + n_rows * (k / QK_K) * 4, 16);
+    p.o_bs = off;
+    off = round_up_u(off + n_rows * (k / 16) * 2, 16);
+    p.stage_off = round_up_u(off, 128);
+    const uint32_t budget = (uint32_t)ctx->max_smem_optin;
+    if (p.stage_off + 2 * stage_bytes > budget) return false;
+    p.stages = std::min<uint32_t>(kQMaxStages, (budget - p.stage_off) / stage_bytes);
+    return true;
+}
+
+uint32_t kq_stage_bytes(const KqJob &jd, bool congruent) {
+    return round_up_u(16 * jd.rb * jd.pstride + (congruent ? 128u : 0u), 128);
+}
+
 }  // namespace
 
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs || !(a.have & RCU_ACT_Q8K)) return false;
     uint64_t bytes = 0;
+    uint32_t n_rows = 0, stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
         KqJob jd{};
         if (!kq_plan(jobs[i].w, a.k, ctx->gemv_kq_congruent, jd)) return false;
         if (jobs[i].sel && jobs[i].w_stride % 16 != 0) return false;
         if (jobs[i].tok + 1 > kQMaxStageRows) return false;
         bytes += (uint64_t)(jobs[i].rows ? jobs[i].rows : jobs[i].w->rows) * jobs[i].w->row_bytes;
+        n_rows = std::max(n_rows, jobs[i].tok + 1);
+        stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd, ctx->gemv_kq_congruent));
     }
+    KqParams lay;
+    if (!kq_smem_layout(ctx, a.k, n_rows, stage_bytes, lay)) return false;
     // Small launches take the lane GEMV: this kernel's start-up (activation staging, the first
     // tile's latency chain) is longer, and with 1-2 tiles per CTA nothing hides it; K = 768
     // expert rows also give it few tiles (256-row tiles). Measured on B200: back-to-back launches
@@ -559,23 +585,12 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         p.n_stage = std::max(p.n_stage, jd.tok + 1);
         jd.tile_begin = tiles;
         tiles += (jd.rows + 16 * jd.rb - 1) / (16 * jd.rb);
-        stage_bytes = std::max(stage_bytes, round_up_u(16 * jd.rb * jd.pstride + (p.congruent ? 128u : 0u), 128));
+        stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd, p.congruent != 0));
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
-    const uint32_t n_rows = p.n_stage, k = a.k;
-    uint32_t off = kQHdrBytes;
-    p.o_q = off;
-    off = round_up_u(off + n_rows * k, 16);
-    p.o_d = off;
-    off = round_up_u(off + n_rows * (k / QK_K) * 4, 16);
-    p.o_bs = off;
-    off = round_up_u(off + n_rows * (k / 16) * 2, 16);
-    p.stage_off = round_up_u(off, 128);
-    const uint32_t budget = (uint32_t)ctx->max_smem_optin;
-    if (p.stage_off + 2 * stage_bytes > budget)
-        return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation row + two weight stages exceed shared memory");
-    p.stages = std::min<uint32_t>(kQMaxStages, (budget - p.stage_off) / stage_bytes);
+    if (!kq_smem_layout(ctx, a.k, p.n_stage, stage_bytes, p))
+        return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation rows + two weight stages exceed shared memory");
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
     if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
