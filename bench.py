@@ -1002,9 +1002,23 @@ META = {  # metric / unit / config of each workload, shared by both arms
     "gemv": {"metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)", "unit": "GB/s",
              "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "workload": "gemv_q4_0_6144x2048_config1"},
     "prefill": {"metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)", "unit": "TOPS",
-                "dtype": "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, f32 block-scale epilogue)",
+                "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 block-scale combine)",
                 "workload": "prefill_q4_0_m512_k4096_config2"},
 }
+
+
+def step_units(workload: str) -> float:
+    """Units of a workload's metric in one step (one pass of the hot path over one batch): the
+    reference arm reports ms_per_step = these units / its measured rate."""
+    if workload in ("decode", "moe"):
+        return 1.0  # one token
+    if workload == "gemv":
+        return gemv_bytes_per_step()[0] / 1e9
+    if workload == "prefill":
+        return 2.0 * PF_M * PF_K * sum(PF_N) / 1e12
+    if workload == "turbo":  # K and V rows of every layer, turbo4 at head_dim 128 (66-byte rows)
+        return 2.0 * T5["n_layer"] * T5["n_head_kv"] * T5["ctx"] * 66 / 1e9
+    raise KeyError(workload)
 
 
 def main():
@@ -1052,6 +1066,7 @@ def main():
             m = META[args.workload]
             print(json.dumps({"impl": "reference", "metric": m["metric"], "value": v, "unit": m["unit"],
                               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": 1e3 * step_units(args.workload) / v,
                               "higher_is_better": True, "scaling": "weak", "dtype": m["dtype"], "data": "synthetic",
                               "config": {"workload": m["workload"]}, "vs_baseline": None, "cpu_baseline": cb,
                               "e2e": {"value": v, "unit": m["unit"], "h2d_bytes_per_step": 0,
