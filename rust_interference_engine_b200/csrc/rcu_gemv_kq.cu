@@ -86,7 +86,9 @@ struct KqParams {
     uint32_t o_q, o_d, o_bs;  // shared-memory offsets of the staged Q8_K activations
     ActsView acts;
     uint32_t *err;
-    float *ar_dst[kQMaxPeers];  // fused all-reduce push (see rcu_gemv.cu)
+    // fused all-reduce push (as in rcu_gemv.cu); left zero by the launcher: launches that push
+    // an all-reduce take the lane GEMV
+    float *ar_dst[kQMaxPeers];
     uint32_t *ar_flag[kQMaxPeers];
     uint32_t ar_ndst, ar_nflag;
 };
@@ -551,17 +553,8 @@ bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int 
     return bytes >= ctx->gemv_kq_min_bytes;
 }
 
-int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
-                   const ArPush *push) {
+int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0) {
     KqParams p{};
-    if (push) {
-        if (n_jobs != 1 || tok0 != 0 || push->n_dst > kQMaxPeers || push->n_flag > kQMaxPeers)
-            return set_err(ctx, RCU_ERR_INVALID, "gemv: all-reduce push needs one job, one launch, <= 8 ranks");
-        p.ar_ndst = push->n_dst;
-        p.ar_nflag = push->n_flag;
-        for (uint32_t q = 0; q < push->n_dst; q++) p.ar_dst[q] = push->dst[q];
-        for (uint32_t q = 0; q < push->n_flag; q++) p.ar_flag[q] = push->flag[q];
-    }
     p.n_jobs = n_jobs;
     p.k = a.k;
     p.nsb = a.k / QK_K;
@@ -593,7 +586,6 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation rows + two weight stages exceed shared memory");
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
-    if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
     static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
     if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
         RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv_kq, cudaFuncAttributeMaxDynamicSharedMemorySize,
