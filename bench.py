@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
 
-Prints ONE JSON line (rank 0). Workloads (seeded synthetic data):
+Prints ONE JSON line (rank 0). Workloads (the reference benchmark configurations 1-5, seeded synthetic data):
   gemv   config 1: Q4_0 x Q8_0 GEMV of the Qwen3-1.7B gate_proj shape (6144 x 2048,
          W ~ N(0, 0.02) quantized with the reference's Q4_0 rule, x ~ N(0, 1)). One step =
          quantize x once + one matmul_multi launch over a stack of 72 distinct weight

@@ -139,7 +139,7 @@ def test_long_and_ragged_rows(env, t, k):
 
 
 def test_config1_gemv_shape(env):
-    # W 6144x2048 ~ N(0, 0.02) -> Q4_0 (quant/mod.rs:279-298), x ~ N(0, 1)
+    # benchmark configuration 1: W 6144x2048 ~ N(0, 0.02) -> Q4_0 (quant/mod.rs:279-298), x ~ N(0, 1)
     rng = np.random.default_rng(1)
     wf = rng.normal(0.0, 0.02, (6144, 2048)).astype(np.float32)
     w = O.quantize_weight(O.Q4_0, wf)
@@ -258,7 +258,7 @@ def test_prefill_gemm_q4_0_int8_kind(env, n_tok, rows, k):
 
 
 def test_prefill_gemm_config2(env):
-    # M = 512 tokens x K = 4096, N = 4096 and 14336, W ~ N(0, 0.02) -> Q4_0
+    # benchmark configuration 2: M = 512 tokens x K = 4096, N = 4096 and 14336, W ~ N(0, 0.02) -> Q4_0
     rng = np.random.default_rng(2)
     x = rng.standard_normal((512, 4096)).astype(np.float32)
     for n in (4096, 14336):

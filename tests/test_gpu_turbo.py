@@ -146,6 +146,6 @@ def test_turbo_attention_equals_attention_over_reconstruction(env):
 
 
 def test_config5_shape_turbo_attention(env):
-    # BASELINE config 5 geometry (64 q / 8 kv heads x 128) at a shortened context
+    # benchmark configuration 5 geometry (64 q / 8 kv heads x 128) at a shortened context
     got, want = _attn_case(env, O.KV_TURBO4, 64, 8, 128, 4096, 1, 4095, seed=9)
     close(got, want, 2e-3)
