@@ -232,10 +232,12 @@ RCU_API int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max
  * compiled into this library (about 322 KB, kept on every GPU that loads it until exit).
  * For callers that cannot cudaMalloc at matmul time, e.g. because all device memory is
  * owned by their own pool or by PyTorch's caching allocator. Limits: n_tok <= 8 and
- * w->cols <= 16384 (larger calls return RCU_ERR_INVALID). All calls share the scratch, so
- * calls that overlap on the GPU race; order them (one stream per device). The first call
- * on a device looks the scratch address up once (cudaGetSymbolAddress): make that first
- * call before any stream capture. */
+ * w->cols <= 16384 (larger calls return RCU_ERR_INVALID); every call within them runs
+ * (batches whose rows do not fit the GEMV's shared memory at once run as two launches).
+ * All calls share the scratch, so calls that overlap on the GPU race; order them (one
+ * stream per device). The first call through a context looks the scratch address up
+ * (cudaGetSymbolAddress) and keeps it in the context: make that first call before any
+ * stream capture. */
 RCU_API int32_t rcu_matmul_f32_static(rcu_ctx *ctx, const rcu_weight *w, const float *x_dev, uint64_t n_tok,
                                       float *out_dev, uint64_t ld);
 

@@ -630,8 +630,20 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     }
     p.stage_off = round_up(off, 128);
     const uint32_t budget = (uint32_t)ctx->max_smem_optin;
-    if (p.stage_off + 2 * stage_bytes > budget)
+    if (p.stage_off + 2 * stage_bytes > budget) {
+        // Long rows at 7-8 tokens (Q8_0 activations of 16384 values: 22.5 KB per staged row)
+        // leave no room for two weight stages: run the tokens as two launches of half the
+        // batch. Each launch offsets the outputs by its first token; indirect (expert) jobs
+        // address their own rows and are never split.
+        bool indirect = false;
+        for (int i = 0; i < n_jobs; i++) indirect |= jobs[i].sel != nullptr;
+        if (n_tok > 1 && !push && !indirect) {
+            const uint32_t h = n_tok / 2;
+            if (int st = launch_gemv(ctx, a, jobs, n_jobs, tok0, h)) return st;
+            return launch_gemv(ctx, a, jobs, n_jobs, tok0 + h, n_tok - h);
+        }
         return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation batch + two weight stages exceed shared memory");
+    }
     p.stages = std::min<uint32_t>(kMaxStages, (budget - p.stage_off) / stage_bytes);
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);

@@ -188,6 +188,9 @@ struct rcu_ctx {
     size_t k_part_cap = 0;
     uint32_t *k_cnt = nullptr;     // split-K tile counters (zero between launches)
     size_t k_cnt_cap = 0;
+    // device address of the allocation-free matmul's static scratch (rcu_static.cu), looked
+    // up by this context's first such call
+    uint8_t *static_scratch = nullptr;
     std::string last_error;
 };
 

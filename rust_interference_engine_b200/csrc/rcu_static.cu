@@ -12,8 +12,6 @@
 // formats (about 322 KB); every GPU that loads this library keeps it until process exit.
 // All calls share it, so calls whose work overlaps on the GPU (different streams, or
 // different contexts on the same device) race on it and must be ordered by the caller.
-#include <mutex>
-
 #include "rcu_kernels.h"
 
 namespace rcu {
@@ -35,13 +33,11 @@ constexpr uint64_t kStaticBytes = kOffBsK + al256(kStaticMaxTok * (kStaticMaxK /
 // The device address comes from cudaGetSymbolAddress (static_base below).
 static __device__ __align__(256) uint8_t g_static_acts[kStaticBytes];
 
-// Device address of g_static_acts on the current device, looked up once per device.
+// Device address of g_static_acts on the context's device, looked up by the context's first
+// call and kept in the context. A context belongs to one device, and one created after a
+// device reset looks the address up again.
 static int static_base(rcu_ctx *ctx, uint8_t **out) {
-    static std::mutex mu;
-    static uint8_t *base[64] = {};
-    std::lock_guard<std::mutex> g(mu);
-    const int dev = ctx->device & 63;
-    if (!base[dev]) {
+    if (!ctx->static_scratch) {
         int cur = -1;
         RCU_CUDA_TRY(ctx, cudaGetDevice(&cur));
         if (cur != ctx->device) RCU_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
@@ -49,9 +45,9 @@ static int static_base(rcu_ctx *ctx, uint8_t **out) {
         const cudaError_t e = cudaGetSymbolAddress(&p, g_static_acts);
         if (cur != ctx->device && cur >= 0) cudaSetDevice(cur);
         if (e != cudaSuccess) return cuda_err(ctx, e, "cudaGetSymbolAddress(g_static_acts)");
-        base[dev] = (uint8_t *)p;
+        ctx->static_scratch = (uint8_t *)p;
     }
-    *out = base[dev];
+    *out = ctx->static_scratch;
     return RCU_OK;
 }
 

@@ -4,9 +4,12 @@ It exists for callers that cannot call cudaMalloc when they need a matmul, for e
 because their device memory is owned by a pool (PyTorch's caching allocator, or an engine
 that reserves HBM for weights and KV cache up front). It quantizes the activations into a
 fixed scratch area compiled into the library instead of an allocated one. These tests call
-it through the C ABI and compare it with the allocating path (rcu_acts_prepare +
-rcu_matmul) on two calls in a row, within the matmul tolerance used everywhere else.
-This file is collected last on purpose.
+it through the C ABI on two calls in a row and compare it with the allocating path
+(rcu_acts_prepare + rcu_matmul: the same kernels, so bit for bit) and with the CPU oracle
+within the matmul tolerance used everywhere else. They cover the largest advertised call
+(8 tokens of 16384 values, in both activation formats), a K-quant weight of more than
+8 MiB (the tensor-core batch-1 GEMV), and check that free device memory does not change
+across calls. This file is collected last on purpose.
 """
 import numpy as np
 import pytest
@@ -29,15 +32,22 @@ def close(a, b):
     assert float(np.max(np.abs(a - b))) <= RTOL * scale
 
 
-@pytest.mark.parametrize("t,rows,k", [(O.Q4_0, 300, 2048), (O.Q4_K, 257, 4096), (O.Q6_K, 64, 12288),
-                                      (O.Q8_0, 100, 16384)])
-def test_static_matmul_matches_allocating_path(env, t, rows, k):
+# (type, rows, k, tokens of the first and second call); Q4_K 4096 x 4096 is 9.4 MB (the
+# tensor-core GEMV at one token), the 16384-value cases at 8 tokens fill the whole scratch
+CASES = [(O.Q4_0, 300, 2048, (1, 3)), (O.Q4_K, 257, 4096, (1, 3)), (O.Q6_K, 64, 12288, (1, 3)),
+         (O.Q8_0, 100, 16384, (1, 3)), (O.Q4_K, 4096, 4096, (1, 1)), (O.Q4_0, 96, 16384, (8, 8)),
+         (O.Q8_0, 40, 16384, (8, 7)), (O.Q4_K, 80, 16384, (8, 8)), (O.Q6_K, 48, 16384, (8, 8))]
+
+
+@pytest.mark.parametrize("t,rows,k,toks", CASES)
+def test_static_matmul_matches_allocating_path_and_oracle(env, t, rows, k, toks):
     torch, rie, ctx = env
-    rng = O.Rng(77 + t)
-    w = rie.Weight.upload(ctx, rie.GgmlType(t), rows, k, rng.weight(t, rows, k))
-    for call in range(2):  # two calls in a row: the shared scratch is rewritten each time
-        n_tok = 1 if call == 0 else 3
-        x = torch.from_numpy(rng.vec(n_tok * k, 1.0 + call).reshape(n_tok, k)).cuda()
+    rng = O.Rng(77 + t + k)
+    wq = rng.weight(t, rows, k)
+    w = rie.Weight.upload(ctx, rie.GgmlType(t), rows, k, wq)
+    for call, n_tok in enumerate(toks):  # two calls in a row: the shared scratch is rewritten each time
+        xh = rng.vec(n_tok * k, 1.0 + call).reshape(n_tok, k)
+        x = torch.from_numpy(xh).cuda()
         got = torch.full((n_tok, rows), float("nan"), device="cuda")
         rie.matmul_f32_static(ctx, w, x, n_tok, got)
         acts = rie.QuantActs(ctx, n_tok, k)
@@ -45,7 +55,31 @@ def test_static_matmul_matches_allocating_path(env, t, rows, k):
         want = torch.zeros((n_tok, rows), device="cuda")
         rie.matmul(ctx, acts, w, want)
         ctx.sync()
-        close(got.cpu().numpy(), want.cpu().numpy())
+        g, a = got.cpu().numpy(), want.cpu().numpy()
+        assert np.array_equal(g.view(np.uint32), a.view(np.uint32)), "static and allocating paths differ"
+        ref = O.matmul_multi(xh, [(t, wq, k)], n_threads=8)[0]
+        close(g, ref)
+    assert ctx.device_error_bits() == 0
+
+
+def test_static_matmul_allocates_nothing(env):
+    torch, rie, ctx = env
+    rng = O.Rng(9)
+    rows, k = 4096, 4096
+    w = rie.Weight.upload(ctx, rie.GgmlType.Q4_K, rows, k, rng.weight(O.Q4_K, rows, k))
+    w0 = rie.Weight.upload(ctx, rie.GgmlType.Q4_0, 64, 16384, rng.weight(O.Q4_0, 64, 16384))
+    x = torch.from_numpy(rng.vec(8 * 16384, 1.0).reshape(8, 16384)).cuda()
+    x1 = x[0, :k].contiguous()
+    out = torch.zeros((8, rows), device="cuda")
+    rie.matmul_f32_static(ctx, w, x1, 1, out)  # first call: looks the scratch up
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(2):  # second and third calls
+        rie.matmul_f32_static(ctx, w, x1, 1, out)
+        rie.matmul_f32_static(ctx, w0, x, 8, out, 4096)
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free0
+    assert ctx.device_error_bits() == 0
 
 
 def test_static_matmul_limits(env):
