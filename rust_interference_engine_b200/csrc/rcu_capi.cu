@@ -94,7 +94,6 @@ int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, s
     c->max_smem_optin = prop.sharedMemPerBlockOptin;
     if (const char *v = std::getenv("RIE_CUDA_PDL")) c->pdl = std::strcmp(v, "0") != 0;
     if (const char *v = std::getenv("RIE_GEMV_KQ")) c->gemv_kq = std::strcmp(v, "0") != 0;
-    if (const char *v = std::getenv("RIE_GEMV_KQ_LAYOUT")) c->gemv_kq_congruent = std::strcmp(v, "congruent") == 0;
     if (const char *v = std::getenv("RIE_GEMV_KQ_MIN_MB")) c->gemv_kq_min_bytes = std::strtoull(v, nullptr, 10) << 20;
     e = cudaMalloc(&c->dev_err, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(cuda_err(c, e, "cudaMalloc(err)"));

@@ -552,9 +552,9 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
                 const ArPush *push) {
     if (n_jobs < 1 || n_jobs > kMaxJobs) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..96 jobs per launch");
     if (n_tok < 1 || n_tok > kMaxTok) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..8 tokens per launch");
-    // one activation row over K-quant weights: the tensor-core GEMV (rcu_gemv_kq.cu); launches
-    // that push a tensor-parallel all-reduce stay here
-    if (n_tok == 1 && !push && gemv_kq_ok(ctx, a, jobs, n_jobs)) return launch_gemv_kq(ctx, a, jobs, n_jobs, tok0);
+    // one activation row over K-quant weights: the tensor-core GEMV (rcu_gemv_kq.cu), also for
+    // launches that push a tensor-parallel all-reduce
+    if (n_tok == 1 && gemv_kq_ok(ctx, a, jobs, n_jobs)) return launch_gemv_kq(ctx, a, jobs, n_jobs, tok0, push);
     GemvParams p{};
     if (push) {
         if (n_jobs != 1 || tok0 != 0 || push->n_dst > kMaxPeers || push->n_flag > kMaxPeers)

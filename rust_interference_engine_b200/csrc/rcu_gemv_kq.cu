@@ -6,10 +6,10 @@
 //
 // Why a second GEMV: the lane-per-block dp4a GEMV issues about 0.2 instructions per weight
 // byte (unpacking, scale decoding, activation loads, per-lane combine). At the HBM rate an
-// SM receives ~24 bytes per cycle, so that kernel would need more than the SM's 4 issue
+// SM receives ~22 bytes per cycle, so that kernel would need close to the SM's 4 issue
 // slots per cycle. Here one mma.sync.m16n8k32 (u8 weights x s8 activations) forms the exact
 // integer products of 16 rows x 32 weights, and each thread decodes the scales of its own
-// sub-blocks only: about 0.05 (Q4_K) / 0.07 (Q6_K) instructions per byte.
+// sub-blocks only.
 //
 // Fragment mapping (a warp's thread: g = lane / 4, c = lane % 4):
 //   * A holds 16 weight rows (rows g and g + 8 of a 16-row block, as the mma layout puts
@@ -17,9 +17,10 @@
 //     8 weights of ONE scale group chosen by c: Q4_K / Q5_K sub-block 2c (low nibbles) or
 //     2c + 1 (high nibbles); Q6_K the 16-value group (n, m, h) with n = c / 2, h = c % 2;
 //   * B is block-diagonal: column j holds the activations of chunk j / 2 and zeros elsewhere
-//     (only the threads with c == g / 2 load activations), so D[row][2c] = D[row][2c+1] is
-//     the exact int32 dot product of chunk c alone. Accumulating D over the steps of a group
-//     leaves thread (g, c) with the group's exact sum for rows g and g + 8;
+//     (only the threads with c == g / 2 load activations; the others load a zero block), so
+//     D[row][2c] = D[row][2c+1] is the exact int32 dot product of chunk c alone.
+//     Accumulating D over the steps of a group leaves thread (g, c) with the group's exact
+//     sum for rows g and g + 8;
 //   * thread c applies the scales / mins of its groups (reference.rs:8-14 unpack, the
 //     d * sumi - dmin * summ combine of :295-350, d * sumi of :352-386) in f32; the 4 threads
 //     of a row add their partials, then the warps that split the row's superblocks add
@@ -27,19 +28,22 @@
 // The per-thread integer pieces add up exactly to the reference's sumi / summ; only the f32
 // grouping differs (per thread share instead of per superblock), as in the lane GEMV.
 //
-// Shared memory: the stage row layout is chosen per context (KqParams::congruent): rows at
-// their source's address mod 128 (whole-line bulk copies; a tile of whole rows is one copy)
-// or at a row stride = 16 (mod 128), which puts the 16-byte loads of a warp's 8 rows in
-// distinct banks. Q6_K superblocks (210 B) are only 2-byte aligned: a thread reads its 16
-// bytes as 4 words in an order rotated by c (word (i + c) % 4 into slot i), which spreads
-// those loads over the banks; the activations use the same rotation, so A and B agree.
+// Shared memory: rows of a stage at a stride = 16 (mod 128), which puts the 16-byte loads of
+// a warp's 8 rows in distinct banks. Q6_K superblocks (210 B) are only 2-byte aligned: a
+// thread reads its 16 bytes as 4 words in an order rotated by c (word (i + c) % 4 into slot
+// i), which spreads those loads over the banks; the activations use the same rotation, so A
+// and B agree.
 //
-// Pipeline: warp 16 is the producer (1-D bulk copies into a ring of stages, completion on
-// mbarriers, L2 evict-first); warps 0..15 consume. A tile is 16 x rb rows of one job, split
-// along k into slices of sl superblocks (one stage each); the warps of a 16-row block split
-// a slice's superblocks. At the end of a tile every warp publishes its row partials to a
-// shared buffer and the last warp to arrive (atomic counter, no barrier) adds and stores
-// them. Every wait is bounded (2 s) and reports through the context's error word.
+// Pipeline: warp 16 is the producer (1-D bulk copies of weight rows into a ring of stages,
+// completion on mbarriers, L2 evict-first); warps 0..15 consume. A stage holds 16 * rb rows
+// x sl superblocks of one job; the 16 / rb warps of each 16-row block split the slice's
+// superblocks (normally one each). A tile is kQG consecutive row groups of one job, so the
+// cross-warp reduction runs once per 32 * rb rows: every warp publishes its row partials to
+// a shared buffer and the last warp to arrive (shared-memory counter, no barrier) adds them
+// in warp order and stores. Activations are read straight from global memory (L1) by the
+// threads that use them, before they wait for the stage: no block-wide staging barrier.
+// Job descriptors are read into registers once per tile. Every wait is bounded (2 s) and
+// reports through the context's error word.
 #include <algorithm>
 #include <atomic>
 
@@ -49,14 +53,19 @@
 namespace rcu {
 namespace {
 
-constexpr int kQW = 16;  // consumer warps
+constexpr int kQW = 8;  // consumer warps
+constexpr int kQWLog2 = 3;
 constexpr int kQThreads = (kQW + 1) * 32;
+constexpr int kQG = 2;  // row groups (stages of 16 * rb rows) per tile
 constexpr int kQMaxJobs = 96;
 constexpr int kQMaxStages = 8;
-constexpr int kQRed = 8;  // tile reduction buffers; must be >= the number of stages
+constexpr int kQRed = 8;  // tile reduction slots; must be >= the number of stages
 constexpr uint32_t kQMaxStage = 64 * 1024;
 constexpr int kQMaxPeers = 8;
-constexpr uint32_t kQMaxStageRows = 64;
+
+// The zero activation block the threads off B's diagonal read (static device memory is
+// zero-initialised).
+__device__ __align__(128) uint8_t g_kq_zero[256];
 
 struct KqJob {
     const uint8_t *w;
@@ -64,30 +73,31 @@ struct KqJob {
     const uint32_t *sel;  // indirect (expert) job: weight = w + (*sel) * w_stride
     uint64_t w_stride;
     uint32_t rows, row_bytes, type, tok;
-    uint32_t rb;           // 16-row blocks per tile
+    uint32_t rb_log2;      // 16-row blocks per stage = 1 << rb_log2
     uint32_t sl;           // superblocks per slice (one pipeline stage)
-    uint32_t nsl;          // slices per tile
+    uint32_t nsl;          // slices per row group
     uint32_t slice_bytes;  // sl * block bytes (a multiple of 16)
-    uint32_t pstride;      // shared-memory row stride (see KqParams::congruent)
+    uint32_t pstride;      // shared-memory row stride, = 16 (mod 128)
     uint32_t tile_begin;
 };
 
+// Jobs of one weight type: their tiles [tile0, tile1) go to CTAs [cta0, cta1), so that every
+// CTA runs the loop of a single type (one register allocation per type, no spills).
+struct KqGroup {
+    uint32_t type, job0, job1, tile0, tile1, cta0, cta1;
+};
+constexpr int kQMaxGroups = 3;
+
 struct KqParams {
     KqJob jobs[kQMaxJobs];
-    int32_t n_jobs;
+    KqGroup groups[kQMaxGroups];
+    int32_t n_jobs, n_groups;
     uint32_t total_tiles, stages, stage_bytes, stage_off;
-    uint32_t k, nsb, tok0, n_stage, early_weights;
-    // Row layout in a stage. congruent: every row lands at the same address mod 128 as its
-    // source (stage start shifted by the source's offset mod 128, row stride = row bytes mod
-    // 128), so the bulk copies move whole 128-byte lines; a tile of whole contiguous rows is
-    // one copy. Otherwise: row stride = 16 (mod 128), which spreads the 8 rows a warp reads
-    // over all banks, at the price of copies whose source and destination lines differ.
-    uint32_t congruent;
-    uint32_t o_q, o_d, o_bs;  // shared-memory offsets of the staged Q8_K activations
+    uint32_t k, tok0, early_weights;
     ActsView acts;
     uint32_t *err;
-    // fused all-reduce push (as in rcu_gemv.cu); left zero by the launcher: launches that push
-    // an all-reduce take the lane GEMV
+    // fused all-reduce push (tensor parallel): outputs also go to ar_dst[q], then each CTA
+    // adds its share of kArUnit to every ar_flag[q] (as in rcu_gemv.cu)
     float *ar_dst[kQMaxPeers];
     uint32_t *ar_flag[kQMaxPeers];
     uint32_t ar_ndst, ar_nflag;
@@ -97,11 +107,24 @@ struct KqHdr {
     uint64_t full[kQMaxStages];
     uint64_t empty[kQMaxStages];
     int cnt[kQRed];
-    float red[kQRed][kQW][16];  // [tile % kQRed][warp][row in the warp's 16-row block]
+    float red[kQRed][kQW][kQG][16];  // [tile % kQRed][warp][group][row in the warp's 16-row block]
 };
-constexpr uint32_t kQHdrBytes = 8448;
-static_assert(sizeof(KqHdr) <= kQHdrBytes, "header too large");
+constexpr uint32_t kQHdrBytes = (sizeof(KqHdr) + 127) / 128 * 128;
 static_assert(kQRed >= kQMaxStages, "a warp can run up to (stages - 1) tiles ahead");
+
+// The fields of one job the loops use, in registers.
+struct JobR {
+    const uint8_t *w;
+    float *out;
+    const uint32_t *sel;
+    uint64_t w_stride;
+    uint32_t rows, row_bytes, type, tok, rb_log2, sl, nsl, slice_bytes, pstride, tile_begin;
+};
+__device__ __forceinline__ void load_job(const KqJob &j, JobR &r) {
+    r.w = j.w, r.out = j.out, r.sel = j.sel, r.w_stride = j.w_stride;
+    r.rows = j.rows, r.row_bytes = j.row_bytes, r.type = j.type, r.tok = j.tok, r.rb_log2 = j.rb_log2;
+    r.sl = j.sl, r.nsl = j.nsl, r.slice_bytes = j.slice_bytes, r.pstride = j.pstride, r.tile_begin = j.tile_begin;
+}
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -110,16 +133,47 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 __device__ __forceinline__ void words8(const uint4 &x, const uint4 &y, uint32_t (&w)[8]) {
     w[0] = x.x, w[1] = x.y, w[2] = x.z, w[3] = x.w, w[4] = y.x, w[5] = y.y, w[6] = y.z, w[7] = y.w;
 }
 
-// Q4_K / Q5_K superblock at byte `so` of rows ra (row g) and rb (row g + 8); act: its 256
-// activation codes, bsw: its 8 bsums pair words, ad: its activation scale.
+// One superblock's activations as thread (g, c) feeds them to B, its bsums and scale.
+struct ActR {
+    uint32_t x[16];  // Q4_K / Q5_K: sub-blocks 2c (x[0..7]) and 2c + 1 (x[8..15]); Q6_K: X[m][i] = x[4m + i]
+    uint4 bs;        // Q4_K / Q5_K: pair words 2c, 2c + 1 in .x, .y; Q6_K: pair words 4n .. 4n + 3
+    float d;
+};
+
 template <int TYPE>
-__device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uint32_t so, const int8_t *act,
-                                       const uint32_t *bsw, float ad, uint32_t c, bool bact, float &accA,
-                                       float &accB) {
+__device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, uint32_t sb,
+                                         uint32_t c, bool bact, ActR &a) {
+    a.d = __ldg(adk + sb);
+    if (TYPE == T_Q6_K) {
+        const uint32_t n = c >> 1, h = c & 1u;
+        const uint8_t *xa = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 128 * n + 16 * h : g_kq_zero;
+#pragma unroll
+        for (int m = 0; m < 4; m++)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                a.x[4 * m + i] = __ldg(reinterpret_cast<const uint32_t *>(xa + 32 * m + 4u * ((i + c) & 3u)));
+        a.bs = ldg128(abw + 8 * sb + 4 * n);
+    } else {
+        const uint8_t *x = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 64 * c : g_kq_zero;
+        uint32_t lo[8], hi[8];
+        words8(ldg128(x), ldg128(x + 16), lo);
+        words8(ldg128(x + 32), ldg128(x + 48), hi);
+#pragma unroll
+        for (int i = 0; i < 8; i++) a.x[i] = lo[i], a.x[8 + i] = hi[i];
+        const uint2 b = __ldg(reinterpret_cast<const uint2 *>(abw + 8 * sb + 2 * c));
+        a.bs = make_uint4(b.x, b.y, 0u, 0u);
+    }
+}
+
+// Q4_K / Q5_K superblock at byte `so` of rows ra (row g) and rb (row g + 8).
+template <int TYPE>
+__device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
+                                       float &accA, float &accB) {
     constexpr uint32_t QO = TYPE == T_Q4_K ? 16 : 48;  // quant bytes (Q5_K: after qh[32])
     const uint8_t *pa = ra + so, *pb = rb + so;
     uint32_t WA[8], WB[8];
@@ -129,15 +183,6 @@ __device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uin
     if (TYPE == T_Q5_K) {
         words8(lds128(pa + 16), lds128(pa + 32), HA);
         words8(lds128(pb + 16), lds128(pb + 32), HB);
-    }
-    uint32_t AL[8], AH[8];  // chunk c's activations: sub-block 2c (low) and 2c + 1 (high)
-    if (bact) {
-        const uint8_t *x = reinterpret_cast<const uint8_t *>(act) + 64 * c;
-        words8(lds128(x), lds128(x + 16), AL);
-        words8(lds128(x + 32), lds128(x + 48), AH);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; i++) AL[i] = AH[i] = 0u;
     }
     int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -156,11 +201,10 @@ __device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uin
                 hi[r] = ((w >> 4) & 0x0F0F0F0Fu) | (((hb >> (2 * c + 1)) & 0x01010101u) << 4);
             }
         }
-        mma_u8s8(dl, lo[0], lo[1], lo[2], lo[3], AL[2 * t], AL[2 * t + 1]);
-        mma_u8s8(dh, hi[0], hi[1], hi[2], hi[3], AH[2 * t], AH[2 * t + 1]);
+        mma_u8s8(dl, lo[0], lo[1], lo[2], lo[3], A.x[2 * t], A.x[2 * t + 1]);
+        mma_u8s8(dh, hi[0], hi[1], hi[2], hi[3], A.x[8 + 2 * t], A.x[8 + 2 * t + 1]);
     }
     // scales of sub-blocks 2c, 2c + 1 and their mins (get_scale_min_k4, reference.rs:8-14)
-    const uint2 bp = *reinterpret_cast<const uint2 *>(bsw + 2 * c);
     const uint32_t sh = 16u * (c & 1u);
 #pragma unroll
     for (int r = 0; r < 2; r++) {
@@ -170,10 +214,10 @@ __device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uin
         const uint32_t mnp = c < 2 ? cc : (((b >> 4) & 0x0F0Fu) | ((cc >> 2) & 0x3030u));
         const int s_lo = dl[2 * r], s_hi = TYPE == T_Q4_K ? (dh[2 * r] >> 4) : dh[2 * r];
         const int I = (int)(scp & 63u) * s_lo + (int)((scp >> 8) & 63u) * s_hi;
-        const int M = dp2a_lo(bp.x, (mnp & 63u) * 0x0101u, dp2a_lo(bp.y, ((mnp >> 8) & 63u) * 0x0101u, 0));
+        const int M = dp2a_lo(A.bs.x, (mnp & 63u) * 0x0101u, dp2a_lo(A.bs.y, ((mnp >> 8) & 63u) * 0x0101u, 0));
         const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
         float &acc = r ? accB : accA;
-        acc = fmaf(ad, fmaf(-f.y, (float)M, f.x * (float)I), acc);
+        acc = fmaf(A.d, fmaf(-f.y, (float)M, f.x * (float)I), acc);
     }
 }
 
@@ -199,11 +243,10 @@ __device__ __forceinline__ void ld4_rot(const uint8_t *row, uint32_t off, uint32
 }
 
 // Q6_K superblock at byte `so` of rows ra / rb (A4: so is a multiple of 4, i.e. an even
-// superblock index).
+// superblock index within the slice).
 template <bool A4>
-__device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint32_t so, const int8_t *act,
-                                      const uint32_t *bsw, float ad, uint32_t c, bool bact, float &accA,
-                                      float &accB) {
+__device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
+                                      float &accA, float &accB) {
     const uint32_t n = c >> 1, h = c & 1u;
     uint32_t LA0[4], LA1[4], HA[4], LB0[4], LB1[4], HB[4];
     ld4_rot<A4>(ra, so + 64 * n + 16 * h, c, LA0);
@@ -212,13 +255,6 @@ __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint
     ld4_rot<A4>(rb, so + 64 * n + 16 * h, c, LB0);
     ld4_rot<A4>(rb, so + 64 * n + 32 + 16 * h, c, LB1);
     ld4_rot<A4>(rb, so + 128 + 32 * n + 16 * h, c, HB);
-    uint32_t X[4][4];  // group (n, m, h) activations, rotated like the weights
-    const uint8_t *xa = reinterpret_cast<const uint8_t *>(act) + 128 * n + 16 * h;
-#pragma unroll
-    for (int m = 0; m < 4; m++)
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            X[m][i] = bact ? *reinterpret_cast<const uint32_t *>(xa + 32 * m + 4u * ((i + c) & 3u)) : 0u;
     int D[4][4];
 #pragma unroll
     for (int m = 0; m < 4; m++) D[m][0] = D[m][1] = D[m][2] = D[m][3] = 0;
@@ -226,18 +262,17 @@ __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint
     for (int u = 0; u < 2; u++) {
         const int i0 = 2 * u, i1 = 2 * u + 1;
         mma_u8s8(D[0], q6v<0>(LA0[i0], LA1[i0], HA[i0]), q6v<0>(LB0[i0], LB1[i0], HB[i0]),
-                 q6v<0>(LA0[i1], LA1[i1], HA[i1]), q6v<0>(LB0[i1], LB1[i1], HB[i1]), X[0][i0], X[0][i1]);
+                 q6v<0>(LA0[i1], LA1[i1], HA[i1]), q6v<0>(LB0[i1], LB1[i1], HB[i1]), A.x[i0], A.x[i1]);
         mma_u8s8(D[1], q6v<1>(LA0[i0], LA1[i0], HA[i0]), q6v<1>(LB0[i0], LB1[i0], HB[i0]),
-                 q6v<1>(LA0[i1], LA1[i1], HA[i1]), q6v<1>(LB0[i1], LB1[i1], HB[i1]), X[1][i0], X[1][i1]);
+                 q6v<1>(LA0[i1], LA1[i1], HA[i1]), q6v<1>(LB0[i1], LB1[i1], HB[i1]), A.x[4 + i0], A.x[4 + i1]);
         mma_u8s8(D[2], q6v<2>(LA0[i0], LA1[i0], HA[i0]), q6v<2>(LB0[i0], LB1[i0], HB[i0]),
-                 q6v<2>(LA0[i1], LA1[i1], HA[i1]), q6v<2>(LB0[i1], LB1[i1], HB[i1]), X[2][i0], X[2][i1]);
+                 q6v<2>(LA0[i1], LA1[i1], HA[i1]), q6v<2>(LB0[i1], LB1[i1], HB[i1]), A.x[8 + i0], A.x[8 + i1]);
         mma_u8s8(D[3], q6v<3>(LA0[i0], LA1[i0], HA[i0]), q6v<3>(LB0[i0], LB1[i0], HB[i0]),
-                 q6v<3>(LA0[i1], LA1[i1], HA[i1]), q6v<3>(LB0[i1], LB1[i1], HB[i1]), X[3][i0], X[3][i1]);
+                 q6v<3>(LA0[i1], LA1[i1], HA[i1]), q6v<3>(LB0[i1], LB1[i1], HB[i1]), A.x[12 + i0], A.x[12 + i1]);
     }
     // q6 - 32: subtract 32 x the group's activation sum (Q8_K bsums are per 16 values, one
     // per Q6_K scale group); groups 8n + 2m + h are the halves h of pair words 4n + m
-    const uint4 bq = *reinterpret_cast<const uint4 *>(bsw + 4 * n);
-    const uint32_t bw[4] = {bq.x, bq.y, bq.z, bq.w};
+    const uint32_t bw[4] = {A.bs.x, A.bs.y, A.bs.z, A.bs.w};
     int bs[4];
 #pragma unroll
     for (int m = 0; m < 4; m++) bs[m] = h ? ((int)bw[m] >> 16) : (int)(int16_t)(bw[m] & 0xffffu);
@@ -260,46 +295,163 @@ __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint
         }
         const uint32_t db = *reinterpret_cast<const uint16_t *>(row + so + 208);
         float &acc = r ? accB : accA;
-        acc = fmaf(f16_bits_to_f32(db) * ad, (float)I, acc);
+        acc = fmaf(f16_bits_to_f32(db) * A.d, (float)I, acc);
     }
 }
 
-// One slice (sl superblocks starting at superblock sb0) of a warp's 16-row block: the
-// warp takes superblocks part, part + wpb, ...
 template <int TYPE>
-__device__ __forceinline__ void kq_slice(const uint8_t *ra, const uint8_t *rb, uint32_t part, uint32_t wpb, uint32_t sl,
-                                         uint32_t sb0, const int8_t *aq, const float *adk, const uint32_t *abw,
-                                         uint32_t c, bool bact, float &accA, float &accB) {
+__device__ __forceinline__ void kq_block(const uint8_t *ra, const uint8_t *rb, uint32_t sbl, const ActR &A, uint32_t c,
+                                         float &accA, float &accB) {
     constexpr uint32_t BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
-    for (uint32_t sbl = part; sbl < sl; sbl += wpb) {
-        const uint32_t sb = sb0 + sbl;
-        const int8_t *act = aq + (size_t)sb * QK_K;
-        const uint32_t *bsw = abw + 8 * sb;
-        if (TYPE == T_Q6_K) {
-            if (sbl & 1u)
-                kq_q6<false>(ra, rb, sbl * BB, act, bsw, adk[sb], c, bact, accA, accB);
-            else
-                kq_q6<true>(ra, rb, sbl * BB, act, bsw, adk[sb], c, bact, accA, accB);
-        } else {
-            kq_q45<TYPE>(ra, rb, sbl * BB, act, bsw, adk[sb], c, bact, accA, accB);
-        }
+    if (TYPE == T_Q6_K) {
+        if (sbl & 1u)
+            kq_q6<false>(ra, rb, sbl * BB, A, c, accA, accB);
+        else
+            kq_q6<true>(ra, rb, sbl * BB, A, c, accA, accB);
+    } else {
+        kq_q45<TYPE>(ra, rb, sbl * BB, A, c, accA, accB);
     }
 }
 
-// Destination shift of a stage whose source starts at `src` (congruent layout: the source's
-// offset mod 128, a multiple of 16).
-__device__ __forceinline__ uint32_t kq_shift(const KqParams &p, const uint8_t *src) {
-    return p.congruent ? (uint32_t)(reinterpret_cast<uintptr_t>(src) & 127u) : 0u;
+struct Ring {  // consumer-side stage ring position
+    uint32_t s, ph;
+};
+
+// The stages of one tile for one consumer warp: kQG row groups x nsl slices; this warp's
+// superblocks of each slice are part, part + wpb, ... (< sl), taken two at a time with
+// independent accumulators (two mma chains in flight) and their activations loaded before
+// the stage wait. Row partials of group gi end in accA[gi] (row g of the warp's 16-row
+// block) / accB[gi] (row g + 8).
+template <int TYPE>
+__device__ __forceinline__ bool kq_tile(const KqParams &p, KqHdr *h, uint8_t *stages, const JobR &J, uint32_t ngrp,
+                                        bool skip, const int8_t *aq, const float *adk, const uint32_t *abw,
+                                        uint32_t rbk, uint32_t part, uint32_t wpb, uint32_t g, uint32_t c, bool bact,
+                                        uint32_t lane, Ring &R, float (&accA)[kQG], float (&accB)[kQG]) {
+    const uint32_t S = p.stages;
+    const uint32_t rofs = (rbk * 16u + g) * J.pstride;
+#pragma unroll
+    for (int gi = 0; gi < kQG; gi++) {
+        if ((uint32_t)gi >= ngrp) break;
+        float a1 = 0.0f, b1 = 0.0f;  // second chain
+        for (uint32_t sli = 0; sli < J.nsl; sli++) {
+            const uint32_t sb0 = sli * J.sl;
+            uint32_t sbl = part;
+            ActR A0, A1;
+            const bool two = sbl + wpb < J.sl;
+            if (!skip) {
+                load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
+                if (two) load_act<TYPE>(aq, adk, abw, sb0 + sbl + wpb, c, bact, A1);
+            }
+            if (!mbar_wait_bounded(&h->full[R.s], R.ph, p.err, ERR_TIMEOUT_FULL)) return false;
+            if (!skip) {
+                const uint8_t *ra = stages + R.s * p.stage_bytes + rofs;
+                const uint8_t *rb = ra + 8u * J.pstride;
+                if (two) {
+                    kq_block<TYPE>(ra, rb, sbl, A0, c, accA[gi], accB[gi]);
+                    kq_block<TYPE>(ra, rb, sbl + wpb, A1, c, a1, b1);
+                    sbl += 2 * wpb;
+                } else {
+                    kq_block<TYPE>(ra, rb, sbl, A0, c, accA[gi], accB[gi]);
+                    sbl += wpb;
+                }
+                for (; sbl < J.sl; sbl += wpb) {  // slices wider than two superblocks per warp
+                    load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
+                    kq_block<TYPE>(ra, rb, sbl, A0, c, a1, b1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&h->empty[R.s]);
+            if (++R.s == S) {
+                R.s = 0;
+                R.ph ^= 1u;
+            }
+        }
+        accA[gi] += a1;
+        accB[gi] += b1;
+    }
+    return true;
 }
 
-__device__ __forceinline__ void kq_store(const KqParams &p, const KqJob &jb, uint32_t row, float v) {
-    jb.out[row] = v;
+__device__ __forceinline__ void kq_store(const KqParams &p, float *out, uint32_t row, float v) {
+    out[row] = v;
     for (uint32_t q = 0; q < p.ar_ndst; q++) p.ar_dst[q][row] = v;
+}
+
+// Consumer warps of a CTA whose tiles all hold weights of type TYPE.
+template <int TYPE>
+__device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t *stages, const KqGroup &G, int warp,
+                                           int lane) {
+    const uint32_t g = lane >> 2, c = lane & 3;
+    const bool bact = c == (g >> 1);
+    const ActsView &AV = p.acts;
+    const uint32_t k = p.k, nsb = k / QK_K;
+    Ring R{0, 0};
+    uint32_t tloc = 0;
+    int ji = (int)G.job0 - 1;
+    JobR J{};
+    uint32_t next_begin = 0;
+    const uint32_t step = G.cta1 - G.cta0;
+    for (uint32_t tile = G.tile0 + (blockIdx.x - G.cta0); tile < G.tile1; tile += step, tloc++) {
+        while (ji + 1 < (int)G.job1 && next_begin <= tile) {
+            load_job(p.jobs[++ji], J);
+            next_begin = ji + 1 < (int)G.job1 ? p.jobs[ji + 1].tile_begin : 0xffffffffu;
+        }
+        const uint32_t wpb = kQW >> J.rb_log2, rbk = warp >> (kQWLog2 - J.rb_log2), part = warp & (wpb - 1);
+        const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (kQG * grows);
+        const uint32_t ngrp = min((uint32_t)kQG, (J.rows - r0 + grows - 1) / grows);
+        const uint32_t ex = J.sel ? *(volatile const uint32_t *)J.sel : 0u;
+        const bool skip = ex == kNoExpert;
+        const uint64_t trow = (uint64_t)p.tok0 + J.tok;
+        const int8_t *aq = AV.qk + trow * k;
+        const float *adk = AV.dk + trow * nsb;
+        const uint32_t *abw = reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
+        float accA[kQG], accB[kQG];
+#pragma unroll
+        for (int gi = 0; gi < kQG; gi++) accA[gi] = accB[gi] = 0.0f;
+        if (!kq_tile<TYPE>(p, h, stages, J, ngrp, skip, aq, adk, abw, rbk, part, wpb, g, c, bact, lane, R, accA, accB))
+            return;
+        // tile done: the 4 threads of each row add their shares, every warp publishes its rows'
+        // partials; the last warp to arrive adds the parts in warp order and stores
+        const uint32_t ri = tloc % kQRed;
+#pragma unroll
+        for (int gi = 0; gi < kQG; gi++) {
+            float a = accA[gi], b = accB[gi];
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            a += __shfl_xor_sync(0xffffffffu, a, 2);
+            b += __shfl_xor_sync(0xffffffffu, b, 1);
+            b += __shfl_xor_sync(0xffffffffu, b, 2);
+            if (c == 0) {
+                h->red[ri][warp][gi][g] = a;
+                h->red[ri][warp][gi][g + 8] = b;
+            }
+        }
+        __syncwarp();
+        __threadfence_block();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&h->cnt[ri], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == kQW - 1) {
+            __threadfence_block();
+            if (!skip) {
+                const uint32_t nrows = min(ngrp * grows, J.rows - r0);
+                for (uint32_t i = lane; i < nrows; i += 32) {
+                    const uint32_t gi = i >> (4 + J.rb_log2), ii = i & (grows - 1), bk = ii >> 4, rr = ii & 15u;
+                    float v = 0.0f;
+                    for (uint32_t q = 0; q < wpb; q++) v += *((volatile float *)&h->red[ri][bk * wpb + q][gi][rr]);
+                    kq_store(p, J.out, r0 + i, v);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) atomicExch(&h->cnt[ri], 0);
+        }
+        __syncwarp();
+    }
 }
 
 __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant__ KqParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     KqHdr *h = reinterpret_cast<KqHdr *>(smem);
+    uint8_t *stages = smem + p.stage_off;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t S = p.stages;
     pdl_trigger();
@@ -312,48 +464,54 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
     }
     if (threadIdx.x < kQRed) h->cnt[threadIdx.x] = 0;
     __syncthreads();
+    int gq = 0;
+    while (gq + 1 < p.n_groups && blockIdx.x >= p.groups[gq].cta1) gq++;
+    const KqGroup &G = p.groups[gq];
 
     if (warp == kQW) {  // ---- producer: one bulk copy per weight row and slice ----
         if (!p.early_weights) pdl_wait();
         const uint64_t pol = policy_evict_first();
         uint32_t li = 0, s = 0, ph = 0;  // stages issued, ring slot, pass parity
-        int ji = 0;
+        int ji = (int)G.job0 - 1;
+        JobR J{};
+        uint32_t next_begin = 0;
         bool ok = true;
-        for (uint32_t tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
-            while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
-            const KqJob &jb = p.jobs[ji];
-            const uint32_t trows = 16u * jb.rb, r0 = (tile - jb.tile_begin) * trows;
-            const uint32_t nrows = min(trows, jb.rows - r0);
-            const uint32_t ex = jb.sel ? *jb.sel : 0u;
-            for (uint32_t sl = 0; sl < jb.nsl; sl++) {
-                if (li >= S) {
-                    int w_ok = 1;
-                    if (lane == 0) w_ok = mbar_wait_bounded(&h->empty[s], ph ^ 1u, p.err, ERR_TIMEOUT_EMPTY);
-                    if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
-                        ok = false;
-                        break;
+        const uint32_t step = G.cta1 - G.cta0;
+        for (uint32_t tile = G.tile0 + (blockIdx.x - G.cta0); ok && tile < G.tile1; tile += step) {
+            while (ji + 1 < (int)G.job1 && next_begin <= tile) {
+                load_job(p.jobs[++ji], J);
+                next_begin = ji + 1 < (int)G.job1 ? p.jobs[ji + 1].tile_begin : 0xffffffffu;
+            }
+            const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (kQG * grows);
+            const uint32_t ex = J.sel ? *(volatile const uint32_t *)J.sel : 0u;
+            for (uint32_t gi = 0; ok && gi < (uint32_t)kQG && r0 + gi * grows < J.rows; gi++) {
+                const uint32_t g0 = r0 + gi * grows, nrows = min(grows, J.rows - g0);
+                for (uint32_t sl = 0; sl < J.nsl; sl++) {
+                    if (li >= S) {
+                        int w_ok = 1;
+                        if (lane == 0) w_ok = mbar_wait_bounded(&h->empty[s], ph ^ 1u, p.err, ERR_TIMEOUT_EMPTY);
+                        if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+                            ok = false;
+                            break;
+                        }
                     }
-                }
-                if (ex == kNoExpert) {  // routed to another rank's expert: nothing to load
-                    if (lane == 0) mbar_arrive(&h->full[s]);
-                } else {
-                    const uint8_t *src = jb.w + (uint64_t)ex * jb.w_stride + (uint64_t)r0 * jb.row_bytes +
-                                         (uint64_t)sl * jb.slice_bytes;
-                    uint8_t *dst = smem + p.stage_off + s * p.stage_bytes + kq_shift(p, src);
-                    if (lane == 0) mbar_arrive_expect_tx(&h->full[s], nrows * jb.slice_bytes);
-                    __syncwarp();
-                    if (jb.nsl == 1 && jb.pstride == jb.row_bytes) {  // whole contiguous rows: one copy
-                        if (lane == 0) bulk_g2s(dst, src, nrows * jb.row_bytes, &h->full[s], pol);
+                    if (ex == kNoExpert) {  // routed to another rank's expert: nothing to load
+                        if (lane == 0) mbar_arrive(&h->full[s]);
                     } else {
+                        const uint8_t *src = J.w + (uint64_t)ex * J.w_stride + (uint64_t)g0 * J.row_bytes +
+                                             (uint64_t)sl * J.slice_bytes;
+                        uint8_t *dst = stages + s * p.stage_bytes;
+                        if (lane == 0) mbar_arrive_expect_tx(&h->full[s], nrows * J.slice_bytes);
+                        __syncwarp();
                         for (uint32_t r = lane; r < nrows; r += 32)
-                            bulk_g2s(dst + r * jb.pstride, src + (uint64_t)r * jb.row_bytes, jb.slice_bytes,
-                                     &h->full[s], pol);
+                            bulk_g2s(dst + r * J.pstride, src + (uint64_t)r * J.row_bytes, J.slice_bytes, &h->full[s],
+                                     pol);
                     }
-                }
-                li++;
-                if (++s == S) {
-                    s = 0;
-                    ph ^= 1u;
+                    li++;
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
             }
         }
@@ -367,95 +525,12 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
         return;
     }
 
-    // ---- consumers: stage this call's Q8_K activations (rows tok0 .. tok0 + n_stage) ----
-    pdl_wait();
-    {
-        const uint32_t nt = p.n_stage, k = p.k, nsb = p.nsb, tid = threadIdx.x, nthr = kQW * 32;
-        const ActsView &A = p.acts;
-        const uint4 *src = reinterpret_cast<const uint4 *>(A.qk + (size_t)p.tok0 * k);
-        uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_q);
-        for (uint32_t i = tid; i < nt * k / 16; i += nthr) dst[i] = src[i];
-        for (uint32_t i = tid; i < nt * nsb; i += nthr)
-            reinterpret_cast<float *>(smem + p.o_d)[i] = A.dk[(size_t)p.tok0 * nsb + i];
-        const uint32_t *bsrc = reinterpret_cast<const uint32_t *>(A.bsk + (size_t)p.tok0 * (k / 16));
-        for (uint32_t i = tid; i < nt * k / 32; i += nthr) reinterpret_cast<uint32_t *>(smem + p.o_bs)[i] = bsrc[i];
-        named_bar_sync(1, nthr);
-    }
-
-    const uint32_t g = lane >> 2, c = lane & 3;
-    const bool bact = c == (g >> 1);
-    uint32_t s = 0, ph = 0, tloc = 0;
-    int ji = 0;
-    bool ok = true;
-    for (uint32_t tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x, tloc++) {
-        while (ji + 1 < p.n_jobs && p.jobs[ji + 1].tile_begin <= tile) ji++;
-        const KqJob &jb = p.jobs[ji];
-        const uint32_t trows = 16u * jb.rb, r0 = (tile - jb.tile_begin) * trows;
-        const uint32_t nrows = min(trows, jb.rows - r0);
-        const uint32_t ex = jb.sel ? *jb.sel : 0u;
-        const bool skip = ex == kNoExpert;
-        // stage shift of slice sl: (tile source + sl * slice bytes) mod 128, as the producer has it
-        const uint32_t sh0 = kq_shift(p, jb.w + (uint64_t)(skip ? 0u : ex) * jb.w_stride + (uint64_t)r0 * jb.row_bytes);
-        const uint32_t wpb = kQW / jb.rb, rbk = warp / wpb, part = warp % wpb;
-        const int8_t *aq = reinterpret_cast<const int8_t *>(smem + p.o_q) + (size_t)jb.tok * p.k;
-        const float *adk = reinterpret_cast<const float *>(smem + p.o_d) + (size_t)jb.tok * p.nsb;
-        const uint32_t *abw = reinterpret_cast<const uint32_t *>(smem + p.o_bs) + (size_t)jb.tok * (p.k / 32);
-        float accA = 0.0f, accB = 0.0f;
-        for (uint32_t sl = 0; sl < jb.nsl; sl++) {
-            if (!mbar_wait_bounded(&h->full[s], ph, p.err, ERR_TIMEOUT_FULL)) {
-                ok = false;
-                break;
-            }
-            if (!skip) {
-                const uint32_t shift = p.congruent ? (sh0 + sl * jb.slice_bytes) & 127u : 0u;
-                const uint8_t *ra = smem + p.stage_off + s * p.stage_bytes + shift + (rbk * 16u + g) * jb.pstride;
-                const uint8_t *rb = ra + 8u * jb.pstride;
-                const uint32_t sb0 = sl * jb.sl;
-                switch (jb.type) {
-                    case T_Q4_K: kq_slice<T_Q4_K>(ra, rb, part, wpb, jb.sl, sb0, aq, adk, abw, c, bact, accA, accB); break;
-                    case T_Q5_K: kq_slice<T_Q5_K>(ra, rb, part, wpb, jb.sl, sb0, aq, adk, abw, c, bact, accA, accB); break;
-                    default: kq_slice<T_Q6_K>(ra, rb, part, wpb, jb.sl, sb0, aq, adk, abw, c, bact, accA, accB); break;
-                }
-            }
-            __syncwarp();
-            if (sl + 1 == jb.nsl) {
-                // tile done: the 4 threads of each row add their shares, every warp publishes
-                // its rows' partials; the last warp to arrive adds the parts in order and stores
-                accA += __shfl_xor_sync(0xffffffffu, accA, 1);
-                accA += __shfl_xor_sync(0xffffffffu, accA, 2);
-                accB += __shfl_xor_sync(0xffffffffu, accB, 1);
-                accB += __shfl_xor_sync(0xffffffffu, accB, 2);
-                const uint32_t ri = tloc % kQRed;
-                if (c == 0) {
-                    h->red[ri][warp][g] = accA;
-                    h->red[ri][warp][g + 8] = accB;
-                }
-                __syncwarp();
-                __threadfence_block();
-                int old = 0;
-                if (lane == 0) old = atomicAdd(&h->cnt[ri], 1);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == kQW - 1) {
-                    __threadfence_block();
-                    if (!skip) {
-                        for (uint32_t i = lane; i < nrows; i += 32) {
-                            const uint32_t bk = i >> 4, rr = i & 15u;
-                            float v = 0.0f;
-                            for (uint32_t q = 0; q < wpb; q++) v += *((volatile float *)&h->red[ri][bk * wpb + q][rr]);
-                            kq_store(p, jb, r0 + i, v);
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) atomicExch(&h->cnt[ri], 0);
-                }
-                __syncwarp();
-            }
-            if (lane == 0) mbar_arrive(&h->empty[s]);
-            if (++s == S) {
-                s = 0;
-                ph ^= 1u;
-            }
-        }
+    // ---- consumers ----
+    pdl_wait();  // the activations come from the kernel before this one
+    switch (G.type) {
+        case T_Q4_K: kq_consume<T_Q4_K>(p, h, stages, G, warp, lane); break;
+        case T_Q5_K: kq_consume<T_Q5_K>(p, h, stages, G, warp, lane); break;
+        default: kq_consume<T_Q6_K>(p, h, stages, G, warp, lane); break;
     }
     if (p.ar_nflag) {  // this CTA's rows are in every receive buffer: count it in
         __threadfence_system();
@@ -469,10 +544,11 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
 uint32_t round_up_u(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 // Tiling of one job: slice length sl (a divisor of the superblock count; Q6_K slices a
-// multiple of 8 superblocks so that 210-byte rows stay 16-byte multiples), 16-row blocks
-// per tile rb (so that the 16 / rb warps of a block have a superblock each), stage bytes
-// <= 64 KB. Prefers slices the block's warps split evenly, then longer slices.
-bool kq_plan(const rcu_weight *w, uint32_t k, bool congruent, KqJob &jd) {
+// multiple of 8 superblocks so that 210-byte rows stay 16-byte multiples), 16-row blocks per
+// stage rb (so that the kQW / rb warps of a block have a superblock each), stage bytes
+// <= 64 KB. Prefers slices the block's warps split evenly, then slices of two superblocks
+// per warp (two independent chains), then longer slices.
+bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
     const int t = w->type;
     if (t != T_Q4_K && t != T_Q5_K && t != T_Q6_K) return false;
     if (w->cols != k || k % QK_K != 0 || w->row_bytes % 16 != 0 || ((uintptr_t)w->data & 15u)) return false;
@@ -481,20 +557,17 @@ bool kq_plan(const rcu_weight *w, uint32_t k, bool congruent, KqJob &jd) {
     for (uint32_t sl = nsb; sl >= 1; sl--) {
         if (nsb % sl || (sl * bb) % 16) continue;
         uint32_t ps = sl * bb;
-        if (congruent)
-            ps += ((uint32_t)w->row_bytes - ps) % 128u;
-        else
-            ps += (16u + 128u - ps % 128u) % 128u;
-        uint32_t rb = 1;
-        while (kQW / rb > sl && rb < (uint32_t)kQW) rb *= 2;
-        if (16u * rb * ps + (congruent ? 128u : 0u) > kQMaxStage) continue;
-        const uint32_t wpb = kQW / rb;
-        const double bal = (double)sl / (double)(wpb * ((sl + wpb - 1) / wpb));
-        const double score = bal * 4.0 + (double)sl / nsb;
+        ps += (16u + 128u - ps % 128u) % 128u;
+        uint32_t rbl = 0;
+        while ((uint32_t)(kQW >> rbl) > sl && rbl < (uint32_t)kQWLog2) rbl++;
+        if ((16u << rbl) * ps > kQMaxStage) continue;
+        const uint32_t wpb = kQW >> rbl, per = (sl + wpb - 1) / wpb;
+        const double bal = (double)sl / (double)(wpb * per);
+        const double score = bal * 8.0 + (per == 2 ? 2.0 : 0.0) + (double)sl / nsb;
         if (score > best) {
             best = score;
             jd.sl = sl;
-            jd.rb = rb;
+            jd.rb_log2 = rbl;
             jd.pstride = ps;
         }
     }
@@ -506,25 +579,15 @@ bool kq_plan(const rcu_weight *w, uint32_t k, bool congruent, KqJob &jd) {
     return true;
 }
 
-// Shared-memory layout of a launch: header, the staged Q8_K rows (codes, scales, bsums), then
-// the weight stages. Returns false when two stages do not fit next to the staged rows.
-bool kq_smem_layout(const rcu_ctx *ctx, uint32_t k, uint32_t n_rows, uint32_t stage_bytes, KqParams &p) {
-    uint32_t off = kQHdrBytes;
-    p.o_q = off;
-    off = round_up_u(off + n_rows * k, 16);
-    p.o_d = off;
-    off = round_up_u(off + n_rows * (k / QK_K) * 4, 16);
-    p.o_bs = off;
-    off = round_up_u(off + n_rows * (k / 16) * 2, 16);
-    p.stage_off = round_up_u(off, 128);
+uint32_t kq_stage_bytes(const KqJob &jd) { return round_up_u((16u << jd.rb_log2) * jd.pstride, 128); }
+
+// Shared-memory layout: header, then the weight stages. False when two stages do not fit.
+bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p) {
+    p.stage_off = kQHdrBytes;
     const uint32_t budget = (uint32_t)ctx->max_smem_optin;
     if (p.stage_off + 2 * stage_bytes > budget) return false;
     p.stages = std::min<uint32_t>(kQMaxStages, (budget - p.stage_off) / stage_bytes);
     return true;
-}
-
-uint32_t kq_stage_bytes(const KqJob &jd, bool congruent) {
-    return round_up_u(16 * jd.rb * jd.pstride + (congruent ? 128u : 0u), 128);
 }
 
 }  // namespace
@@ -532,60 +595,93 @@ uint32_t kq_stage_bytes(const KqJob &jd, bool congruent) {
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs || !(a.have & RCU_ACT_Q8K)) return false;
     uint64_t bytes = 0;
-    uint32_t n_rows = 0, stage_bytes = 0;
+    uint32_t stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
         KqJob jd{};
-        if (!kq_plan(jobs[i].w, a.k, ctx->gemv_kq_congruent, jd)) return false;
+        if (!kq_plan(jobs[i].w, a.k, jd)) return false;
         if (jobs[i].sel && jobs[i].w_stride % 16 != 0) return false;
-        if (jobs[i].tok + 1 > kQMaxStageRows) return false;
         bytes += (uint64_t)(jobs[i].rows ? jobs[i].rows : jobs[i].w->rows) * jobs[i].w->row_bytes;
-        n_rows = std::max(n_rows, jobs[i].tok + 1);
-        stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd, ctx->gemv_kq_congruent));
+        stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd));
     }
     KqParams lay;
-    if (!kq_smem_layout(ctx, a.k, n_rows, stage_bytes, lay)) return false;
-    // Small launches take the lane GEMV: this kernel's start-up (activation staging, the first
-    // tile's latency chain) is longer, and with 1-2 tiles per CTA nothing hides it; K = 768
-    // expert rows also give it few tiles (256-row tiles). Measured on B200: back-to-back launches
-    // of one shape, 7 MB Q4_K 12.4 us here vs 6.0 lane, 9.4 MB 12.6 vs 8.1, 28 MB 12.5 vs 17.0,
-    // 41 MB Q6_K 13.0 vs 21.5, 510 MB Q6_K 131 vs 260; serialized (profiler) 9.4 MB Q4_K 9.4 vs
-    // 10.4 us, and the Qwen3-8B decode step (every launch >= 9.4 MB here) 2.67 ms vs 3.48 ms.
+    if (!kq_smem_layout(ctx, stage_bytes, lay)) return false;
+    // Small launches take the lane GEMV: with 1-2 tiles per CTA this kernel's start-up is not
+    // hidden; K = 768 expert rows also give it few tiles.
     return bytes >= ctx->gemv_kq_min_bytes;
 }
 
-int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0) {
+int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
+                   const ArPush *push) {
     KqParams p{};
     p.n_jobs = n_jobs;
     p.k = a.k;
-    p.nsb = a.k / QK_K;
     p.tok0 = tok0;
     p.acts = a;
     p.err = ctx->dev_err;
     p.early_weights = ctx->early_weights ? 1u : 0u;
-    p.congruent = ctx->gemv_kq_congruent ? 1u : 0u;
+    if (push) {
+        if (n_jobs != 1 || tok0 != 0 || push->n_dst > kQMaxPeers || push->n_flag > kQMaxPeers)
+            return set_err(ctx, RCU_ERR_INVALID, "gemv: all-reduce push needs one job, one launch, <= 8 ranks");
+        p.ar_ndst = push->n_dst;
+        p.ar_nflag = push->n_flag;
+        for (uint32_t q = 0; q < push->n_dst; q++) p.ar_dst[q] = push->dst[q];
+        for (uint32_t q = 0; q < push->n_flag; q++) p.ar_flag[q] = push->flag[q];
+    }
+    // jobs grouped by weight type (each group's tiles run on CTAs of their own)
     uint32_t tiles = 0, stage_bytes = 0;
-    for (int i = 0; i < n_jobs; i++) {
-        KqJob &jd = p.jobs[i];
-        if (!kq_plan(jobs[i].w, a.k, ctx->gemv_kq_congruent, jd))
-            return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: weight not K-quant tileable");
-        jd.w = jobs[i].w->data;
-        jd.out = jobs[i].out + (jobs[i].sel ? 0 : (uint64_t)tok0 * jobs[i].ld);  // indirect jobs: own rows
-        jd.sel = jobs[i].sel;
-        jd.w_stride = jobs[i].w_stride;
-        jd.tok = jobs[i].tok;
-        jd.rows = jobs[i].rows ? jobs[i].rows : (uint32_t)jobs[i].w->rows;
-        if (jd.sel) p.early_weights = 0;  // the producer reads the router's choice: wait first
-        p.n_stage = std::max(p.n_stage, jd.tok + 1);
-        jd.tile_begin = tiles;
-        tiles += (jd.rows + 16 * jd.rb - 1) / (16 * jd.rb);
-        stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd, p.congruent != 0));
+    uint64_t gbytes[kQMaxGroups] = {};
+    int nj = 0;
+    for (const int ty : {T_Q4_K, T_Q5_K, T_Q6_K}) {
+        KqGroup &G = p.groups[p.n_groups];
+        G.type = (uint32_t)ty;
+        G.job0 = (uint32_t)nj;
+        G.tile0 = tiles;
+        for (int i = 0; i < n_jobs; i++) {
+            if (jobs[i].w->type != ty) continue;
+            KqJob &jd = p.jobs[nj++];
+            if (!kq_plan(jobs[i].w, a.k, jd))
+                return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: weight not K-quant tileable");
+            jd.w = jobs[i].w->data;
+            jd.out = jobs[i].out + (jobs[i].sel ? 0 : (uint64_t)tok0 * jobs[i].ld);  // indirect jobs: own rows
+            jd.sel = jobs[i].sel;
+            jd.w_stride = jobs[i].w_stride;
+            jd.tok = jobs[i].tok;
+            jd.rows = jobs[i].rows ? jobs[i].rows : (uint32_t)jobs[i].w->rows;
+            if (jd.sel) p.early_weights = 0;  // the producer reads the router's choice: wait first
+            jd.tile_begin = tiles;
+            const uint32_t trows = kQG * (16u << jd.rb_log2);
+            tiles += (jd.rows + trows - 1) / trows;
+            stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd));
+            gbytes[p.n_groups] += (uint64_t)jd.rows * jd.row_bytes;
+        }
+        G.job1 = (uint32_t)nj;
+        G.tile1 = tiles;
+        if (G.job1 > G.job0) p.n_groups++;
+    }
+    if (nj != n_jobs) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: weight not K-quant tileable");
+    // CTAs per group in proportion to its bytes (at least one, at most one per tile)
+    uint64_t total_bytes = 0;
+    for (int q = 0; q < p.n_groups; q++) total_bytes += gbytes[q];
+    const uint32_t sms = std::max<uint32_t>((uint32_t)ctx->num_sms, (uint32_t)p.n_groups);
+    uint32_t cta = 0;
+    for (int q = 0; q < p.n_groups; q++) {
+        KqGroup &G = p.groups[q];
+        const uint32_t gt = G.tile1 - G.tile0;
+        uint32_t n = q + 1 == p.n_groups ? sms - cta
+                                         : (uint32_t)((double)sms * (double)gbytes[q] / (double)std::max<uint64_t>(total_bytes, 1) + 0.5);
+        n = std::max<uint32_t>(1u, std::min<uint32_t>(n, gt));
+        n = std::min<uint32_t>(n, sms - cta - (uint32_t)(p.n_groups - 1 - q));  // leave one for each group after
+        G.cta0 = cta;
+        G.cta1 = cta + n;
+        cta += n;
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
-    if (!kq_smem_layout(ctx, a.k, p.n_stage, stage_bytes, p))
-        return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: activation rows + two weight stages exceed shared memory");
+    if (!kq_smem_layout(ctx, stage_bytes, p))
+        return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: two weight stages exceed shared memory");
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
-    const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
+    const uint32_t grid = cta;
+    if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
     static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
     if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
         RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv_kq, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -180,7 +180,6 @@ struct rcu_ctx {
     bool static_weights = false;  // caller promise (rcu_set_static_weights): early_weights outside the forward too
     bool gemm_i8 = false;          // prefill: int8 GEMM with exact block sums for Q4_0 weights
     bool gemv_kq = true;           // batch-1 K-quant GEMV on the tensor cores (RIE_GEMV_KQ=0: lane GEMV)
-    bool gemv_kq_congruent = false;  // its stage row layout (RIE_GEMV_KQ_LAYOUT=congruent: source-aligned rows)
     uint64_t gemv_kq_min_bytes = 8ull << 20;  // ... for launches of at least this many weight bytes (RIE_GEMV_KQ_MIN_MB)
     void *h_act = nullptr;         // f16 activations of the prefill GEMM (grown on demand)
     size_t h_act_cap = 0;

@@ -36,7 +36,8 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
 // Batch-1 GEMV over Q4_K / Q5_K / Q6_K weights with the block dot products on the integer
 // tensor-core path (launch_gemv uses it when gemv_kq_ok holds; same job semantics).
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs);
-int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0);
+int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
+                   const ArPush *push = nullptr);
 // Prefill GEMM on the tensor cores (n_tok > 8). Returns RCU_ERR_UNSUPPORTED for shapes it
 // lacks (the caller then runs GEMV slices). launch_gemm_f16: every weight type, operands
 // dequantized to f16; the int8 kernel (exact per-block sums, Q4_0) when ctx->gemm_i8.
