@@ -92,6 +92,17 @@ bool attention_prefill_ok(int kv_type, uint64_t hd, uint64_t group, uint64_t n_t
 int launch_attention_prefill(rcu_ctx *ctx, const void *kc, const void *vc, uint64_t n_kv, uint64_t hd, uint64_t slots,
                              const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0, const uint64_t *pos_ptr,
                              uint64_t window, float softcap, float *out);
+// Decode attention at head_dim 128 with 4 or 8 query heads per KV head (rcu_attn_dec.cu): the
+// context of each (token, KV head) split over a cluster of CTAs (up to 8; more clusters merge
+// through `parts`, per-(token, query head, cluster) rows of hd + 2 floats, with the counters
+// `done`, zero between launches). max_len: the longest context the plan covers.
+bool attention_dec_ok(int kv_type, uint64_t hd, uint64_t group);
+uint32_t attention_dec_max_clusters(uint64_t max_len, uint64_t n_tok, uint64_t n_kv, int num_sms);
+struct ActOut;
+int launch_attention_dec(rcu_ctx *ctx, const uint8_t *kc, const uint8_t *vc, int kv_type, uint64_t n_kv,
+                         uint64_t slots, uint64_t row_bytes, const float *q, uint64_t n_tok, uint64_t n_head,
+                         uint64_t pos0, const uint64_t *pos_ptr, uint64_t max_len, uint64_t window, float softcap,
+                         float *out, const ActOut *aq, uint32_t *done, float *parts);
 // Whether the merge can quantize in the same kernel for this head shape and act format
 // (a GQA group's output must hold whole activation blocks).
 bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt);

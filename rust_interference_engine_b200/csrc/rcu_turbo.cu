@@ -19,6 +19,7 @@
 #include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
+#include "rcu_turbo.cuh"
 
 struct rcu_kv {
     rcu_ctx *ctx = nullptr;
@@ -28,58 +29,6 @@ struct rcu_kv {
 };
 
 namespace rcu {
-
-constexpr uint64_t KV_SEED = 0x75426F5175616E74ull;          // turbo.rs:122
-constexpr int kMaxHd = 512;                                   // cpu.rs:106 (turbo needs hd <= 512)
-__constant__ int8_t c_levels[16] = {-126, -95, -74, -58, -43, -30, -18, -6, 6, 18, 30, 43, 58, 74, 95, 126};
-__constant__ float c_signs[kMaxHd];                            // sign(KV_SEED, i)
-
-static float host_sign(uint64_t seed, uint64_t i) {  // turbo.rs:80-89
-    uint64_t z = seed + i * 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return ((z ^ (z >> 31)) & 1) == 0 ? 1.0f : -1.0f;
-}
-static int ensure_signs(rcu_ctx *ctx) {
-    static bool done[64] = {};
-    if (done[ctx->device & 63]) return RCU_OK;
-    float s[kMaxHd];
-    for (int i = 0; i < kMaxHd; i++) s[i] = host_sign(KV_SEED, i);
-    RCU_CUDA_TRY(ctx, cudaMemcpyToSymbol(c_signs, s, sizeof(s)));
-    done[ctx->device & 63] = true;
-    return RCU_OK;
-}
-__host__ __device__ inline uint32_t turbo_block(uint32_t d) {  // turbo.rs:52-58
-    uint32_t b = 1;
-    while (d % (b * 2) == 0 && b < 256) b *= 2;
-    return b;
-}
-__host__ __device__ inline uint32_t turbo_row_bytes(uint32_t d) { return 2 * (d / turbo_block(d)) + d / 2; }
-
-// x <- R x (signs then normalised block FWHT) or x <- R^T x, on a warp-owned shared row.
-__device__ void rotate_row(float *x, uint32_t d, bool inverse, int lane) {
-    const uint32_t b = turbo_block(d);
-    if (!inverse)
-        for (uint32_t i = lane; i < d; i += 32) x[i] = __fmul_rn(x[i], c_signs[i]);
-    __syncwarp();
-    for (uint32_t h = 1; h < b; h *= 2) {
-        for (uint32_t pr = lane; pr < d / 2; pr += 32) {
-            const uint32_t blk = pr / (b / 2), q = pr % (b / 2);
-            const uint32_t j = blk * b + (q / h) * 2 * h + (q % h);
-            const float a = x[j], c = x[j + h];
-            x[j] = __fadd_rn(a, c);
-            x[j + h] = __fsub_rn(a, c);
-        }
-        __syncwarp();
-    }
-    const float s = 1.0f / sqrtf((float)b);
-    for (uint32_t i = lane; i < d; i += 32) {
-        float v = __fmul_rn(x[i], s);
-        if (inverse) v = __fmul_rn(v, c_signs[i]);
-        x[i] = v;
-    }
-    __syncwarp();
-}
 
 // quantize_rotated_4 (turbo.rs:141-164) of a rotated shared row into a reference row.
 __device__ void encode_rotated_row(const float *y, uint32_t d, uint8_t *out, uint8_t *qtmp, int lane) {
@@ -125,17 +74,6 @@ __device__ void encode_rotated_row(const float *y, uint32_t d, uint8_t *out, uin
         codes[m] = (uint8_t)(qtmp[g] | (qtmp[g + 16] << 4));
     }
     __syncwarp();
-}
-
-// One value of a 32-wide Q8_0 block per lane (quant/mod.rs:175-189 / avx2.rs:153-184).
-__device__ __forceinline__ int quant32(float v, int rounding, float &d_out) {
-    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
-    const float d = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
-    const float p = __fmul_rn(v, id);
-    const int r = rounding == RCU_ROUND_HALF_AWAY ? __float2int_rz(roundf(p)) : __float2int_rn(p);
-    d_out = d;
-    return max(-127, min(127, r));
 }
 
 // ---- KV append ----------------------------------------------------------------------------
@@ -860,6 +798,26 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
             return launch_quantize(ctx, v, o, (uint32_t)n_tok, (uint32_t)(n_head * kv->hd), aq->fmt);
         }
         return RCU_OK;
+    }
+    if (attention_dec_ok(kv->type, kv->hd, group)) {
+        // head_dim 128, 4 or 8 query heads per KV head: warp-per-chunk kernel, splits merged in
+        // a thread-block cluster (rcu_attn_dec.cu); fixed plans (graph replay) cover the whole cache
+        const uint64_t cap = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
+        const uint64_t last = pos0 + n_tok - 1;
+        const uint64_t max_len = n_split != 0 ? cap : (window > 0 ? std::min<uint64_t>(window, last + 1) : last + 1);
+        const uint64_t parts = n_tok * n_head * attention_dec_max_clusters(max_len, n_tok, kv->n_kv, ctx->num_sms);
+        uint8_t *scr = reinterpret_cast<uint8_t *>(scratch);
+        if (!scr) {
+            void *v = nullptr;
+            if (int st = scratch_get(ctx, counters_bytes(n_tok, kv->n_kv) + parts * (kv->hd + 2) * sizeof(float), &v))
+                return st;
+            scr = reinterpret_cast<uint8_t *>(v);
+            RCU_CUDA_TRY(ctx, cudaMemsetAsync(scr, 0, counters_bytes(n_tok, kv->n_kv), ctx->stream));
+        }
+        return launch_attention_dec(ctx, kv->k, kv->v, kv->type, kv->n_kv, kv->slots, kv->row_bytes, q, n_tok, n_head,
+                                    pos0, pos_ptr, max_len, window, softcap, out, aq,
+                                    reinterpret_cast<uint32_t *>(scr),
+                                    reinterpret_cast<float *>(scr + counters_bytes(n_tok, kv->n_kv)));
     }
     AttnParams p{};
     p.kc = kv->k;

@@ -1,0 +1,74 @@
+// rcu_turbo.cuh -- turbo4 pieces shared by the KV-cache / attention translation units:
+// the random-sign Hadamard rotation (turbo.rs:51-118) and the per-lane Q8_0 quantizer of
+// the rotated queries (quant/mod.rs:175-189). Each translation unit that includes this
+// header has its own copy of the sign table and fills it with ensure_signs() before its
+// first launch.
+#pragma once
+#include "rcu_internal.cuh"
+
+namespace rcu {
+
+constexpr uint64_t KV_SEED = 0x75426F5175616E74ull;          // turbo.rs:122
+constexpr int kMaxHd = 512;                                   // cpu.rs:106 (turbo needs hd <= 512)
+static __constant__ int8_t c_levels[16] = {-126, -95, -74, -58, -43, -30, -18, -6, 6, 18, 30, 43, 58, 74, 95, 126};
+static __constant__ float c_signs[kMaxHd];                            // sign(KV_SEED, i)
+
+static float host_sign(uint64_t seed, uint64_t i) {  // turbo.rs:80-89
+    uint64_t z = seed + i * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return ((z ^ (z >> 31)) & 1) == 0 ? 1.0f : -1.0f;
+}
+static int ensure_signs(rcu_ctx *ctx) {
+    static bool done[64] = {};
+    if (done[ctx->device & 63]) return RCU_OK;
+    float s[kMaxHd];
+    for (int i = 0; i < kMaxHd; i++) s[i] = host_sign(KV_SEED, i);
+    RCU_CUDA_TRY(ctx, cudaMemcpyToSymbol(c_signs, s, sizeof(s)));
+    done[ctx->device & 63] = true;
+    return RCU_OK;
+}
+__host__ __device__ inline uint32_t turbo_block(uint32_t d) {  // turbo.rs:52-58
+    uint32_t b = 1;
+    while (d % (b * 2) == 0 && b < 256) b *= 2;
+    return b;
+}
+__host__ __device__ inline uint32_t turbo_row_bytes(uint32_t d) { return 2 * (d / turbo_block(d)) + d / 2; }
+
+// x <- R x (signs then normalised block FWHT) or x <- R^T x, on a warp-owned shared row.
+static __device__ void rotate_row(float *x, uint32_t d, bool inverse, int lane) {
+    const uint32_t b = turbo_block(d);
+    if (!inverse)
+        for (uint32_t i = lane; i < d; i += 32) x[i] = __fmul_rn(x[i], c_signs[i]);
+    __syncwarp();
+    for (uint32_t h = 1; h < b; h *= 2) {
+        for (uint32_t pr = lane; pr < d / 2; pr += 32) {
+            const uint32_t blk = pr / (b / 2), q = pr % (b / 2);
+            const uint32_t j = blk * b + (q / h) * 2 * h + (q % h);
+            const float a = x[j], c = x[j + h];
+            x[j] = __fadd_rn(a, c);
+            x[j + h] = __fsub_rn(a, c);
+        }
+        __syncwarp();
+    }
+    const float s = 1.0f / sqrtf((float)b);
+    for (uint32_t i = lane; i < d; i += 32) {
+        float v = __fmul_rn(x[i], s);
+        if (inverse) v = __fmul_rn(v, c_signs[i]);
+        x[i] = v;
+    }
+    __syncwarp();
+}
+
+// One value of a 32-wide Q8_0 block per lane (quant/mod.rs:175-189 / avx2.rs:153-184).
+__device__ __forceinline__ int quant32(float v, int rounding, float &d_out) {
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    const float p = __fmul_rn(v, id);
+    const int r = rounding == RCU_ROUND_HALF_AWAY ? __float2int_rz(roundf(p)) : __float2int_rn(p);
+    d_out = d;
+    return max(-127, min(127, r));
+}
+
+}  // namespace rcu
