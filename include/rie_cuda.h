@@ -97,6 +97,13 @@ RCU_API int32_t rcu_weight_upload(rcu_ctx *ctx, uint32_t ggml_type, uint64_t row
  * the next multiple of 16. */
 RCU_API int32_t rcu_weight_view(rcu_ctx *ctx, uint32_t ggml_type, uint64_t rows, uint64_t cols, const void *dev_bytes,
                         rcu_weight **out);
+/* Quantizes f32 weights (rows x cols, row stride ld floats, device) into GGUF blocks of
+ * ggml_type (rows x rcu_row_bytes(type, cols) bytes, device), asynchronously on the context
+ * stream. Q8_0 and Q4_0 follow the reference's weight quantizers (quant/mod.rs:262-307); the
+ * reference has none for Q4_1, Q5_0, Q5_1, Q4_K, Q5_K, Q6_K, which use this library's own rules
+ * (valid blocks of the reference layouts, quant/reference.rs:53-207). */
+RCU_API int32_t rcu_quantize_weight(rcu_ctx *ctx, uint32_t ggml_type, uint64_t rows, uint64_t cols, const float *x_dev,
+                                    uint64_t ld, void *out_dev);
 /* Rows [start, start+n) of w (Weight::slice_rows, tensor.rs:64-69); shares storage. */
 RCU_API int32_t rcu_weight_slice_rows(const rcu_weight *w, uint64_t start, uint64_t n, rcu_weight **out);
 RCU_API void rcu_weight_free(rcu_weight *w);
@@ -185,6 +192,11 @@ RCU_API int32_t rcu_model_create(rcu_ctx *ctx, const rcu_model_config *cfg, rcu_
 RCU_API void rcu_model_free(rcu_model *m);
 RCU_API int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
                                      const void *host_bytes);
+/* rcu_model_set_tensor from the tensor's GGUF bytes in device memory (no counterpart in the
+ * reference: its weights come from a memory-mapped file). The model keeps its own copy (this
+ * rank's shard under tensor parallelism); dev_bytes may be freed after the call. */
+RCU_API int32_t rcu_model_set_tensor_device(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows,
+                                            uint64_t cols, const void *dev_bytes);
 /* CpuBackend::with_kv_type (model/cpu.rs:100-177): KV caches and scratch for n_ctx
  * positions and batches of up to max_batch tokens. Validates the model's tensors. */
 RCU_API int32_t rcu_backend_create(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, int32_t kv_type,
@@ -201,6 +213,14 @@ RCU_API int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint
 /* Same on device buffers, asynchronous on the context stream (tokens_dev: n uint32). */
 RCU_API int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, uint64_t n, uint64_t pos,
                                            int32_t all_logits, float *logits_dev);
+/* Partial forward (no counterpart in the reference): layers [layer0, layer1) for n tokens at
+ * positions pos..pos+n-1, starting from hidden rows x_dev (n x n_embd f32, device) instead of
+ * the token embeddings; those layers' KV caches are appended as by rcu_backend_forward. Writes
+ * the residual stream after layer layer1 - 1 to x_out_dev (n x n_embd, may be NULL) and, when
+ * logits_dev is not NULL (layer1 must be n_layer), every row's logits (n x n_vocab).
+ * Asynchronous on the context stream. For pipeline stages and layer-by-layer parity checks. */
+RCU_API int32_t rcu_backend_forward_layers(rcu_backend *b, const float *x_dev, uint64_t n, uint64_t pos,
+                                           uint64_t layer0, uint64_t layer1, float *x_out_dev, float *logits_dev);
 /* Backend::hidden (model/mod.rs:318): final normed rows of the last forward (rows x n_embd). */
 RCU_API int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out);
 /* The KV cache of one layer (owned by the backend), e.g. to fill it with rcu_kv_import. */

@@ -82,6 +82,8 @@ def _declare(L):
         "orc_backend_create": (P, [P, U64, U64, I, I, I]), "orc_backend_free": (None, [P]),
         "orc_backend_forward": (I, [P, P, U64, U64, I, P]), "orc_backend_error": (C.c_char_p, [P]),
         "orc_backend_hidden": (I, [P, P, U64]),
+        "orc_backend_set_capture": (None, [P, I]), "orc_backend_layer_x": (C.c_int64, [P, P, U64]),
+        "orc_backend_set_teacher": (None, [P, P, U64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -424,6 +426,27 @@ class OracleBackend:
         if st != 0:
             raise RuntimeError(lib().orc_backend_error(self.ptr).decode())
         return out
+
+    def set_capture(self, on: bool) -> None:
+        """Record the residual stream at every layer's entry (and after the last layer)."""
+        lib().orc_backend_set_capture(self.ptr, int(bool(on)))
+
+    def set_teacher(self, x) -> None:
+        """Teacher forcing: replace the residual rows at every layer's entry and before the head by
+        x ([n_layer + 1, n, n_embd]) in the following forwards (None: off)."""
+        if x is None:
+            lib().orc_backend_set_teacher(self.ptr, None, 0)
+        else:
+            self._teacher = np.ascontiguousarray(x, dtype=np.float32)
+            lib().orc_backend_set_teacher(self.ptr, _p(self._teacher), self._teacher.size)
+
+    def layer_x(self) -> np.ndarray:
+        """[n_layer + 1, n, n_embd] residual rows of the latest forward (capture on)."""
+        cnt = int(lib().orc_backend_layer_x(self.ptr, None, 0))
+        out = np.zeros(cnt, dtype=np.float32)
+        assert lib().orc_backend_layer_x(self.ptr, _p(out), cnt) == cnt
+        L, e = self.model.cfg.n_layer, self.model.cfg.n_embd
+        return out.reshape(L + 1, -1, e)
 
     def __del__(self):
         try:

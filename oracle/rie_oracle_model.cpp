@@ -67,6 +67,13 @@ struct Backend {
     std::vector<std::vector<uint8_t>> kc, vc;
     std::vector<size_t> slots;
     std::vector<float> hidden;
+    // when capture is set: the residual stream at the entry of layer 0 and after every layer
+    // ([n_layer + 1][n][n_embd] of the latest forward), for layer-by-layer parity checks
+    bool capture = false;
+    std::vector<float> layer_x;
+    // teacher forcing: when set ([n_layer + 1][n][n_embd]), the residual stream is replaced by
+    // these rows at the entry of every layer and before the head
+    std::vector<float> teacher;
     std::string err;
 };
 
@@ -147,7 +154,11 @@ int forward(Backend &b, const uint32_t *tokens, size_t n, size_t pos0, bool all_
             orc_rope_table(c.rope_dim, c.rope_base_swa, 1.0f, pos0 + t, coss.data() + t * half, sins.data() + t * half);
     }
     std::vector<float> q(n * qd), k(n * kvd), v(n * kvd), att(n * qd), o(n * e);
+    if (b.capture) b.layer_x.clear();
+    const bool teach = b.teacher.size() == (c.n_layer + 1) * n * e;
     for (size_t il = 0; il < c.n_layer; il++) {
+        if (teach) std::copy(b.teacher.begin() + il * n * e, b.teacher.begin() + (il + 1) * n * e, x.begin());
+        if (b.capture && il == 0) b.layer_x.insert(b.layer_x.end(), x.begin(), x.end());
         const std::string p = "blk." + std::to_string(il) + ".";
         const bool swa = is_swa(c, il);
         const std::vector<float> attn_norm = m.vec(p + "attn_norm.weight");
@@ -269,7 +280,9 @@ int forward(Backend &b, const uint32_t *tokens, size_t n, size_t pos0, bool all_
         if (!pfn.empty())
             for (size_t t = 0; t < n; t++) rmsnorm_inplace(o.data() + t * e, pfn.data(), e, c.rms_eps, b.path);
         for (size_t i = 0; i < n * e; i++) x[i] += c.residual_scale == 1.0f ? o[i] : o[i] * c.residual_scale;
+        if (b.capture) b.layer_x.insert(b.layer_x.end(), x.begin(), x.end());
     }
+    if (teach) std::copy(b.teacher.begin() + c.n_layer * n * e, b.teacher.end(), x.begin());
     const size_t first = all_logits ? 0 : n - 1, mrows = n - first, nv = c.n_vocab;
     const std::vector<float> on = m.vec("output_norm.weight");
     for (size_t t = 0; t < mrows; t++) orc_rmsnorm(xn.data() + t * e, x.data() + (first + t) * e, on.data(), e, c.rms_eps, b.path);
@@ -335,6 +348,21 @@ int orc_backend_forward(void *bp, const uint32_t *tokens, uint64_t n, uint64_t p
     return forward(*(Backend *)bp, tokens, n, pos, all_logits != 0, logits);
 }
 const char *orc_backend_error(void *bp) { return ((Backend *)bp)->err.c_str(); }
+void orc_backend_set_capture(void *bp, int on) { ((Backend *)bp)->capture = on != 0; }
+// Teacher rows for the next forwards ([n_layer + 1][n][n_embd]); count 0 turns it off.
+void orc_backend_set_teacher(void *bp, const float *x, uint64_t count) {
+    Backend *b = (Backend *)bp;
+    if (!x || count == 0) b->teacher.clear();
+    else b->teacher.assign(x, x + count);
+}
+// Residual rows captured by the latest forward: [n_layer + 1][n][n_embd]; returns the count.
+int64_t orc_backend_layer_x(void *bp, float *out, uint64_t cap) {
+    Backend *b = (Backend *)bp;
+    if (!out) return (int64_t)b->layer_x.size();
+    if (cap < b->layer_x.size()) return -1;
+    std::copy(b->layer_x.begin(), b->layer_x.end(), out);
+    return (int64_t)b->layer_x.size();
+}
 int orc_backend_hidden(void *bp, float *out, uint64_t cap) {
     Backend *b = (Backend *)bp;
     if (cap < b->hidden.size()) return -1;

@@ -28,7 +28,8 @@ from . import _lib
 from ._lib import RcuError, RcuJob
 
 __all__ = ["GgmlType", "ActFormat", "KvType", "Rounding", "PrefillGemm", "Context", "Weight", "QuantActs", "MatmulJob",
-           "matmul", "matmul_multi", "matmul_f32_static", "formats_for", "block_sums", "LayerCache", "attention", "turbo", "RcuError"]
+           "matmul", "matmul_multi", "matmul_f32_static", "formats_for", "block_sums", "quantize_weight", "LayerCache",
+           "attention", "turbo", "RcuError"]
 
 
 class GgmlType(enum.IntEnum):  # quant/mod.rs:15-68 (GGUF ids)
@@ -295,6 +296,14 @@ def matmul_f32_static(ctx: Context, w: Weight, x, n_tok: int, out, ld: int | Non
     scratch and must not run concurrently."""
     _check(ctx.ptr, ctx._lib.rcu_matmul_f32_static(ctx.ptr, w.ptr, C.c_void_p(_dptr(x)), n_tok,
                                                    C.c_void_p(_dptr(out)), w.rows if ld is None else ld))
+
+
+def quantize_weight(ctx: Context, ty: GgmlType, rows: int, cols: int, x, out, ld: int | None = None) -> None:
+    """f32 weights (rows x cols, row stride ld, device) -> GGUF blocks of `ty` in `out` (device,
+    rows x row_bytes(cols) bytes). Q8_0 / Q4_0 follow the reference's quantizers
+    (quant/mod.rs:262-307); the other block types use this library's own rules."""
+    _check(ctx.ptr, ctx._lib.rcu_quantize_weight(ctx.ptr, int(ty), rows, cols, C.c_void_p(_dptr(x)),
+                                                 cols if ld is None else ld, C.c_void_p(_dptr(out))))
 
 
 def block_sums(ctx: Context, acts: QuantActs, w: Weight, row: int, tok: int, out) -> None:

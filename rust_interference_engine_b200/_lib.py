@@ -52,12 +52,15 @@ SIGNATURES = {
     "rcu_model_create": (I32, [P, P, C.POINTER(P)]),
     "rcu_model_free": (None, [P]),
     "rcu_model_set_tensor": (I32, [P, C.c_char_p, U32, U64, U64, P]),
+    "rcu_model_set_tensor_device": (I32, [P, C.c_char_p, U32, U64, U64, P]),
+    "rcu_quantize_weight": (I32, [P, U32, U64, U64, P, U64, P]),
     "rcu_backend_create": (I32, [P, U64, U64, I32, C.POINTER(P)]),
     "rcu_backend_free": (None, [P]),
     "rcu_backend_max_batch": (U64, [P]),
     "rcu_backend_n_ctx": (U64, [P]),
     "rcu_backend_forward": (I32, [P, P, U64, U64, I32, P, U64]),
     "rcu_backend_forward_device": (I32, [P, P, U64, U64, I32, P]),
+    "rcu_backend_forward_layers": (I32, [P, P, U64, U64, U64, U64, P, P]),
     "rcu_backend_hidden": (I32, [P, P, U64, C.POINTER(U64)]),
     "rcu_matmul_f32_static": (I32, [P, P, P, U64, P, U64]),
     "rcu_backend_kv": (I32, [P, U64, C.POINTER(P)]),

@@ -850,7 +850,12 @@ static int moe_ffn(rcu_backend *b, const LayerW &L, uint64_t n, const float *o_a
     return RCU_OK;
 }
 
-static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
+// Layers [l0, l1) of n tokens: from token embeddings (x_in == nullptr) or from hidden rows
+// x_in (n x n_embd, device). x_out: the residual stream after layer l1 - 1 (the pending
+// residual added first). logits: the head over the last row (or all rows), only with l1 ==
+// n_layer.
+static int forward_span(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid,
+                        const float *x_in, uint32_t l0, uint32_t l1, float *x_out) {
     rcu_ctx *ctx = b->ctx;
     const rcu_model_config &c = b->cfg;
     const int P = b->m->tp_world;
@@ -862,8 +867,12 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         return r == ncclSuccess ? RCU_OK : nccl_err(ctx, r, "ncclAllReduce");
     };
     const uint32_t e = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd;
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type, b->embd->data,
-                               b->embd->row_bytes, e, c.embd_scale, b->x));
+    if (x_in) {
+        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->x, x_in, n * e * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    } else {
+        RCU_CUDA_TRY(ctx, launch_k(ctx, (k_embed), dim3((uint32_t)n), dim3(128), 0, b->tokens, b->embd->type,
+                                   b->embd->data, b->embd->row_bytes, e, c.embd_scale, b->x));
+    }
     // [residual +] RMSNorm + quantize (its own kernel), then the matmuls that consume it.
     // x_ready: x was written three or more launches back (the norm kernel may load it early).
     auto norm_matmul = [&](uint64_t rows, uint64_t row0, const float *o, const float *post, const float *w,
@@ -908,11 +917,11 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
     ArSum pend_ar{};                                       // (or the ranks' partial rows)
     uint32_t ar_j = 0;
     int st;
-    for (uint32_t il = 0; il < c.n_layer; il++) {
+    for (uint32_t il = l0; il < l1; il++) {
         const LayerW &L = b->layers[il];
-        // x comes from k_embed (the launch just before) in layer 0, else from this layer's
-        // previous norm (four launches back)
-        if ((st = norm_matmul(n, 0, pend_o, pend_post, L.attn_norm, nullptr, il > 0, pend_ar,
+        // x comes from k_embed (or the copy of x_in: the launch just before) in the first layer,
+        // else from this layer's previous norm (four launches back)
+        if ((st = norm_matmul(n, 0, pend_o, pend_post, L.attn_norm, nullptr, il > l0, pend_ar,
                               {{L.wq, b->q, qd}, {L.wk, b->k, kvd}, {L.wv, b->v, kvd}})))
             return st;
         const bool swa_rope = L.swa && c.rope_base_swa > 0.0f;
@@ -952,6 +961,15 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
         pend_o = fused ? nullptr : b->o;
         pend_post = L.post_ffn;
     }
+    if (x_out) {  // add the pending residual (no quantization), then copy the rows out
+        if (pend_o || pend_ar.P)
+            if ((st = norm_q(b, n, b->x, pend_o, pend_post, b->out_norm, nullptr, 0, l1 > l0, pend_ar))) return st;
+        pend_o = nullptr;
+        pend_post = nullptr;
+        pend_ar = ArSum{};
+        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(x_out, b->x, n * e * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    if (!logits) return RCU_OK;
     const uint64_t first = all_logits ? 0 : n - 1, m = n - first;
     b->hidden_rows = m;
     // vocab-parallel head: each rank computes its rows of the vocabulary, then all-gather
@@ -974,6 +992,10 @@ static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logit
     }
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
+}
+
+static int forward_dev(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logits, float *logits, bool fixed_grid) {
+    return forward_span(b, n, pos0, all_logits, logits, fixed_grid, nullptr, 0, b->cfg.n_layer, nullptr);
 }
 
 static bool ends_with(const std::string &s, const char *suf) {
@@ -1204,6 +1226,75 @@ void rcu_model_free(rcu_model *m) {
     cudaSetDevice(m->ctx->device);
     for (auto &kv : m->vec) cudaFree(kv.second);
     delete m;
+}
+
+// rcu_model_set_tensor from device bytes: this rank's shard is cut with device-to-device copies
+// (whole row ranges, or each row's run of blocks for the row-parallel matrices); 1-D vectors
+// and float matrices take the host path.
+int32_t rcu_model_set_tensor_device(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                                    const void *dev_bytes) {
+    if (!m || !name || !dev_bytes) return RCU_ERR_INVALID;
+    rcu_ctx *ctx = m->ctx;
+    const std::string n(name);
+    if (rows == 1 || ggml_type == T_F32 || ggml_type == T_F16 || ggml_type == T_BF16) {
+        const uint64_t bytes = ggml_type == T_F32 ? 4 * rows * cols
+                               : (ggml_type == T_F16 || ggml_type == T_BF16) ? 2 * rows * cols
+                                                                             : rows * rcu_row_bytes(ggml_type, cols);
+        std::vector<uint8_t> h(bytes);
+        RCU_CUDA_TRY(ctx, cudaMemcpy(h.data(), dev_bytes, bytes, cudaMemcpyDeviceToHost));
+        return rcu_model_set_tensor(m, name, ggml_type, rows, cols, h.data());
+    }
+    const uint64_t rb = rcu_row_bytes(ggml_type, cols);
+    if (rb == 0) return set_err(ctx, RCU_ERR_INVALID, "tensor " + n + ": bad row length");
+    uint64_t r2 = rows, c2 = cols;
+    const int kind = m->tp_world > 1 ? tp_kind(n, m->cfg, rows) : TP_REPL;
+    if (kind != TP_REPL)
+        if (int st = tp_shard(ctx, m->cfg, n, ggml_type, rows, cols, nullptr, m->tp_rank, m->tp_world, nullptr, &r2, &c2))
+            return st;
+    const uint64_t srb = rcu_row_bytes(ggml_type, c2);
+    uint8_t *d = nullptr;
+    RCU_CUDA_TRY(ctx, cudaMalloc(&d, r2 * srb + 256));
+    RCU_CUDA_TRY(ctx, cudaMemset(d + r2 * srb, 0, 256));
+    const uint8_t *src = (const uint8_t *)dev_bytes;
+    auto rows_at = [&](uint64_t r0, uint64_t nr, uint64_t at) -> cudaError_t {
+        return cudaMemcpy(d + at * srb, src + r0 * rb, nr * rb, cudaMemcpyDeviceToDevice);
+    };
+    cudaError_t e = cudaSuccess;
+    const int P = m->tp_world, rank = m->tp_rank;
+    const rcu_model_config &c = m->cfg;
+    switch (kind) {
+        case TP_REPL: e = rows_at(0, rows, 0); break;
+        case TP_ROWS:
+        case TP_EXPERTS: e = rows_at((uint64_t)rank * r2, r2, 0); break;
+        case TP_QKV: {
+            const uint64_t qd = (uint64_t)c.n_head * c.head_dim, kvd = (uint64_t)c.n_head_kv * c.head_dim;
+            const uint64_t nq = qd / P, nk = kvd / P;
+            e = rows_at(rank * nq, nq, 0);
+            if (e == cudaSuccess) e = rows_at(qd + rank * nk, nk, nq);
+            if (e == cudaSuccess) e = rows_at(qd + kvd + rank * nk, nk, nq + nk);
+            break;
+        }
+        case TP_UPGATE: {
+            const uint64_t nf = c.n_ff / P;
+            e = rows_at(rank * nf, nf, 0);
+            if (e == cudaSuccess) e = rows_at(c.n_ff + rank * nf, nf, nf);
+            break;
+        }
+        default:  // TP_COLS: each row keeps its rank's run of blocks
+            e = cudaMemcpy2D(d, srb, src + rank * srb, rb, srb, rows, cudaMemcpyDeviceToDevice);
+            break;
+    }
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_err(ctx, e, "set_tensor_device copy");
+    }
+    rcu_weight *w = new rcu_weight();
+    w->ctx = ctx, w->type = (int)ggml_type, w->rows = r2, w->cols = c2, w->row_bytes = srb, w->data = d;
+    w->owned = true, w->padded = true;
+    auto it = m->w.find(n);
+    if (it != m->w.end()) rcu_weight_free(it->second);
+    m->w[n] = w;
+    return RCU_OK;
 }
 
 int32_t rcu_model_set_tensor(rcu_model *m, const char *name, uint32_t ggml_type, uint64_t rows, uint64_t cols,
@@ -1629,6 +1720,38 @@ int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, u
     if (decode && logits_dev != b->logits)
         RCU_CUDA_TRY(b->ctx, cudaMemcpyAsync(logits_dev, b->logits, b->m->cfg.n_vocab * 4, cudaMemcpyDeviceToDevice,
                                              b->ctx->stream));
+    return RCU_OK;
+}
+
+int32_t rcu_backend_forward_layers(rcu_backend *b, const float *x_dev, uint64_t n, uint64_t pos, uint64_t layer0,
+                                   uint64_t layer1, float *x_out_dev, float *logits_dev) {
+    if (!b || !x_dev) return b ? set_err(b->ctx, RCU_ERR_INVALID, "null argument") : RCU_ERR_INVALID;
+    if (int32_t st = check_forward(b, n, pos)) return st;
+    if (layer0 > layer1 || layer1 > b->cfg.n_layer) return set_err(b->ctx, RCU_ERR_INVALID, "layer range out of bounds");
+    if (logits_dev && layer1 != b->cfg.n_layer) return set_err(b->ctx, RCU_ERR_INVALID, "logits need the last layer");
+    if (!x_out_dev && !logits_dev) return set_err(b->ctx, RCU_ERR_INVALID, "nothing to write");
+    rcu_ctx *ctx = b->ctx;
+    cudaStream_t caller = ctx->stream;
+    RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_in, caller));
+    RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(b->stream, b->ev_in, 0));
+    ctx->stream = b->stream;
+    ctx->early_weights = true;
+    struct Restore {
+        rcu_ctx *c;
+        cudaStream_t s;
+        ~Restore() {
+            c->stream = s;
+            c->early_weights = c->static_weights;
+        }
+    } restore{ctx, caller};
+    const bool fused_ar = b->m->tp_world > 1 && b->ar_ok && n <= 8;  // must match forward_span's choice
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_set_pos), dim3(1), dim3(1), 0, b->pos_dev, pos,
+                               fused_ar ? b->ar_epoch : (uint64_t *)nullptr));
+    if (int32_t st = forward_span(b, n, pos, true, logits_dev, false, x_dev, (uint32_t)layer0, (uint32_t)layer1,
+                                  x_out_dev))
+        return st;
+    RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_out, b->stream));
+    RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(caller, b->ev_out, 0));
     return RCU_OK;
 }
 

@@ -222,6 +222,11 @@ class Model:
         _check(self.ctx.ptr, _lib.load().rcu_model_set_tensor(self.ptr, name.encode(), int(ty), rows, cols,
                                                               a.ctypes.data_as(C.c_void_p)))
 
+    def set_tensor_device(self, name: str, ty: int, rows: int, cols: int, dev) -> None:
+        """set_tensor from GGUF bytes already in device memory (a CUDA tensor or pointer)."""
+        _check(self.ctx.ptr, _lib.load().rcu_model_set_tensor_device(self.ptr, name.encode(), int(ty), rows, cols,
+                                                                     C.c_void_p(_dptr(dev))))
+
     def free(self):
         if getattr(self, "ptr", None):
             _lib.load().rcu_model_free(self.ptr)
@@ -269,6 +274,21 @@ class CudaBackend:
     def forward_device(self, tokens_dev, n: int, pos: int, logits_dev, all_logits: bool = False) -> None:
         _check(self.ctx.ptr, _lib.load().rcu_backend_forward_device(self.ptr, C.c_void_p(_dptr(tokens_dev)), n, pos,
                                                                     int(all_logits), C.c_void_p(_dptr(logits_dev))))
+
+    def forward_layers(self, x, pos: int, layer0: int, layer1: int, logits: bool = False):
+        """Layers [layer0, layer1) from hidden rows x (n x n_embd f32, numpy or CUDA tensor) at
+        positions pos..pos+n-1: the residual rows after layer1 - 1 and, with logits (layer1 =
+        n_layer), every row's logits, as numpy arrays."""
+        import torch
+        xd = torch.as_tensor(np.ascontiguousarray(x, dtype=np.float32)).cuda() if isinstance(x, np.ndarray) else x
+        n = xd.shape[0]
+        xo = torch.empty_like(xd)
+        lg = torch.empty((n, self.n_vocab), device=xd.device) if logits else None
+        _check(self.ctx.ptr, _lib.load().rcu_backend_forward_layers(
+            self.ptr, C.c_void_p(_dptr(xd)), n, pos, layer0, layer1, C.c_void_p(_dptr(xo)),
+            C.c_void_p(_dptr(lg)) if logits else None))
+        self.ctx.sync()
+        return xo.cpu().numpy(), (lg.cpu().numpy() if logits else None)
 
     def kv_cache(self, layer: int):
         """The rcu_kv handle of one layer's cache (owned by the backend)."""

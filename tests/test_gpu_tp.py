@@ -37,7 +37,7 @@ def _tensors(spec):
 PROMPT = [5, 17, 200, 3, 99, 42]
 
 
-def _rank(rank, world, q_uid, q_out, kv_type, fused, arch, wtype):
+def _rank(rank, world, q_uid, q_out, kv_type, fused, arch, wtype, device_load=False):
     import os
     os.environ["RIE_TP_FUSED"] = "1" if fused else "0"
     import torch
@@ -54,7 +54,11 @@ def _rank(rank, world, q_uid, q_out, kv_type, fused, arch, wtype):
         uid = q_uid.get(timeout=120)
     m = M.Model(ctx, spec.config(), rank, world)
     for name, t, rows, cols, data in _tensors(spec):
-        m.set_tensor(name, int(t), rows, cols, data)
+        if device_load and rows > 1:  # full tensor in device memory; the library cuts the shard
+            dev = torch.from_numpy(np.ascontiguousarray(data).view(np.uint8).reshape(-1).copy()).cuda()
+            m.set_tensor_device(name, int(t), rows, cols, dev)
+        else:
+            m.set_tensor(name, int(t), rows, cols, data)
     be = M.CudaBackend(m, 64, 16, rie.KvType(kv_type), comm_id=uid)
     out = [be.forward(np.array(PROMPT, np.uint32), 0, True)]
     pos = len(PROMPT)
@@ -66,22 +70,26 @@ def _rank(rank, world, q_uid, q_out, kv_type, fused, arch, wtype):
     m.free()
 
 
-@pytest.mark.parametrize("kv_type,fused,arch,wtype", [(0, False, "qwen3", GgmlType.Q4_K),
-                                                     (2, False, "qwen3", GgmlType.Q4_K),
-                                                     (0, True, "qwen3", GgmlType.Q4_K),
-                                                     (0, False, "qwen3moe", GgmlType.Q4_K),
-                                                     (0, False, "qwen2moe", GgmlType.Q8_0)],
-                         ids=["f16", "turbo4", "fused", "moe_ep", "moe_ep_shared"])
-def test_tp2_forward_matches_oracle(kv_type, fused, arch, wtype):
+@pytest.mark.parametrize("kv_type,fused,arch,wtype,device_load", [(0, False, "qwen3", GgmlType.Q4_K, False),
+                                                                 (2, False, "qwen3", GgmlType.Q4_K, False),
+                                                                 (0, True, "qwen3", GgmlType.Q4_K, False),
+                                                                 (0, False, "qwen3moe", GgmlType.Q4_K, False),
+                                                                 (0, False, "qwen2moe", GgmlType.Q8_0, False),
+                                                                 (0, False, "qwen3", GgmlType.Q4_K, True),
+                                                                 (0, False, "qwen3moe", GgmlType.Q4_K, True)],
+                         ids=["f16", "turbo4", "fused", "moe_ep", "moe_ep_shared", "device_load", "moe_device_load"])
+def test_tp2_forward_matches_oracle(kv_type, fused, arch, wtype, device_load):
     """fused: the all-reduce pushed over NVLink by the GEMVs instead of NCCL; moe: experts
-    split across the two ranks (expert parallelism), the shared expert on rank 0."""
+    split across the two ranks (expert parallelism), the shared expert on rank 0; device_load:
+    every matrix handed over in device memory (rcu_model_set_tensor_device cuts the shards)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q_uid, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, q_uid, q_out, kv_type, fused, arch, wtype)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, q_uid, q_out, kv_type, fused, arch, wtype, device_load))
+             for r in range(2)]
     for p in procs:
         p.start()
     try:

@@ -149,3 +149,19 @@ def test_config5_shape_turbo_attention(env):
     # benchmark configuration 5 geometry (64 q / 8 kv heads x 128) at a shortened context
     got, want = _attn_case(env, O.KV_TURBO4, 64, 8, 128, 4096, 1, 4095, seed=9)
     close(got, want, 2e-3)
+
+
+@pytest.mark.parametrize("pos0,n_tok", [(32767, 1), (20000, 1), (32766, 2)], ids=["last", "mid", "two_tokens"])
+def test_config5_turbo_attention_full_context(env, pos0, n_tok):
+    """Benchmark configuration 5 as measured: 64 query / 8 KV heads x 128, turbo4 cache of 32768
+    positions (the decode kernel splits it over two clusters per KV head and merges them through
+    global memory), within the 2e-3 of the turbo4 attention tests."""
+    got, want = _attn_case(env, O.KV_TURBO4, 64, 8, 128, 32768, n_tok, pos0, seed=10)
+    close(got, want, 2e-3)
+
+
+@pytest.mark.parametrize("kv_type,tol", [(O.KV_F16, 1e-3), (O.KV_Q8_0, 1e-3)], ids=["f16", "q8_0"])
+def test_config3_shape_attention_long_context(env, kv_type, tol):
+    """Configuration 3 heads (32 query / 8 KV x 128) over 8192 positions."""
+    got, want = _attn_case(env, kv_type, 32, 8, 128, 8192, 1, 8191, seed=12)
+    close(got, want, tol)

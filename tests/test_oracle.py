@@ -328,3 +328,30 @@ def test_rope_preserves_norm_and_matches_complex_rotation():
     x = O.rope_apply(x0, False, c, s)
     assert abs(float(np.dot(x0, x0)) - float(np.dot(x, x))) < 1e-4
     assert abs(x[0] - (x0[0] * math.cos(5.0) - x0[1] * math.sin(5.0))) < 1e-5
+
+
+def test_teacher_forcing_reproduces_the_trajectory():
+    """Teacher forcing with the oracle's own residual rows leaves its forward unchanged (the
+    layer-by-layer GPU checks rely on this)."""
+    from rust_interference_engine_b200 import GgmlType
+    from rust_interference_engine_b200 import model as M
+    spec = M.SyntheticSpec.tiny("qwen3", GgmlType.Q4_K)
+    rng = O.Rng(5)
+    cfg = spec.config()
+    om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(cfg)))
+    for name, t, rows, cols, data in M.synthetic_tensors(spec, lambda t, r, c: rng.weight(int(t), r, c),
+                                                         lambda n, s: rng.vec(n, s),
+                                                         lambda n: (1.0 + 0.1 * rng.vec(n, 1.0)).astype(np.float32)):
+        om.set_tensor(name, int(t), rows, cols, data)
+    a = O.OracleBackend(om, 16, 8, n_threads=2)
+    b = O.OracleBackend(om, 16, 8, n_threads=2)
+    a.set_capture(True)
+    b.set_capture(True)
+    toks = np.array([3, 9, 27], np.uint32)
+    la = a.forward(toks, 0, all_logits=True)
+    X = a.layer_x()
+    assert X.shape == (spec.n_layer + 1, 3, spec.n_embd)
+    b.set_teacher(X)
+    lb = b.forward(toks, 0, all_logits=True)
+    np.testing.assert_array_equal(la, lb)
+    np.testing.assert_array_equal(X, b.layer_x())
