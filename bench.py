@@ -348,6 +348,18 @@ def measured_int8_peak(torch):
         return 4500.0, f"nominal 4.5 POPS dense int8 ({type(e).__name__})"
 
 
+def prefill_meta(gemm: str):
+    """The prefill line names the arithmetic it measures: f16 tensor-core MMA on dequantized
+    operands (default) or int8 MMA with the reference's exact block sums (--gemm i8)."""
+    if gemm == "i8":
+        return {"metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096, exact int8 block sums)",
+                "unit": "TOPS", "dtype": "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, f32 block-scale epilogue)",
+                "workload": "prefill_q4_0_m512_k4096_config2_i8"}
+    return {"metric": "prefill Q4_0 GEMM f16 TFLOP/s (config 2, M=512 K=4096 N=14336+4096, f16 MMA on dequantized operands)",
+            "unit": "TFLOP/s", "dtype": "f16 MMA on dequantized Q4_0 weights x Q8_0 activations (d*q), f32 accumulate",
+            "workload": "prefill_q4_0_m512_k4096_config2_f16"}
+
+
 def run_prefill(args, world, rank, local):
     import torch
 
@@ -422,24 +434,25 @@ def run_prefill(args, world, rank, local):
         kernel = "k_acts_f16 + k_gemm_f16<Q4_0> (tcgen05 kind::f16, both weights in one launch)"
         dtype = "f16 MMA on dequantized Q4_0 weights x Q8_0 activations (d*q), f32 accumulate"
         launches = 3
+    pm = prefill_meta(args.gemm)
     return {
-        "metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)",
+        "metric": pm["metric"],
         "value": world * flops / (ms * 1e-3) / 1e12,
-        "unit": "TOPS",
+        "unit": pm["unit"],
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
         "dtype": dtype,
-        "config": {"workload": "prefill_q4_0_m512_k4096_config2", "m": PF_M, "k": PF_K, "n": list(PF_N),
+        "config": {"workload": pm["workload"], "m": PF_M, "k": PF_K, "n": list(PF_N),
                    "ops_per_step": flops, "l2": "weights 42 MB + activations (L2-resident re-use by design)",
                    "parallelism": f"replicas x{world}", "gemm": args.gemm,
                    "int8_peak_tops": i8_peak, "frac_of_int8_peak": achieved / i8_peak},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": pm["unit"], "frac": achieved / peak,
                      "peak_source": peak_kind,
                      "traffic": profile_traffic("gemm_q4_0_config2" if i8 else "gemm_f16_q4_0_config2"),
                      "kernel": kernel, "launch_ms": kern_ms,
                      "note": "achieved = 2*M*K*N over the matmul_multi call (activation f16 prep + GEMM)"},
-        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": pm["unit"],
                 "h2d_bytes_per_step": PF_M * PF_K * 4, "d2h_bytes_per_step": sum(PF_M * n * 4 for n in PF_N),
                 "ms_per_step": e2e_ms},
         "gpu_launches": launches * args.steps,
@@ -499,6 +512,49 @@ class RandomBlocks:
         return (1.0 + 0.1 * (self.rng.random(n, dtype=np.float32) * 2 - 1)).astype(np.float32)
 
 
+class DeviceWeights:
+    """Benchmark weights as the configurations state them: N(0, 0.02) values drawn on the device
+    (torch generator with a fixed seed, so every rank draws the same full tensors) and quantized
+    there by the library (rcu_quantize_weight: Q4_0 / Q8_0 by the reference's rules, Q4_K / Q6_K
+    by the library's own). Norm and bias vectors come from the host generator."""
+
+    def __init__(self, ctx, seed):
+        import torch
+        self.ctx = ctx
+        self.gen = torch.Generator(device="cuda").manual_seed(seed)
+        self.host = RandomBlocks(seed)
+
+    def weight(self, t, rows, cols):
+        import torch
+
+        import rust_interference_engine_b200 as rie
+        ty = rie.GgmlType(int(t))
+        rb = ty.row_bytes(cols)
+        out = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+        chunk = max(1, (1 << 28) // cols)  # rows per 1 GiB f32 draft
+        for r0 in range(0, rows, chunk):
+            n = min(chunk, rows - r0)
+            x = torch.empty(n, cols, device="cuda").normal_(0.0, 0.02, generator=self.gen)
+            rie.quantize_weight(self.ctx, ty, n, cols, x, out[r0 * rb:])
+        return out
+
+    def vec(self, n, scale):
+        return self.host.vec(n, scale)
+
+    def norm(self, n):
+        return self.host.norm(n)
+
+
+def set_synthetic(model, spec, gen):
+    """Loads every tensor of a synthetic model (device bytes go in without a host copy)."""
+    for name, t, rows, cols, data in __import__("rust_interference_engine_b200.model", fromlist=["x"]).synthetic_tensors(
+            spec, gen.weight, gen.vec, gen.norm):
+        if hasattr(data, "is_cuda"):
+            model.set_tensor_device(name, int(t), rows, cols, data)
+        else:
+            model.set_tensor(name, int(t), rows, cols, data)
+
+
 def weight_bytes_per_token(spec):
     from rust_interference_engine_b200 import GgmlType as G
     e, ff, qd, kvd = spec.n_embd, spec.n_ff, spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim
@@ -518,12 +574,12 @@ def run_decode(args, world, rank, local):
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
     spec = qwen3_8b_spec()
-    gen = RandomBlocks(3)  # same seed on every rank: every rank sees the same full tensors
+    gen = DeviceWeights(ctx, 3)  # same seed on every rank: every rank sees the same full tensors
     # N > 1: one model split tensor-parallel over the N GPUs (each rank keeps its shard)
     model = M.Model(ctx, spec.config(), rank, world)
     t_build = time.perf_counter()
-    for name, t, rows, cols, data in M.synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
-        model.set_tensor(name, int(t), rows, cols, data)
+    set_synthetic(model, spec, gen)
+    torch.cuda.synchronize()
     t_build = time.perf_counter() - t_build
     n_gen = max(args.warmup, 3) + args.steps
     n_ctx = DEC_PROMPT + n_gen + 1
@@ -585,8 +641,8 @@ def run_decode(args, world, rank, local):
 
     # dominant kernel: the gate+up GEMV launch (2 x 12288 x 4096 Q4_K), timed alone over
     # 8 layers' worth of distinct weights (453 MB > L2)
-    gu = [rie.Weight.upload(ctx, rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd, gen.weight(rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd))
-          for _ in range(16)]
+    gu_bytes = [gen.weight(rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd) for _ in range(16)]
+    gu = [rie.Weight.view(ctx, rie.GgmlType.Q4_K, spec.n_ff, spec.n_embd, b) for b in gu_bytes]
     xg = torch.randn(1, spec.n_embd, device="cuda")
     acts = rie.QuantActs(ctx, 1, spec.n_embd)
     acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
@@ -595,14 +651,28 @@ def run_decode(args, world, rank, local):
     ctx.set_static_weights(True)  # as inside the forward: weights stream while the previous launch ends
     for j in jobs:
         rie.matmul_multi(ctx, acts, j)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 40
-    g0.record(stream)
-    for r in range(reps):
-        rie.matmul_multi(ctx, acts, jobs[r % 8])
-    g1.record(stream)
     torch.cuda.synchronize()
-    gemv_ms = g0.elapsed_time(g1) / reps
+    # 40 launches captured in one CUDA graph (as the decode step runs them: no host launch cost
+    # between kernels), replayed three times; the fastest replay counts
+    reps = 40
+    gs = torch.cuda.Stream()
+    ctx.set_stream(gs)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for r in range(reps):
+            rie.matmul_multi(ctx, acts, jobs[r % 8])
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(4):
+        with torch.cuda.stream(gs):
+            g0.record(gs)
+            graph.replay()
+            g1.record(gs)
+        gs.synchronize()
+        times.append(g0.elapsed_time(g1) / reps)
+    gemv_ms = min(times[1:])
+    del graph
+    ctx.set_stream(stream)
     gemv_bytes = 2 * rie.GgmlType.Q4_K.row_bytes(spec.n_embd) * spec.n_ff
     peak, peak_kind = peaks()
     achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
@@ -631,6 +701,7 @@ def run_decode(args, world, rank, local):
                                                 "k_gemv<1,16>" else "gemv_kq_q4_k_gate_up"),
                      "kernel": gemv_kernel_name("Q4_K", gemv_bytes) + " (gate+up, 2 x 12288 x 4096 Q4_K)",
                      "bytes_per_launch": gemv_bytes,
+                     "timing": "40 launches over 8 layers' distinct weights (453 MB > L2) in one CUDA graph",
                      "launch_ms": gemv_ms,
                      "whole_step_weight_gb_s": (wbytes + kv_bytes) / (ms * 1e-3) / 1e9},
         "e2e": {"value": dist_min(e2e_tps, world), "unit": "tok/s", "h2d_bytes_per_step": 4,
@@ -678,12 +749,12 @@ def run_moe(args, world, rank, local):
     stream = torch.cuda.current_stream()
     ctx = rie.Context(local, stream)
     spec = qwen3_moe_spec()
-    gen = RandomBlocks(4)  # same seed on every rank: every rank sees the same full tensors
+    gen = DeviceWeights(ctx, 4)  # same seed on every rank: every rank sees the same full tensors
     # N > 1: attention tensor-parallel, experts split across the ranks (expert parallelism)
     model = M.Model(ctx, spec.config(), rank, world)
     t_build = time.perf_counter()
-    for name, t, rows, cols, data in M.synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
-        model.set_tensor(name, int(t), rows, cols, data)
+    set_synthetic(model, spec, gen)
+    torch.cuda.synchronize()
     t_build = time.perf_counter() - t_build
     n_gen = max(args.warmup, 3) + args.steps
     be = M.CudaBackend(model, MOE_PROMPT + n_gen + 1, 64, rie.KvType.F16, comm_id=tp_comm_id(world, rank))
@@ -739,8 +810,8 @@ def run_moe(args, world, rank, local):
     be3.free()
     # dominant kernel: the expert gate+up GEMV of one token (16 x 768 x 2048 Q4_K), timed alone
     # over distinct copies (> L2)
-    ws = [rie.Weight.upload(ctx, rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd,
-                            gen.weight(rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd)) for _ in range(16 * 12)]
+    ws_bytes = [gen.weight(rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd) for _ in range(16 * 12)]
+    ws = [rie.Weight.view(ctx, rie.GgmlType.Q4_K, spec.n_ff_exp, spec.n_embd, b) for b in ws_bytes]
     xg = torch.randn(1, spec.n_embd, device="cuda")
     acts = rie.QuantActs(ctx, 1, spec.n_embd)
     acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8K)
@@ -950,19 +1021,23 @@ def cpu_decode_sample(seconds: float, threads: int):
     om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(spec.config())))
     for name, t, rows, cols, data in synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
         om.set_tensor(name, int(t), rows, cols, data)
-    ob = O.OracleBackend(om, 256, 16, kv_type=O.KV_F16, n_threads=threads)
+    # decode at the GPU arm's context (after its 512-token prompt): a 16-token prompt fills the
+    # first cache rows, the rows up to the prompt length stay zero (the same attention work; a
+    # real 512-token CPU prefill would take about a minute)
+    ob = O.OracleBackend(om, DEC_PROMPT + 256, 16, kv_type=O.KV_F16, n_threads=threads)
     ob.forward(np.arange(16, dtype=np.uint32), 0)
-    n, pos, t0 = 0, 16, time.perf_counter()
+    n, pos, t0 = 0, DEC_PROMPT, time.perf_counter()
     tok = np.array([1], dtype=np.uint32)
     while True:
         out = ob.forward(tok, pos)
         tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
         n, pos = n + 1, pos + 1
         el = time.perf_counter() - t0
-        if el >= seconds or pos >= 255:
+        if el >= seconds or pos >= DEC_PROMPT + 255:
             break
     return {"value": n / el, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} decode steps of the 36-layer Qwen3-8B-shape Q4_K_M model at context 16-{pos}, {el:.1f} s",
+            "sample": f"{n} decode steps of the 36-layer Qwen3-8B-shape Q4_K_M model at context {DEC_PROMPT}-{pos} "
+                      f"(random weight blocks; the CPU time does not depend on the values), {el:.1f} s",
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
@@ -986,13 +1061,203 @@ def cpu_prefill_sample(seconds: float, threads: int):
             "path": "avx2" if O.have_avx2() else "scalar"}
 
 
+# ---- workload: config 5 as a whole model: Llama-3.1-70B-shape decode, Q4_0, turbo4 KV ------
+# (BASELINE.json names hidden 8192, 80 layers, 64/8 heads x 128, context 32768, Q4_0 weight
+# GEMVs tensor-parallel over 8 GPUs; FFN 28672 and vocabulary 128256 are the public
+# Llama-3.1-70B values, RoPE base 500000, RMS eps 1e-5)
+LLAMA70B = dict(arch="llama", n_vocab=128256, n_embd=8192, n_layer=80, n_head=64, n_head_kv=8, head_dim=128,
+                n_ff=28672, rope_dim=128, rope_base=500000.0, rms_eps=1e-5)
+L70_CTX = 32768
+
+
+def llama70b_spec(n_layer=None):
+    from rust_interference_engine_b200 import GgmlType as G
+    from rust_interference_engine_b200.model import SyntheticSpec
+    kw = dict(LLAMA70B)
+    if n_layer is not None:
+        kw["n_layer"] = n_layer
+    return SyntheticSpec(wtype=G.Q4_0, embd_type=G.Q4_0, qk_norm=False, **kw)
+
+
+def run_llama70b(args, world, rank, local):
+    """Decode of one sequence through the whole 80-layer model at context 32768: N > 1 splits the
+    model tensor-parallel (column-parallel q/k/v/gate/up, row-parallel o/down with an all-reduce,
+    vocabulary-parallel head with an all-gather); each rank's turbo4 KV cache holds its 8/N KV
+    heads, filled with K, V ~ N(0, 1) for the positions before the timed tokens."""
+    import torch
+
+    import rust_interference_engine_b200 as rie
+    from rust_interference_engine_b200 import _check, _dptr, _lib
+    from rust_interference_engine_b200 import model as M
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    ctx = rie.Context(local, stream)
+    spec = llama70b_spec()
+    gen = DeviceWeights(ctx, 5)  # same seed on every rank: every rank draws the same full tensors
+    model = M.Model(ctx, spec.config(), rank, world)
+    t_build = time.perf_counter()
+    set_synthetic(model, spec, gen)
+    torch.cuda.synchronize()
+    t_build = time.perf_counter() - t_build
+    n_gen = max(args.warmup, 3) + args.steps
+    fill = L70_CTX - n_gen
+    be = M.CudaBackend(model, L70_CTX + n_gen, 8, rie.KvType.Turbo4, comm_id=tp_comm_id(world, rank))
+    kvl, hd = spec.n_head_kv // world, spec.head_dim
+    g = torch.Generator(device="cuda").manual_seed(77 + rank)
+    t_fill = time.perf_counter()
+    lib = _lib.load()
+    for il in range(spec.n_layer):  # K, V ~ N(0, 1) through the library's turbo4 append
+        kv = be.kv_cache(il)
+        for p0 in range(0, fill, 4096):
+            n = min(4096, fill - p0)
+            k = torch.randn(n, kvl * hd, device="cuda", generator=g)
+            v = torch.randn(n, kvl * hd, device="cuda", generator=g)
+            _check(ctx.ptr, lib.rcu_kv_store(ctx.ptr, kv, _dptr(k), _dptr(v), n, p0))
+    torch.cuda.synchronize()
+    t_fill = time.perf_counter() - t_fill
+    toks = torch.from_numpy(np.random.default_rng(6).integers(0, spec.n_vocab, 2 * n_gen).astype(np.int32)).cuda()
+    logits = torch.zeros(spec.n_vocab, device="cuda")
+    pos = fill
+    for i in range(max(args.warmup, 3)):  # the second decode step captures the CUDA graph
+        be.forward_device(toks[i:], 1, pos, logits)
+        pos += 1
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(args.steps):
+            be.forward_device(toks[max(args.warmup, 3) + i:], 1, pos + i, logits)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = dist_max(t0.elapsed_time(t1) / args.steps, world)
+    pos += args.steps
+    finite = bool(torch.isfinite(logits).all())
+    # e2e: the host API, token in and logits out through host memory
+    tok = np.array([1], dtype=np.uint32)
+    for i in range(max(args.warmup, 3)):
+        be.forward(tok, pos)
+        pos += 1
+    barrier(world)
+    e0 = time.perf_counter()
+    n_e2e = max(1, min(args.steps, n_gen - max(args.warmup, 3)))
+    for i in range(n_e2e):
+        out = be.forward(tok, pos)
+        tok = np.array([int(np.argmax(out[0]))], dtype=np.uint32)
+        pos += 1
+    e2e_s = dist_max((time.perf_counter() - e0) / n_e2e, world)
+    # dominant kernel: this rank's gate+up GEMV (2 x 28672 / N x 8192 Q4_0), timed in a CUDA graph
+    ff = spec.n_ff // world
+    gu_bytes = [gen.weight(rie.GgmlType.Q4_0, ff, spec.n_embd) for _ in range(4)]
+    gu = [rie.Weight.view(ctx, rie.GgmlType.Q4_0, ff, spec.n_embd, b) for b in gu_bytes]
+    xg = torch.randn(1, spec.n_embd, device="cuda")
+    acts = rie.QuantActs(ctx, 1, spec.n_embd)
+    acts.prepare(xg, 1, spec.n_embd, rie.ActFormat.Q8_0)
+    og = torch.zeros(2, ff, device="cuda")
+    jobs = [[rie.MatmulJob(gu[2 * i], og[0]), rie.MatmulJob(gu[2 * i + 1], og[1])] for i in range(2)]
+    ctx.set_static_weights(True)
+    for j in jobs:
+        rie.matmul_multi(ctx, acts, j)
+    torch.cuda.synchronize()
+    reps = 20
+    gs = torch.cuda.Stream()
+    ctx.set_stream(gs)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for r in range(reps):
+            rie.matmul_multi(ctx, acts, jobs[r % 2])
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(4):
+        with torch.cuda.stream(gs):
+            ev0.record(gs)
+            graph.replay()
+            ev1.record(gs)
+        gs.synchronize()
+        times.append(ev0.elapsed_time(ev1) / reps)
+    gemv_ms = min(times[1:])
+    del graph
+    ctx.set_stream(stream)
+    be.free()
+    gemv_bytes = 2 * rie.GgmlType.Q4_0.row_bytes(spec.n_embd) * ff
+    peak, peak_kind = peaks()
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    wbytes = weight_bytes_per_token(spec) // world
+    kv_bytes = spec.n_layer * 2 * kvl * (L70_CTX - n_gen // 2) * rie.turbo.row_bytes_4(hd)
+    return {
+        "metric": META["llama70b"]["metric"],
+        "value": 1000.0 / ms,  # one sequence: N > 1 splits the model (tensor parallel), not the work
+        "unit": "tok/s",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "dtype": META["llama70b"]["dtype"],
+        "config": {"workload": META["llama70b"]["workload"], "layers": spec.n_layer, "hidden": spec.n_embd,
+                   "ffn": spec.n_ff, "heads": f"{spec.n_head}/{spec.n_head_kv}x{hd}", "vocab": spec.n_vocab,
+                   "context_at_timing": L70_CTX - n_gen // 2, "kv": "turbo4", "batch": 1,
+                   "weight_bytes_per_token_per_gpu": wbytes, "kv_bytes_per_token_per_gpu": kv_bytes,
+                   "l2": f"inputs larger than L2 ({(wbytes + kv_bytes) / 1e9:.1f} GB streamed per token per GPU)",
+                   "parallelism": f"tp{world} (all-reduce of Wo/down, all-gather of logits)" if world > 1 else "tp1",
+                   "decode": "CUDA graph replay per token", "model_build_s": t_build, "kv_fill_s": t_fill},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": None,
+                     "kernel": gemv_kernel_name("Q4_0", gemv_bytes) + f" (gate+up, 2 x {ff} x 8192 Q4_0, this rank's shard)",
+                     "bytes_per_launch": gemv_bytes, "launch_ms": gemv_ms,
+                     "timing": "20 launches over 2 distinct weight pairs in one CUDA graph",
+                     "whole_step_gb_s_per_gpu": (wbytes + kv_bytes) / (ms * 1e-3) / 1e9},
+        "e2e": {"value": 1.0 / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.n_vocab * 4,
+                "ms_per_step": 1e3 * e2e_s, "api": "CudaBackend.forward (rcu_backend_forward, host tokens/logits, greedy)"},
+        "gpu_launches": args.steps * (9 * spec.n_layer + 4),
+        "clocks": clk.summary(),
+        "check": {"logits_finite": finite},
+    }
+
+
+def cpu_llama70b_sample(seconds: float, threads: int):
+    """The oracle's CPU forward (AVX2 tier, all host threads) at the 70B shape with a turbo4
+    cache of 32768 positions, extrapolated from models of one and two of its layers (the head
+    and embedding in both): tok/s = 1 / (t1 + 79 (t2 - t1)). The cache rows are zero (the
+    same attention work as filled rows)."""
+    import oracle as O
+    from rust_interference_engine_b200.model import synthetic_tensors
+    per = []
+    for nl in (1, 2):
+        spec = llama70b_spec(nl)
+        gen = RandomBlocks(5)
+        om = O.OracleModel(O.ModelConfig.from_buffer_copy(bytes(spec.config())))
+        for name, t, rows, cols, data in synthetic_tensors(spec, gen.weight, gen.vec, gen.norm):
+            om.set_tensor(name, int(t), rows, cols, data)
+        ob = O.OracleBackend(om, L70_CTX + 64, 1, kv_type=O.KV_TURBO4, n_threads=threads)
+        pos, tok = L70_CTX - 64, np.array([1], dtype=np.uint32)
+        ob.forward(tok, pos)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            ob.forward(tok, pos + 1 + n)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds / 2 or n >= 60:
+                break
+        per.append(el / n)
+        del ob, om
+    t_tok = per[0] + 79 * max(per[1] - per[0], 0.0)
+    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"decode steps of 1- and 2-layer models of the 70B shape at context {L70_CTX - 63} "
+                      f"({per[0] * 1e3:.0f} / {per[1] * 1e3:.0f} ms per token), extrapolated to 80 layers",
+            "path": "avx2" if O.have_avx2() else "scalar"}
+
+
 WORKLOADS = {"gemv": (run_gemv, cpu_gemv_sample), "prefill": (run_prefill, cpu_prefill_sample),
              "decode": (run_decode, cpu_decode_sample), "moe": (run_moe, cpu_moe_sample),
-             "turbo": (run_turbo, cpu_turbo_sample)}
+             "turbo": (run_turbo, cpu_turbo_sample), "llama70b": (run_llama70b, cpu_llama70b_sample)}
 META = {  # metric / unit / config of each workload, shared by both arms
     "turbo": {"metric": "turbo4 KV attention HBM GB/s (config 5, Llama-3.1-70B shape, context 32768)", "unit": "GB/s",
               "dtype": "u4 codes x int8 query (rotated domain, byte-shuffle lookup), f32 softmax",
               "workload": "turbo4_attention_70b_ctx32768_config5"},
+    "llama70b": {"metric": "Llama-3.1-70B-shape Q4_0 decode tg tok/s, turbo4 KV at context 32768 (config 5, batch 1)",
+                 "unit": "tok/s", "dtype": "int8 x Q4_0 blocks (Q8_0 activations), turbo4 KV (u4 codes x int8 query), f32 glue",
+                 "workload": "llama31_70b_q4_0_turbo4_decode_config5"},
     "moe": {"metric": "Qwen3-30B-A3B-shape MoE decode tg tok/s (config 4, batch 1)", "unit": "tok/s",
             "dtype": "int8 x Q4_K blocks (Q8_K activations), f32 router / glue, f16 KV",
             "workload": "qwen3_30b_a3b_moe_decode_config4"},
@@ -1001,16 +1266,14 @@ META = {  # metric / unit / config of each workload, shared by both arms
                "workload": "qwen3_8b_q4_k_m_decode_config3"},
     "gemv": {"metric": "quant-matmul HBM GB/s (Q4_0 x Q8_0 GEMV, config 1)", "unit": "GB/s",
              "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 combine)", "workload": "gemv_q4_0_6144x2048_config1"},
-    "prefill": {"metric": "prefill Q4_0 GEMM int8 TOPS (config 2, M=512 K=4096 N=14336+4096)", "unit": "TOPS",
-                "dtype": "int8 (Q4_0 x Q8_0 blocks, f32 block-scale combine)",
-                "workload": "prefill_q4_0_m512_k4096_config2"},
+    "prefill": prefill_meta("f16"),
 }
 
 
 def step_units(workload: str) -> float:
     """Units of a workload's metric in one step (one pass of the hot path over one batch): the
     reference arm reports ms_per_step = these units / its measured rate."""
-    if workload in ("decode", "moe"):
+    if workload in ("decode", "moe", "llama70b"):
         return 1.0  # one token
     if workload == "gemv":
         return gemv_bytes_per_step()[0] / 1e9
@@ -1048,6 +1311,7 @@ def main():
     DEC_PROMPT = args.prompt
     DEC_BATCH = args.batch
     META["gemv"] = gemv_meta()
+    META["prefill"] = prefill_meta(args.gemm)
     world, rank, local = dist_init()
 
     if args.impl == "reference":
