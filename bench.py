@@ -181,12 +181,14 @@ def gemv_bytes_per_step():
     return GEMV_COPIES * (w + GEMV_K * 4 + GEMV_ROWS * 4), w
 
 
-def gemv_kernel_name(wtype: str, launch_bytes: int) -> str:
-    """The batch-1 GEMV kernel the library picks: the tensor-core K-quant kernel for Q4_K /
-    Q5_K / Q6_K launches of at least 8 MiB of weights (default of RIE_GEMV_KQ_MIN_MB), else
-    the lane kernel."""
+def gemv_kernel_name(wtype: str, launch_bytes: int, k: int = 4096) -> str:
+    """The batch-1 GEMV kernel the library picks: the tensor-core kernel for Q4_K / Q5_K / Q6_K /
+    Q4_0 launches of at least 8 MiB of weights (default of RIE_GEMV_KQ_MIN_MB), else the lane
+    kernel."""
     min_mb = int(os.environ.get("RIE_GEMV_KQ_MIN_MB", "8"))
-    if wtype in ("Q4_K", "Q5_K", "Q6_K") and launch_bytes >= (min_mb << 20) and os.environ.get("RIE_GEMV_KQ") != "0":
+    if wtype == "Q4_0" and k < 4096:  # short Q4_0 rows stay on the lane kernel
+        return "k_gemv<1,16>"
+    if wtype in ("Q4_K", "Q5_K", "Q6_K", "Q4_0") and launch_bytes >= (min_mb << 20) and os.environ.get("RIE_GEMV_KQ") != "0":
         return "k_gemv_kq"
     return "k_gemv<1,16>"
 
@@ -292,7 +294,7 @@ def run_gemv(args, world, rank, local):
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic(gm["workload"]),
-                     "kernel": gemv_kernel_name(GEMV_TYPE, step_bytes // (1 if not GEMV_EACH else GEMV_COPIES)),
+                     "kernel": gemv_kernel_name(GEMV_TYPE, step_bytes // (1 if not GEMV_EACH else GEMV_COPIES), GEMV_K),
                      "bytes_per_launch": step_bytes, "launch_ms": kern_ms},
         "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_COPIES * GEMV_ROWS * 4,

@@ -83,6 +83,16 @@ RCU_API const char *rcu_last_error(const rcu_ctx *ctx);
  * device wait expired since the last check (the bits are then cleared). */
 RCU_API int32_t rcu_sync(rcu_ctx *ctx);
 RCU_API int32_t rcu_check_device(rcu_ctx *ctx, uint32_t *bits_out);
+/* Limit of the device-side waits on other ranks (the fused all-reduce), 1..600000 ms; default
+ * 2000 ms or RIE_WAIT_LIMIT_MS at context creation. A wait that runs out sets a device error
+ * bit (RCU_ERR_TIMEOUT from rcu_sync / rcu_check_device) and the kernel finishes. No counterpart
+ * in the reference (no device waits there). */
+RCU_API int32_t rcu_set_wait_limit_ms(rcu_ctx *ctx, uint64_t ms);
+/* Diagnostics (no counterpart in the reference): launches the fused all-reduce norm of one row
+ * against arrival counters that no rank will raise, so its bounded wait runs out after the
+ * context's wait limit; returns what rcu_sync then reports (RCU_ERR_TIMEOUT, error bits 0x10).
+ * The context stays usable. */
+RCU_API int32_t rcu_diag_expire_peer_wait(rcu_ctx *ctx);
 RCU_API int32_t rcu_version(void);
 
 /* ---- weights (tensor.rs:6-98 Weight) -------------------------------------------------- */

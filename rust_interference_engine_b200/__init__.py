@@ -137,6 +137,10 @@ class Context:
         stream them before the previous kernel finishes)."""
         _check(self.ptr, self._lib.rcu_set_static_weights(self.ptr, int(bool(on))))
 
+    def set_wait_limit_ms(self, ms: int) -> None:
+        """Limit of the device-side waits on other ranks (the fused all-reduce)."""
+        _check(self.ptr, self._lib.rcu_set_wait_limit_ms(self.ptr, int(ms)))
+
     def set_prefill_gemm(self, kind: "PrefillGemm") -> None:
         _check(self.ptr, self._lib.rcu_set_prefill_gemm(self.ptr, int(kind)))
 

@@ -27,6 +27,8 @@ SIGNATURES = {
     "rcu_last_error": (C.c_char_p, [P]),
     "rcu_sync": (I32, [P]),
     "rcu_check_device": (I32, [P, C.POINTER(U32)]),
+    "rcu_set_wait_limit_ms": (I32, [P, U64]),
+    "rcu_diag_expire_peer_wait": (I32, [P]),
     "rcu_row_bytes": (U64, [U32, U64]),
     "rcu_weight_upload": (I32, [P, U32, U64, U64, P, C.POINTER(P)]),
     "rcu_weight_view": (I32, [P, U32, U64, U64, P, C.POINTER(P)]),

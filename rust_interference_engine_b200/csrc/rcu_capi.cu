@@ -93,6 +93,10 @@ int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, s
     c->num_sms = prop.multiProcessorCount;
     c->max_smem_optin = prop.sharedMemPerBlockOptin;
     if (const char *v = std::getenv("RIE_CUDA_PDL")) c->pdl = std::strcmp(v, "0") != 0;
+    if (const char *v = std::getenv("RIE_WAIT_LIMIT_MS")) {
+        const uint64_t ms = std::strtoull(v, nullptr, 10);
+        if (ms > 0) c->wait_limit_ns = ms * 1000000ull;
+    }
     if (const char *v = std::getenv("RIE_GEMV_KQ")) c->gemv_kq = std::strcmp(v, "0") != 0;
     if (const char *v = std::getenv("RIE_GEMV_KQ_MIN_MB")) c->gemv_kq_min_bytes = std::strtoull(v, nullptr, 10) << 20;
     e = cudaMalloc(&c->dev_err, sizeof(uint32_t));
@@ -155,6 +159,12 @@ int32_t rcu_check_device(rcu_ctx *ctx, uint32_t *bits_out) {
         std::snprintf(m, sizeof m, "bounded device wait expired (error bits 0x%x)", bits);
         return set_err(ctx, RCU_ERR_TIMEOUT, m);
     }
+    return RCU_OK;
+}
+
+int32_t rcu_set_wait_limit_ms(rcu_ctx *ctx, uint64_t ms) {
+    if (!ctx || ms == 0 || ms > 600000) return set_err(ctx, RCU_ERR_INVALID, "wait limit must be 1..600000 ms");
+    ctx->wait_limit_ns = ms * 1000000ull;
     return RCU_OK;
 }
 

@@ -235,6 +235,7 @@ struct ArSum {
     const uint64_t *epoch;  // forwards run with the fused all-reduce, this one included
     uint32_t expect, P, stride;
     uint32_t *err;
+    uint64_t limit_ns;  // the context's wait limit
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
@@ -252,7 +253,7 @@ __device__ __forceinline__ void ar_wait(const ArSum &ar) {
         bool ok = true;
         for (uint32_t q = 0; q < ar.P && ok; q++) {
             while ((int32_t)(ld_acquire_sys(ar.flag + q) - target) < 0) {
-                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                if (globaltimer_ns() - t0 > ar.limit_ns) {
                     atomicOr(ar.err, (uint32_t)ERR_TIMEOUT_PEER);
                     ok = false;
                     break;
@@ -910,7 +911,7 @@ static int forward_span(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logi
         const HostJob hj{w, b->ar_buf + slot + rank * stride, e};
         if (int st = launch_gemv(ctx, a, &hj, 1, 0, (uint32_t)n, &push)) return st;
         *sum = ArSum{b->ar_buf + slot, b->ar_flags + (uint64_t)j * P, b->ar_epoch, kArUnit, (uint32_t)P,
-                     (uint32_t)stride, ctx->dev_err};
+                     (uint32_t)stride, ctx->dev_err, ctx->wait_limit_ns};
         return RCU_OK;
     };
     const float *pend_o = nullptr, *pend_post = nullptr;  // residual not yet added to x
@@ -1753,6 +1754,32 @@ int32_t rcu_backend_forward_layers(rcu_backend *b, const float *x_dev, uint64_t 
     RCU_CUDA_TRY(ctx, cudaEventRecord(b->ev_out, b->stream));
     RCU_CUDA_TRY(ctx, cudaStreamWaitEvent(caller, b->ev_out, 0));
     return RCU_OK;
+}
+
+int32_t rcu_diag_expire_peer_wait(rcu_ctx *ctx) {
+    if (!ctx) return RCU_ERR_INVALID;
+    // one 256-value row through the fused all-reduce norm, waiting for a second rank's partial
+    // rows that never arrive: arrival counters at zero, one forward already counted
+    constexpr uint32_t e = 256, P = 2;
+    uint8_t *mem = nullptr;
+    const size_t bytes = 2 * P * e * sizeof(float) + 64;
+    RCU_CUDA_TRY(ctx, cudaMalloc(&mem, bytes));
+    struct Free {
+        uint8_t *p;
+        ~Free() { cudaFree(p); }
+    } free_mem{mem};
+    RCU_CUDA_TRY(ctx, cudaMemsetAsync(mem, 0, bytes, ctx->stream));
+    float *x = reinterpret_cast<float *>(mem), *src = x + e, *w = src + P * e;
+    uint32_t *flag = reinterpret_cast<uint32_t *>(mem + 2 * P * e * sizeof(float));
+    uint64_t *epoch = reinterpret_cast<uint64_t *>(flag + 8);
+    const uint64_t one = 1;
+    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(epoch, &one, sizeof(one), cudaMemcpyHostToDevice, ctx->stream));
+    const ArSum ar{src, flag, epoch, kArUnit, P, e, ctx->dev_err, ctx->wait_limit_ns};
+    const ActOut ao{};
+    RCU_CUDA_TRY(ctx, launch_k(ctx, k_norm_q8, dim3(1), dim3(e / 8), 0, x, (const float *)nullptr, (const float *)nullptr,
+                               1.0f, (const float *)w, e, 1e-6f, (float *)nullptr, ao, 0, ar));
+    RCU_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return rcu_check_device(ctx, nullptr);
 }
 
 int32_t rcu_backend_hidden(const rcu_backend *b, float *host_out, uint64_t cap, uint64_t *rows_out) {

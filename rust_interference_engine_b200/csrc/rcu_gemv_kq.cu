@@ -28,6 +28,14 @@
 // The per-thread integer pieces add up exactly to the reference's sumi / summ; only the f32
 // grouping differs (per thread share instead of per superblock), as in the lane GEMV.
 //
+// Q4_0 (x Q8_0 activations, vec_dot_q4_0 of quant/reference.rs:221-233) runs on the same tiles:
+// eight 18-byte blocks make a 144-byte unit, like a Q4_K superblock. One mma takes one block
+// of 16 rows: A's column chunk c carries bytes 4c..4c+3 of the block (weights 4c..4c+3 from
+// the low nibbles, 16+4c..16+4c+3 from the high ones), B holds the block's 32 activation codes
+// in every column, so every thread ends with the exact int32 sums of its rows g and g + 8.
+// Of four consecutive blocks, thread c combines block c: d_w * d_a * (sum - 8 * sum(q_a)),
+// the activations' code sum exact (ActsView::sum0).
+//
 // Shared memory: rows of a stage at a stride = 16 (mod 128), which puts the 16-byte loads of
 // a warp's 8 rows in distinct banks. Q6_K superblocks (210 B) are only 2-byte aligned: a
 // thread reads its 16 bytes as 4 words in an order rotated by c (word (i + c) % 4 into slot
@@ -86,7 +94,7 @@ struct KqJob {
 struct KqGroup {
     uint32_t type, job0, job1, tile0, tile1, cta0, cta1;
 };
-constexpr int kQMaxGroups = 3;
+constexpr int kQMaxGroups = 4;
 
 struct KqParams {
     KqJob jobs[kQMaxJobs];
@@ -148,6 +156,18 @@ struct ActR {
 template <int TYPE>
 __device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, uint32_t sb,
                                          uint32_t c, bool bact, ActR &a) {
+    if (TYPE == T_Q4_0) {  // unit sb = Q8_0 blocks 8 sb .. 8 sb + 7; adk = d0 row, abw = sum0 row
+        const uint8_t *x = reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 4 * c;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            a.x[2 * j] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j));
+            a.x[2 * j + 1] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j + 16));
+        }
+        a.bs = make_uint4(__float_as_uint(__ldg(adk + 8 * sb + c)), __float_as_uint(__ldg(adk + 8 * sb + 4 + c)),
+                          __ldg(abw + 8 * sb + c), __ldg(abw + 8 * sb + 4 + c));
+        a.d = 0.0f;
+        return;
+    }
     a.d = __ldg(adk + sb);
     if (TYPE == T_Q6_K) {
         const uint32_t n = c >> 1, h = c & 1u;
@@ -299,11 +319,41 @@ __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint
     }
 }
 
+// Q4_0 unit (8 blocks) at byte `so` of rows ra / rb.
+__device__ __forceinline__ void kq_q40(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
+                                       float &accA, float &accB) {
+#pragma unroll
+    for (int s4 = 0; s4 < 2; s4++) {
+        int D[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t b = 4 * s4 + j, off = so + 18 * b + 2 + 4 * c;  // 4-aligned for odd blocks
+            const uint32_t wa = (b & 1) ? *reinterpret_cast<const uint32_t *>(ra + off) : lds_u32_at(ra, off);
+            const uint32_t wb = (b & 1) ? *reinterpret_cast<const uint32_t *>(rb + off) : lds_u32_at(rb, off);
+            D[j][0] = D[j][1] = D[j][2] = D[j][3] = 0;
+            mma_u8s8(D[j], wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, (wa >> 4) & 0x0F0F0F0Fu, (wb >> 4) & 0x0F0F0F0Fu,
+                     A.x[2 * b], A.x[2 * b + 1]);
+        }
+        // this thread's block of the four: 4 s4 + c
+        const int sg = c == 0 ? D[0][0] : c == 1 ? D[1][0] : c == 2 ? D[2][0] : D[3][0];
+        const int sh = c == 0 ? D[0][2] : c == 1 ? D[1][2] : c == 2 ? D[2][2] : D[3][2];
+        const uint32_t bo = so + 18 * (4 * s4 + c);
+        const float da = __uint_as_float(s4 ? A.bs.y : A.bs.x);
+        const int sa8 = 8 * (int)(s4 ? A.bs.w : A.bs.z);
+        const float dwa = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ra + bo));
+        const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(rb + bo));
+        accA = fmaf(dwa * da, (float)(sg - sa8), accA);
+        accB = fmaf(dwb * da, (float)(sh - sa8), accB);
+    }
+}
+
 template <int TYPE>
 __device__ __forceinline__ void kq_block(const uint8_t *ra, const uint8_t *rb, uint32_t sbl, const ActR &A, uint32_t c,
                                          float &accA, float &accB) {
-    constexpr uint32_t BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
-    if (TYPE == T_Q6_K) {
+    constexpr uint32_t BB = TYPE == T_Q4_K || TYPE == T_Q4_0 ? 144 : TYPE == T_Q5_K ? 176 : 210;
+    if (TYPE == T_Q4_0) {
+        kq_q40(ra, rb, sbl * BB, A, c, accA, accB);
+    } else if (TYPE == T_Q6_K) {
         if (sbl & 1u)
             kq_q6<false>(ra, rb, sbl * BB, A, c, accA, accB);
         else
@@ -402,9 +452,12 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
         const uint32_t ex = J.sel ? *(volatile const uint32_t *)J.sel : 0u;
         const bool skip = ex == kNoExpert;
         const uint64_t trow = (uint64_t)p.tok0 + J.tok;
-        const int8_t *aq = AV.qk + trow * k;
-        const float *adk = AV.dk + trow * nsb;
-        const uint32_t *abw = reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
+        // Q8_K rows (codes, superblock scales, bsum pairs) or, for Q4_0, Q8_0 rows (codes, block
+        // scales, exact code sums)
+        const int8_t *aq = TYPE == T_Q4_0 ? AV.q0 + trow * k : AV.qk + trow * k;
+        const float *adk = TYPE == T_Q4_0 ? AV.d0 + trow * (k / QK) : AV.dk + trow * nsb;
+        const uint32_t *abw = TYPE == T_Q4_0 ? reinterpret_cast<const uint32_t *>(AV.sum0 + trow * (k / QK))
+                                             : reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
         float accA[kQG], accB[kQG];
 #pragma unroll
         for (int gi = 0; gi < kQG; gi++) accA[gi] = accB[gi] = 0.0f;
@@ -530,6 +583,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
     switch (G.type) {
         case T_Q4_K: kq_consume<T_Q4_K>(p, h, stages, G, warp, lane); break;
         case T_Q5_K: kq_consume<T_Q5_K>(p, h, stages, G, warp, lane); break;
+        case T_Q4_0: kq_consume<T_Q4_0>(p, h, stages, G, warp, lane); break;
         default: kq_consume<T_Q6_K>(p, h, stages, G, warp, lane); break;
     }
     if (p.ar_nflag) {  // this CTA's rows are in every receive buffer: count it in
@@ -550,25 +604,29 @@ uint32_t round_up_u(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 // per warp (two independent chains), then longer slices.
 bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
     const int t = w->type;
-    if (t != T_Q4_K && t != T_Q5_K && t != T_Q6_K) return false;
+    if (t != T_Q4_K && t != T_Q5_K && t != T_Q6_K && t != T_Q4_0) return false;
     if (w->cols != k || k % QK_K != 0 || w->row_bytes % 16 != 0 || ((uintptr_t)w->data & 15u)) return false;
-    const uint32_t bb = (uint32_t)block_bytes(t), nsb = k / QK_K;
+    // units of 256 values: a K-quant superblock, or eight Q4_0 blocks (144 bytes)
+    const uint32_t bb = t == T_Q4_0 ? 8u * 18u : (uint32_t)block_bytes(t), nsb = k / QK_K;
     double best = -1.0;
     for (uint32_t sl = nsb; sl >= 1; sl--) {
         if (nsb % sl || (sl * bb) % 16) continue;
         uint32_t ps = sl * bb;
         ps += (16u + 128u - ps % 128u) % 128u;
-        uint32_t rbl = 0;
-        while ((uint32_t)(kQW >> rbl) > sl && rbl < (uint32_t)kQWLog2) rbl++;
-        if ((16u << rbl) * ps > kQMaxStage) continue;
-        const uint32_t wpb = kQW >> rbl, per = (sl + wpb - 1) / wpb;
-        const double bal = (double)sl / (double)(wpb * per);
-        const double score = bal * 8.0 + (per == 2 ? 2.0 : 0.0) + (double)sl / nsb;
-        if (score > best) {
-            best = score;
-            jd.sl = sl;
-            jd.rb_log2 = rbl;
-            jd.pstride = ps;
+        uint32_t rbl0 = 0;
+        while ((uint32_t)(kQW >> rbl0) > sl && rbl0 < (uint32_t)kQWLog2) rbl0++;
+        // taller stages (more 16-row blocks, fewer warps per block) give each warp two units
+        for (uint32_t rbl = rbl0; rbl <= (uint32_t)kQWLog2; rbl++) {
+            if ((16u << rbl) * ps > kQMaxStage) break;
+            const uint32_t wpb = kQW >> rbl, per = (sl + wpb - 1) / wpb;
+            const double bal = (double)sl / (double)(wpb * per);
+            const double score = bal * 8.0 + (per == 2 ? 2.0 : 0.0) + (double)sl / nsb - 0.01 * rbl;
+            if (score > best) {
+                best = score;
+                jd.sl = sl;
+                jd.rb_log2 = rbl;
+                jd.pstride = ps;
+            }
         }
     }
     if (best < 0.0) return false;
@@ -593,7 +651,13 @@ bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p) {
 }  // namespace
 
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
-    if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs || !(a.have & RCU_ACT_Q8K)) return false;
+    if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs) return false;
+    for (int i = 0; i < n_jobs; i++)
+        if (!(a.have & act_format(jobs[i].w->type))) return false;
+    // Q4_0 rows shorter than 4096 values stay on the lane GEMV, which measured faster there
+    // (config 1, 6144 x 2048: 3.5 vs 2.8 TB/s; 2 x 28672 x 8192: 2.7 vs 3.8 TB/s here)
+    for (int i = 0; i < n_jobs; i++)
+        if (jobs[i].w->type == T_Q4_0 && a.k < 4096) return false;
     uint64_t bytes = 0;
     uint32_t stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
@@ -631,7 +695,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
     uint32_t tiles = 0, stage_bytes = 0;
     uint64_t gbytes[kQMaxGroups] = {};
     int nj = 0;
-    for (const int ty : {T_Q4_K, T_Q5_K, T_Q6_K}) {
+    for (const int ty : {T_Q4_K, T_Q5_K, T_Q6_K, T_Q4_0}) {
         KqGroup &G = p.groups[p.n_groups];
         G.type = (uint32_t)ty;
         G.job0 = (uint32_t)nj;

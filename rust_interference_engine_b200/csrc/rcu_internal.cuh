@@ -174,6 +174,8 @@ struct rcu_ctx {
     size_t max_smem_optin = 0;
     uint32_t *dev_err = nullptr;  // device error bits
     bool pdl = true;              // programmatic dependent launch for the kernels of this library
+    // limit of the waits on other ranks (fused all-reduce): RIE_WAIT_LIMIT_MS, rcu_set_wait_limit_ms
+    uint64_t wait_limit_ns = 2000000000ull;
     // GEMV weights may be streamed before the previous kernel has finished (set while the
     // forward scheduler runs: its weights are written once, at load time)
     bool early_weights = false;

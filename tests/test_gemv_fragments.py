@@ -213,3 +213,57 @@ def test_shared_loads_conflict_free(t, k):
                     ad = [(g * ps + so + base(c >> 1, c & 1) + 4 * ((i + c) & 3)) & ~3 for g, c in lanes]
                     assert conflict_factor(ad, 4) == 1
                     assert conflict_factor([a + 4 for a in ad], 4) == 1
+
+
+def emulate_q4_0(rows, act_blocks, n_units):
+    """Q4_0 units (8 blocks of 18 bytes) as k_gemv_kq forms them: per block one mma with A's
+    chunk c = bytes 4c..4c+3 of the block (low nibbles at k 4c.., high at 16 + 4c..) and B the
+    block's 32 codes in every column; thread c of each row group combines block 4 s + c of every
+    four. Returns the per-(row, block) integer sums sum(nib * q) - 8 * sum(q) the threads form."""
+    ps = pad_stride(n_units * 144)
+    stage = np.zeros(16 * ps, np.uint8)
+    for r in range(16):
+        stage[r * ps:r * ps + n_units * 144] = rows[r]
+    qs = act_blocks["qs"].astype(np.int8).view(np.uint8)  # [blocks][32]
+    lanes = [(l >> 2, l & 3) for l in range(32)]
+    out = np.zeros((16, 8 * n_units), np.int64)
+    for u in range(n_units):
+        so = u * 144
+        for s4 in range(2):
+            D = []
+            for j in range(4):
+                b = 4 * s4 + j
+                blk = 8 * u + b
+                a, bb = [], []
+                for l, (g, c) in enumerate(lanes):
+                    off = so + 18 * b + 2 + 4 * c
+                    wa, wb = word(stage, g * ps + off), word(stage, (g + 8) * ps + off)
+                    a.append((wa & M4, wb & M4, (wa >> 4) & M4, (wb >> 4) & M4))
+                    bb.append((word(qs[blk], 4 * c), word(qs[blk], 16 + 4 * c)))
+                D.append(mma(a, bb))
+            for l, (g, c) in enumerate(lanes):
+                blk = 8 * u + 4 * s4 + c
+                sa = int(act_blocks["qs"][blk].astype(np.int64).sum())
+                for r, row in ((0, g), (2, g + 8)):
+                    out[row, blk] = int(D[c][l][r]) - 8 * sa
+    return out
+
+
+def test_q4_0_fragment_sums_match_oracle():
+    n_units = 2
+    k = 256 * n_units
+    rng = O.Rng(404)
+    w = rng.weight(O.Q4_0, 16, k)
+    x = rng.vec(k, 1.0)
+    act = O.quantize_row_q8_0(x, O.PATH_AVX2)
+    got = emulate_q4_0(w, act, n_units)
+    for r in range(16):
+        np.testing.assert_array_equal(got[r], O.block_sums(O.Q4_0, w[r], act, k))
+
+
+def test_q4_0_shared_loads_conflict_free():
+    ps = pad_stride(16 * 144)
+    lanes = [(l >> 2, l & 3) for l in range(32)]
+    for b in range(8):
+        ad = [(g * ps + 18 * b + 2 + 4 * c) & ~3 for g, c in lanes]
+        assert conflict_factor(ad, 4) == 1
