@@ -975,7 +975,7 @@ def run_turbo(args, world, rank, local):
                    "parallelism": f"tp{world} (KV heads split, no exchange)", "kv_fill_s": t_fill},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic("attn_turbo4_70b_ctx32k"),
-                     "kernel": "k_attn<turbo4, G=8> (80 launches per step)", "bytes_per_launch": kv_bytes // L,
+                     "kernel": "k_attn_dec_t4<G=8> (80 launches per step)", "bytes_per_launch": kv_bytes // L,
                      "launch_ms": float(np.mean([a.elapsed_time(b) for a, b in kern])) / L},
         "e2e": {"value": world * kv_bytes / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(q.numel() * 4),
                 "d2h_bytes_per_step": int(out.numel() * 4), "ms_per_step": e2e_s * 1e3},

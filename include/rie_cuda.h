@@ -149,6 +149,15 @@ RCU_API int32_t rcu_matmul(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight 
 RCU_API int32_t rcu_block_sums(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, uint64_t row, uint64_t tok,
                        int32_t *out_dev);
 
+/* The batch-1 matmul of activation row 0 with every row of w, as rcu_matmul runs it, on the
+ * kernel named by `kernel` (0: the lane GEMV, any block type; 1: the tensor-core GEMV, Q4_K /
+ * Q5_K / Q6_K / Q4_0), with the exact per-block integer sums that kernel forms captured on the
+ * way: sums_dev[row * n + i] in the layout of rcu_block_sums (n of them per row). A validation
+ * variant of the same kernels (quant/reference.rs:221-386 block sums; kernels/matmul.rs:136-241
+ * for the f32 outputs in `out`). sums_dev is cleared first. */
+RCU_API int32_t rcu_matmul_block_sums(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, float *out,
+                                      int32_t *sums_dev, int32_t kernel);
+
 /* ---- turbo4 (turbo.rs) --------------------------------------------------------------- */
 /* row_bytes_4 (turbo.rs:136-138): f16 scale per rotation block + hd/2 code bytes. */
 RCU_API uint64_t rcu_turbo4_row_bytes(uint64_t hd);

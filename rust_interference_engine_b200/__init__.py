@@ -315,6 +315,14 @@ def block_sums(ctx: Context, acts: QuantActs, w: Weight, row: int, tok: int, out
     _check(ctx.ptr, ctx._lib.rcu_block_sums(ctx.ptr, acts.ptr, w.ptr, row, tok, C.c_void_p(_dptr(out))))
 
 
+def matmul_block_sums(ctx: Context, acts: QuantActs, w: Weight, out, sums, kernel: int) -> None:
+    """Row 0 of acts times every row of w on the named GEMV (0: lane kernel, 1: tensor-core
+    kernel), f32 results in `out` and the exact per-block int32 sums that kernel formed in
+    `sums` (rows x blocks per row, the block_sums layout; device buffers)."""
+    _check(ctx.ptr, ctx._lib.rcu_matmul_block_sums(ctx.ptr, acts.ptr, w.ptr, C.c_void_p(_dptr(out)),
+                                                   C.c_void_p(_dptr(sums)), int(kernel)))
+
+
 class LayerCache:
     """One layer's KV cache, layout [kv_head][slot][row] (model/cpu.rs:38-50)."""
 

@@ -42,6 +42,7 @@ SIGNATURES = {
     "rcu_matmul_multi": (I32, [P, P, P, U64]),
     "rcu_matmul": (I32, [P, P, P, P]),
     "rcu_block_sums": (I32, [P, P, P, U64, U64, P]),
+    "rcu_matmul_block_sums": (I32, [P, P, P, P, P, I32]),
     "rcu_turbo4_row_bytes": (U64, [U64]),
     "rcu_turbo4_quantize": (I32, [P, P, U64, U64, P]),
     "rcu_turbo4_rotate": (I32, [P, P, U64, U64, I32]),

@@ -99,6 +99,7 @@ int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, s
     }
     if (const char *v = std::getenv("RIE_GEMV_KQ")) c->gemv_kq = std::strcmp(v, "0") != 0;
     if (const char *v = std::getenv("RIE_GEMV_KQ_MIN_MB")) c->gemv_kq_min_bytes = std::strtoull(v, nullptr, 10) << 20;
+    if (const char *v = std::getenv("RIE_GEMV_PROLOGUE")) c->gemv_prologue = std::strcmp(v, "0") != 0;
     e = cudaMalloc(&c->dev_err, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(cuda_err(c, e, "cudaMalloc(err)"));
     e = cudaMemset(c->dev_err, 0, sizeof(uint32_t));
@@ -405,6 +406,32 @@ int32_t rcu_matmul(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, floa
     if (!w) return set_err(ctx, RCU_ERR_INVALID, "null weight");
     rcu_job j{w, out, w->rows};
     return rcu_matmul_multi(ctx, acts, &j, 1);
+}
+
+int32_t rcu_matmul_block_sums(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, float *out,
+                              int32_t *sums_dev, int32_t kernel) {
+    if (!ctx || !acts || !w || !out || !sums_dev) return set_err(ctx, RCU_ERR_INVALID, "null argument");
+    if (kernel != 0 && kernel != 1) return set_err(ctx, RCU_ERR_INVALID, "kernel: 0 (lane GEMV) or 1 (tensor-core GEMV)");
+    const int t = w->type;
+    if (!gemv_supported(t)) return set_err(ctx, RCU_ERR_UNSUPPORTED, "type");
+    if (kernel == 1 && t != T_Q4_K && t != T_Q5_K && t != T_Q6_K && t != T_Q4_0)
+        return set_err(ctx, RCU_ERR_UNSUPPORTED, "the tensor-core GEMV takes Q4_K, Q5_K, Q6_K and Q4_0 weights");
+    if (w->cols != acts->v.k || !(acts->v.have & act_format(t)))
+        return set_err(ctx, RCU_ERR_INVALID, "activations do not match the weight");
+    RCU_GUARD_BEGIN
+    const uint64_t k = w->cols;
+    const uint32_t nbs = (uint32_t)(block_size(t) == QK ? k / QK : (t == T_Q6_K ? k / QK_K : 2 * (k / QK_K)));
+    RCU_CUDA_TRY(ctx, cudaMemsetAsync(sums_dev, 0, w->rows * nbs * sizeof(int32_t), ctx->stream));
+    ctx->dbg_sums = sums_dev;
+    ctx->dbg_nbs = nbs;
+    ctx->dbg_kernel = kernel;
+    const HostJob hj{w, out, w->rows};
+    const int st = launch_gemv(ctx, acts->v, &hj, 1, 0, 1);
+    ctx->dbg_sums = nullptr;
+    ctx->dbg_nbs = 0;
+    ctx->dbg_kernel = -1;
+    return st;
+    RCU_GUARD_END(ctx)
 }
 
 int32_t rcu_block_sums(rcu_ctx *ctx, const rcu_acts *acts, const rcu_weight *w, uint64_t row, uint64_t tok,

@@ -65,6 +65,11 @@ struct GemvParams {
     float *ar_dst[kMaxPeers];
     uint32_t *ar_flag[kMaxPeers];
     uint32_t ar_ndst, ar_nflag;
+    // block-sum capture (the k_gemv<1, 16, true> instantiation only): every exact per-block
+    // integer sum of a row of token 0, in the layout of rcu_block_sums, added into
+    // dbg[row * dbg_nbs + i]
+    int32_t *dbg;
+    uint32_t dbg_nbs;
 };
 
 struct SmemHdr {
@@ -169,7 +174,7 @@ __device__ __forceinline__ void finish_rows(const GemvParams &p, SmemHdr *h, int
 }
 
 // ---- 32-value block types: one block per lane per step ----------------------------------
-template <int TYPE, int T>
+template <int TYPE, int T, bool DBG>
 __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
                                        uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
     constexpr uint32_t BB = blk_bytes_c<TYPE>();
@@ -222,6 +227,9 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
 #pragma unroll
                 for (int t = 0; t < T; t++) {
                     const int si = blk_int<TYPE>(w, a[t], asum[t]);
+                    if constexpr (DBG) {
+                        if (t == 0) p.dbg[(uint64_t)(r0 + row_first + r) * p.dbg_nbs + b] = si;
+                    }
                     float c = (w.d * da[t]) * (float)si;  // f16(d) * ab.d * s
                     if (TYPE == T_Q4_1 || TYPE == T_Q5_1) c += w.m * sa[t];
                     acc[r][t] += c;
@@ -236,7 +244,7 @@ __device__ __forceinline__ void tile_q(const GemvParams &p, SmemHdr *h, int s, c
 // Each lane keeps its own f32 partial of every row; one warp reduction per row at the end
 // (the sum of per-lane partials differs from the reference's per-superblock order only by
 // f32 rounding).
-template <int TYPE, int T>
+template <int TYPE, int T, bool DBG>
 __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, const uint8_t *wsm, const GemvJobDev &jb,
                                        uint32_t r0, uint32_t nrows, const uint8_t *sm, int warp, int lane) {
     constexpr uint32_t BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
@@ -290,6 +298,9 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
                         int I;
                         const uint32_t db = q6_lane_dot(l, wsm, wrow0 + r * rb + sb * BB, a[t], bs2[t], I);
                         acc[r][t] += (f16_bits_to_f32(db) * ad[t]) * (float)I;
+                        if constexpr (DBG) {
+                            if (t == 0) atomicAdd(p.dbg + (uint64_t)(r0 + row_first + r) * p.dbg_nbs + sb, I);
+                        }
                     }
                 }
             }
@@ -317,6 +328,13 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
                     for (int t = 0; t < T; t++) {
                         int I, M;
                         const uint32_t dm = k_lane_dot<TYPE>(l, sbp, alo[t], ahi[t], bs2[t], I, M);
+                        if constexpr (DBG) {
+                            if (t == 0) {
+                                int32_t *d = p.dbg + (uint64_t)(r0 + row_first + r) * p.dbg_nbs + 2 * sb;
+                                atomicAdd(d, I);
+                                atomicAdd(d + 1, M);
+                            }
+                        }
                         // d * sumi - dmin * summ with d = f16(d)*ab.d, dmin = f16(dmin)*ab.d
                         const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&dm));
                         acc[r][t] = fmaf(ad[t], fmaf(-f.y, (float)M, f.x * (float)I), acc[r][t]);
@@ -328,7 +346,7 @@ __device__ __forceinline__ void tile_k(const GemvParams &p, SmemHdr *h, int s, c
     finish_rows<T>(p, h, s, jb, r0, row_first, nr, part, acc, lane);
 }
 
-template <int T, int NW>
+template <int T, int NW, bool DBG = false>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     SmemHdr *h = reinterpret_cast<SmemHdr *>(smem);
@@ -423,14 +441,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) k_gemv(const __grid_constant
         const uint32_t nrows = min(jb.rows_per_tile, jb.rows - r0);
         const uint8_t *wsm = smem + p.stage_off + s * p.stage_bytes;
         switch (jb.sel && *jb.sel == kNoExpert ? -1 : jb.type) {
-            case T_Q4_0: tile_q<T_Q4_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q4_1: tile_q<T_Q4_1, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q5_0: tile_q<T_Q5_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q5_1: tile_q<T_Q5_1, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q8_0: tile_q<T_Q8_0, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q4_K: tile_k<T_Q4_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q5_K: tile_k<T_Q5_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
-            case T_Q6_K: tile_k<T_Q6_K, T>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q4_0: tile_q<T_Q4_0, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q4_1: tile_q<T_Q4_1, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_0: tile_q<T_Q5_0, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_1: tile_q<T_Q5_1, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q8_0: tile_q<T_Q8_0, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q4_K: tile_k<T_Q4_K, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q5_K: tile_k<T_Q5_K, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
+            case T_Q6_K: tile_k<T_Q6_K, T, DBG>(p, h, s, wsm, jb, r0, nrows, smem, warp, lane); break;
             default: break;
         }
         __syncwarp();
@@ -535,15 +553,15 @@ int launch_block_sums(rcu_ctx *ctx, const ActsView &a, const rcu_weight *w, uint
 // ---- host side -------------------------------------------------------------------------
 static uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
-template <int T, int NW>
+template <int T, int NW, bool DBG = false>
 static int launch_t(rcu_ctx *ctx, GemvParams &p, uint32_t smem_bytes, uint32_t grid) {
     static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
     if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
-        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv<T, NW, DBG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)ctx->max_smem_optin));
         attr_set[ctx->device & 63].store(true, std::memory_order_release);
     }
-    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_gemv<T, NW>), dim3(grid), dim3((NW + 1) * 32), smem_bytes, p));
+    RCU_CUDA_TRY(ctx, launch_k(ctx, (k_gemv<T, NW, DBG>), dim3(grid), dim3((NW + 1) * 32), smem_bytes, p));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }
@@ -554,7 +572,12 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     if (n_tok < 1 || n_tok > kMaxTok) return set_err(ctx, RCU_ERR_INVALID, "gemv: 1..8 tokens per launch");
     // one activation row over K-quant weights: the tensor-core GEMV (rcu_gemv_kq.cu), also for
     // launches that push a tensor-parallel all-reduce
-    if (n_tok == 1 && gemv_kq_ok(ctx, a, jobs, n_jobs)) return launch_gemv_kq(ctx, a, jobs, n_jobs, tok0, push);
+    if (ctx->dbg_sums) {  // block-sum capture: the kernel the caller named, one job, token 0
+        if (n_jobs != 1 || push || n_tok != 1) return set_err(ctx, RCU_ERR_INVALID, "block-sum capture: one job, one token");
+        if (ctx->dbg_kernel == 1) return launch_gemv_kq(ctx, a, jobs, n_jobs, tok0, push);
+    } else if (n_tok == 1 && gemv_kq_ok(ctx, a, jobs, n_jobs)) {
+        return launch_gemv_kq(ctx, a, jobs, n_jobs, tok0, push);
+    }
     GemvParams p{};
     if (push) {
         if (n_jobs != 1 || tok0 != 0 || push->n_dst > kMaxPeers || push->n_flag > kMaxPeers)
@@ -648,6 +671,11 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = std::min<uint32_t>(tiles, (uint32_t)ctx->num_sms);
     if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
+    if (ctx->dbg_sums) {
+        p.dbg = ctx->dbg_sums;
+        p.dbg_nbs = ctx->dbg_nbs;
+        return launch_t<1, 16, true>(ctx, p, smem_bytes, grid);
+    }
     switch (n_tok) {
         case 1: return launch_t<1, 16>(ctx, p, smem_bytes, grid);
         case 2: return launch_t<2, 16>(ctx, p, smem_bytes, grid);

@@ -55,6 +55,7 @@
 #include <algorithm>
 #include <atomic>
 
+#include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
 
@@ -109,6 +110,15 @@ struct KqParams {
     float *ar_dst[kQMaxPeers];
     uint32_t *ar_flag[kQMaxPeers];
     uint32_t ar_ndst, ar_nflag;
+    // block-sum capture (the k_gemv_kq<true> instantiation only): every exact per-block
+    // integer sum of a row, in the layout of rcu_block_sums, atomically added into
+    // dbg[row * dbg_nbs + i]
+    int32_t *dbg;
+    uint32_t dbg_nbs;
+    // activation prologue (the k_gemv_kq<false, true> instantiation): the launch computes its
+    // one activation row into shared memory at these byte offsets
+    GemvPrologue pro;
+    uint32_t a_zero, a_qk, a_dk, a_bsk, a_q0, a_d0, a_s0, a_sum0, a_red;
 };
 
 struct KqHdr {
@@ -153,47 +163,65 @@ struct ActR {
     float d;
 };
 
-template <int TYPE>
-__device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, uint32_t sb,
-                                         uint32_t c, bool bact, ActR &a) {
+// Activation loads: read-only global memory (a prepared ActsView), or this CTA's shared memory
+// (SM: the activations the launch computed itself).
+template <bool SM>
+__device__ __forceinline__ uint32_t lda32(const void *p) {
+    if constexpr (SM) return *reinterpret_cast<const uint32_t *>(p);
+    else return __ldg(reinterpret_cast<const uint32_t *>(p));
+}
+template <bool SM>
+__device__ __forceinline__ uint2 lda64(const void *p) {
+    if constexpr (SM) return *reinterpret_cast<const uint2 *>(p);
+    else return __ldg(reinterpret_cast<const uint2 *>(p));
+}
+template <bool SM>
+__device__ __forceinline__ uint4 lda128(const void *p) {
+    if constexpr (SM) return *reinterpret_cast<const uint4 *>(p);
+    else return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+// zero: 256 zero bytes (the activations of threads whose B column is zero).
+template <int TYPE, bool SM>
+__device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, const uint8_t *zero,
+                                         uint32_t sb, uint32_t c, bool bact, ActR &a) {
     if (TYPE == T_Q4_0) {  // unit sb = Q8_0 blocks 8 sb .. 8 sb + 7; adk = d0 row, abw = sum0 row
         const uint8_t *x = reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 4 * c;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            a.x[2 * j] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j));
-            a.x[2 * j + 1] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j + 16));
+            a.x[2 * j] = lda32<SM>(x + 32 * j);
+            a.x[2 * j + 1] = lda32<SM>(x + 32 * j + 16);
         }
-        a.bs = make_uint4(__float_as_uint(__ldg(adk + 8 * sb + c)), __float_as_uint(__ldg(adk + 8 * sb + 4 + c)),
-                          __ldg(abw + 8 * sb + c), __ldg(abw + 8 * sb + 4 + c));
+        a.bs = make_uint4(lda32<SM>(adk + 8 * sb + c), lda32<SM>(adk + 8 * sb + 4 + c), lda32<SM>(abw + 8 * sb + c),
+                          lda32<SM>(abw + 8 * sb + 4 + c));
         a.d = 0.0f;
         return;
     }
-    a.d = __ldg(adk + sb);
+    a.d = __uint_as_float(lda32<SM>(adk + sb));
     if (TYPE == T_Q6_K) {
         const uint32_t n = c >> 1, h = c & 1u;
-        const uint8_t *xa = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 128 * n + 16 * h : g_kq_zero;
+        const uint8_t *xa = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 128 * n + 16 * h : zero;
 #pragma unroll
         for (int m = 0; m < 4; m++)
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                a.x[4 * m + i] = __ldg(reinterpret_cast<const uint32_t *>(xa + 32 * m + 4u * ((i + c) & 3u)));
-        a.bs = ldg128(abw + 8 * sb + 4 * n);
+            for (int i = 0; i < 4; i++) a.x[4 * m + i] = lda32<SM>(xa + 32 * m + 4u * ((i + c) & 3u));
+        a.bs = lda128<SM>(abw + 8 * sb + 4 * n);
     } else {
-        const uint8_t *x = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 64 * c : g_kq_zero;
+        const uint8_t *x = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 64 * c : zero;
         uint32_t lo[8], hi[8];
-        words8(ldg128(x), ldg128(x + 16), lo);
-        words8(ldg128(x + 32), ldg128(x + 48), hi);
+        words8(lda128<SM>(x), lda128<SM>(x + 16), lo);
+        words8(lda128<SM>(x + 32), lda128<SM>(x + 48), hi);
 #pragma unroll
         for (int i = 0; i < 8; i++) a.x[i] = lo[i], a.x[8 + i] = hi[i];
-        const uint2 b = __ldg(reinterpret_cast<const uint2 *>(abw + 8 * sb + 2 * c));
+        const uint2 b = lda64<SM>(abw + 8 * sb + 2 * c);
         a.bs = make_uint4(b.x, b.y, 0u, 0u);
     }
 }
 
 // Q4_K / Q5_K superblock at byte `so` of rows ra (row g) and rb (row g + 8).
-template <int TYPE>
+template <int TYPE, bool DBG>
 __device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
-                                       float &accA, float &accB) {
+                                       float &accA, float &accB, int32_t *dA, int32_t *dB, uint32_t sbg) {
     constexpr uint32_t QO = TYPE == T_Q4_K ? 16 : 48;  // quant bytes (Q5_K: after qh[32])
     const uint8_t *pa = ra + so, *pb = rb + so;
     uint32_t WA[8], WB[8];
@@ -238,6 +266,12 @@ __device__ __forceinline__ void kq_q45(const uint8_t *ra, const uint8_t *rb, uin
         const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
         float &acc = r ? accB : accA;
         acc = fmaf(A.d, fmaf(-f.y, (float)M, f.x * (float)I), acc);
+        if constexpr (DBG) {
+            if (int32_t *d = r ? dB : dA) {
+                atomicAdd(d + 2 * sbg, I);
+                atomicAdd(d + 2 * sbg + 1, M);
+            }
+        }
     }
 }
 
@@ -264,9 +298,9 @@ __device__ __forceinline__ void ld4_rot(const uint8_t *row, uint32_t off, uint32
 
 // Q6_K superblock at byte `so` of rows ra / rb (A4: so is a multiple of 4, i.e. an even
 // superblock index within the slice).
-template <bool A4>
+template <bool A4, bool DBG>
 __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
-                                      float &accA, float &accB) {
+                                      float &accA, float &accB, int32_t *dA, int32_t *dB, uint32_t sbg) {
     const uint32_t n = c >> 1, h = c & 1u;
     uint32_t LA0[4], LA1[4], HA[4], LB0[4], LB1[4], HB[4];
     ld4_rot<A4>(ra, so + 64 * n + 16 * h, c, LA0);
@@ -316,12 +350,16 @@ __device__ __forceinline__ void kq_q6(const uint8_t *ra, const uint8_t *rb, uint
         const uint32_t db = *reinterpret_cast<const uint16_t *>(row + so + 208);
         float &acc = r ? accB : accA;
         acc = fmaf(f16_bits_to_f32(db) * A.d, (float)I, acc);
+        if constexpr (DBG) {
+            if (int32_t *d = r ? dB : dA) atomicAdd(d + sbg, I);
+        }
     }
 }
 
 // Q4_0 unit (8 blocks) at byte `so` of rows ra / rb.
+template <bool DBG>
 __device__ __forceinline__ void kq_q40(const uint8_t *ra, const uint8_t *rb, uint32_t so, const ActR &A, uint32_t c,
-                                       float &accA, float &accB) {
+                                       float &accA, float &accB, int32_t *dA, int32_t *dB, uint32_t sbg) {
 #pragma unroll
     for (int s4 = 0; s4 < 2; s4++) {
         int D[4][4];
@@ -344,22 +382,27 @@ __device__ __forceinline__ void kq_q40(const uint8_t *ra, const uint8_t *rb, uin
         const float dwb = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(rb + bo));
         accA = fmaf(dwa * da, (float)(sg - sa8), accA);
         accB = fmaf(dwb * da, (float)(sh - sa8), accB);
+        if constexpr (DBG) {  // Q8_0 block 8 unit + 4 s4 + c
+            if (dA) atomicAdd(dA + 8 * sbg + 4 * s4 + c, sg - sa8);
+            if (dB) atomicAdd(dB + 8 * sbg + 4 * s4 + c, sh - sa8);
+        }
     }
 }
 
-template <int TYPE>
+// Unit sbl of the stage's slice (sbg: the unit's index in the row, for the block-sum capture).
+template <int TYPE, bool DBG>
 __device__ __forceinline__ void kq_block(const uint8_t *ra, const uint8_t *rb, uint32_t sbl, const ActR &A, uint32_t c,
-                                         float &accA, float &accB) {
+                                         float &accA, float &accB, int32_t *dA, int32_t *dB, uint32_t sbg) {
     constexpr uint32_t BB = TYPE == T_Q4_K || TYPE == T_Q4_0 ? 144 : TYPE == T_Q5_K ? 176 : 210;
     if (TYPE == T_Q4_0) {
-        kq_q40(ra, rb, sbl * BB, A, c, accA, accB);
+        kq_q40<DBG>(ra, rb, sbl * BB, A, c, accA, accB, dA, dB, sbg);
     } else if (TYPE == T_Q6_K) {
         if (sbl & 1u)
-            kq_q6<false>(ra, rb, sbl * BB, A, c, accA, accB);
+            kq_q6<false, DBG>(ra, rb, sbl * BB, A, c, accA, accB, dA, dB, sbg);
         else
-            kq_q6<true>(ra, rb, sbl * BB, A, c, accA, accB);
+            kq_q6<true, DBG>(ra, rb, sbl * BB, A, c, accA, accB, dA, dB, sbg);
     } else {
-        kq_q45<TYPE>(ra, rb, sbl * BB, A, c, accA, accB);
+        kq_q45<TYPE, DBG>(ra, rb, sbl * BB, A, c, accA, accB, dA, dB, sbg);
     }
 }
 
@@ -372,41 +415,48 @@ struct Ring {  // consumer-side stage ring position
 // independent accumulators (two mma chains in flight) and their activations loaded before
 // the stage wait. Row partials of group gi end in accA[gi] (row g of the warp's 16-row
 // block) / accB[gi] (row g + 8).
-template <int TYPE>
+template <int TYPE, bool DBG, bool PRO>
 __device__ __forceinline__ bool kq_tile(const KqParams &p, KqHdr *h, uint8_t *stages, const JobR &J, uint32_t ngrp,
                                         bool skip, const int8_t *aq, const float *adk, const uint32_t *abw,
+                                        const uint8_t *zero,
                                         uint32_t rbk, uint32_t part, uint32_t wpb, uint32_t g, uint32_t c, bool bact,
-                                        uint32_t lane, Ring &R, float (&accA)[kQG], float (&accB)[kQG]) {
+                                        uint32_t lane, Ring &R, float (&accA)[kQG], float (&accB)[kQG], uint32_t r0) {
     const uint32_t S = p.stages;
     const uint32_t rofs = (rbk * 16u + g) * J.pstride;
 #pragma unroll
     for (int gi = 0; gi < kQG; gi++) {
         if ((uint32_t)gi >= ngrp) break;
         float a1 = 0.0f, b1 = 0.0f;  // second chain
+        int32_t *dA = nullptr, *dB = nullptr;  // block-sum capture rows (rows of the tile only)
+        if constexpr (DBG) {
+            const uint32_t row = r0 + gi * (16u << J.rb_log2) + rbk * 16u + g;
+            if (row < J.rows) dA = p.dbg + (uint64_t)row * p.dbg_nbs;
+            if (row + 8 < J.rows) dB = p.dbg + (uint64_t)(row + 8) * p.dbg_nbs;
+        }
         for (uint32_t sli = 0; sli < J.nsl; sli++) {
             const uint32_t sb0 = sli * J.sl;
             uint32_t sbl = part;
             ActR A0, A1;
             const bool two = sbl + wpb < J.sl;
             if (!skip) {
-                load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
-                if (two) load_act<TYPE>(aq, adk, abw, sb0 + sbl + wpb, c, bact, A1);
+                load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl, c, bact, A0);
+                if (two) load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl + wpb, c, bact, A1);
             }
             if (!mbar_wait_bounded(&h->full[R.s], R.ph, p.err, ERR_TIMEOUT_FULL)) return false;
             if (!skip) {
                 const uint8_t *ra = stages + R.s * p.stage_bytes + rofs;
                 const uint8_t *rb = ra + 8u * J.pstride;
                 if (two) {
-                    kq_block<TYPE>(ra, rb, sbl, A0, c, accA[gi], accB[gi]);
-                    kq_block<TYPE>(ra, rb, sbl + wpb, A1, c, a1, b1);
+                    kq_block<TYPE, DBG>(ra, rb, sbl, A0, c, accA[gi], accB[gi], dA, dB, sb0 + sbl);
+                    kq_block<TYPE, DBG>(ra, rb, sbl + wpb, A1, c, a1, b1, dA, dB, sb0 + sbl + wpb);
                     sbl += 2 * wpb;
                 } else {
-                    kq_block<TYPE>(ra, rb, sbl, A0, c, accA[gi], accB[gi]);
+                    kq_block<TYPE, DBG>(ra, rb, sbl, A0, c, accA[gi], accB[gi], dA, dB, sb0 + sbl);
                     sbl += wpb;
                 }
                 for (; sbl < J.sl; sbl += wpb) {  // slices wider than two superblocks per warp
-                    load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
-                    kq_block<TYPE>(ra, rb, sbl, A0, c, a1, b1);
+                    load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl, c, bact, A0);
+                    kq_block<TYPE, DBG>(ra, rb, sbl, A0, c, a1, b1, dA, dB, sb0 + sbl);
                 }
             }
             __syncwarp();
@@ -428,9 +478,9 @@ __device__ __forceinline__ void kq_store(const KqParams &p, float *out, uint32_t
 }
 
 // Consumer warps of a CTA whose tiles all hold weights of type TYPE.
-template <int TYPE>
-__device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t *stages, const KqGroup &G, int warp,
-                                           int lane) {
+template <int TYPE, bool DBG, bool PRO>
+__device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t *smem, uint8_t *stages,
+                                           const KqGroup &G, int warp, int lane) {
     const uint32_t g = lane >> 2, c = lane & 3;
     const bool bact = c == (g >> 1);
     const ActsView &AV = p.acts;
@@ -454,14 +504,27 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
         const uint64_t trow = (uint64_t)p.tok0 + J.tok;
         // Q8_K rows (codes, superblock scales, bsum pairs) or, for Q4_0, Q8_0 rows (codes, block
         // scales, exact code sums)
-        const int8_t *aq = TYPE == T_Q4_0 ? AV.q0 + trow * k : AV.qk + trow * k;
-        const float *adk = TYPE == T_Q4_0 ? AV.d0 + trow * (k / QK) : AV.dk + trow * nsb;
-        const uint32_t *abw = TYPE == T_Q4_0 ? reinterpret_cast<const uint32_t *>(AV.sum0 + trow * (k / QK))
-                                             : reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
+        const int8_t *aq;
+        const float *adk;
+        const uint32_t *abw;
+        const uint8_t *zero;
+        if constexpr (PRO) {  // the row this launch computed, in shared memory
+            aq = reinterpret_cast<const int8_t *>(smem + (TYPE == T_Q4_0 ? p.a_q0 : p.a_qk));
+            adk = reinterpret_cast<const float *>(smem + (TYPE == T_Q4_0 ? p.a_d0 : p.a_dk));
+            abw = reinterpret_cast<const uint32_t *>(smem + (TYPE == T_Q4_0 ? p.a_sum0 : p.a_bsk));
+            zero = smem + p.a_zero;
+        } else {
+            aq = TYPE == T_Q4_0 ? AV.q0 + trow * k : AV.qk + trow * k;
+            adk = TYPE == T_Q4_0 ? AV.d0 + trow * (k / QK) : AV.dk + trow * nsb;
+            abw = TYPE == T_Q4_0 ? reinterpret_cast<const uint32_t *>(AV.sum0 + trow * (k / QK))
+                                 : reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
+            zero = g_kq_zero;
+        }
         float accA[kQG], accB[kQG];
 #pragma unroll
         for (int gi = 0; gi < kQG; gi++) accA[gi] = accB[gi] = 0.0f;
-        if (!kq_tile<TYPE>(p, h, stages, J, ngrp, skip, aq, adk, abw, rbk, part, wpb, g, c, bact, lane, R, accA, accB))
+        if (!kq_tile<TYPE, DBG, PRO>(p, h, stages, J, ngrp, skip, aq, adk, abw, zero, rbk, part, wpb, g, c, bact, lane,
+                                     R, accA, accB, r0))
             return;
         // tile done: the 4 threads of each row add their shares, every warp publishes its rows'
         // partials; the last warp to arrive adds the parts in warp order and stores
@@ -501,6 +564,129 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
     }
 }
 
+// The consumer warps compute the launch's activation row into shared memory (GemvPrologue),
+// 8 values per lane: round r of warp w is superblock w + 8r (values 8 lane .. 8 lane + 7), the
+// layout the quantizers q8_k_block8 / q8_0_block8 take. Sums over the row (RMS) go through the
+// warps' partials in shared memory (two slots: the post-norm of o, then the norm of v).
+__device__ __forceinline__ float kq_act(float a, int act) {  // ops.rs:41-58, as k_glu_q8
+    return act == 1 ? 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a))) : a / (1.0f + expf(-a));
+}
+__device__ __forceinline__ void ld8f(const float *p, float (&v)[8]) {
+    const float4 a = __ldcg(reinterpret_cast<const float4 *>(p)), b = __ldcg(reinterpret_cast<const float4 *>(p) + 1);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void st8f(float *p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ float kq_row_sum(float v, float *red, uint32_t warp, uint32_t lane) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    named_bar_sync(1, kQW * 32);
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kQW; w++) s += red[w];
+    return s;
+}
+constexpr int kQProRounds = 4;  // rows of up to 8192 values (kind 2)
+
+__device__ void kq_prologue(const KqParams &p, uint8_t *smem, uint32_t tid) {
+    const GemvPrologue &P = p.pro;
+    const uint32_t k = p.k, warp = tid >> 5, lane = tid & 31, nsb = k / QK_K;
+    ActOut ao{};
+    ao.q0 = reinterpret_cast<int8_t *>(smem + p.a_q0);
+    ao.d0 = reinterpret_cast<float *>(smem + p.a_d0);
+    ao.s0 = reinterpret_cast<float *>(smem + p.a_s0);
+    ao.sum0 = reinterpret_cast<int32_t *>(smem + p.a_sum0);
+    ao.qk = reinterpret_cast<int8_t *>(smem + p.a_qk);
+    ao.dk = reinterpret_cast<float *>(smem + p.a_dk);
+    ao.bsk = reinterpret_cast<int16_t *>(smem + p.a_bsk);
+    ao.fmt = P.fmt;
+    ao.rounding = P.rounding;
+    if (tid < 64) reinterpret_cast<uint32_t *>(smem + p.a_zero)[tid] = 0u;
+    if (P.kind == 1) {
+        for (uint32_t sb = warp; sb < nsb; sb += kQW) {
+            const uint32_t i0 = sb * QK_K + 8 * lane;
+            float gv[8], uv[8], f[8];
+            ld8f(P.g + i0, gv);
+            ld8f(P.u + i0, uv);
+#pragma unroll
+            for (int j = 0; j < 8; j++) f[j] = kq_act(gv[j], P.act) * uv[j];
+            if (P.fmt & RCU_ACT_Q8_0) q8_0_block8(f, i0 / QK, lane, true, ao);
+            if (P.fmt & RCU_ACT_Q8K) q8_k_block8(f, sb, lane, ao);
+        }
+        return;
+    }
+    float *red = reinterpret_cast<float *>(smem + p.a_red);  // [2][kQW]
+    float v[kQProRounds][8];
+#pragma unroll
+    for (int r = 0; r < kQProRounds; r++) {
+        const uint32_t sb = warp + kQW * r;
+        if (sb < nsb) {
+            ld8f(P.x + sb * QK_K + 8 * lane, v[r]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
+        }
+    }
+    if (P.o) {
+        float ov[kQProRounds][8];
+        float ss = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kQProRounds; r++) {
+            const uint32_t sb = warp + kQW * r;
+#pragma unroll
+            for (int j = 0; j < 8; j++) ov[r][j] = 0.0f;
+            if (sb < nsb) ld8f(P.o + sb * QK_K + 8 * lane, ov[r]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) ss += ov[r][j] * ov[r][j];
+        }
+        if (P.post) {
+            ss = kq_row_sum(ss, red, warp, lane);
+            const float scale = 1.0f / sqrtf(ss / (float)k + P.eps);
+#pragma unroll
+            for (int r = 0; r < kQProRounds; r++) {
+                const uint32_t sb = warp + kQW * r;
+                if (sb < nsb) {
+                    float pw[8];
+                    ld8f(P.post + sb * QK_K + 8 * lane, pw);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) ov[r][j] *= scale * pw[j];
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kQProRounds; r++) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[r][j] += P.rs == 1.0f ? ov[r][j] : ov[r][j] * P.rs;
+            const uint32_t sb = warp + kQW * r;
+            if (blockIdx.x == 0 && sb < nsb) st8f(P.x_out + sb * QK_K + 8 * lane, v[r]);
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kQProRounds; r++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) ss += v[r][j] * v[r][j];
+    ss = kq_row_sum(ss, red + kQW, warp, lane);
+    const float scale = 1.0f / sqrtf(ss / (float)k + P.eps);
+#pragma unroll
+    for (int r = 0; r < kQProRounds; r++) {
+        const uint32_t sb = warp + kQW * r;
+        if (sb >= nsb) continue;  // uniform over the warp
+        const uint32_t i0 = sb * QK_K + 8 * lane;
+        float wv[8], xn[8];
+        ld8f(P.w + i0, wv);
+#pragma unroll
+        for (int j = 0; j < 8; j++) xn[j] = v[r][j] * scale * wv[j];
+        if (blockIdx.x == 0 && P.xn_out) st8f(P.xn_out + i0, xn);
+        if (P.fmt & RCU_ACT_Q8_0) q8_0_block8(xn, i0 / QK, lane, true, ao);
+        if (P.fmt & RCU_ACT_Q8K) q8_k_block8(xn, sb, lane, ao);
+    }
+}
+
+template <bool DBG, bool PRO>
 __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant__ KqParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     KqHdr *h = reinterpret_cast<KqHdr *>(smem);
@@ -579,12 +765,16 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
     }
 
     // ---- consumers ----
-    pdl_wait();  // the activations come from the kernel before this one
+    pdl_wait();  // the activations (or the prologue's inputs) come from the kernel before this one
+    if constexpr (PRO) {
+        kq_prologue(p, smem, threadIdx.x);
+        named_bar_sync(1, kQW * 32);
+    }
     switch (G.type) {
-        case T_Q4_K: kq_consume<T_Q4_K>(p, h, stages, G, warp, lane); break;
-        case T_Q5_K: kq_consume<T_Q5_K>(p, h, stages, G, warp, lane); break;
-        case T_Q4_0: kq_consume<T_Q4_0>(p, h, stages, G, warp, lane); break;
-        default: kq_consume<T_Q6_K>(p, h, stages, G, warp, lane); break;
+        case T_Q4_K: kq_consume<T_Q4_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
+        case T_Q5_K: kq_consume<T_Q5_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
+        case T_Q4_0: kq_consume<T_Q4_0, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
+        default: kq_consume<T_Q6_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
     }
     if (p.ar_nflag) {  // this CTA's rows are in every receive buffer: count it in
         __threadfence_system();
@@ -640,43 +830,84 @@ bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
 uint32_t kq_stage_bytes(const KqJob &jd) { return round_up_u((16u << jd.rb_log2) * jd.pstride, 128); }
 
 // Shared-memory layout: header, then the weight stages. False when two stages do not fit.
-bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p) {
-    p.stage_off = kQHdrBytes;
+// act_bytes: the prologue's activation area after the header (0: none).
+bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p, uint32_t act_bytes = 0) {
+    p.stage_off = kQHdrBytes + (act_bytes + 127) / 128 * 128;
     const uint32_t budget = (uint32_t)ctx->max_smem_optin;
     if (p.stage_off + 2 * stage_bytes > budget) return false;
     p.stages = std::min<uint32_t>(kQMaxStages, (budget - p.stage_off) / stage_bytes);
     return true;
 }
 
+// The prologue's activation area (offsets from the shared-memory base, after the header): 256
+// zero bytes, the Q8_K row (codes, d, bsums) and / or the Q8_0 row (codes, d, s, code sums), the
+// RMS partials. Returns its size.
+uint32_t kq_act_layout(uint32_t k, uint32_t fmt, KqParams *p) {
+    uint32_t off = kQHdrBytes;
+    auto take = [&](uint32_t bytes) {
+        const uint32_t o = off;
+        off = round_up_u(off + bytes, 16);
+        return o;
+    };
+    const uint32_t zero = take(256), red = take(2 * kQW * 4);
+    uint32_t qk = 0, dk = 0, bsk = 0, q0 = 0, d0 = 0, s0 = 0, sum0 = 0;
+    if (fmt & RCU_ACT_Q8K) qk = take(k), dk = take(k / QK_K * 4), bsk = take(k / 16 * 2);
+    if (fmt & RCU_ACT_Q8_0) q0 = take(k), d0 = take(k / QK * 4), s0 = take(k / QK * 4), sum0 = take(k / QK * 4);
+    if (p) {
+        p->a_zero = zero, p->a_red = red, p->a_qk = qk, p->a_dk = dk, p->a_bsk = bsk;
+        p->a_q0 = q0, p->a_d0 = d0, p->a_s0 = s0, p->a_sum0 = sum0;
+    }
+    return off - kQHdrBytes;
+}
+
 }  // namespace
 
+static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes);
+
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
+    return kq_ok(ctx, a.k, a.have, jobs, n_jobs, 0);
+}
+
+bool gemv_kq_pro_ok(const rcu_ctx *ctx, uint32_t k, uint32_t fmt, const HostJob *jobs, int n_jobs) {
+    if (k % QK_K != 0) return false;
+    return kq_ok(ctx, k, fmt, jobs, n_jobs, kq_act_layout(k, fmt, nullptr));
+}
+
+static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes) {
     if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs) return false;
     for (int i = 0; i < n_jobs; i++)
-        if (!(a.have & act_format(jobs[i].w->type))) return false;
+        if (!(have & act_format(jobs[i].w->type))) return false;
     // Q4_0 rows shorter than 4096 values stay on the lane GEMV, which measured faster there
     // (config 1, 6144 x 2048: 3.5 vs 2.8 TB/s; 2 x 28672 x 8192: 2.7 vs 3.8 TB/s here)
     for (int i = 0; i < n_jobs; i++)
-        if (jobs[i].w->type == T_Q4_0 && a.k < 4096) return false;
+        if (jobs[i].w->type == T_Q4_0 && k < 4096) return false;
     uint64_t bytes = 0;
     uint32_t stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {
         KqJob jd{};
-        if (!kq_plan(jobs[i].w, a.k, jd)) return false;
+        if (!kq_plan(jobs[i].w, k, jd)) return false;
         if (jobs[i].sel && jobs[i].w_stride % 16 != 0) return false;
         bytes += (uint64_t)(jobs[i].rows ? jobs[i].rows : jobs[i].w->rows) * jobs[i].w->row_bytes;
         stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd));
     }
     KqParams lay;
-    if (!kq_smem_layout(ctx, stage_bytes, lay)) return false;
+    if (!kq_smem_layout(ctx, stage_bytes, lay, act_bytes)) return false;
     // Small launches take the lane GEMV: with 1-2 tiles per CTA this kernel's start-up is not
     // hidden; K = 768 expert rows also give it few tiles.
     return bytes >= ctx->gemv_kq_min_bytes;
 }
 
 int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
-                   const ArPush *push) {
+                   const ArPush *push, const GemvPrologue *pro) {
     KqParams p{};
+    uint32_t act_bytes = 0;
+    if (pro) {
+        if (tok0 != 0 || a.k % QK_K != 0 || (pro->kind == 2 && a.k > kQProRounds * kQW * QK_K) ||
+            (pro->kind != 1 && pro->kind != 2) || (pro->kind == 2 && pro->x_out == pro->x))
+            return set_err(ctx, RCU_ERR_INVALID, "gemv prologue: one row of k <= 8192 (norm) values, x_out apart from x");
+        p.pro = *pro;
+        act_bytes = kq_act_layout(a.k, pro->fmt, &p);
+    }
     p.n_jobs = n_jobs;
     p.k = a.k;
     p.tok0 = tok0;
@@ -741,18 +972,27 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
-    if (!kq_smem_layout(ctx, stage_bytes, p))
+    if (!kq_smem_layout(ctx, stage_bytes, p, act_bytes))
         return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: two weight stages exceed shared memory");
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = cta;
     if (push && grid > kArUnit) return set_err(ctx, RCU_ERR_INVALID, "gemv: grid above the all-reduce counter unit");
-    static std::atomic<bool> attr_set[64] = {};  // per device; contexts may live on several threads
-    if (!attr_set[ctx->device & 63].load(std::memory_order_acquire)) {
-        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemv_kq, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)ctx->max_smem_optin));
-        attr_set[ctx->device & 63].store(true, std::memory_order_release);
+    const bool dbg = ctx->dbg_sums != nullptr;
+    if (dbg) {
+        if (n_jobs != 1 || push) return set_err(ctx, RCU_ERR_INVALID, "block-sum capture: one job, no push");
+        p.dbg = ctx->dbg_sums;
+        p.dbg_nbs = ctx->dbg_nbs;
     }
-    RCU_CUDA_TRY(ctx, launch_k(ctx, k_gemv_kq, dim3(grid), dim3(kQThreads), smem_bytes, p));
+    if (dbg && pro) return set_err(ctx, RCU_ERR_INVALID, "block-sum capture: no prologue");
+    auto kern = dbg ? k_gemv_kq<true, false> : pro ? k_gemv_kq<false, true> : k_gemv_kq<false, false>;
+    static std::atomic<bool> attr_set[3][64] = {};  // per instantiation and device; contexts may live on several threads
+    std::atomic<bool> &set = attr_set[dbg ? 1 : pro ? 2 : 0][ctx->device & 63];
+    if (!set.load(std::memory_order_acquire)) {
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)ctx->max_smem_optin));
+        set.store(true, std::memory_order_release);
+    }
+    RCU_CUDA_TRY(ctx, launch_k(ctx, kern, dim3(grid), dim3(kQThreads), smem_bytes, p));
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
 }

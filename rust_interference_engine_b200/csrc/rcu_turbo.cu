@@ -805,7 +805,7 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
         const uint64_t cap = window > 0 ? std::min<uint64_t>(window, kv->slots) : kv->slots;
         const uint64_t last = pos0 + n_tok - 1;
         const uint64_t max_len = n_split != 0 ? cap : (window > 0 ? std::min<uint64_t>(window, last + 1) : last + 1);
-        const uint64_t parts = n_tok * n_head * attention_dec_max_clusters(max_len, n_tok, kv->n_kv, ctx->num_sms);
+        const uint64_t parts = n_tok * n_head * attention_dec_max_clusters(kv->type, max_len, n_tok, kv->n_kv, ctx->num_sms);
         uint8_t *scr = reinterpret_cast<uint8_t *>(scratch);
         if (!scr) {
             void *v = nullptr;

@@ -35,8 +35,52 @@ __host__ __device__ inline uint32_t turbo_block(uint32_t d) {  // turbo.rs:52-58
 }
 __host__ __device__ inline uint32_t turbo_row_bytes(uint32_t d) { return 2 * (d / turbo_block(d)) + d / 2; }
 
+// rotate_row for rows that are one rotation block of 32 V values: lane l holds values V l ..
+// V l + V - 1 in registers; the butterflies of stride h < V stay in the lane, those of stride
+// h >= V pair lanes l and l ^ (h / V) through a shuffle. The same pairs in the same order of
+// strides as rotate_row below, with the same IEEE operations, so the results are identical.
+template <int V>
+static __device__ __forceinline__ void rotate_regs(float *x, bool inverse, int lane) {
+    float v[V];
+#pragma unroll
+    for (int i = 0; i < V; i++) v[i] = x[V * lane + i];
+    if (!inverse)
+#pragma unroll
+        for (int i = 0; i < V; i++) v[i] = __fmul_rn(v[i], c_signs[V * lane + i]);
+#pragma unroll
+    for (int h = 1; h < V; h <<= 1)
+#pragma unroll
+        for (int i = 0; i < V; i++)
+            if ((i & h) == 0) {
+                const float a = v[i], c = v[i + h];
+                v[i] = __fadd_rn(a, c);
+                v[i + h] = __fsub_rn(a, c);
+            }
+#pragma unroll
+    for (int hl = 1; hl < 32; hl <<= 1) {
+        const bool upper = (lane & hl) != 0;
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], hl);
+            v[i] = upper ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+        }
+    }
+    const float s = 1.0f / sqrtf((float)(32 * V));
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        float o = __fmul_rn(v[i], s);
+        if (inverse) o = __fmul_rn(o, c_signs[V * lane + i]);
+        x[V * lane + i] = o;
+    }
+    __syncwarp();
+}
+
 // x <- R x (signs then normalised block FWHT) or x <- R^T x, on a warp-owned shared row.
 static __device__ void rotate_row(float *x, uint32_t d, bool inverse, int lane) {
+    __syncwarp();
+    if (d == 128) return rotate_regs<4>(x, inverse, lane);
+    if (d == 64) return rotate_regs<2>(x, inverse, lane);
+    if (d == 256) return rotate_regs<8>(x, inverse, lane);
     const uint32_t b = turbo_block(d);
     if (!inverse)
         for (uint32_t i = lane; i < d; i += 32) x[i] = __fmul_rn(x[i], c_signs[i]);
