@@ -846,7 +846,7 @@ def run_moe(args, world, rank, local):
                    "decode": "CUDA graph replay per token", "model_build_s": t_build},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": profile_traffic("gemv_q4_k_moe_experts"),
-                     "kernel": "k_gemv<1,16> (8 experts' gate+up, 16 x 768 x 2048 Q4_K)",
+                     "kernel": gemv_kernel_name("Q4_K", gemv_bytes) + " (8 experts' gate+up, 16 x 768 x 2048 Q4_K)",
                      "bytes_per_launch": gemv_bytes, "launch_ms": gemv_ms,
                      "whole_step_weight_gb_s": wb / (ms * 1e-3) / 1e9},
         "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.n_vocab * 4,
@@ -1204,7 +1204,9 @@ def run_llama70b(args, world, rank, local):
                    "parallelism": f"tp{world} (all-reduce of Wo/down, all-gather of logits)" if world > 1 else "tp1",
                    "decode": "CUDA graph replay per token", "model_build_s": t_build, "kv_fill_s": t_fill},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": None,
+                     "peak_source": peak_kind,
+                     # ncu figure of the one-GPU launch (the tensor-parallel shards are 1/N of it)
+                     "traffic": profile_traffic("gemv_kq_q4_0_gate_up_70b") if world == 1 else None,
                      "kernel": gemv_kernel_name("Q4_0", gemv_bytes) + f" (gate+up, 2 x {ff} x 8192 Q4_0, this rank's shard)",
                      "bytes_per_launch": gemv_bytes, "launch_ms": gemv_ms,
                      "timing": "20 launches over 2 distinct weight pairs in one CUDA graph",

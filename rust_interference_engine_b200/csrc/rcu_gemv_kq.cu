@@ -568,8 +568,8 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
 // 8 values per lane: round r of warp w is superblock w + 8r (values 8 lane .. 8 lane + 7), the
 // layout the quantizers q8_k_block8 / q8_0_block8 take. Sums over the row (RMS) go through the
 // warps' partials in shared memory (two slots: the post-norm of o, then the norm of v).
-__device__ __forceinline__ float kq_act(float a, int act) {  // ops.rs:41-58, as k_glu_q8
-    return act == 1 ? 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a))) : a / (1.0f + expf(-a));
+__device__ __forceinline__ float kq_act(float a, int act) {  // ops.rs:41-58 (SiLU with the SFU exponential)
+    return act == 1 ? 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a))) : a / (1.0f + __expf(-a));
 }
 __device__ __forceinline__ void ld8f(const float *p, float (&v)[8]) {
     const float4 a = __ldcg(reinterpret_cast<const float4 *>(p)), b = __ldcg(reinterpret_cast<const float4 *>(p) + 1);
@@ -792,7 +792,7 @@ uint32_t round_up_u(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 // stage rb (so that the kQW / rb warps of a block have a superblock each), stage bytes
 // <= 64 KB. Prefers slices the block's warps split evenly, then slices of two superblocks
 // per warp (two independent chains), then longer slices.
-bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
+bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd, uint32_t max_stage = kQMaxStage) {
     const int t = w->type;
     if (t != T_Q4_K && t != T_Q5_K && t != T_Q6_K && t != T_Q4_0) return false;
     if (w->cols != k || k % QK_K != 0 || w->row_bytes % 16 != 0 || ((uintptr_t)w->data & 15u)) return false;
@@ -807,7 +807,7 @@ bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
         while ((uint32_t)(kQW >> rbl0) > sl && rbl0 < (uint32_t)kQWLog2) rbl0++;
         // taller stages (more 16-row blocks, fewer warps per block) give each warp two units
         for (uint32_t rbl = rbl0; rbl <= (uint32_t)kQWLog2; rbl++) {
-            if ((16u << rbl) * ps > kQMaxStage) break;
+            if ((16u << rbl) * ps > max_stage) break;
             const uint32_t wpb = kQW >> rbl, per = (sl + wpb - 1) / wpb;
             const double bal = (double)sl / (double)(wpb * per);
             const double score = bal * 8.0 + (per == 2 ? 2.0 : 0.0) + (double)sl / nsb - 0.01 * rbl;
@@ -864,13 +864,36 @@ uint32_t kq_act_layout(uint32_t k, uint32_t fmt, KqParams *p) {
 
 static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes);
 
+// The stage-size limit that keeps the most weight bytes in flight once act_bytes of shared
+// memory go to the prologue's activations (the default 64 KB stages can lose a whole stage to a
+// few KB; smaller ones fit more stages).
+static uint32_t kq_max_stage(const rcu_ctx *ctx, uint32_t k, const HostJob *jobs, int n_jobs, uint32_t act_bytes) {
+    uint32_t best = kQMaxStage;
+    uint64_t best_ring = 0;
+    for (const uint32_t cand : {kQMaxStage, 48u * 1024u, 32u * 1024u}) {
+        uint32_t stage = 0;
+        bool ok = true;
+        for (int i = 0; i < n_jobs && ok; i++) {
+            KqJob jd{};
+            ok = kq_plan(jobs[i].w, k, jd, cand);
+            stage = std::max(stage, kq_stage_bytes(jd));
+        }
+        KqParams lay;
+        if (!ok || !kq_smem_layout(ctx, stage, lay, act_bytes)) continue;
+        const uint64_t ring = (uint64_t)lay.stages * stage;
+        if (ring > best_ring) best_ring = ring, best = cand;
+    }
+    return best;
+}
+
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     return kq_ok(ctx, a.k, a.have, jobs, n_jobs, 0);
 }
 
 bool gemv_kq_pro_ok(const rcu_ctx *ctx, uint32_t k, uint32_t fmt, const HostJob *jobs, int n_jobs) {
     if (k % QK_K != 0) return false;
-    return kq_ok(ctx, k, fmt, jobs, n_jobs, kq_act_layout(k, fmt, nullptr));
+    const uint32_t act = kq_act_layout(k, fmt, nullptr);
+    return kq_ok(ctx, k, fmt, jobs, n_jobs, act);
 }
 
 static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes) {
@@ -908,6 +931,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         p.pro = *pro;
         act_bytes = kq_act_layout(a.k, pro->fmt, &p);
     }
+    const uint32_t max_stage = pro ? kq_max_stage(ctx, a.k, jobs, n_jobs, act_bytes) : kQMaxStage;
     p.n_jobs = n_jobs;
     p.k = a.k;
     p.tok0 = tok0;
@@ -934,7 +958,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         for (int i = 0; i < n_jobs; i++) {
             if (jobs[i].w->type != ty) continue;
             KqJob &jd = p.jobs[nj++];
-            if (!kq_plan(jobs[i].w, a.k, jd))
+            if (!kq_plan(jobs[i].w, a.k, jd, max_stage))
                 return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: weight not K-quant tileable");
             jd.w = jobs[i].w->data;
             jd.out = jobs[i].out + (jobs[i].sel ? 0 : (uint64_t)tok0 * jobs[i].ld);  // indirect jobs: own rows
