@@ -80,7 +80,7 @@ struct rcu_backend {
     const float *out_norm = nullptr;
     std::vector<rcu_kv *> kv;
     rcu_acts *acts = nullptr;
-    float *x = nullptr, *x2 = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
     float *g = nullptr, *u = nullptr, *logits = nullptr, *inv_freq = nullptr, *inv_freq_swa = nullptr;
     uint32_t *tokens = nullptr;
     uint64_t *pos_dev = nullptr;  // position of the batch, read by the kernels (graph replay)
@@ -876,31 +876,10 @@ static int forward_span(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logi
     }
     // [residual +] RMSNorm + quantize (its own kernel), then the matmuls that consume it.
     // x_ready: x was written three or more launches back (the norm kernel may load it early).
-    // Decode (one row, one GPU or NCCL all-reduces): the tensor-core GEMV computes the norm
-    // itself when it takes every job; the updated residual goes to the spare buffer, which
-    // becomes b->x (every CTA of that launch reads the old one).
-    const bool pro_ok = ctx->gemv_prologue && n == 1 && e % QK_K == 0 && e <= 8192;
     auto norm_matmul = [&](uint64_t rows, uint64_t row0, const float *o, const float *post, const float *w,
                            float *xn_f32, bool x_ready, const ArSum &ar, std::vector<rcu_job> jobs) -> int {
         uint32_t fmt = 0;
         for (auto &j : jobs) fmt |= act_format(j.w->type);
-        if (pro_ok && rows == 1 && row0 == 0 && !ar.P && jobs.size() <= 8) {
-            HostJob hj[8];
-            for (size_t i = 0; i < jobs.size(); i++) hj[i] = HostJob{jobs[i].w, jobs[i].out, jobs[i].ld};
-            if (gemv_kq_pro_ok(ctx, e, fmt, hj, (int)jobs.size())) {
-                GemvPrologue pro;
-                pro.kind = 2, pro.fmt = fmt, pro.x = b->x, pro.o = o, pro.post = post, pro.w = w;
-                pro.rs = c.residual_scale, pro.eps = c.rms_eps, pro.x_out = b->x2, pro.xn_out = xn_f32;
-                pro.rounding = ctx->rounding;
-                ActsView a{};
-                a.k = e;
-                a.n_tok = 1;
-                a.have = fmt;
-                if (int st = launch_gemv_kq(ctx, a, hj, (int)jobs.size(), 0, nullptr, &pro)) return st;
-                if (o) std::swap(b->x, b->x2);
-                return RCU_OK;
-            }
-        }
         ArSum a = ar;
         if (a.P) a.src += row0 * e;
         if (int st = norm_q(b, rows, b->x + row0 * e, o ? o + row0 * e : nullptr, post, w, xn_f32, fmt, x_ready, a))
@@ -978,23 +957,8 @@ static int forward_span(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logi
                               {{L.gate, b->g, ff}, {L.up, b->u, ff}})))
             return st;
         const uint32_t fd = formats({L.down});
-        const HostJob dj{L.down, b->o, e};
-        if (pro_ok && !fused && ff % QK_K == 0 && gemv_kq_pro_ok(ctx, ff, fd, &dj, 1)) {
-            // SwiGLU / GELU computed by the down GEMV itself
-            GemvPrologue pro;
-            pro.kind = 1, pro.fmt = fd, pro.g = b->g, pro.u = b->u, pro.act = c.act, pro.rounding = ctx->rounding;
-            ActsView a{};
-            a.k = ff;
-            a.n_tok = 1;
-            a.have = fd;
-            if ((st = launch_gemv_kq(ctx, a, &dj, 1, 0, nullptr, &pro))) return st;
-            if ((st = all_reduce(b->o, n * e))) return st;
-            ar_j++;
-            pend_ar = ArSum{};
-        } else {
-            if ((st = launch_glu(ctx, b->g, b->u, ff, (uint32_t)n, c.act, acts_out(b, fd)))) return st;
-            if ((st = row_parallel(L.down, ff, ar_j++, &pend_ar))) return st;
-        }
+        if ((st = launch_glu(ctx, b->g, b->u, ff, (uint32_t)n, c.act, acts_out(b, fd)))) return st;
+        if ((st = row_parallel(L.down, ff, ar_j++, &pend_ar))) return st;
         pend_o = fused ? nullptr : b->o;
         pend_post = L.post_ffn;
     }
@@ -1584,7 +1548,7 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     struct {
         float **p;
         uint64_t n;
-    } bufs[] = {{&b->x, T * e}, {&b->x2, T * e}, {&b->xn, T * e}, {&b->q, T * qd}, {&b->k, T * kvd}, {&b->v, T * kvd}, {&b->att, T * qd},
+    } bufs[] = {{&b->x, T * e}, {&b->xn, T * e}, {&b->q, T * qd}, {&b->k, T * kvd}, {&b->v, T * kvd}, {&b->att, T * qd},
                 {&b->o, T * e}, {&b->g, T * b->ff_max}, {&b->u, T * b->ff_max},
                 {&b->logits, T * (uint64_t)c.n_vocab * P}, {&b->logits_local, P > 1 ? T * (uint64_t)c.n_vocab : 1},
                 {&b->logits_gather, P > 1 ? T * (uint64_t)c.n_vocab * P : 1}};

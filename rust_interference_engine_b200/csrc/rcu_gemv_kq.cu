@@ -55,7 +55,6 @@
 #include <algorithm>
 #include <atomic>
 
-#include "rcu_actq.cuh"
 #include "rcu_blocks.cuh"
 #include "rcu_kernels.h"
 
@@ -115,10 +114,6 @@ struct KqParams {
     // dbg[row * dbg_nbs + i]
     int32_t *dbg;
     uint32_t dbg_nbs;
-    // activation prologue (the k_gemv_kq<false, true> instantiation): the launch computes its
-    // one activation row into shared memory at these byte offsets
-    GemvPrologue pro;
-    uint32_t a_zero, a_qk, a_dk, a_bsk, a_q0, a_d0, a_s0, a_sum0, a_red;
 };
 
 struct KqHdr {
@@ -163,57 +158,39 @@ struct ActR {
     float d;
 };
 
-// Activation loads: read-only global memory (a prepared ActsView), or this CTA's shared memory
-// (SM: the activations the launch computed itself).
-template <bool SM>
-__device__ __forceinline__ uint32_t lda32(const void *p) {
-    if constexpr (SM) return *reinterpret_cast<const uint32_t *>(p);
-    else return __ldg(reinterpret_cast<const uint32_t *>(p));
-}
-template <bool SM>
-__device__ __forceinline__ uint2 lda64(const void *p) {
-    if constexpr (SM) return *reinterpret_cast<const uint2 *>(p);
-    else return __ldg(reinterpret_cast<const uint2 *>(p));
-}
-template <bool SM>
-__device__ __forceinline__ uint4 lda128(const void *p) {
-    if constexpr (SM) return *reinterpret_cast<const uint4 *>(p);
-    else return __ldg(reinterpret_cast<const uint4 *>(p));
-}
-
-// zero: 256 zero bytes (the activations of threads whose B column is zero).
-template <int TYPE, bool SM>
-__device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, const uint8_t *zero,
-                                         uint32_t sb, uint32_t c, bool bact, ActR &a) {
+template <int TYPE>
+__device__ __forceinline__ void load_act(const int8_t *aq, const float *adk, const uint32_t *abw, uint32_t sb,
+                                         uint32_t c, bool bact, ActR &a) {
     if (TYPE == T_Q4_0) {  // unit sb = Q8_0 blocks 8 sb .. 8 sb + 7; adk = d0 row, abw = sum0 row
         const uint8_t *x = reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 4 * c;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            a.x[2 * j] = lda32<SM>(x + 32 * j);
-            a.x[2 * j + 1] = lda32<SM>(x + 32 * j + 16);
+            a.x[2 * j] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j));
+            a.x[2 * j + 1] = __ldg(reinterpret_cast<const uint32_t *>(x + 32 * j + 16));
         }
-        a.bs = make_uint4(lda32<SM>(adk + 8 * sb + c), lda32<SM>(adk + 8 * sb + 4 + c), lda32<SM>(abw + 8 * sb + c),
-                          lda32<SM>(abw + 8 * sb + 4 + c));
+        a.bs = make_uint4(__float_as_uint(__ldg(adk + 8 * sb + c)), __float_as_uint(__ldg(adk + 8 * sb + 4 + c)),
+                          __ldg(abw + 8 * sb + c), __ldg(abw + 8 * sb + 4 + c));
         a.d = 0.0f;
         return;
     }
-    a.d = __uint_as_float(lda32<SM>(adk + sb));
+    a.d = __ldg(adk + sb);
     if (TYPE == T_Q6_K) {
         const uint32_t n = c >> 1, h = c & 1u;
-        const uint8_t *xa = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 128 * n + 16 * h : zero;
+        const uint8_t *xa = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 128 * n + 16 * h : g_kq_zero;
 #pragma unroll
         for (int m = 0; m < 4; m++)
 #pragma unroll
-            for (int i = 0; i < 4; i++) a.x[4 * m + i] = lda32<SM>(xa + 32 * m + 4u * ((i + c) & 3u));
-        a.bs = lda128<SM>(abw + 8 * sb + 4 * n);
+            for (int i = 0; i < 4; i++)
+                a.x[4 * m + i] = __ldg(reinterpret_cast<const uint32_t *>(xa + 32 * m + 4u * ((i + c) & 3u)));
+        a.bs = ldg128(abw + 8 * sb + 4 * n);
     } else {
-        const uint8_t *x = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 64 * c : zero;
+        const uint8_t *x = bact ? reinterpret_cast<const uint8_t *>(aq) + (size_t)sb * QK_K + 64 * c : g_kq_zero;
         uint32_t lo[8], hi[8];
-        words8(lda128<SM>(x), lda128<SM>(x + 16), lo);
-        words8(lda128<SM>(x + 32), lda128<SM>(x + 48), hi);
+        words8(ldg128(x), ldg128(x + 16), lo);
+        words8(ldg128(x + 32), ldg128(x + 48), hi);
 #pragma unroll
         for (int i = 0; i < 8; i++) a.x[i] = lo[i], a.x[8 + i] = hi[i];
-        const uint2 b = lda64<SM>(abw + 8 * sb + 2 * c);
+        const uint2 b = __ldg(reinterpret_cast<const uint2 *>(abw + 8 * sb + 2 * c));
         a.bs = make_uint4(b.x, b.y, 0u, 0u);
     }
 }
@@ -415,10 +392,9 @@ struct Ring {  // consumer-side stage ring position
 // independent accumulators (two mma chains in flight) and their activations loaded before
 // the stage wait. Row partials of group gi end in accA[gi] (row g of the warp's 16-row
 // block) / accB[gi] (row g + 8).
-template <int TYPE, bool DBG, bool PRO>
+template <int TYPE, bool DBG>
 __device__ __forceinline__ bool kq_tile(const KqParams &p, KqHdr *h, uint8_t *stages, const JobR &J, uint32_t ngrp,
                                         bool skip, const int8_t *aq, const float *adk, const uint32_t *abw,
-                                        const uint8_t *zero,
                                         uint32_t rbk, uint32_t part, uint32_t wpb, uint32_t g, uint32_t c, bool bact,
                                         uint32_t lane, Ring &R, float (&accA)[kQG], float (&accB)[kQG], uint32_t r0) {
     const uint32_t S = p.stages;
@@ -439,8 +415,8 @@ __device__ __forceinline__ bool kq_tile(const KqParams &p, KqHdr *h, uint8_t *st
             ActR A0, A1;
             const bool two = sbl + wpb < J.sl;
             if (!skip) {
-                load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl, c, bact, A0);
-                if (two) load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl + wpb, c, bact, A1);
+                load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
+                if (two) load_act<TYPE>(aq, adk, abw, sb0 + sbl + wpb, c, bact, A1);
             }
             if (!mbar_wait_bounded(&h->full[R.s], R.ph, p.err, ERR_TIMEOUT_FULL)) return false;
             if (!skip) {
@@ -455,7 +431,7 @@ __device__ __forceinline__ bool kq_tile(const KqParams &p, KqHdr *h, uint8_t *st
                     sbl += wpb;
                 }
                 for (; sbl < J.sl; sbl += wpb) {  // slices wider than two superblocks per warp
-                    load_act<TYPE, PRO>(aq, adk, abw, zero, sb0 + sbl, c, bact, A0);
+                    load_act<TYPE>(aq, adk, abw, sb0 + sbl, c, bact, A0);
                     kq_block<TYPE, DBG>(ra, rb, sbl, A0, c, a1, b1, dA, dB, sb0 + sbl);
                 }
             }
@@ -478,9 +454,9 @@ __device__ __forceinline__ void kq_store(const KqParams &p, float *out, uint32_t
 }
 
 // Consumer warps of a CTA whose tiles all hold weights of type TYPE.
-template <int TYPE, bool DBG, bool PRO>
-__device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t *smem, uint8_t *stages,
-                                           const KqGroup &G, int warp, int lane) {
+template <int TYPE, bool DBG>
+__device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t *stages, const KqGroup &G, int warp,
+                                           int lane) {
     const uint32_t g = lane >> 2, c = lane & 3;
     const bool bact = c == (g >> 1);
     const ActsView &AV = p.acts;
@@ -504,27 +480,15 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
         const uint64_t trow = (uint64_t)p.tok0 + J.tok;
         // Q8_K rows (codes, superblock scales, bsum pairs) or, for Q4_0, Q8_0 rows (codes, block
         // scales, exact code sums)
-        const int8_t *aq;
-        const float *adk;
-        const uint32_t *abw;
-        const uint8_t *zero;
-        if constexpr (PRO) {  // the row this launch computed, in shared memory
-            aq = reinterpret_cast<const int8_t *>(smem + (TYPE == T_Q4_0 ? p.a_q0 : p.a_qk));
-            adk = reinterpret_cast<const float *>(smem + (TYPE == T_Q4_0 ? p.a_d0 : p.a_dk));
-            abw = reinterpret_cast<const uint32_t *>(smem + (TYPE == T_Q4_0 ? p.a_sum0 : p.a_bsk));
-            zero = smem + p.a_zero;
-        } else {
-            aq = TYPE == T_Q4_0 ? AV.q0 + trow * k : AV.qk + trow * k;
-            adk = TYPE == T_Q4_0 ? AV.d0 + trow * (k / QK) : AV.dk + trow * nsb;
-            abw = TYPE == T_Q4_0 ? reinterpret_cast<const uint32_t *>(AV.sum0 + trow * (k / QK))
-                                 : reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
-            zero = g_kq_zero;
-        }
+        const int8_t *aq = TYPE == T_Q4_0 ? AV.q0 + trow * k : AV.qk + trow * k;
+        const float *adk = TYPE == T_Q4_0 ? AV.d0 + trow * (k / QK) : AV.dk + trow * nsb;
+        const uint32_t *abw = TYPE == T_Q4_0 ? reinterpret_cast<const uint32_t *>(AV.sum0 + trow * (k / QK))
+                                             : reinterpret_cast<const uint32_t *>(AV.bsk + trow * (k / 16));
         float accA[kQG], accB[kQG];
 #pragma unroll
         for (int gi = 0; gi < kQG; gi++) accA[gi] = accB[gi] = 0.0f;
-        if (!kq_tile<TYPE, DBG, PRO>(p, h, stages, J, ngrp, skip, aq, adk, abw, zero, rbk, part, wpb, g, c, bact, lane,
-                                     R, accA, accB, r0))
+        if (!kq_tile<TYPE, DBG>(p, h, stages, J, ngrp, skip, aq, adk, abw, rbk, part, wpb, g, c, bact, lane, R, accA,
+                                accB, r0))
             return;
         // tile done: the 4 threads of each row add their shares, every warp publishes its rows'
         // partials; the last warp to arrive adds the parts in warp order and stores
@@ -564,129 +528,7 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
     }
 }
 
-// The consumer warps compute the launch's activation row into shared memory (GemvPrologue),
-// 8 values per lane: round r of warp w is superblock w + 8r (values 8 lane .. 8 lane + 7), the
-// layout the quantizers q8_k_block8 / q8_0_block8 take. Sums over the row (RMS) go through the
-// warps' partials in shared memory (two slots: the post-norm of o, then the norm of v).
-__device__ __forceinline__ float kq_act(float a, int act) {  // ops.rs:41-58 (SiLU with the SFU exponential)
-    return act == 1 ? 0.5f * a * (1.0f + tanhf(0.7978846f * a * (1.0f + 0.044715f * a * a))) : a / (1.0f + __expf(-a));
-}
-__device__ __forceinline__ void ld8f(const float *p, float (&v)[8]) {
-    const float4 a = __ldcg(reinterpret_cast<const float4 *>(p)), b = __ldcg(reinterpret_cast<const float4 *>(p) + 1);
-    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-}
-__device__ __forceinline__ void st8f(float *p, const float (&v)[8]) {
-    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
-}
-__device__ __forceinline__ float kq_row_sum(float v, float *red, uint32_t warp, uint32_t lane) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[warp] = v;
-    named_bar_sync(1, kQW * 32);
-    float s = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kQW; w++) s += red[w];
-    return s;
-}
-constexpr int kQProRounds = 4;  // rows of up to 8192 values (kind 2)
-
-__device__ void kq_prologue(const KqParams &p, uint8_t *smem, uint32_t tid) {
-    const GemvPrologue &P = p.pro;
-    const uint32_t k = p.k, warp = tid >> 5, lane = tid & 31, nsb = k / QK_K;
-    ActOut ao{};
-    ao.q0 = reinterpret_cast<int8_t *>(smem + p.a_q0);
-    ao.d0 = reinterpret_cast<float *>(smem + p.a_d0);
-    ao.s0 = reinterpret_cast<float *>(smem + p.a_s0);
-    ao.sum0 = reinterpret_cast<int32_t *>(smem + p.a_sum0);
-    ao.qk = reinterpret_cast<int8_t *>(smem + p.a_qk);
-    ao.dk = reinterpret_cast<float *>(smem + p.a_dk);
-    ao.bsk = reinterpret_cast<int16_t *>(smem + p.a_bsk);
-    ao.fmt = P.fmt;
-    ao.rounding = P.rounding;
-    if (tid < 64) reinterpret_cast<uint32_t *>(smem + p.a_zero)[tid] = 0u;
-    if (P.kind == 1) {
-        for (uint32_t sb = warp; sb < nsb; sb += kQW) {
-            const uint32_t i0 = sb * QK_K + 8 * lane;
-            float gv[8], uv[8], f[8];
-            ld8f(P.g + i0, gv);
-            ld8f(P.u + i0, uv);
-#pragma unroll
-            for (int j = 0; j < 8; j++) f[j] = kq_act(gv[j], P.act) * uv[j];
-            if (P.fmt & RCU_ACT_Q8_0) q8_0_block8(f, i0 / QK, lane, true, ao);
-            if (P.fmt & RCU_ACT_Q8K) q8_k_block8(f, sb, lane, ao);
-        }
-        return;
-    }
-    float *red = reinterpret_cast<float *>(smem + p.a_red);  // [2][kQW]
-    float v[kQProRounds][8];
-#pragma unroll
-    for (int r = 0; r < kQProRounds; r++) {
-        const uint32_t sb = warp + kQW * r;
-        if (sb < nsb) {
-            ld8f(P.x + sb * QK_K + 8 * lane, v[r]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[r][j] = 0.0f;
-        }
-    }
-    if (P.o) {
-        float ov[kQProRounds][8];
-        float ss = 0.0f;
-#pragma unroll
-        for (int r = 0; r < kQProRounds; r++) {
-            const uint32_t sb = warp + kQW * r;
-#pragma unroll
-            for (int j = 0; j < 8; j++) ov[r][j] = 0.0f;
-            if (sb < nsb) ld8f(P.o + sb * QK_K + 8 * lane, ov[r]);
-#pragma unroll
-            for (int j = 0; j < 8; j++) ss += ov[r][j] * ov[r][j];
-        }
-        if (P.post) {
-            ss = kq_row_sum(ss, red, warp, lane);
-            const float scale = 1.0f / sqrtf(ss / (float)k + P.eps);
-#pragma unroll
-            for (int r = 0; r < kQProRounds; r++) {
-                const uint32_t sb = warp + kQW * r;
-                if (sb < nsb) {
-                    float pw[8];
-                    ld8f(P.post + sb * QK_K + 8 * lane, pw);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) ov[r][j] *= scale * pw[j];
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < kQProRounds; r++) {
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[r][j] += P.rs == 1.0f ? ov[r][j] : ov[r][j] * P.rs;
-            const uint32_t sb = warp + kQW * r;
-            if (blockIdx.x == 0 && sb < nsb) st8f(P.x_out + sb * QK_K + 8 * lane, v[r]);
-        }
-    }
-    float ss = 0.0f;
-#pragma unroll
-    for (int r = 0; r < kQProRounds; r++)
-#pragma unroll
-        for (int j = 0; j < 8; j++) ss += v[r][j] * v[r][j];
-    ss = kq_row_sum(ss, red + kQW, warp, lane);
-    const float scale = 1.0f / sqrtf(ss / (float)k + P.eps);
-#pragma unroll
-    for (int r = 0; r < kQProRounds; r++) {
-        const uint32_t sb = warp + kQW * r;
-        if (sb >= nsb) continue;  // uniform over the warp
-        const uint32_t i0 = sb * QK_K + 8 * lane;
-        float wv[8], xn[8];
-        ld8f(P.w + i0, wv);
-#pragma unroll
-        for (int j = 0; j < 8; j++) xn[j] = v[r][j] * scale * wv[j];
-        if (blockIdx.x == 0 && P.xn_out) st8f(P.xn_out + i0, xn);
-        if (P.fmt & RCU_ACT_Q8_0) q8_0_block8(xn, i0 / QK, lane, true, ao);
-        if (P.fmt & RCU_ACT_Q8K) q8_k_block8(xn, sb, lane, ao);
-    }
-}
-
-template <bool DBG, bool PRO>
+template <bool DBG>
 __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant__ KqParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     KqHdr *h = reinterpret_cast<KqHdr *>(smem);
@@ -765,16 +607,12 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
     }
 
     // ---- consumers ----
-    pdl_wait();  // the activations (or the prologue's inputs) come from the kernel before this one
-    if constexpr (PRO) {
-        kq_prologue(p, smem, threadIdx.x);
-        named_bar_sync(1, kQW * 32);
-    }
+    pdl_wait();  // the activations come from the kernel before this one
     switch (G.type) {
-        case T_Q4_K: kq_consume<T_Q4_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
-        case T_Q5_K: kq_consume<T_Q5_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
-        case T_Q4_0: kq_consume<T_Q4_0, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
-        default: kq_consume<T_Q6_K, DBG, PRO>(p, h, smem, stages, G, warp, lane); break;
+        case T_Q4_K: kq_consume<T_Q4_K, DBG>(p, h, stages, G, warp, lane); break;
+        case T_Q5_K: kq_consume<T_Q5_K, DBG>(p, h, stages, G, warp, lane); break;
+        case T_Q4_0: kq_consume<T_Q4_0, DBG>(p, h, stages, G, warp, lane); break;
+        default: kq_consume<T_Q6_K, DBG>(p, h, stages, G, warp, lane); break;
     }
     if (p.ar_nflag) {  // this CTA's rows are in every receive buffer: count it in
         __threadfence_system();
@@ -792,7 +630,7 @@ uint32_t round_up_u(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 // stage rb (so that the kQW / rb warps of a block have a superblock each), stage bytes
 // <= 64 KB. Prefers slices the block's warps split evenly, then slices of two superblocks
 // per warp (two independent chains), then longer slices.
-bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd, uint32_t max_stage = kQMaxStage) {
+bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd) {
     const int t = w->type;
     if (t != T_Q4_K && t != T_Q5_K && t != T_Q6_K && t != T_Q4_0) return false;
     if (w->cols != k || k % QK_K != 0 || w->row_bytes % 16 != 0 || ((uintptr_t)w->data & 15u)) return false;
@@ -807,7 +645,7 @@ bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd, uint32_t max_stage = kQ
         while ((uint32_t)(kQW >> rbl0) > sl && rbl0 < (uint32_t)kQWLog2) rbl0++;
         // taller stages (more 16-row blocks, fewer warps per block) give each warp two units
         for (uint32_t rbl = rbl0; rbl <= (uint32_t)kQWLog2; rbl++) {
-            if ((16u << rbl) * ps > max_stage) break;
+            if ((16u << rbl) * ps > kQMaxStage) break;
             const uint32_t wpb = kQW >> rbl, per = (sl + wpb - 1) / wpb;
             const double bal = (double)sl / (double)(wpb * per);
             const double score = bal * 8.0 + (per == 2 ? 2.0 : 0.0) + (double)sl / nsb - 0.01 * rbl;
@@ -830,73 +668,23 @@ bool kq_plan(const rcu_weight *w, uint32_t k, KqJob &jd, uint32_t max_stage = kQ
 uint32_t kq_stage_bytes(const KqJob &jd) { return round_up_u((16u << jd.rb_log2) * jd.pstride, 128); }
 
 // Shared-memory layout: header, then the weight stages. False when two stages do not fit.
-// act_bytes: the prologue's activation area after the header (0: none).
-bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p, uint32_t act_bytes = 0) {
-    p.stage_off = kQHdrBytes + (act_bytes + 127) / 128 * 128;
+bool kq_smem_layout(const rcu_ctx *ctx, uint32_t stage_bytes, KqParams &p) {
+    p.stage_off = kQHdrBytes;
     const uint32_t budget = (uint32_t)ctx->max_smem_optin;
     if (p.stage_off + 2 * stage_bytes > budget) return false;
     p.stages = std::min<uint32_t>(kQMaxStages, (budget - p.stage_off) / stage_bytes);
     return true;
 }
 
-// The prologue's activation area (offsets from the shared-memory base, after the header): 256
-// zero bytes, the Q8_K row (codes, d, bsums) and / or the Q8_0 row (codes, d, s, code sums), the
-// RMS partials. Returns its size.
-uint32_t kq_act_layout(uint32_t k, uint32_t fmt, KqParams *p) {
-    uint32_t off = kQHdrBytes;
-    auto take = [&](uint32_t bytes) {
-        const uint32_t o = off;
-        off = round_up_u(off + bytes, 16);
-        return o;
-    };
-    const uint32_t zero = take(256), red = take(2 * kQW * 4);
-    uint32_t qk = 0, dk = 0, bsk = 0, q0 = 0, d0 = 0, s0 = 0, sum0 = 0;
-    if (fmt & RCU_ACT_Q8K) qk = take(k), dk = take(k / QK_K * 4), bsk = take(k / 16 * 2);
-    if (fmt & RCU_ACT_Q8_0) q0 = take(k), d0 = take(k / QK * 4), s0 = take(k / QK * 4), sum0 = take(k / QK * 4);
-    if (p) {
-        p->a_zero = zero, p->a_red = red, p->a_qk = qk, p->a_dk = dk, p->a_bsk = bsk;
-        p->a_q0 = q0, p->a_d0 = d0, p->a_s0 = s0, p->a_sum0 = sum0;
-    }
-    return off - kQHdrBytes;
-}
-
 }  // namespace
 
-static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes);
-
-// The stage-size limit that keeps the most weight bytes in flight once act_bytes of shared
-// memory go to the prologue's activations (the default 64 KB stages can lose a whole stage to a
-// few KB; smaller ones fit more stages).
-static uint32_t kq_max_stage(const rcu_ctx *ctx, uint32_t k, const HostJob *jobs, int n_jobs, uint32_t act_bytes) {
-    uint32_t best = kQMaxStage;
-    uint64_t best_ring = 0;
-    for (const uint32_t cand : {kQMaxStage, 48u * 1024u, 32u * 1024u}) {
-        uint32_t stage = 0;
-        bool ok = true;
-        for (int i = 0; i < n_jobs && ok; i++) {
-            KqJob jd{};
-            ok = kq_plan(jobs[i].w, k, jd, cand);
-            stage = std::max(stage, kq_stage_bytes(jd));
-        }
-        KqParams lay;
-        if (!ok || !kq_smem_layout(ctx, stage, lay, act_bytes)) continue;
-        const uint64_t ring = (uint64_t)lay.stages * stage;
-        if (ring > best_ring) best_ring = ring, best = cand;
-    }
-    return best;
-}
+static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs);
 
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
-    return kq_ok(ctx, a.k, a.have, jobs, n_jobs, 0);
+    return kq_ok(ctx, a.k, a.have, jobs, n_jobs);
 }
 
-bool gemv_kq_pro_ok(const rcu_ctx *ctx, uint32_t k, uint32_t fmt, const HostJob *jobs, int n_jobs) {
-    if (k % QK_K != 0) return false;
-    const uint32_t act = kq_act_layout(k, fmt, nullptr);
-    return kq_ok(ctx, k, fmt, jobs, n_jobs, act);
-}
-
-static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs, uint32_t act_bytes) {
+static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *jobs, int n_jobs) {
     if (!ctx->gemv_kq || n_jobs < 1 || n_jobs > kQMaxJobs) return false;
     for (int i = 0; i < n_jobs; i++)
         if (!(have & act_format(jobs[i].w->type))) return false;
@@ -914,24 +702,15 @@ static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *
         stage_bytes = std::max(stage_bytes, kq_stage_bytes(jd));
     }
     KqParams lay;
-    if (!kq_smem_layout(ctx, stage_bytes, lay, act_bytes)) return false;
+    if (!kq_smem_layout(ctx, stage_bytes, lay)) return false;
     // Small launches take the lane GEMV: with 1-2 tiles per CTA this kernel's start-up is not
     // hidden; K = 768 expert rows also give it few tiles.
     return bytes >= ctx->gemv_kq_min_bytes;
 }
 
 int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
-                   const ArPush *push, const GemvPrologue *pro) {
+                   const ArPush *push) {
     KqParams p{};
-    uint32_t act_bytes = 0;
-    if (pro) {
-        if (tok0 != 0 || a.k % QK_K != 0 || (pro->kind == 2 && a.k > kQProRounds * kQW * QK_K) ||
-            (pro->kind != 1 && pro->kind != 2) || (pro->kind == 2 && pro->x_out == pro->x))
-            return set_err(ctx, RCU_ERR_INVALID, "gemv prologue: one row of k <= 8192 (norm) values, x_out apart from x");
-        p.pro = *pro;
-        act_bytes = kq_act_layout(a.k, pro->fmt, &p);
-    }
-    const uint32_t max_stage = pro ? kq_max_stage(ctx, a.k, jobs, n_jobs, act_bytes) : kQMaxStage;
     p.n_jobs = n_jobs;
     p.k = a.k;
     p.tok0 = tok0;
@@ -958,7 +737,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         for (int i = 0; i < n_jobs; i++) {
             if (jobs[i].w->type != ty) continue;
             KqJob &jd = p.jobs[nj++];
-            if (!kq_plan(jobs[i].w, a.k, jd, max_stage))
+            if (!kq_plan(jobs[i].w, a.k, jd))
                 return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: weight not K-quant tileable");
             jd.w = jobs[i].w->data;
             jd.out = jobs[i].out + (jobs[i].sel ? 0 : (uint64_t)tok0 * jobs[i].ld);  // indirect jobs: own rows
@@ -996,7 +775,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
-    if (!kq_smem_layout(ctx, stage_bytes, p, act_bytes))
+    if (!kq_smem_layout(ctx, stage_bytes, p))
         return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemv: two weight stages exceed shared memory");
     const uint32_t smem_bytes = p.stage_off + p.stages * stage_bytes;
     const uint32_t grid = cta;
@@ -1007,10 +786,9 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         p.dbg = ctx->dbg_sums;
         p.dbg_nbs = ctx->dbg_nbs;
     }
-    if (dbg && pro) return set_err(ctx, RCU_ERR_INVALID, "block-sum capture: no prologue");
-    auto kern = dbg ? k_gemv_kq<true, false> : pro ? k_gemv_kq<false, true> : k_gemv_kq<false, false>;
-    static std::atomic<bool> attr_set[3][64] = {};  // per instantiation and device; contexts may live on several threads
-    std::atomic<bool> &set = attr_set[dbg ? 1 : pro ? 2 : 0][ctx->device & 63];
+    auto kern = dbg ? k_gemv_kq<true> : k_gemv_kq<false>;
+    static std::atomic<bool> attr_set[2][64] = {};  // per instantiation and device; contexts may live on several threads
+    std::atomic<bool> &set = attr_set[dbg ? 1 : 0][ctx->device & 63];
     if (!set.load(std::memory_order_acquire)) {
         RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)ctx->max_smem_optin));

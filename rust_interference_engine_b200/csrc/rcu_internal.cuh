@@ -183,7 +183,6 @@ struct rcu_ctx {
     bool gemm_i8 = false;          // prefill: int8 GEMM with exact block sums for Q4_0 weights
     bool gemv_kq = true;           // batch-1 K-quant GEMV on the tensor cores (RIE_GEMV_KQ=0: lane GEMV)
     uint64_t gemv_kq_min_bytes = 8ull << 20;  // ... for launches of at least this many weight bytes (RIE_GEMV_KQ_MIN_MB)
-    bool gemv_prologue = false;  // decode: norm / GLU computed inside the tensor-core GEMV (RIE_GEMV_PROLOGUE=1)
     void *h_act = nullptr;         // f16 activations of the prefill GEMM (grown on demand)
     size_t h_act_cap = 0;
     void *k_part = nullptr;        // split-K partial tiles of the prefill GEMM (grown on demand)

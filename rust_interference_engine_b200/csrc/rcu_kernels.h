@@ -36,24 +36,8 @@ int launch_gemv(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs
 // Batch-1 GEMV over Q4_K / Q5_K / Q6_K weights with the block dot products on the integer
 // tensor-core path (launch_gemv uses it when gemv_kq_ok holds; same job semantics).
 bool gemv_kq_ok(const rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs);
-// The activations of a batch-1 tensor-core GEMV computed by the GEMV itself, into shared
-// memory (no ActsView): kind 1, act(g) * u of the FFN (ops.rs:41-58); kind 2, the residual add
-// and RMSNorm before a matmul (model/cpu.rs:230-262): v = x + [RMSNorm(o) * post] * rs (x alone
-// when o is null), xn = RMSNorm(v) * w, with v written to x_out and xn to xn_out (if set) by
-// CTA 0 (x_out must not alias x: every CTA reads x). Rows of k values, k a multiple of 256,
-// k <= 8192 for kind 2.
-struct GemvPrologue {
-    uint32_t kind = 0, fmt = 0;
-    const float *g = nullptr, *u = nullptr;
-    int act = 0;
-    const float *x = nullptr, *o = nullptr, *post = nullptr, *w = nullptr;
-    float rs = 1.0f, eps = 0.0f;
-    float *x_out = nullptr, *xn_out = nullptr;
-    int rounding = 0;
-};
-bool gemv_kq_pro_ok(const rcu_ctx *ctx, uint32_t k, uint32_t fmt, const HostJob *jobs, int n_jobs);
 int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs, uint32_t tok0,
-                   const ArPush *push = nullptr, const GemvPrologue *pro = nullptr);
+                   const ArPush *push = nullptr);
 // Prefill GEMM on the tensor cores (n_tok > 8). Returns RCU_ERR_UNSUPPORTED for shapes it
 // lacks (the caller then runs GEMV slices). launch_gemm_f16: every weight type, operands
 // dequantized to f16; the int8 kernel (exact per-block sums, Q4_0) when ctx->gemm_i8.
