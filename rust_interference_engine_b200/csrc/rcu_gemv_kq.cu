@@ -86,6 +86,7 @@ struct KqJob {
     uint32_t nsl;          // slices per row group
     uint32_t slice_bytes;  // sl * block bytes (a multiple of 16)
     uint32_t pstride;      // shared-memory row stride, = 16 (mod 128)
+    uint32_t gpt;          // row groups per tile: kQG, or 1 when half-height tiles balance the CTAs better
     uint32_t tile_begin;
 };
 
@@ -131,12 +132,13 @@ struct JobR {
     float *out;
     const uint32_t *sel;
     uint64_t w_stride;
-    uint32_t rows, row_bytes, type, tok, rb_log2, sl, nsl, slice_bytes, pstride, tile_begin;
+    uint32_t rows, row_bytes, type, tok, rb_log2, sl, nsl, slice_bytes, pstride, gpt, tile_begin;
 };
 __device__ __forceinline__ void load_job(const KqJob &j, JobR &r) {
     r.w = j.w, r.out = j.out, r.sel = j.sel, r.w_stride = j.w_stride;
     r.rows = j.rows, r.row_bytes = j.row_bytes, r.type = j.type, r.tok = j.tok, r.rb_log2 = j.rb_log2;
-    r.sl = j.sl, r.nsl = j.nsl, r.slice_bytes = j.slice_bytes, r.pstride = j.pstride, r.tile_begin = j.tile_begin;
+    r.sl = j.sl, r.nsl = j.nsl, r.slice_bytes = j.slice_bytes, r.pstride = j.pstride, r.gpt = j.gpt;
+    r.tile_begin = j.tile_begin;
 }
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -473,8 +475,8 @@ __device__ __forceinline__ void kq_consume(const KqParams &p, KqHdr *h, uint8_t 
             next_begin = ji + 1 < (int)G.job1 ? p.jobs[ji + 1].tile_begin : 0xffffffffu;
         }
         const uint32_t wpb = kQW >> J.rb_log2, rbk = warp >> (kQWLog2 - J.rb_log2), part = warp & (wpb - 1);
-        const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (kQG * grows);
-        const uint32_t ngrp = min((uint32_t)kQG, (J.rows - r0 + grows - 1) / grows);
+        const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (J.gpt * grows);
+        const uint32_t ngrp = min(J.gpt, (J.rows - r0 + grows - 1) / grows);
         const uint32_t ex = J.sel ? *(volatile const uint32_t *)J.sel : 0u;
         const bool skip = ex == kNoExpert;
         const uint64_t trow = (uint64_t)p.tok0 + J.tok;
@@ -563,9 +565,9 @@ __global__ void __launch_bounds__(kQThreads, 1) k_gemv_kq(const __grid_constant_
                 load_job(p.jobs[++ji], J);
                 next_begin = ji + 1 < (int)G.job1 ? p.jobs[ji + 1].tile_begin : 0xffffffffu;
             }
-            const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (kQG * grows);
+            const uint32_t grows = 16u << J.rb_log2, r0 = (tile - J.tile_begin) * (J.gpt * grows);
             const uint32_t ex = J.sel ? *(volatile const uint32_t *)J.sel : 0u;
-            for (uint32_t gi = 0; ok && gi < (uint32_t)kQG && r0 + gi * grows < J.rows; gi++) {
+            for (uint32_t gi = 0; ok && gi < J.gpt && r0 + gi * grows < J.rows; gi++) {
                 const uint32_t g0 = r0 + gi * grows, nrows = min(grows, J.rows - g0);
                 for (uint32_t sl = 0; sl < J.nsl; sl++) {
                     if (li >= S) {
@@ -746,6 +748,7 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
             jd.tok = jobs[i].tok;
             jd.rows = jobs[i].rows ? jobs[i].rows : (uint32_t)jobs[i].w->rows;
             if (jd.sel) p.early_weights = 0;  // the producer reads the router's choice: wait first
+            jd.gpt = kQG;
             jd.tile_begin = tiles;
             const uint32_t trows = kQG * (16u << jd.rb_log2);
             tiles += (jd.rows + trows - 1) / trows;
@@ -772,6 +775,32 @@ int launch_gemv_kq(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_j
         G.cta0 = cta;
         G.cta1 = cta + n;
         cta += n;
+    }
+    // A group whose CTAs get one or two tiles balances better with half-height tiles when that
+    // shortens the longest CTA's share (e.g. 160 tiles on 115 CTAs: 2 tiles; 320 half tiles: 3
+    // halves); tile numbers are then assigned again. (With more tiles per CTA the extra
+    // per-tile reductions cost more than the balance gains: measured on the gate+up launch.)
+    tiles = 0;
+    for (int q = 0; q < p.n_groups; q++) {
+        KqGroup &G = p.groups[q];
+        const uint32_t n = G.cta1 - G.cta0;
+        uint32_t t2 = 0, t1 = 0;
+        for (uint32_t j = G.job0; j < G.job1; j++) {
+            const uint32_t grows = 16u << p.jobs[j].rb_log2;
+            t2 += (p.jobs[j].rows + kQG * grows - 1) / (kQG * grows);
+            t1 += (p.jobs[j].rows + grows - 1) / grows;
+        }
+        const uint32_t full = (t2 + n - 1) / n;  // the longest CTA's share in full tiles
+        const uint32_t gpt = full <= 2 && (t1 + n - 1) / n < kQG * full ? 1u : (uint32_t)kQG;
+        G.tile0 = tiles;
+        for (uint32_t j = G.job0; j < G.job1; j++) {
+            KqJob &jd = p.jobs[j];
+            jd.gpt = gpt;
+            jd.tile_begin = tiles;
+            const uint32_t trows = gpt * (16u << jd.rb_log2);
+            tiles += (jd.rows + trows - 1) / trows;
+        }
+        G.tile1 = tiles;
     }
     p.total_tiles = tiles;
     p.stage_bytes = stage_bytes;
