@@ -55,6 +55,14 @@ struct DecParams {
     const uint64_t *pos_ptr;
     float softcap;
     int rounding;
+    // decode with the q/k post-processing fused in (post != 0): q holds the raw query heads of
+    // the QKV matmul, kraw / vraw its key / value heads; each CTA prepares its group's queries and
+    // the CTA holding the newest position writes that position's K and V rows into the cache
+    int post;
+    const float *kraw, *vraw, *bq, *bk, *bv, *qn, *kn, *inv_freq;
+    uint32_t rope_dim;
+    int neox;
+    float eps, attn_scale;
 };
 
 // Lane bit -> score index bit of the transposing butterfly (stages at lane offsets 4, 2, 1,
@@ -151,11 +159,12 @@ __device__ __forceinline__ Runs plan_runs(uint64_t head_base, uint32_t slots, ui
 
 // The producer warp's lane 0: bulk copies of the split's K and V rows, stage by stage, into the
 // ring of n_stages buffers (full[s] completes with the bytes; empty[s] when every consumer warp
-// has read the stage), and each stage's row map in maps[s]. Rows of earlier positions were written at least two launches back; this
-// step's rows (logical index >= fresh) by the kernel just before: wait for it before copying them.
+// has read the stage), and each stage's row map in maps[s]. Rows of earlier positions were
+// written at least two launches back; this step's rows (logical index >= fresh) by the kernel
+// just before (wait for it), or, with the fused post-processing, by this CTA (wait on newrow).
 __device__ __forceinline__ void dec_produce(const DecParams &p, uint8_t *dsm, uint64_t *full, uint64_t *empty,
-                                            RowMap *maps, uint32_t c0, uint32_t c1, uint32_t n_stage, uint64_t start,
-                                            uint64_t pos_b, uint64_t head_base) {
+                                            RowMap *maps, uint64_t *newrow, uint32_t c0, uint32_t c1,
+                                            uint32_t n_stage, uint64_t start, uint64_t pos_b, uint64_t head_base) {
     const uint32_t rb = p.row_bytes, SR = p.stage_rows, NS = p.n_stages, BB = p.buf_bytes;
     const uint32_t fresh = pos_b > start ? (uint32_t)(pos_b - start) : 0;
     bool waited = false;
@@ -167,7 +176,12 @@ __device__ __forceinline__ void dec_produce(const DecParams &p, uint8_t *dsm, ui
         if (j >= NS && !mbar_wait_bounded(&empty[s], ((j / NS) - 1) & 1u, p.err, ERR_TIMEOUT_EMPTY)) break;
         const uint32_t ra = c0 + j * SR, n = min(SR, c1 - ra);
         if (!waited && ra + n > fresh) {
-            pdl_wait();
+            if (p.post) {  // this CTA's consumers write the newest row (fused q/k post-processing)
+                if (!mbar_wait_bounded(newrow, 0, p.err, ERR_TIMEOUT_FULL)) break;
+                fence_proxy_async_global();
+            } else {
+                pdl_wait();
+            }
             waited = true;
         }
         const Runs r = plan_runs(head_base, p.slots, rb, slot, n);
@@ -195,9 +209,19 @@ __device__ __forceinline__ void dec_query(const DecParams &p, float (*qf)[kDHd],
                                           float (*qds)[kDHd / 32], uint32_t t, uint32_t g, uint32_t warp,
                                           uint32_t lane) {
     for (uint32_t hh = warp; hh < (uint32_t)G; hh += kDW) {
-        const float *qsrc = p.q + ((uint64_t)t * p.n_head + (uint64_t)g * G + hh) * kDHd;
+        const uint64_t head = (uint64_t)g * G + hh;
+        const float *qsrc = p.q + ((uint64_t)t * p.n_head + head) * kDHd;
         *reinterpret_cast<float4 *>(&qf[hh][4 * lane]) = *reinterpret_cast<const float4 *>(qsrc + 4 * lane);
         __syncwarp();
+        if (p.post) {  // bias, q norm, RoPE and attn_scale (the standalone post-processing's arithmetic)
+            const uint64_t pos = (p.pos_ptr ? *p.pos_ptr : p.pos0) + t;
+            if (p.bq)
+                for (uint32_t i = lane; i < kDHd; i += 32) qf[hh][i] = qf[hh][i] + p.bq[head * kDHd + i];
+            __syncwarp();
+            qk_post_vec(qf[hh], kDHd, p.qn, p.eps, true, p.inv_freq, pos, p.rope_dim, p.neox, (int)lane);
+            for (uint32_t i = lane; i < kDHd; i += 32) qf[hh][i] = qf[hh][i] * p.attn_scale;
+            __syncwarp();
+        }
         if (KV == RCU_KV_TURBO4) rotate_row(qf[hh], kDHd, false, (int)lane);
         if (KV != RCU_KV_F16) {
 #pragma unroll
@@ -210,6 +234,26 @@ __device__ __forceinline__ void dec_query(const DecParams &p, float (*qf)[kDHd],
         }
         __syncwarp();
     }
+}
+
+// The fused post-processing's K (which = 0) or V (1) row of the newest position for KV head g,
+// one warp each: bias, and on the key k norm and RoPE, then encoded into the cache as the
+// standalone kernel does; the writes are ordered before the producer's bulk copies (proxy
+// fence, then an arrival on newrow, which completes with both rows).
+template <int KV>
+__device__ void dec_new_row(const DecParams &p, int which, uint32_t g, uint64_t pos, float *x, uint8_t *qtmp,
+                            uint64_t *newrow, uint32_t lane) {
+    const uint64_t slot = pos % p.slots;
+    const float *src = (which ? p.vraw : p.kraw) + (uint64_t)g * kDHd;
+    const float *bias = which ? p.bv : p.bk;
+    for (uint32_t i = lane; i < kDHd; i += 32) x[i] = src[i] + (bias ? bias[(uint64_t)g * kDHd + i] : 0.0f);
+    __syncwarp();
+    if (!which) qk_post_vec(x, kDHd, p.kn, p.eps, true, p.inv_freq, pos, p.rope_dim, p.neox, (int)lane);
+    uint8_t *dst = const_cast<uint8_t *>(which ? p.vc : p.kc) + ((uint64_t)g * p.slots + slot) * p.row_bytes;
+    store_row(KV, x, kDHd, dst, qtmp, (int)lane);
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(newrow);
 }
 
 // The split's partial rows (one per consumer warp: running max in natural-log units, sum of
@@ -340,6 +384,9 @@ __global__ void __launch_bounds__(kDThreads) k_attn_dec(const __grid_constant__ 
     extern __shared__ __align__(128) uint8_t dsm[];  // stages: [stage][K rows, V rows]
     __shared__ __align__(8) uint64_t full[kDMaxStages], empty[kDMaxStages];
     __shared__ RowMap maps[kDMaxStages];
+    __shared__ __align__(8) uint64_t newrow;  // the fused post-processing's new K / V rows are in the cache
+    __shared__ float nrx[2][kDHd];
+    __shared__ uint8_t nrq[2][kDHd];
     __shared__ __align__(16) float qf[G][kDHd];
     __shared__ __align__(16) int8_t qi[G][kDHd];
     __shared__ float qds[G][kDHd / 32];
@@ -361,17 +408,25 @@ __global__ void __launch_bounds__(kDThreads) k_attn_dec(const __grid_constant__ 
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kDW);
         }
+        mbar_init(&newrow, 2);
         fence_mbar_init();
     }
     __syncthreads();
     pdl_trigger();
 
     if (warp == kDW) {  // ---- producer: bulk copies of the CTA's rows, stage by stage ----
-        if (lane == 0) dec_produce(p, dsm, full, empty, maps, c0, c1, n_stage, start, pos_b, head_base);
+        if (lane == 0) dec_produce(p, dsm, full, empty, maps, &newrow, c0, c1, n_stage, start, pos_b, head_base);
         return;
     }
 
-    pdl_wait();  // q comes from the kernel before
+    pdl_wait();  // q (and with the fused post-processing k / v) come from the kernel before
+    {
+        // fused post-processing: the CTA holding the newest position writes its K / V rows first
+        // (its producer waits for them before the last stage), in the last two consumer warps
+        const uint64_t fresh = pos_b - start;
+        if (p.post && warp >= kDW - 2 && fresh >= c0 && fresh < c1)
+            dec_new_row<KV>(p, (int)(kDW - 1 - warp), g, pos_b, nrx[kDW - 1 - warp], nrq[kDW - 1 - warp], &newrow, lane);
+    }
     dec_query<KV, G>(p, qf, qi, qds, t, g, warp, lane);
     named_bar_sync(1, kDW * 32);
     // this lane's query dims 4l..4l+3 of every head
@@ -618,6 +673,7 @@ __global__ void __launch_bounds__(kDThreads, 2) k_attn_dec_t4(const __grid_const
     extern __shared__ __align__(128) uint8_t dsm[];  // stages: [stage][K rows, V rows]
     __shared__ __align__(8) uint64_t full[kDMaxStages], empty[kDMaxStages];
     __shared__ RowMap maps[kDMaxStages];
+    __shared__ __align__(8) uint64_t newrow;  // (unused: turbo4 keeps the standalone post-processing)
     __shared__ __align__(16) float qf[G][kDHd];
     __shared__ __align__(16) int8_t qi[G][kDHd];
     __shared__ float qds[G][kDHd / 32];
@@ -637,15 +693,16 @@ __global__ void __launch_bounds__(kDThreads, 2) k_attn_dec_t4(const __grid_const
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kDW);
         }
+        mbar_init(&newrow, 2);
         fence_mbar_init();
     }
     __syncthreads();
     pdl_trigger();
     if (warp == kDW) {
-        if (lane == 0) dec_produce(p, dsm, full, empty, maps, c0, c1, n_stage, start, pos_b, head_base);
+        if (lane == 0) dec_produce(p, dsm, full, empty, maps, &newrow, c0, c1, n_stage, start, pos_b, head_base);
         return;
     }
-    pdl_wait();  // q comes from the kernel before
+    pdl_wait();  // q comes from the kernel before (turbo4 does not fuse the post-processing)
     dec_query<RCU_KV_TURBO4, G>(p, qf, qi, qds, t, g, warp, lane);
     named_bar_sync(1, kDW * 32);
 
@@ -949,10 +1006,18 @@ static int launch_dec_kv(rcu_ctx *ctx, DecParams &p, uint64_t max_len, uint64_t 
 int launch_attention_dec(rcu_ctx *ctx, const uint8_t *kc, const uint8_t *vc, int kv_type, uint64_t n_kv,
                          uint64_t slots, uint64_t row_bytes, const float *q, uint64_t n_tok, uint64_t n_head,
                          uint64_t pos0, const uint64_t *pos_ptr, uint64_t max_len, uint64_t window, float softcap,
-                         float *out, const ActOut *aq, uint32_t *done, float *parts) {
+                         float *out, const ActOut *aq, uint32_t *done, float *parts,
+                         const QkvPostParams *post) {
     if (kv_type == RCU_KV_TURBO4)
         if (int st = ensure_signs(ctx)) return st;
     DecParams p{};
+    if (post) {
+        if (n_tok != 1) return set_err(ctx, RCU_ERR_INVALID, "attention: fused post-processing takes one token");
+        p.post = 1;
+        p.kraw = post->k, p.vraw = post->v, p.bq = post->bq, p.bk = post->bk, p.bv = post->bv;
+        p.qn = post->qn, p.kn = post->kn, p.inv_freq = post->inv_freq, p.rope_dim = post->rope_dim;
+        p.neox = post->neox, p.eps = post->eps, p.attn_scale = post->attn_scale;
+    }
     p.kc = kc;
     p.vc = vc;
     p.q = q;

@@ -929,17 +929,21 @@ static int forward_span(rcu_backend *b, uint64_t n, uint64_t pos0, bool all_logi
         QkvPostParams qp{b->q, b->k, b->v, L.bq, L.bk, L.bv, L.q_norm, L.k_norm,
                          swa_rope ? b->inv_freq_swa : b->inv_freq, b->pos_dev, (uint32_t)n, c.n_head, hd,
                          c.rope_dim, c.rope_neox, c.rms_eps, c.attn_scale};
-        if ((st = launch_qkv_post_store(ctx, b->kv[il], qp))) return st;
+        // decode steps over the head_dim-128 decode attention fold the post-processing and KV
+        // append into it (one launch less per layer)
+        const bool fuse_post = ctx->fuse_post && attention_fuses_post(b->kv[il], n, c.n_head);
+        if (!fuse_post && (st = launch_qkv_post_store(ctx, b->kv[il], qp))) return st;
+        const QkvPostParams *post = fuse_post ? &qp : nullptr;
         const uint64_t window = L.swa ? c.swa_window : 0;
         const uint32_t fo = formats({L.wo});
         const ActOut ao = acts_out(b, fo);
         const uint32_t nsp = fixed_grid ? attention_max_splits(b->kv[il], window) : 0;
         if (b->fused_merge) {
             st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, nullptr,
-                                  nsp, b->attn_scratch, &ao);
+                                  nsp, b->attn_scratch, &ao, post);
         } else {
             st = launch_attention(ctx, b->kv[il], b->q, n, c.n_head, pos0, b->pos_dev, window, c.attn_softcap, b->att,
-                                  nsp, b->attn_scratch, nullptr);
+                                  nsp, b->attn_scratch, nullptr, post);
             if (!st) st = launch_quantize(ctx, b->acts->v, b->att, (uint32_t)n, qd, fo);
         }
         if (st) return st;

@@ -192,6 +192,7 @@ struct rcu_ctx {
     // device address of the allocation-free matmul's static scratch (rcu_static.cu), looked
     // up by this context's first such call
     uint8_t *static_scratch = nullptr;
+    bool fuse_post = true;  // decode attention does the q/k post-processing and KV append (RIE_FUSE_POST=0: own kernel)
     // block-sum capture (rcu_matmul_block_sums): set only for the duration of that call
     int32_t *dbg_sums = nullptr;
     uint32_t dbg_nbs = 0;
@@ -228,6 +229,9 @@ namespace rcu {
 // kernel has completed and its writes are visible; on a plain launch both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Orders this thread's generic-proxy global writes before later async-proxy accesses (bulk
+// copies) that another thread issues after synchronizing with it.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Every kernel of the library runs with the largest shared-memory carveout, so that an SM
 // never has to drain and re-split L1 / shared memory between consecutive kernels (the GEMV

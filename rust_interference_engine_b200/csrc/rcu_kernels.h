@@ -69,9 +69,13 @@ int launch_kv_store(rcu_ctx *ctx, rcu_kv *kv, const float *k, const float *v, ui
 // aq != nullptr fuses the activation quantization (for the Wo matmul) into the merge; out
 // may then be nullptr.
 struct ActOut;
+struct QkvPostParams;
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
                      const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
-                     float *scratch, const ActOut *aq);
+                     float *scratch, const ActOut *aq, const QkvPostParams *post = nullptr);
+// Decode steps (one token) whose attention runs the head_dim-128 decode kernels can leave the
+// q/k post-processing and KV append to them (launch_attention with `post`, q then raw).
+bool attention_fuses_post(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head);
 
 // Bias, q/k norm, RoPE and attn_scale on the fused QKV output, with k and v appended to the
 // cache at slot (*pos_ptr + t) % slots (q is updated in place).
@@ -102,7 +106,8 @@ struct ActOut;
 int launch_attention_dec(rcu_ctx *ctx, const uint8_t *kc, const uint8_t *vc, int kv_type, uint64_t n_kv,
                          uint64_t slots, uint64_t row_bytes, const float *q, uint64_t n_tok, uint64_t n_head,
                          uint64_t pos0, const uint64_t *pos_ptr, uint64_t max_len, uint64_t window, float softcap,
-                         float *out, const ActOut *aq, uint32_t *done, float *parts);
+                         float *out, const ActOut *aq, uint32_t *done, float *parts,
+                         const QkvPostParams *post = nullptr);
 // Whether the merge can quantize in the same kernel for this head shape and act format
 // (a GQA group's output must hold whole activation blocks).
 bool attention_fused_merge_ok(uint64_t n_head, uint64_t n_kv, uint64_t hd, uint32_t fmt);

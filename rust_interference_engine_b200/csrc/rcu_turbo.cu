@@ -30,74 +30,6 @@ struct rcu_kv {
 
 namespace rcu {
 
-// quantize_rotated_4 (turbo.rs:141-164) of a rotated shared row into a reference row.
-__device__ void encode_rotated_row(const float *y, uint32_t d, uint8_t *out, uint8_t *qtmp, int lane) {
-    const uint32_t b = turbo_block(d), nb = d / b;
-    float c[16], thr[15];
-#pragma unroll
-    for (int i = 0; i < 16; i++) c[i] = (float)c_levels[i] / 46.0f;
-#pragma unroll
-    for (int i = 0; i < 15; i++) thr[i] = __fmul_rn(0.5f, __fadd_rn(c[i], c[i + 1]));
-    for (uint32_t bi = 0; bi < nb; bi++) {
-        const float *yb = y + bi * b;
-        float inv = 0.0f;
-        if (lane == 0) {
-            float ss = 0.0f;
-            for (uint32_t j = 0; j < b; j++) ss = __fadd_rn(ss, __fmul_rn(yb[j], yb[j]));
-            const float rms = sqrtf(ss / (float)b);
-            inv = rms > 0.0f ? 1.0f / rms : 0.0f;
-        }
-        inv = __shfl_sync(0xffffffffu, inv, 0);
-        for (uint32_t j = lane; j < b; j += 32) {
-            const float v = __fmul_rn(yb[j], inv);
-            uint32_t q = 0;
-#pragma unroll
-            for (int i = 0; i < 15; i++) q += v > thr[i] ? 1u : 0u;
-            qtmp[bi * b + j] = (uint8_t)q;
-        }
-        __syncwarp();
-        if (lane == 0) {
-            float num = 0.0f, den = 0.0f;
-            for (uint32_t j = 0; j < b; j++) {
-                const float cq = c[qtmp[bi * b + j]];
-                num = __fadd_rn(num, __fmul_rn(yb[j], cq));
-                den = __fadd_rn(den, __fmul_rn(cq, cq));
-            }
-            const float s = den > 0.0f ? num / den : 0.0f;
-            *reinterpret_cast<unsigned short *>(out + 2 * bi) = __half_as_ushort(__float2half_rn(s));
-        }
-    }
-    __syncwarp();
-    uint8_t *codes = out + 2 * nb;
-    for (uint32_t m = lane; m < d / 2; m += 32) {
-        const uint32_t g = (m / 16) * 32 + m % 16;
-        codes[m] = (uint8_t)(qtmp[g] | (qtmp[g + 16] << 4));
-    }
-    __syncwarp();
-}
-
-// ---- KV append ----------------------------------------------------------------------------
-// Encodes one warp-owned shared row x (hd values; turbo rotates it in place) into cache row dst.
-__device__ void store_row(int type, float *x, uint32_t hd, uint8_t *dst, uint8_t *qtmp, int lane) {
-    if (type == RCU_KV_F16) {
-        unsigned short *o = reinterpret_cast<unsigned short *>(dst);
-        for (uint32_t i = lane; i < hd; i += 32) o[i] = __half_as_ushort(__float2half_rn(x[i]));
-        return;
-    }
-    if (type == RCU_KV_Q8_0) {  // store_q8_0 (cpu.rs:637-647): scalar rounding, f16 scale
-        for (uint32_t b = 0; b < hd / 32; b++) {
-            float d;
-            const int q = quant32(x[b * 32 + lane], RCU_ROUND_HALF_AWAY, d);
-            uint8_t *ob = dst + b * 34;
-            if (lane == 0) *reinterpret_cast<unsigned short *>(ob) = __half_as_ushort(__float2half_rn(d));
-            ob[2 + lane] = (uint8_t)(int8_t)q;
-        }
-        return;
-    }
-    rotate_row(x, hd, false, lane);
-    encode_rotated_row(x, hd, dst, qtmp, lane);
-}
-
 // One warp per (token, kv head, k|v). Rows land at slot (pos0 + t) % slots.
 __global__ void __launch_bounds__(128) k_kv_store(int type, const float *__restrict__ k, const float *__restrict__ v,
                                                   uint32_t n_tok, uint32_t n_kv, uint32_t hd, uint32_t slots,
@@ -767,9 +699,19 @@ static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 gri
     }
 }
 
+// Not for turbo4 caches: the new row's encode (sequential sums, as the reference) would sit on
+// the path of the CTA holding the newest position (measured on the 70B shape: 59.7 vs 61.1
+// tok/s), while the standalone kernel encodes all heads' rows in parallel.
+bool attention_fuses_post(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head) {
+    return n_tok == 1 && kv->n_kv > 0 && kv->type != RCU_KV_TURBO4 &&
+           attention_dec_ok(kv->type, kv->hd, n_head / kv->n_kv);
+}
+
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,
                      const uint64_t *pos_ptr, uint64_t window, float softcap, float *out, uint32_t n_split,
-                     float *scratch, const ActOut *aq) {
+                     float *scratch, const ActOut *aq, const QkvPostParams *post) {
+    if (post && !attention_fuses_post(kv, n_tok, n_head))
+        return set_err(ctx, RCU_ERR_INVALID, "attention: this shape does not fuse the q/k post-processing");
     const uint64_t group = n_head / kv->n_kv;
     if (group > kMaxGroup) return set_err(ctx, RCU_ERR_UNSUPPORTED, "attention: more than 16 query heads per kv head");
     if (aq && !attention_fused_merge_ok(n_head, kv->n_kv, kv->hd, aq->fmt))
@@ -817,7 +759,7 @@ int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_
         return launch_attention_dec(ctx, kv->k, kv->v, kv->type, kv->n_kv, kv->slots, kv->row_bytes, q, n_tok, n_head,
                                     pos0, pos_ptr, max_len, window, softcap, out, aq,
                                     reinterpret_cast<uint32_t *>(scr),
-                                    reinterpret_cast<float *>(scr + counters_bytes(n_tok, kv->n_kv)));
+                                    reinterpret_cast<float *>(scr + counters_bytes(n_tok, kv->n_kv)), post);
     }
     AttnParams p{};
     p.kc = kv->k;

@@ -12,6 +12,7 @@ constexpr uint64_t KV_SEED = 0x75426F5175616E74ull;          // turbo.rs:122
 constexpr int kMaxHd = 512;                                   // cpu.rs:106 (turbo needs hd <= 512)
 static __constant__ int8_t c_levels[16] = {-126, -95, -74, -58, -43, -30, -18, -6, 6, 18, 30, 43, 58, 74, 95, 126};
 static __constant__ float c_signs[kMaxHd];                            // sign(KV_SEED, i)
+static __constant__ float c_levels46[16];  // the levels / 46 (kv_levels, turbo.rs:129-131), IEEE f32 division
 
 static float host_sign(uint64_t seed, uint64_t i) {  // turbo.rs:80-89
     uint64_t z = seed + i * 0x9E3779B97F4A7C15ull;
@@ -25,6 +26,10 @@ static int ensure_signs(rcu_ctx *ctx) {
     float s[kMaxHd];
     for (int i = 0; i < kMaxHd; i++) s[i] = host_sign(KV_SEED, i);
     RCU_CUDA_TRY(ctx, cudaMemcpyToSymbol(c_signs, s, sizeof(s)));
+    static const int8_t lv[16] = {-126, -95, -74, -58, -43, -30, -18, -6, 6, 18, 30, 43, 58, 74, 95, 126};
+    float c[16];
+    for (int i = 0; i < 16; i++) c[i] = (float)lv[i] / 46.0f;
+    RCU_CUDA_TRY(ctx, cudaMemcpyToSymbol(c_levels46, c, sizeof(c)));
     done[ctx->device & 63] = true;
     return RCU_OK;
 }
@@ -113,6 +118,101 @@ __device__ __forceinline__ int quant32(float v, int rounding, float &d_out) {
     const int r = rounding == RCU_ROUND_HALF_AWAY ? __float2int_rz(roundf(p)) : __float2int_rn(p);
     d_out = d;
     return max(-127, min(127, r));
+}
+
+// ---- KV rows ----------------------------------------------------------------------------
+// quantize_rotated_4 (turbo.rs:141-164) of a rotated shared row into a reference row.
+static __device__ void encode_rotated_row(const float *y, uint32_t d, uint8_t *out, uint8_t *qtmp, int lane) {
+    const uint32_t b = turbo_block(d), nb = d / b;
+    float thr[15];
+#pragma unroll
+    for (int i = 0; i < 15; i++) thr[i] = __fmul_rn(0.5f, __fadd_rn(c_levels46[i], c_levels46[i + 1]));
+    for (uint32_t bi = 0; bi < nb; bi++) {
+        const float *yb = y + bi * b;
+        float inv = 0.0f;
+        if (lane == 0) {
+            float ss = 0.0f;
+            for (uint32_t j = 0; j < b; j++) ss = __fadd_rn(ss, __fmul_rn(yb[j], yb[j]));
+            const float rms = sqrtf(ss / (float)b);
+            inv = rms > 0.0f ? 1.0f / rms : 0.0f;
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (uint32_t j = lane; j < b; j += 32) {
+            const float v = __fmul_rn(yb[j], inv);
+            uint32_t q = 0;
+#pragma unroll
+            for (int i = 0; i < 15; i++) q += v > thr[i] ? 1u : 0u;
+            qtmp[bi * b + j] = (uint8_t)q;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            float num = 0.0f, den = 0.0f;
+            for (uint32_t j = 0; j < b; j++) {
+                const float cq = c_levels46[qtmp[bi * b + j]];
+                num = __fadd_rn(num, __fmul_rn(yb[j], cq));
+                den = __fadd_rn(den, __fmul_rn(cq, cq));
+            }
+            const float s = den > 0.0f ? num / den : 0.0f;
+            *reinterpret_cast<unsigned short *>(out + 2 * bi) = __half_as_ushort(__float2half_rn(s));
+        }
+    }
+    __syncwarp();
+    uint8_t *codes = out + 2 * nb;
+    for (uint32_t m = lane; m < d / 2; m += 32) {
+        const uint32_t g = (m / 16) * 32 + m % 16;
+        codes[m] = (uint8_t)(qtmp[g] | (qtmp[g + 16] << 4));
+    }
+    __syncwarp();
+}
+
+// Encodes one warp-owned shared row x (hd values; turbo rotates it in place) into cache row dst.
+static __device__ void store_row(int type, float *x, uint32_t hd, uint8_t *dst, uint8_t *qtmp, int lane) {
+    if (type == RCU_KV_F16) {
+        unsigned short *o = reinterpret_cast<unsigned short *>(dst);
+        for (uint32_t i = lane; i < hd; i += 32) o[i] = __half_as_ushort(__float2half_rn(x[i]));
+        return;
+    }
+    if (type == RCU_KV_Q8_0) {  // store_q8_0 (cpu.rs:637-647): scalar rounding, f16 scale
+        for (uint32_t b = 0; b < hd / 32; b++) {
+            float d;
+            const int q = quant32(x[b * 32 + lane], RCU_ROUND_HALF_AWAY, d);
+            uint8_t *ob = dst + b * 34;
+            if (lane == 0) *reinterpret_cast<unsigned short *>(ob) = __half_as_ushort(__float2half_rn(d));
+            ob[2 + lane] = (uint8_t)(int8_t)q;
+        }
+        return;
+    }
+    rotate_row(x, hd, false, lane);
+    encode_rotated_row(x, hd, dst, qtmp, lane);
+}
+
+
+// Bias-added q or k head vector x (warp-owned shared row): RMSNorm with weights `norm` (when
+// given) and RoPE at position pos (ops.rs:7-14, 65-99; cpu.rs:280-300), as the standalone q/k
+// post-processing kernel and the decode attention's fused path both do it.
+static __device__ void qk_post_vec(float *x, uint32_t hd, const float *norm, float eps, bool rope,
+                                   const float *inv_freq, uint64_t pos, uint32_t rope_dim, int neox, int lane) {
+    if (norm) {
+        float ss = 0.0f;
+        for (uint32_t i = lane; i < hd; i += 32) ss += x[i] * x[i];
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float scale = 1.0f / sqrtf(ss / (float)hd + eps);
+        for (uint32_t i = lane; i < hd; i += 32) x[i] *= scale * norm[i];
+        __syncwarp();
+    }
+    if (rope) {
+        const uint32_t half = rope_dim / 2;
+        const float fpos = (float)pos;
+        for (uint32_t i = lane; i < half; i += 32) {
+            float sn, cs;
+            sincosf(fpos * inv_freq[i], &sn, &cs);
+            const uint32_t i0 = neox ? i : 2 * i, i1 = neox ? i + half : 2 * i + 1;
+            const float a = x[i0], b = x[i1];
+            x[i0] = a * cs - b * sn;
+            x[i1] = a * sn + b * cs;
+        }
+        __syncwarp();
+    }
 }
 
 }  // namespace rcu

@@ -182,3 +182,20 @@ def test_layerwise_qwen3_moe_config4(env):
     gm, om, ob = build_pair(env, spec, O.KV_F16, seed=4)
     w = teacher_forced(env, gm, om, ob, spec, O.KV_F16, [3, 1000, 77, 12345, 8], [19, 151000])
     print("config 4 teacher-forced worst rel errors (rows, layer contribution, logits, rows bound, median contribution):", w)
+
+
+@pytest.mark.parametrize("group", [4, 8])
+@pytest.mark.parametrize("kv", [O.KV_F16, O.KV_Q8_0, O.KV_TURBO4], ids=["f16", "q8_0", "turbo4"])
+def test_layerwise_decode_attention_hd128(env, kv, group):
+    """head_dim 128 with 4 or 8 query heads per KV head over every cache type: the decode steps
+    run the decode attention kernels, for f16 and Q8_0 caches with the q/k post-processing (q/k
+    norm, RoPE, KV append) folded into them; the prompt and turbo4 caches use the standalone
+    kernels. All held to the layer bounds above."""
+    from rust_interference_engine_b200 import model as M
+    spec = M.SyntheticSpec(arch="qwen3", wtype=GgmlType.Q4_K, embd_type=GgmlType.Q8_0, qk_norm=True, n_vocab=512,
+                           n_embd=1024, n_layer=2, n_head=8, n_head_kv=8 // group, head_dim=128, n_ff=2048,
+                           rope_dim=128, rope_base=1_000_000.0, rms_eps=1e-6)
+    gm, om, ob = build_pair(env, spec, kv, seed=40 + group)
+    w = teacher_forced(env, gm, om, ob, spec, kv, [5, 17, 200, 3, 99, 42, 7], [11, 12, 13, 14])
+    print("hd128 G", group, "kv", kv, "worst (rows, contribution, logits, rows bound, median contribution):", w)
+
