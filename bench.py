@@ -350,6 +350,16 @@ def measured_int8_peak(torch):
         return 4500.0, f"nominal 4.5 POPS dense int8 ({type(e).__name__})"
 
 
+def fma_peak() -> float:
+    """f32 FMAs per second of the FP32 pipe: 148 SMs x 128 lanes x the maximum SM clock."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f).get("sm_max_mhz", 1965.0))
+    except Exception:
+        mhz = 1965.0
+    return 148 * 128 * mhz * 1e6
+
+
 def prefill_meta(gemm: str):
     """The prefill line names the arithmetic it measures: f16 tensor-core MMA on dequantized
     operands (default) or int8 MMA with the reference's exact block sums (--gemm i8)."""
@@ -428,9 +438,9 @@ def run_prefill(args, world, rank, local):
     i8_peak, i8_kind = measured_int8_peak(torch)
     achieved = flops / (kern_ms * 1e-3) / 1e12
     if i8:
-        peak, peak_kind, kernel = i8_peak, i8_kind, "k_gemm<Q4_0> (tcgen05 kind::i8)"
+        peak, peak_kind, kernel = i8_peak, i8_kind, "k_gemm_i8 (tcgen05 kind::i8, both weights in one launch)"
         dtype = "int8 (Q4_0 x Q8_0 blocks, tcgen05 kind::i8, exact block sums, f32 block-scale epilogue)"
-        launches = 1 + len(PF_N)
+        launches = 2  # activation quantization + one GEMM launch
     else:
         peak, peak_kind = bf16_peak()
         kernel = "k_acts_f16 + k_gemm_f16<Q4_0> (tcgen05 kind::f16, both weights in one launch)"
@@ -448,10 +458,14 @@ def run_prefill(args, world, rank, local):
         "config": {"workload": pm["workload"], "m": PF_M, "k": PF_K, "n": list(PF_N),
                    "ops_per_step": flops, "l2": "weights 42 MB + activations (L2-resident re-use by design)",
                    "parallelism": f"replicas x{world}", "gemm": args.gemm,
-                   "int8_peak_tops": i8_peak, "frac_of_int8_peak": achieved / i8_peak},
+                   "int8_peak_tops": i8_peak, "frac_of_int8_peak": achieved / i8_peak,
+                   # exact block sums cost two f32 FMAs per output per 32-value block (d_w, then d_a):
+                   # at 128 FMA per clock per SM that work alone bounds the int8 kernel
+                   "fp32_epilogue_bound_tops": flops / (2 * PF_M * sum(PF_N) * (PF_K // 32) / fma_peak()) / 1e12,
+                   "frac_of_epilogue_bound": achieved / (flops / (2 * PF_M * sum(PF_N) * (PF_K // 32) / fma_peak()) / 1e12)},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": pm["unit"], "frac": achieved / peak,
                      "peak_source": peak_kind,
-                     "traffic": profile_traffic("gemm_q4_0_config2" if i8 else "gemm_f16_q4_0_config2"),
+                     "traffic": profile_traffic("gemm_i8_q4_0_config2" if i8 else "gemm_f16_q4_0_config2"),
                      "kernel": kernel, "launch_ms": kern_ms,
                      "note": "achieved = 2*M*K*N over the matmul_multi call (activation f16 prep + GEMM)"},
         "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": pm["unit"],

@@ -1,38 +1,54 @@
-// rcu_gemm.cu -- prefill GEMM (n_tok > 8) on the 5th-generation tensor cores.
+// rcu_gemm.cu -- prefill GEMM (n_tok >= 32) with the reference's exact int8 block sums, on the
+// 5th-generation tensor cores (Q4_0 weights x Q8_0 activations).
 //
 // Y[t][n] = sum_b d_a[t][b] * d_w[n][b] * S_b[t][n], with S_b the exact int32 dot of block b
 // (the reference forms the same per-block ints one row at a time:
 // crates/rie-core/src/kernels/matmul.rs:178-241 via vec_dot / vec_dot_x4,
 // crates/rie-core/src/quant/reference.rs:221-293).
 //
-// Per CTA: a 128-weight-row x 128-token output tile.
-//   * warp 0   TMA producer: raw GGUF weight bytes (2-D tensor map over [rows][row_bytes],
-//              8 blocks = K 256 per stage), int8 activation codes (128B-swizzled, K-major)
-//              and the activation block scales;
-//   * warps 1-4 unpack: GGUF blocks -> int8 weight tile in the canonical 128B-swizzled
-//              K-major layout the tensor core reads, plus per-row f32 block scales;
-//   * warp 5   MMA issuer: one tcgen05.mma.kind::i8 (M=128, N=128, K=32) per 32-value
-//              block into one of two TMEM accumulators (double buffered);
-//   * warps 6-13 epilogue: tcgen05.ld the block's int32 sums, re-arm the accumulator with
-//              the f32 magic 1.5*2^23 (so the next block's int sum S reads back as the
-//              float 1.5*2^23 + S exactly), and fold each block into f32 accumulators with
-//              two packed FMAs: t = fma(X, d_w, -1.5*2^23*d_w) = round(S * d_w) exactly
-//              once, acc = fma(t, d_a, acc).
+// Roofline: one tcgen05 kind::i8 MMA (M 128, N 128, K 32) per block forms every S_b of a tile,
+// but each S_b then needs its own f32 scaling -- two FMAs per output per 32 values of K -- so
+// the kernel is bound by the FP32 pipe (128 FMA per clock per SM), not by the tensor pipe.
+//
+// Per CTA: a 128-weight-row x 128-token output tile; the grid walks the row tiles of up to
+// four weights that share the activations (q/k/v, gate/up) in one launch.
+//   * warp 0    TMA producer: raw GGUF rows (8 blocks = K 256 per stage), int8 activation codes
+//               (128B-swizzled, K-major) and the activation block scales; 2 operand stages,
+//               released by the MMA commit;
+//   * warps 1-2 unpack: GGUF blocks -> int8 weight tile in the 128B-swizzled K-major layout
+//               the tensor core reads; the block scales d_w and the transposed d_a go to a
+//               4-slot scale ring that only the epilogue releases;
+//   * warp 3    MMA issuer: one tcgen05.mma.kind::i8 per block into one of four TMEM
+//               accumulators (128 columns each, the whole tensor memory), so the tensor core
+//               runs up to four blocks ahead of the epilogue;
+//   * warps 4-19 epilogue: warp w reads TMEM lanes 32*(w%4).. and one quarter of the tokens:
+//               tcgen05.ld of the block's 32 int32 sums, re-arm the accumulator with the f32
+//               magic 1.5*2^23 (the next block's int sum S then reads back as the float
+//               1.5*2^23 + S exactly), and two packed FMAs per pair of outputs:
+//               t = fma(X, d_w, -1.5*2^23*d_w) = round(S * d_w), acc = fma(t, d_a, acc).
 // All waits are bounded; TMEM is freed on every exit path.
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstring>
 
 #include "rcu_kernels.h"
 #include "rcu_tc.cuh"
 
 namespace rcu {
 
-constexpr int kTileN = 128;   // weight rows per CTA (MMA M)
-constexpr int kTileM = 128;   // tokens per CTA (MMA N)
-constexpr int kStageBlocks = 8;  // 32-value blocks per stage (K = 256)
-constexpr int kStages = 2;
-constexpr int kGemmThreads = 14 * 32;
+constexpr int kTileN = 128;        // weight rows per CTA (MMA M, TMEM lanes)
+constexpr int kTileM = 128;        // tokens per CTA (MMA N)
+constexpr int kStageBlocks = 8;    // 32-value blocks per operand stage (K = 256)
+constexpr int kStages = 2;         // operand stages (raw weights, unpacked weights, activations)
+constexpr int kScaleSlots = 4;     // scale ring (d_w, transposed d_a), one slot per stage
+constexpr int kTBufs = 2;          // TMEM accumulator pairs: two blocks of 128 columns each
+constexpr int kEpiWarps = 16;
+constexpr int kEpiWarp0 = 4;       // warps: 0 producer, 1-2 unpack, 3 MMA, 4.. epilogue
+constexpr int kGemmThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kRawBox = kStageBlocks * 18;  // Q4_0 bytes per row per stage (144, 16-byte multiple)
+constexpr int kMaxI8Jobs = 4;
 constexpr uint32_t kGemmMinTok = 32;  // below this the 8-token GEMV slices are faster
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
@@ -41,20 +57,27 @@ struct GemmSmem {
     // 1024-aligned operand tiles first
     uint8_t a[kStages][2][kTileN * 128];   // unpacked weights, 2 swizzle atoms of K 128
     uint8_t b[kStages][2][kTileM * 128];   // activation codes (TMA, 128B swizzle)
-    uint8_t raw[kStages][kTileN * 144];    // raw GGUF bytes, 8 Q4_0 blocks (or 4.x Q8_0) per row
-    float da[kStages][kTileM][kStageBlocks];
-    float dw[kStages][kStageBlocks][kTileN];
-    float nm[kStages][kStageBlocks][kTileN];
+    uint8_t raw[kStages][kTileN * kRawBox];
+    float da[kStages][kTileM][kStageBlocks];      // activation block scales as TMA lands them
+    float daT[kScaleSlots][kStageBlocks][kTileM];  // ... transposed: one block's 128 tokens contiguous
+    float dw[kScaleSlots][kStageBlocks][kTileN];
     uint64_t full[kStages], unpacked[kStages], empty[kStages];
-    uint64_t tfull[2], tempty[2];
+    uint64_t sfull[kScaleSlots], sempty[kScaleSlots];
+    uint64_t tfull[kTBufs], tempty[kTBufs];  // one handoff per pair of blocks
     uint32_t tmem_base;
 };
 
-struct GemmParams {
-    const uint8_t *w;          // unused by the kernel (tensor map), kept for bounds
+struct I8Job {
     float *out;
     uint64_t ld;
-    uint32_t rows, k, n_tok, type, row_bytes, raw_box;  // raw_box: bytes per row per stage
+    uint32_t rows, tile0;  // weight rows; first grid-x tile of this job
+};
+struct I8Maps {
+    CUtensorMap w[kMaxI8Jobs];  // raw GGUF bytes [rows][row_bytes] of each job
+};
+struct GemmParams {
+    I8Job job[kMaxI8Jobs];
+    uint32_t n_jobs, k, n_tok;
     uint32_t *err;
 };
 
@@ -78,88 +101,94 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return *reinterpret_cast<float2 *>(&r);
 }
 
-// Unpack one 32-value block into 32 int8 codes (two 16-byte chunks, element order).
-template <int TYPE>
-__device__ __forceinline__ void unpack_block(const uint8_t *raw, uint32_t off, uint4 &c0, uint4 &c1, float &d) {
-    if (TYPE == T_Q4_0) {
-        uint32_t w[5];
-        {
-            const uint32_t *p = reinterpret_cast<const uint32_t *>(raw + (off & ~3u));
-            const uint32_t sh = (off & 3u) * 8u;
-            uint32_t r[6];
+// A raw row of 8 Q4_0 blocks (144 bytes) as 36 words: 9 16-byte loads, conflict-free for the
+// 8 lanes of a load phase (row stride 144 B = 9 chunks, odd).
+__device__ __forceinline__ void load_raw_row(const uint8_t *row, uint32_t (&w)[36]) {
 #pragma unroll
-            for (int i = 0; i < 6; i++) r[i] = p[i];
-#pragma unroll
-            for (int i = 0; i < 5; i++) w[i] = __funnelshift_rc(r[i], r[i + 1], sh);
-        }
-        d = f16_bits_to_f32(w[0]);
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t q = __funnelshift_r(w[i], w[i + 1], 16);
-            // nibble -> int8 (nib - 8): flip bit 3 then sign-extend the 4-bit value
-            const uint32_t l = (q & 0x0F0F0F0Fu) ^ 0x08080808u, h = ((q >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-            lo[i] = l | ((l & 0x08080808u) * 30u);
-            hi[i] = h | ((h & 0x08080808u) * 30u);
-        }
-        c0 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        c1 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    } else {  // Q8_0: 34-byte blocks, codes already int8
-        uint32_t w[9];
-        const uint32_t *p = reinterpret_cast<const uint32_t *>(raw + (off & ~3u));
-        const uint32_t sh = (off & 3u) * 8u;
-        uint32_t r[10];
-#pragma unroll
-        for (int i = 0; i < 10; i++) r[i] = p[i];
-#pragma unroll
-        for (int i = 0; i < 9; i++) w[i] = __funnelshift_rc(r[i], r[i + 1], sh);
-        d = f16_bits_to_f32(w[0]);
-        uint32_t q[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
-        c0 = make_uint4(q[0], q[1], q[2], q[3]);
-        c1 = make_uint4(q[4], q[5], q[6], q[7]);
+    for (int i = 0; i < 9; i++) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(row + 16 * i);
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
     }
 }
+// Block J of the row (bytes 18J..18J+17): its f32 scale and 32 int8 codes (nib - 8) in element
+// order as two 16-byte chunks. J is a compile-time constant, so every shift is one too.
+template <int J>
+__device__ __forceinline__ void unpack_q4_0(const uint32_t (&w)[36], uint4 &c0, uint4 &c1, float &d) {
+    constexpr int W = (18 * J) / 4;  // word holding the scale
+    uint32_t q[4];
+    if ((J & 1) == 0) {  // scale in the low half of word W, nibbles from byte 2 of it
+        d = f16_bits_to_f32(w[W] & 0xFFFFu);
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(w[W + i], w[W + i + 1], 16);
+    } else {  // scale in the high half of word W, nibbles word-aligned after it
+        d = f16_bits_to_f32(w[W] >> 16);
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = w[W + 1 + i];
+    }
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        // nibble -> int8 (nib - 8): flip bit 3 then sign-extend the 4-bit value
+        const uint32_t l = (q[i] & 0x0F0F0F0Fu) ^ 0x08080808u, h = ((q[i] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+        lo[i] = l | ((l & 0x08080808u) * 30u);
+        hi[i] = h | ((h & 0x08080808u) * 30u);
+    }
+    c0 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    c1 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+}
+template <int J>
+__device__ __forceinline__ void unpack_store(const uint32_t (&w)[36], uint8_t *a0, uint8_t *a1, uint32_t r,
+                                             float *dw_j0) {
+    uint4 c0, c1;
+    float d;
+    unpack_q4_0<J>(w, c0, c1, d);
+    uint8_t *rowp = (J < 4 ? a0 : a1) + r * 128;
+    constexpr uint32_t ch = 2 * (J & 3);
+    *reinterpret_cast<uint4 *>(rowp + (((ch) ^ (r & 7)) << 4)) = c0;
+    *reinterpret_cast<uint4 *>(rowp + (((ch + 1) ^ (r & 7)) << 4)) = c1;
+    dw_j0[J * kTileN + r] = d;
+}
 
-template <int TYPE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    k_gemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
-           const __grid_constant__ CUtensorMap map_da, const __grid_constant__ GemmParams p) {
+    k_gemm_i8(const __grid_constant__ I8Maps maps, const __grid_constant__ CUtensorMap map_a,
+              const __grid_constant__ CUtensorMap map_da, const __grid_constant__ GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     GemmSmem &S = *reinterpret_cast<GemmSmem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    constexpr uint32_t BB = TYPE == T_Q4_0 ? 18 : 34;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * kTileN, m0 = blockIdx.y * kTileM;
-    const uint32_t nb = p.k / QK, n_iter = nb / kStageBlocks;
+    uint32_t ji = 0;
+    while (ji + 1 < p.n_jobs && blockIdx.x >= p.job[ji + 1].tile0) ji++;
+    const I8Job &jb = p.job[ji];
+    const uint32_t n0 = (blockIdx.x - jb.tile0) * kTileN, m0 = blockIdx.y * kTileM;
+    const uint32_t n_iter = p.k / QK / kStageBlocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.unpacked[s], 4);
-            mbar_init(&S.empty[s], 1 + 8);  // MMA commit + 8 epilogue warps
+            mbar_init(&S.unpacked[s], 2);
+            mbar_init(&S.empty[s], 1);  // the MMA commit of the stage's blocks
         }
-        for (int b = 0; b < 2; b++) {
+        for (int j = 0; j < kScaleSlots; j++) {
+            mbar_init(&S.sfull[j], 2);
+            mbar_init(&S.sempty[j], kEpiWarps);
+        }
+        for (int b = 0; b < kTBufs; b++) {
             mbar_init(&S.tfull[b], 1);
-            mbar_init(&S.tempty[b], 8);
+            mbar_init(&S.tempty[b], kEpiWarps);
         }
         fence_mbar_init();
     }
-    if (warp == 5) {  // TMEM: 2 accumulators x 128 columns
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&S.tmem_base))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == 3) tmem_alloc<kTBufs * 256>(&S.tmem_base);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
+    const int q = warp & 3, cq = (warp - kEpiWarp0) >> 2;  // epilogue: TMEM lane quarter, token quarter
 
-    if (warp >= 6) {  // arm both accumulators with the magic offset
-        const int e = warp - 6, q = warp & 3, h = e >> 2;
-        for (int b = 0; b < 2; b++)
-            for (int c = 0; c < 2; c++)
-                tmem_st32_const(tmem + ((uint32_t)(32 * q) << 16) + b * 128 + 64 * h + 32 * c, kMagicBits);
+    if (warp >= kEpiWarp0) {  // arm every accumulator with the magic offset
+        for (int b = 0; b < 2 * kTBufs; b++) tmem_st32_const(tmem + ((uint32_t)(32 * q) << 16) + b * 128 + 32 * cq, kMagicBits);
         tmem_wait_st();
     }
     tc_fence_before();
@@ -168,132 +197,147 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (warp == 0) {  // ---- TMA producer ----
         if (lane == 0) {
+            const CUtensorMap *mw = &maps.w[ji];
             for (uint32_t it = 0; it < n_iter; it++) {
                 const uint32_t s = it % kStages;
-                if (it >= kStages && !mbar_wait_bounded(&S.empty[s], ((it / kStages) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
+                if (it >= kStages && !mbar_wait_sleep(&S.empty[s], ((it / kStages) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
                     break;
-                const uint32_t bytes = kTileN * p.raw_box + 2 * kTileM * 128 + kTileM * kStageBlocks * 4;
+                constexpr uint32_t bytes = kTileN * kRawBox + 2 * kTileM * 128 + kTileM * kStageBlocks * 4;
                 mbar_arrive_expect_tx(&S.full[s], bytes);
-                tma_load_2d(S.raw[s], &map_w, (int)(it * kStageBlocks * BB), (int)n0, &S.full[s]);
+                tma_load_2d(S.raw[s], mw, (int)(it * kRawBox), (int)n0, &S.full[s]);
                 tma_load_2d(S.b[s][0], &map_a, (int)(it * 256), (int)m0, &S.full[s]);
                 tma_load_2d(S.b[s][1], &map_a, (int)(it * 256 + 128), (int)m0, &S.full[s]);
                 tma_load_2d(S.da[s], &map_da, (int)(it * kStageBlocks), (int)m0, &S.full[s]);
             }
         }
-    } else if (warp <= 4) {  // ---- unpack (128 threads, one weight row each) ----
-        const uint32_t r = threadIdx.x - 32;
+    } else if (warp <= 2) {  // ---- unpack (64 threads: weight rows r and r + 64, their tokens' scales) ----
+        const uint32_t t = threadIdx.x - 32;
         for (uint32_t it = 0; it < n_iter; it++) {
-            const uint32_t s = it % kStages;
-            if (!mbar_wait_bounded(&S.full[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL)) break;
-            const uint8_t *raw = S.raw[s] + r * p.raw_box;
-#pragma unroll 2
-            for (int j = 0; j < kStageBlocks; j++) {
-                uint4 c0, c1;
-                float d;
-                unpack_block<TYPE>(raw, j * BB, c0, c1, d);
-                uint8_t *rowp = S.a[s][j >> 2] + r * 128;
-                const uint32_t ch = 2 * (j & 3);
-                *reinterpret_cast<uint4 *>(rowp + (((ch) ^ (r & 7)) << 4)) = c0;
-                *reinterpret_cast<uint4 *>(rowp + (((ch + 1) ^ (r & 7)) << 4)) = c1;
-                S.dw[s][j][r] = d;
-                S.nm[s][j][r] = -kMagic * d;
+            const uint32_t s = it % kStages, slot = it % kScaleSlots;
+            if (!mbar_wait_sleep(&S.full[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+            if (it >= kScaleSlots &&
+                !mbar_wait_sleep(&S.sempty[slot], ((it / kScaleSlots) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
+                break;
+#pragma unroll 1
+            for (uint32_t r = t; r < kTileN; r += 64) {
+                uint32_t w[36];
+                load_raw_row(S.raw[s] + r * kRawBox, w);
+                uint8_t *a0 = S.a[s][0], *a1 = S.a[s][1];
+                float *dwp = &S.dw[slot][0][0];
+                unpack_store<0>(w, a0, a1, r, dwp);
+                unpack_store<1>(w, a0, a1, r, dwp);
+                unpack_store<2>(w, a0, a1, r, dwp);
+                unpack_store<3>(w, a0, a1, r, dwp);
+                unpack_store<4>(w, a0, a1, r, dwp);
+                unpack_store<5>(w, a0, a1, r, dwp);
+                unpack_store<6>(w, a0, a1, r, dwp);
+                unpack_store<7>(w, a0, a1, r, dwp);
+                const float4 v0 = *reinterpret_cast<const float4 *>(&S.da[s][r][0]);
+                const float4 v1 = *reinterpret_cast<const float4 *>(&S.da[s][r][4]);
+                S.daT[slot][0][r] = v0.x;
+                S.daT[slot][1][r] = v0.y;
+                S.daT[slot][2][r] = v0.z;
+                S.daT[slot][3][r] = v0.w;
+                S.daT[slot][4][r] = v1.x;
+                S.daT[slot][5][r] = v1.y;
+                S.daT[slot][6][r] = v1.z;
+                S.daT[slot][7][r] = v1.w;
             }
-            fence_async_smem();
+            fence_async_smem();  // the unpacked tile is read by the tensor core (async proxy)
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.unpacked[s]);
+            if (lane == 0) {
+                mbar_arrive(&S.unpacked[s]);
+                mbar_arrive(&S.sfull[slot]);
+            }
         }
-    } else if (warp == 5) {  // ---- MMA issuer ----
+    } else if (warp == 3) {  // ---- MMA issuer ----
         if (lane == 0) {
             uint32_t b = 0;
             bool ok = true;
             for (uint32_t it = 0; it < n_iter && ok; it++) {
                 const uint32_t s = it % kStages;
-                if (!mbar_wait_bounded(&S.unpacked[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL) ||
-                    !mbar_wait_bounded(&S.full[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL)) {
-                    ok = false;
+                if (!mbar_wait_sleep(&S.unpacked[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL) ||
+                    !mbar_wait_sleep(&S.full[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL))
                     break;
-                }
                 tc_fence_after();
-                for (int j = 0; j < kStageBlocks; j++, b++) {
-                    const uint32_t buf = b & 1;
-                    if (!mbar_wait_bounded(&S.tempty[buf], ((b >> 1) + 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+                for (int j = 0; j < kStageBlocks; j += 2, b++) {  // b counts pairs of blocks
+                    const uint32_t buf = b % kTBufs;
+                    if (b >= kTBufs && !mbar_wait_sleep(&S.tempty[buf], ((b / kTBufs) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = sw128_desc(S.a[s][j >> 2] + 32 * (j & 3));
-                    const uint64_t bd = sw128_desc(S.b[s][j >> 2] + 32 * (j & 3));
-                    mma_i8(tmem + buf * 128, ad, bd);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const uint64_t ad = sw128_desc(S.a[s][(j + h) >> 2] + 32 * ((j + h) & 3));
+                        const uint64_t bd = sw128_desc(S.b[s][(j + h) >> 2] + 32 * ((j + h) & 3));
+                        mma_i8(tmem + buf * 256 + h * 128, ad, bd);
+                    }
                     mma_commit(&S.tfull[buf]);
                 }
                 mma_commit(&S.empty[s]);
             }
         }
-    } else {  // ---- epilogue (warps 6..13) ----
-        const int e = warp - 6, q = warp & 3, h = e >> 2;
+    } else {  // ---- epilogue (warps 4..19) ----
         const uint32_t nrow = 32 * q + lane;  // weight row within the tile
-        float2 acc[32];
+        float2 acc[16];
 #pragma unroll
-        for (int c = 0; c < 32; c++) acc[c] = make_float2(0.0f, 0.0f);
+        for (int c = 0; c < 16; c++) acc[c] = make_float2(0.0f, 0.0f);
         uint32_t b = 0;
         bool ok = true;
         for (uint32_t it = 0; it < n_iter && ok; it++) {
-            const uint32_t s = it % kStages;
-            // scales of this stage: d_a landed by TMA (full), d_w written by the unpack warps
-            if (!mbar_wait_bounded(&S.full[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL) ||
-                !mbar_wait_bounded(&S.unpacked[s], (it / kStages) & 1, p.err, ERR_TIMEOUT_FULL))
-                break;
-            for (int j = 0; j < kStageBlocks; j++, b++) {
-                const uint32_t buf = b & 1;
-                if (!mbar_wait_bounded(&S.tfull[buf], (b >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) {
+            const uint32_t slot = it % kScaleSlots;
+            if (!mbar_wait_sleep(&S.sfull[slot], (it / kScaleSlots) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+            for (int j = 0; j < kStageBlocks; j += 2, b++) {  // b counts pairs of blocks
+                const uint32_t buf = b % kTBufs;
+                if (!mbar_wait_sleep(&S.tfull[buf], (b / kTBufs) & 1, p.err, ERR_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + buf * 128 + 64 * h;
-                const float dw = S.dw[s][j][nrow], nm = S.nm[s][j][nrow];
-                const float2 dw2 = make_float2(dw, dw), nm2 = make_float2(nm, nm);
-                const float *dap = &S.da[s][64 * h][j];
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
+#pragma unroll 1
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + buf * 256 + h * 128 + 32 * cq;
+                    const float dw = S.dw[slot][j + h][nrow];
+                    const float2 dw2 = make_float2(dw, dw), nm2 = make_float2(-kMagic * dw, -kMagic * dw);
+                    const float4 *dap = reinterpret_cast<const float4 *>(&S.daT[slot][j + h][32 * cq]);
                     uint32_t x[32];
-                    tmem_ld32(ta + 32 * half, x);
+                    tmem_ld32(ta, x);
                     tmem_wait_ld();
-                    tmem_st32_const(ta + 32 * half, kMagicBits);  // re-arm for the block after next
-                    if (half == 1) {
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S.tempty[buf]);
-                    }
 #pragma unroll
-                    for (int c = 0; c < 16; c++) {
-                        const int col = 32 * half + 2 * c;
-                        const float2 xv = make_float2(__uint_as_float(x[2 * c]), __uint_as_float(x[2 * c + 1]));
-                        const float2 da = make_float2(dap[col * kStageBlocks], dap[(col + 1) * kStageBlocks]);
-                        acc[16 * half + c] = ffma2(ffma2(xv, dw2, nm2), da, acc[16 * half + c]);
+                    for (int i = 0; i < 8; i++) {
+                        const float4 d4 = dap[i];
+                        const float2 x0 = make_float2(__uint_as_float(x[4 * i]), __uint_as_float(x[4 * i + 1]));
+                        const float2 x1 = make_float2(__uint_as_float(x[4 * i + 2]), __uint_as_float(x[4 * i + 3]));
+                        acc[2 * i] = ffma2(ffma2(x0, dw2, nm2), make_float2(d4.x, d4.y), acc[2 * i]);
+                        acc[2 * i + 1] = ffma2(ffma2(x1, dw2, nm2), make_float2(d4.z, d4.w), acc[2 * i + 1]);
                     }
+                    tmem_st32_const(ta, kMagicBits);  // re-arm for the pair after next
                 }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.tempty[buf]);
             }
             __syncwarp();
-            if (ok && lane == 0) mbar_arrive(&S.empty[s]);
+            if (ok && lane == 0) mbar_arrive(&S.sempty[slot]);
         }
         const uint32_t n = n0 + nrow;
-        if (n < p.rows) {
+        if (n < jb.rows) {
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                const uint32_t m = m0 + 64 * h + 2 * c;
-                if (m < p.n_tok) p.out[(uint64_t)m * p.ld + n] = acc[c].x;
-                if (m + 1 < p.n_tok) p.out[(uint64_t)(m + 1) * p.ld + n] = acc[c].y;
+            for (int c = 0; c < 16; c++) {
+                const uint32_t m = m0 + 32 * cq + 2 * c;
+                if (m < p.n_tok) jb.out[(uint64_t)m * jb.ld + n] = acc[c].x;
+                if (m + 1 < p.n_tok) jb.out[(uint64_t)(m + 1) * jb.ld + n] = acc[c].y;
             }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 3) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+        tmem_free<kTBufs * 256>(tmem);
     }
 }
 
@@ -328,55 +372,56 @@ int make_map_2d(rcu_ctx *ctx, CUtensorMap *m, CUtensorMapDataType dt, const void
     return RCU_OK;
 }
 
-template <int TYPE>
-static int launch_type(rcu_ctx *ctx, const ActsView &a, const HostJob &j) {
+static bool gemm_ok(const ActsView &a, const HostJob &j) {
     const rcu_weight *w = j.w;
-    constexpr uint32_t BB = TYPE == T_Q4_0 ? 18 : 34;
+    if (w->type != T_Q4_0) return false;  // other types run the f16 GEMM
+    if (a.k % 256 != 0 || (w->row_bytes & 15) != 0 || (((uintptr_t)w->data) & 15) != 0) return false;
+    return a.n_tok >= kGemmMinTok;
+}
+
+// One launch for up to four Q4_0 weights over the same activations.
+static int launch_i8_group(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     GemmParams p{};
-    p.out = j.out;
-    p.ld = j.ld;
-    p.rows = (uint32_t)w->rows;
+    I8Maps maps;
+    memset(&maps, 0, sizeof(maps));
+    uint32_t tiles = 0;
+    for (int i = 0; i < n_jobs; i++) {
+        const rcu_weight *w = jobs[i].w;
+        p.job[i] = I8Job{jobs[i].out, jobs[i].ld, (uint32_t)w->rows, tiles};
+        tiles += (uint32_t)((w->rows + kTileN - 1) / kTileN);
+        if (int st = make_map_2d(ctx, &maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->row_bytes, w->rows,
+                                 w->row_bytes, kRawBox, kTileN, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return st;
+    }
+    p.n_jobs = (uint32_t)n_jobs;
     p.k = a.k;
     p.n_tok = a.n_tok;
-    p.type = TYPE;
-    p.row_bytes = (uint32_t)w->row_bytes;
-    p.raw_box = kStageBlocks * BB;  // 144 (Q4_0) or 272 (Q8_0) bytes per row per stage
     p.err = ctx->dev_err;
-    CUtensorMap mw, ma, mda;
-    int st = make_map_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->row_bytes, w->rows, w->row_bytes,
-                         p.raw_box, kTileN, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st) return st;
-    st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.q0, a.k, a.n_tok, a.k, 128, kTileM,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap ma, mda;
+    int st = make_map_2d(ctx, &ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.q0, a.k, a.n_tok, a.k, 128, kTileM,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     st = make_map_2d(ctx, &mda, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.d0, a.k / QK, a.n_tok, (uint64_t)(a.k / QK) * 4,
                      kStageBlocks, kTileM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
     const size_t smem = sizeof(GemmSmem) + 1024;
-    static bool attr[64] = {};
-    if (!attr[ctx->device & 63]) {
-        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemm<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr[ctx->device & 63] = true;
+    static std::atomic<bool> attr[64];
+    if (!attr[ctx->device & 63].load(std::memory_order_acquire)) {
+        RCU_CUDA_TRY(ctx, cudaFuncSetAttribute(k_gemm_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr[ctx->device & 63].store(true, std::memory_order_release);
     }
-    dim3 grid((p.rows + kTileN - 1) / kTileN, (p.n_tok + kTileM - 1) / kTileM);
-    k_gemm<TYPE><<<grid, kGemmThreads, smem, ctx->stream>>>(mw, ma, mda, p);
+    const dim3 grid(tiles, (p.n_tok + kTileM - 1) / kTileM);
+    k_gemm_i8<<<grid, kGemmThreads, smem, ctx->stream>>>(maps, ma, mda, p);
     RCU_CUDA_TRY(ctx, cudaGetLastError());
     return RCU_OK;
-}
-
-static bool gemm_ok(const ActsView &a, const HostJob &j) {
-    const rcu_weight *w = j.w;
-    if (w->type != T_Q4_0) return false;  // other types run the GEMV in 8-token slices
-    if (a.k % 256 != 0 || (w->row_bytes & 15) != 0 || (((uintptr_t)w->data) & 15) != 0) return false;
-    return a.n_tok >= kGemmMinTok;
 }
 
 static int launch_gemm_i8(rcu_ctx *ctx, const ActsView &a, const HostJob *jobs, int n_jobs) {
     if (sizeof(GemmSmem) + 1024 > ctx->max_smem_optin) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: smem");
     for (int i = 0; i < n_jobs; i++)
         if (!gemm_ok(a, jobs[i])) return set_err(ctx, RCU_ERR_UNSUPPORTED, "gemm: type or shape not supported");
-    for (int i = 0; i < n_jobs; i++) {
-        const int st = launch_type<T_Q4_0>(ctx, a, jobs[i]);
+    for (int i = 0; i < n_jobs; i += kMaxI8Jobs) {
+        const int st = launch_i8_group(ctx, a, jobs + i, std::min(kMaxI8Jobs, n_jobs - i));
         if (st) return st;
     }
     return RCU_OK;

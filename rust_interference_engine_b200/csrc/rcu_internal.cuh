@@ -125,6 +125,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
         }
     }
 }
+// As mbar_wait_bounded, but each try_wait may suspend the thread for up to `hint_ns` until the
+// phase completes (fewer spin instructions taken from the warps doing the work).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code) {
+    constexpr uint32_t kHintNs = 100000;  // 0.1 ms; the phase completing wakes the thread earlier
+    if (mbar_try_wait_hint(bar, parity, kHintNs)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, kHintNs)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(err, code);
+            return false;
+        }
+    }
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

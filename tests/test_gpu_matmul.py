@@ -241,20 +241,54 @@ def test_prefill_gemm_f16_large_activations(env, t):
         close(got[i], want[i])
 
 
-@pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 512), (128, 256, 4096)])
-def test_prefill_gemm_q4_0_int8_kind(env, n_tok, rows, k):
-    # the int8 GEMM (exact per-block sums) stays selectable for Q4_0
+def gpu_matmul_i8(env, weights, x):
+    """gpu_matmul through the int8 GEMM (exact per-block int32 sums, Q4_0 weights)."""
     torch, rie, ctx = env
+    ctx.set_prefill_gemm(rie.PrefillGemm.I8)
+    try:
+        return gpu_matmul(env, weights, x)[0]
+    finally:
+        ctx.set_prefill_gemm(rie.PrefillGemm.F16)
+
+
+@pytest.mark.parametrize("n_tok,rows,k", [(32, 200, 512), (128, 256, 4096), (64, 333, 4096), (100, 1000, 2048),
+                                          (200, 130, 1024), (300, 129, 4096), (512, 4096, 4096)])
+def test_prefill_gemm_q4_0_int8_kind(env, n_tok, rows, k):
+    # the int8 GEMM (tcgen05 kind::i8, exact per-block sums): ragged token and row tiles, several K
     rng = O.Rng(3000 + n_tok + rows)
     w = rng.weight(O.Q4_0, rows, k)
     x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
-    ctx.set_prefill_gemm(rie.PrefillGemm.I8)
-    try:
-        got = gpu_matmul(env, [(O.Q4_0, w, k)], x)[0][0]
-    finally:
-        ctx.set_prefill_gemm(rie.PrefillGemm.F16)
+    got = gpu_matmul_i8(env, [(O.Q4_0, w, k)], x)[0]
     want = O.matmul_multi(x, [(O.Q4_0, w, k)], n_threads=8)[0]
     close(got, want)
+
+
+def test_prefill_gemm_int8_jobs_share_a_launch(env):
+    # up to four weights over the same activations run as one launch (five jobs: 4 + 1), each
+    # with ragged rows; repeated calls agree bit for bit (one thread owns each output)
+    rng = O.Rng(31)
+    k, n_tok = 2048, 160
+    x = rng.vec(n_tok * k, 1.0).reshape(n_tok, k)
+    ws = [(O.Q4_0, rng.weight(O.Q4_0, r, k), k) for r in (512, 130, 128, 1, 300)]
+    got = gpu_matmul_i8(env, ws, x)
+    want = O.matmul_multi(x, ws, n_threads=8)
+    for g, wv in zip(got, want):
+        close(g, wv)
+    again = gpu_matmul_i8(env, ws, x)
+    assert all(np.array_equal(a, b) for a, b in zip(got, again))
+
+
+def test_prefill_gemm_int8_config2(env):
+    # benchmark configuration 2 through the int8 GEMM: M = 512 tokens x K = 4096 against the
+    # N = 14336 and N = 4096 weights (W ~ N(0, 0.02) -> Q4_0) in one launch
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((512, 4096)).astype(np.float32)
+    ws = [(O.Q4_0, O.quantize_weight(O.Q4_0, rng.normal(0.0, 0.02, (n, 4096)).astype(np.float32)), 4096)
+          for n in (14336, 4096)]
+    got = gpu_matmul_i8(env, ws, x)
+    want = O.matmul_multi(x, ws, n_threads=8)
+    for g, wv in zip(got, want):
+        close(g, wv)
 
 
 def test_prefill_gemm_config2(env):
