@@ -338,20 +338,40 @@ __device__ void dec_finish(const DecParams &p, uint8_t *dsm, float (*wm)[G], flo
         named_bar_sync(1, kDW * 32);
         if (!s_last) return;
         __threadfence();
-        for (uint32_t e = tid; e < (uint32_t)G * kDHd; e += kDW * 32) {
-            const uint32_t h = e / kDHd, d = e % kDHd;
+        // the clusters' weights per head, one warp per head: f[h][c] = exp(m_c - M), L = sum f l
+        float *fw = vals + G * kDHd;  // [G][n_cl], after the merged rows in the stage buffers
+        for (uint32_t h = warp; h < (uint32_t)G; h += kDW) {
             const uint64_t bh = base + (uint64_t)h * n_cl;
             float M = -INFINITY;
-            for (uint32_t c = 0; c < n_cl; c++) M = fmaxf(M, __ldcg(p.m_part + bh + c));
-            float o = 0.0f, L = 0.0f;
-            for (uint32_t c = 0; c < n_cl; c++) {
+            for (uint32_t c = lane; c < n_cl; c += 32) M = fmaxf(M, __ldcg(p.m_part + bh + c));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float L = 0.0f;
+            for (uint32_t c = lane; c < n_cl; c += 32) {
                 const float m = __ldcg(p.m_part + bh + c);
                 const float f = m == -INFINITY ? 0.0f : __expf(m - M);
-                o = fmaf(f, __ldcg(p.o_part + (bh + c) * kDHd + d), o);
+                fw[h * n_cl + c] = f;
                 L = fmaf(f, __ldcg(p.l_part + bh + c), L);
             }
-            vals[e] = o;
-            if (d == 0) fl[h] = L;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            if (lane == 0) fl[h] = L;
+        }
+        named_bar_sync(1, kDW * 32);
+        for (uint32_t e = tid; e < (uint32_t)G * kDHd; e += kDW * 32) {
+            const uint32_t h = e / kDHd, d = e % kDHd;
+            const float *op = p.o_part + (base + (uint64_t)h * n_cl) * kDHd + d;
+            const float *f = fw + h * n_cl;
+            float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;  // four chains: the loads overlap
+            uint32_t c = 0;
+            for (; c + 4 <= n_cl; c += 4) {
+                o0 = fmaf(f[c], __ldcg(op + (uint64_t)c * kDHd), o0);
+                o1 = fmaf(f[c + 1], __ldcg(op + (uint64_t)(c + 1) * kDHd), o1);
+                o2 = fmaf(f[c + 2], __ldcg(op + (uint64_t)(c + 2) * kDHd), o2);
+                o3 = fmaf(f[c + 3], __ldcg(op + (uint64_t)(c + 3) * kDHd), o3);
+            }
+            for (; c < n_cl; c++) o0 = fmaf(f[c], __ldcg(op + (uint64_t)c * kDHd), o0);
+            vals[e] = (o0 + o1) + (o2 + o3);
         }
         named_bar_sync(1, kDW * 32);
         if (tid == 0) *done = 0u;
@@ -673,7 +693,9 @@ __global__ void __launch_bounds__(kDThreads, 2) k_attn_dec_t4(const __grid_const
     extern __shared__ __align__(128) uint8_t dsm[];  // stages: [stage][K rows, V rows]
     __shared__ __align__(8) uint64_t full[kDMaxStages], empty[kDMaxStages];
     __shared__ RowMap maps[kDMaxStages];
-    __shared__ __align__(8) uint64_t newrow;  // (unused: turbo4 keeps the standalone post-processing)
+    __shared__ __align__(8) uint64_t newrow;  // the fused post-processing's new K / V rows are in the cache
+    __shared__ __align__(16) float nrx[2][kDHd];
+    __shared__ uint8_t nrq[2][kDHd];
     __shared__ __align__(16) float qf[G][kDHd];
     __shared__ __align__(16) int8_t qi[G][kDHd];
     __shared__ float qds[G][kDHd / 32];
@@ -702,7 +724,15 @@ __global__ void __launch_bounds__(kDThreads, 2) k_attn_dec_t4(const __grid_const
         if (lane == 0) dec_produce(p, dsm, full, empty, maps, &newrow, c0, c1, n_stage, start, pos_b, head_base);
         return;
     }
-    pdl_wait();  // q comes from the kernel before (turbo4 does not fuse the post-processing)
+    pdl_wait();  // q (and with the fused post-processing k / v) come from the kernel before
+    {
+        // fused post-processing: the CTA holding the newest position rotates and encodes its K / V
+        // rows first (its producer waits for them before the last stage), in the last two warps
+        const uint64_t fresh = pos_b - start;
+        if (p.post && warp >= kDW - 2 && fresh >= c0 && fresh < c1)
+            dec_new_row<RCU_KV_TURBO4>(p, (int)(kDW - 1 - warp), g, pos_b, nrx[kDW - 1 - warp], nrq[kDW - 1 - warp],
+                                       &newrow, lane);
+    }
     dec_query<RCU_KV_TURBO4, G>(p, qf, qi, qds, t, g, warp, lane);
     named_bar_sync(1, kDW * 32);
 
@@ -865,10 +895,10 @@ bool attention_dec_ok(int kv_type, uint64_t hd, uint64_t group) {
 // merged through global memory when a head has more than one cluster.
 template <typename Cap>
 static void dec_plan(uint64_t per_sm, uint64_t max_len, uint64_t n_tok, uint64_t n_kv, int num_sms, Cap cap,
-                     uint32_t *n_split, uint32_t *cs, uint32_t *rows) {
+                     uint64_t min_rows, uint32_t *n_split, uint32_t *cs, uint32_t *rows) {
     const uint64_t heads = std::max<uint64_t>(1, n_kv * n_tok);
     const uint64_t want = std::max<uint64_t>(1, per_sm * (uint64_t)num_sms / heads);
-    const uint64_t ns_max = std::max<uint64_t>(1, std::min<uint64_t>((max_len + 63) / 64, want));
+    const uint64_t ns_max = std::max<uint64_t>(1, std::min<uint64_t>((max_len + min_rows - 1) / min_rows, want));
     uint64_t best_ns = 1, best_c = 1;
     if (ns_max <= kDMaxCluster) {
         best_ns = best_c = ns_max;
@@ -890,6 +920,21 @@ static void dec_plan(uint64_t per_sm, uint64_t max_len, uint64_t n_tok, uint64_t
     *n_split = (uint32_t)best_ns;
     *cs = (uint32_t)best_c;
     *rows = (uint32_t)((max_len + best_ns - 1) / best_ns);
+}
+
+// Shortest split of the context (rows). The turbo4 kernel's fixed cost per CTA (query rotation
+// and quantization, cluster merge, output rotation) is large next to a 64-row split: with one KV
+// head at context 32768 (the 70B shape at 8 GPUs) 256-row splits measured 5.56 ms per token
+// against 6.61 ms for 64-row splits and 6.47 ms for 1024-row ones. The f16 / Q8_0 kernel keeps
+// 64 (config 3, context ~540, is fastest with eight 68-row splits per KV head).
+// RIE_ATTN_MIN_ROWS overrides both.
+static uint64_t dec_min_rows(bool turbo) {
+    static const long env = [] {
+        const char *e = getenv("RIE_ATTN_MIN_ROWS");
+        return e ? atol(e) : 0L;
+    }();
+    if (env >= 16) return (uint64_t)env;
+    return turbo ? 256 : 64;
 }
 
 // An upper bound of the clusters a decode launch merges through global memory (its splits).
@@ -961,7 +1006,8 @@ static int launch_dec(rcu_ctx *ctx, DecParams &p, DecKern &K, int per_sm, uint32
         }
         return K.cap[c];
     };
-    dec_plan((uint64_t)per_sm, max_len, n_tok, p.n_kv, ctx->num_sms, cap, &p.n_split, &p.cs, &p.rows_per_split);
+    dec_plan((uint64_t)per_sm, max_len, n_tok, p.n_kv, ctx->num_sms, cap, dec_min_rows(per_sm > 1), &p.n_split,
+             &p.cs, &p.rows_per_split);
     const uint64_t n_cl = p.n_split / p.cs, parts_n = n_tok * p.n_head * n_cl;
     p.o_part = parts;
     p.m_part = parts + parts_n * kDHd;

@@ -702,9 +702,13 @@ static int dispatch_group(rcu_ctx *ctx, const AttnParams &p, int group, dim3 gri
 // Not for turbo4 caches: the new row's encode (sequential sums, as the reference) would sit on
 // the path of the CTA holding the newest position (measured on the 70B shape: 59.7 vs 61.1
 // tok/s), while the standalone kernel encodes all heads' rows in parallel.
+// turbo4 caches fuse only with one or two KV heads: the CTA holding the newest position rotates
+// and encodes its K / V rows on two of its warps before their tiles, which lengthens the launch by
+// more than the standalone kernel costs when each CTA streams long splits (70B shape, 8 KV heads:
+// 59.7 fused vs 61.2 tok/s) and by less when the splits are short (1 KV head: 179.7 vs 155.9).
 bool attention_fuses_post(const rcu_kv *kv, uint64_t n_tok, uint64_t n_head) {
-    return n_tok == 1 && kv->n_kv > 0 && kv->type != RCU_KV_TURBO4 &&
-           attention_dec_ok(kv->type, kv->hd, n_head / kv->n_kv);
+    if (kv->type == RCU_KV_TURBO4 && kv->n_kv > 2) return false;
+    return n_tok == 1 && kv->n_kv > 0 && attention_dec_ok(kv->type, kv->hd, n_head / kv->n_kv);
 }
 
 int launch_attention(rcu_ctx *ctx, const rcu_kv *kv, const float *q, uint64_t n_tok, uint64_t n_head, uint64_t pos0,

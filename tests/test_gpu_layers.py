@@ -188,9 +188,9 @@ def test_layerwise_qwen3_moe_config4(env):
 @pytest.mark.parametrize("kv", [O.KV_F16, O.KV_Q8_0, O.KV_TURBO4], ids=["f16", "q8_0", "turbo4"])
 def test_layerwise_decode_attention_hd128(env, kv, group):
     """head_dim 128 with 4 or 8 query heads per KV head over every cache type: the decode steps
-    run the decode attention kernels, for f16 and Q8_0 caches with the q/k post-processing (q/k
-    norm, RoPE, KV append) folded into them; the prompt and turbo4 caches use the standalone
-    kernels. All held to the layer bounds above."""
+    run the decode attention kernels with the q/k post-processing (q/k norm, RoPE, KV append)
+    folded into them (turbo4 caches fold it at one or two KV heads, as here); the prompt uses the
+    standalone kernels. All held to the layer bounds above."""
     from rust_interference_engine_b200 import model as M
     spec = M.SyntheticSpec(arch="qwen3", wtype=GgmlType.Q4_K, embd_type=GgmlType.Q8_0, qk_norm=True, n_vocab=512,
                            n_embd=1024, n_layer=2, n_head=8, n_head_kv=8 // group, head_dim=128, n_ff=2048,
