@@ -99,6 +99,7 @@ int32_t rcu_ctx_create(int32_t device, void *stream, rcu_ctx **out, char *err, s
     }
     if (const char *v = std::getenv("RIE_GEMV_KQ")) c->gemv_kq = std::strcmp(v, "0") != 0;
     if (const char *v = std::getenv("RIE_GEMV_KQ_MIN_MB")) c->gemv_kq_min_bytes = std::strtoull(v, nullptr, 10) << 20;
+    if (const char *v = std::getenv("RIE_GEMV_KQ_Q4_0_MIN_K")) c->gemv_kq_q4_0_min_k = (uint32_t)std::strtoul(v, nullptr, 10);
     if (const char *v = std::getenv("RIE_FUSE_POST")) c->fuse_post = std::strcmp(v, "0") != 0;
     e = cudaMalloc(&c->dev_err, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(cuda_err(c, e, "cudaMalloc(err)"));

@@ -693,7 +693,7 @@ static bool kq_ok(const rcu_ctx *ctx, uint32_t k, uint32_t have, const HostJob *
     // Q4_0 rows shorter than 4096 values stay on the lane GEMV, which measured faster there
     // (config 1, 6144 x 2048: 3.5 vs 2.8 TB/s; 2 x 28672 x 8192: 2.7 vs 3.8 TB/s here)
     for (int i = 0; i < n_jobs; i++)
-        if (jobs[i].w->type == T_Q4_0 && k < 4096) return false;
+        if (jobs[i].w->type == T_Q4_0 && k < ctx->gemv_kq_q4_0_min_k) return false;
     uint64_t bytes = 0;
     uint32_t stage_bytes = 0;
     for (int i = 0; i < n_jobs; i++) {

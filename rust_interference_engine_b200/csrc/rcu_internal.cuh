@@ -206,6 +206,7 @@ struct rcu_ctx {
     bool gemm_i8 = false;          // prefill: int8 GEMM with exact block sums for Q4_0 weights
     bool gemv_kq = true;           // batch-1 K-quant GEMV on the tensor cores (RIE_GEMV_KQ=0: lane GEMV)
     uint64_t gemv_kq_min_bytes = 8ull << 20;  // ... for launches of at least this many weight bytes (RIE_GEMV_KQ_MIN_MB)
+    uint32_t gemv_kq_q4_0_min_k = 4096;       // ... and Q4_0 rows of at least this many values (RIE_GEMV_KQ_Q4_0_MIN_K)
     void *h_act = nullptr;         // f16 activations of the prefill GEMM (grown on demand)
     size_t h_act_cap = 0;
     void *k_part = nullptr;        // split-K partial tiles of the prefill GEMM (grown on demand)

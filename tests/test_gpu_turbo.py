@@ -160,6 +160,18 @@ def test_config5_turbo_attention_full_context(env, pos0, n_tok):
     close(got, want, 2e-3)
 
 
+@pytest.mark.parametrize("kv_type,tol", [(O.KV_TURBO4, 2e-3), (O.KV_F16, 1e-3), (O.KV_Q8_0, 1e-3)],
+                         ids=["turbo4", "f16", "q8_0"])
+@pytest.mark.parametrize("pos0", [32767, 23456])
+def test_one_kv_head_long_context(env, kv_type, tol, pos0):
+    """One KV head with 8 query heads over up to 32768 positions (the 70B shape's shard at 8
+    GPUs): the context is split over many clusters (turbo4: 256-row splits; f16 / Q8_0: 64-row
+    splits), so the last cluster merges 16 or more cluster partials through global memory, in
+    four chains plus a remainder."""
+    got, want = _attn_case(env, kv_type, 8, 1, 128, 32768, 1, pos0, seed=14)
+    close(got, want, tol)
+
+
 @pytest.mark.parametrize("kv_type,tol", [(O.KV_F16, 1e-3), (O.KV_Q8_0, 1e-3)], ids=["f16", "q8_0"])
 def test_config3_shape_attention_long_context(env, kv_type, tol):
     """Configuration 3 heads (32 query / 8 KV x 128) over 8192 positions."""
