@@ -8,7 +8,8 @@
 //
 // Roofline: one tcgen05 kind::i8 MMA (M 128, N 128, K 32) per block forms every S_b of a tile,
 // but each S_b then needs its own f32 scaling -- two FMAs per output per 32 values of K -- so
-// the kernel is bound by the FP32 pipe (128 FMA per clock per SM), not by the tensor pipe.
+// the FP32 work (128 FMA per clock per SM) bounds the kernel, not the tensor pipe. Measured, the
+// round trip of each block (MMA commit -> epilogue -> re-arm) is the larger cost.
 //
 // Per CTA: a 128-weight-row x 128-token output tile; the grid walks the row tiles of up to
 // four weights that share the activations (q/k/v, gate/up) in one launch.
@@ -18,11 +19,12 @@
 //   * warps 1-2 unpack: GGUF blocks -> int8 weight tile in the 128B-swizzled K-major layout
 //               the tensor core reads; the block scales d_w and the transposed d_a go to a
 //               4-slot scale ring that only the epilogue releases;
-//   * warp 3    MMA issuer: one tcgen05.mma.kind::i8 per block into one of four TMEM
-//               accumulators (128 columns each, the whole tensor memory), so the tensor core
-//               runs up to four blocks ahead of the epilogue;
-//   * warps 4-19 epilogue: warp w reads TMEM lanes 32*(w%4).. and one quarter of the tokens:
-//               tcgen05.ld of the block's 32 int32 sums, re-arm the accumulator with the f32
+//   * warp 3    MMA issuer: one tcgen05.mma.kind::i8 per block, two blocks per commit, into
+//               one of two TMEM accumulator pairs (2 x 128 columns each, the whole tensor
+//               memory), so the tensor core runs up to four blocks ahead of the epilogue;
+//   * warps 4-19 epilogue: warp w reads TMEM lanes 32*(w%4).. and one quarter of the tokens,
+//               for both blocks of a pair: tcgen05.ld of the block's 32 int32 sums, the FMAs
+//               below, then re-arm the accumulator with the f32
 //               magic 1.5*2^23 (the next block's int sum S then reads back as the float
 //               1.5*2^23 + S exactly), and two packed FMAs per pair of outputs:
 //               t = fma(X, d_w, -1.5*2^23*d_w) = round(S * d_w), acc = fma(t, d_a, acc).
