@@ -253,7 +253,8 @@ RCU_API int32_t rcu_backend_kv(rcu_backend *b, uint64_t layer, rcu_kv **out);
 RCU_API int32_t rcu_model_create_tp(rcu_ctx *ctx, const rcu_model_config *cfg, int32_t rank, int32_t world,
                                     rcu_model **out);
 /* Host-only: the shard rcu_model_set_tensor keeps for (rank, world); out == NULL reports the
- * shape only. */
+ * shape only. With fewer KV heads than ranks, k / v rows and biases are those of KV head
+ * rank / (world / n_head_kv): each KV head is replicated on world / n_head_kv ranks. */
 RCU_API int32_t rcu_tp_shard(const rcu_model_config *cfg, const char *name, uint32_t ggml_type, uint64_t rows,
                              uint64_t cols, const void *host_bytes, int32_t rank, int32_t world, void *out,
                              uint64_t out_cap, uint64_t *out_rows, uint64_t *out_cols);

@@ -1011,8 +1011,24 @@ static bool ends_with(const std::string &s, const char *suf) {
 // ---- tensor-parallel sharding (host side) ---------------------------------------------------
 // Column-parallel (rows split): q/k/v (by head), gate/up, the vocabulary rows of the output
 // head, q/k/v biases. Row-parallel (columns split, whole blocks): attn_output, ffn_down.
-// Everything else (embeddings, norms) is replicated.
-enum TpKind { TP_REPL = 0, TP_ROWS = 1, TP_COLS = 2, TP_QKV = 3, TP_UPGATE = 4, TP_EXPERTS = 5 };
+// Everything else (embeddings, norms) is replicated. With fewer KV heads than ranks each KV
+// head is replicated on world / n_head_kv consecutive ranks, whose query heads are all in its
+// group (Qwen3-30B-A3B: 4 KV heads at 8 GPUs).
+enum TpKind { TP_REPL = 0, TP_ROWS = 1, TP_COLS = 2, TP_QKV = 3, TP_UPGATE = 4, TP_EXPERTS = 5, TP_KV = 6 };
+
+// The KV heads [kv0, kv0 + nkv) that `rank` holds; false when the split is not even.
+static bool kv_slice(const rcu_model_config &c, int rank, int world, uint64_t *kv0, uint64_t *nkv) {
+    const uint64_t nk = c.n_head_kv, P = (uint64_t)world;
+    if (nk == 0 || c.n_head % P) return false;
+    if (nk % P == 0) {
+        *nkv = nk / P, *kv0 = (uint64_t)rank * (nk / P);
+        return true;
+    }
+    if (P % nk) return false;
+    *nkv = 1, *kv0 = (uint64_t)rank / (P / nk);
+    return true;
+}
+
 static int tp_kind(const std::string &n, const rcu_model_config &c, uint64_t rows) {
     if (n == "output.weight") return TP_ROWS;  // (not "blk.N.attn_output.weight")
     if (ends_with(n, ".attn_output.weight") || ends_with(n, ".ffn_down.weight")) return TP_COLS;
@@ -1023,8 +1039,9 @@ static int tp_kind(const std::string &n, const rcu_model_config &c, uint64_t row
         ends_with(n, ".ffn_down_exps.weight"))
         return TP_EXPERTS;
     if (ends_with(n, ".ffn_up.weight") && rows == 2ull * c.n_ff) return TP_UPGATE;
-    for (const char *suf : {".attn_q.weight", ".attn_k.weight", ".attn_v.weight", ".ffn_gate.weight", ".ffn_up.weight",
-                            ".attn_q.bias", ".attn_k.bias", ".attn_v.bias"})
+    for (const char *suf : {".attn_k.weight", ".attn_v.weight", ".attn_k.bias", ".attn_v.bias"})
+        if (ends_with(n, suf)) return TP_KV;
+    for (const char *suf : {".attn_q.weight", ".ffn_gate.weight", ".ffn_up.weight", ".attn_q.bias"})
         if (ends_with(n, suf)) return TP_ROWS;
     return TP_REPL;
 }
@@ -1035,7 +1052,7 @@ static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &
                     uint64_t cols, const uint8_t *host, int rank, int world, std::vector<uint8_t> *out, uint64_t *out_rows,
                     uint64_t *out_cols) {
     const int kind = world > 1 ? tp_kind(name, c, rows) : TP_REPL;
-    const bool vec1d = rows == 1 && (type == T_F32 || type == T_F16 || type == T_BF16) && kind == TP_ROWS;
+    const bool vec1d = rows == 1 && (type == T_F32 || type == T_F16 || type == T_BF16) && (kind == TP_ROWS || kind == TP_KV);
     const uint64_t rb = vec1d ? (type == T_F32 ? 4 : 2) * cols : rcu_row_bytes(type, cols);
     if (!vec1d && rb == 0) return set_err(ctx, RCU_ERR_INVALID, "tensor " + name + ": bad row length");
     auto bad = [&](const char *why) { return set_err(ctx, RCU_ERR_INVALID, "tensor parallel: " + name + " " + why); };
@@ -1064,6 +1081,22 @@ static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &
             copy_rows(rank * n, n, 0);
             return RCU_OK;
         }
+        case TP_KV: {  // k / v rows (or bias elements) of this rank's KV heads
+            uint64_t kv0 = 0, nkv = 0;
+            const uint64_t kvd = (uint64_t)c.n_head_kv * c.head_dim, len = vec1d ? cols : rows;
+            if (!kv_slice(c, rank, world, &kv0, &nkv) || len != kvd) return bad("KV heads do not split over the ranks");
+            const uint64_t r0 = kv0 * c.head_dim, n = nkv * c.head_dim;
+            if (vec1d) {
+                const uint64_t es = rb / cols;
+                *out_rows = 1, *out_cols = n;
+                if (out) out->assign(host + r0 * es, host + (r0 + n) * es);
+                return RCU_OK;
+            }
+            *out_rows = n, *out_cols = cols;
+            if (out) out->resize(n * rb);
+            copy_rows(r0, n, 0);
+            return RCU_OK;
+        }
         case TP_EXPERTS: {
             const uint64_t ne = c.n_expert;
             if (ne == 0 || rows % ne || ne % world) return bad("experts do not split evenly");
@@ -1075,13 +1108,15 @@ static int tp_shard(rcu_ctx *ctx, const rcu_model_config &c, const std::string &
         }
         case TP_QKV: {
             const uint64_t qd = (uint64_t)c.n_head * c.head_dim, kvd = (uint64_t)c.n_head_kv * c.head_dim;
-            if (rows != qd + 2 * kvd || qd % world || kvd % world) return bad("q/k/v rows do not split evenly");
-            const uint64_t nq = qd / world, nk = kvd / world;
+            uint64_t kv0 = 0, nkv = 0;
+            if (rows != qd + 2 * kvd || qd % world || !kv_slice(c, rank, world, &kv0, &nkv))
+                return bad("q/k/v rows do not split evenly");
+            const uint64_t nq = qd / world, nk = nkv * c.head_dim, k0 = kv0 * c.head_dim;
             *out_rows = nq + 2 * nk, *out_cols = cols;
             if (out) out->resize((nq + 2 * nk) * rb);
             copy_rows(rank * nq, nq, 0);
-            copy_rows(qd + rank * nk, nk, nq);
-            copy_rows(qd + kvd + rank * nk, nk, nq + nk);
+            copy_rows(qd + k0, nk, nq);
+            copy_rows(qd + kvd + k0, nk, nq + nk);
             return RCU_OK;
         }
         case TP_UPGATE: {
@@ -1271,12 +1306,20 @@ int32_t rcu_model_set_tensor_device(rcu_model *m, const char *name, uint32_t ggm
         case TP_REPL: e = rows_at(0, rows, 0); break;
         case TP_ROWS:
         case TP_EXPERTS: e = rows_at((uint64_t)rank * r2, r2, 0); break;
+        case TP_KV: {  // r2 rows of this rank's KV heads (tp_shard checked the split)
+            uint64_t kv0 = 0, nkv = 0;
+            kv_slice(c, rank, P, &kv0, &nkv);
+            e = rows_at(kv0 * c.head_dim, r2, 0);
+            break;
+        }
         case TP_QKV: {
             const uint64_t qd = (uint64_t)c.n_head * c.head_dim, kvd = (uint64_t)c.n_head_kv * c.head_dim;
-            const uint64_t nq = qd / P, nk = kvd / P;
+            uint64_t kv0 = 0, nkv = 0;
+            kv_slice(c, rank, P, &kv0, &nkv);
+            const uint64_t nq = qd / P, nk = nkv * c.head_dim, k0 = kv0 * c.head_dim;
             e = rows_at(rank * nq, nq, 0);
-            if (e == cudaSuccess) e = rows_at(qd + rank * nk, nk, nq);
-            if (e == cudaSuccess) e = rows_at(qd + kvd + rank * nk, nk, nq + nk);
+            if (e == cudaSuccess) e = rows_at(qd + k0, nk, nq);
+            if (e == cudaSuccess) e = rows_at(qd + kvd + k0, nk, nq + nk);
             break;
         }
         case TP_UPGATE: {
@@ -1379,14 +1422,17 @@ int32_t rcu_backend_create_tp(rcu_model *m, uint64_t n_ctx, uint64_t max_batch, 
     if (P > 1 && !uid) return set_err(ctx, RCU_ERR_INVALID, "tensor-parallel backend needs the communicator id");
     if (n_ctx == 0) return set_err(ctx, RCU_ERR_INVALID, "n_ctx must be positive");
     if (kv_type < RCU_KV_F16 || kv_type > RCU_KV_TURBO4) return set_err(ctx, RCU_ERR_INVALID, "unknown kv type");
-    if (m->cfg.n_head % P || m->cfg.n_head_kv % P || m->cfg.n_ff % P || m->cfg.n_vocab % P || m->cfg.n_expert % P)
+    uint64_t kv0 = 0, n_kv_loc = 0;
+    if (!kv_slice(m->cfg, m->tp_rank, P, &kv0, &n_kv_loc) || m->cfg.n_ff % P || m->cfg.n_vocab % P ||
+        m->cfg.n_expert % P)
         return set_err(ctx, RCU_ERR_INVALID,
-                       "heads, KV heads, FFN rows, vocabulary and experts must divide by the tensor-parallel degree");
+                       "heads, FFN rows, vocabulary and experts must divide by the tensor-parallel degree, and KV "
+                       "heads must divide by it or divide it");
     rcu_backend *b = new (std::nothrow) rcu_backend();
     if (!b) return RCU_ERR_OOM;
     b->cfg = m->cfg;
     b->cfg.n_head /= P;
-    b->cfg.n_head_kv /= P;
+    b->cfg.n_head_kv = (uint32_t)n_kv_loc;
     b->cfg.n_ff /= P;
     b->cfg.n_vocab /= P;
     if (m->cfg.n_expert > 0) {  // expert parallelism

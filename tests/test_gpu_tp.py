@@ -16,9 +16,12 @@ RTOL = 1e-2
 
 
 def _spec(arch="qwen3", wtype=GgmlType.Q4_K):
+    """arch "<name>_kv1": the same model with one KV head, replicated on both ranks."""
     from rust_interference_engine_b200 import model as M
+    kv1 = arch.endswith("_kv1")
+    arch = arch[:-4] if kv1 else arch
     s = M.SyntheticSpec.tiny(arch, wtype)
-    s.n_head, s.n_head_kv, s.head_dim, s.rope_dim = 8, 4, 64, 64
+    s.n_head, s.n_head_kv, s.head_dim, s.rope_dim = 8, 1 if kv1 else 4, 64, 64
     s.n_embd, s.n_ff = 512, 1024
     if arch == "qwen3":
         s.type_overrides = {"attn_v.weight": GgmlType.Q6_K, "ffn_down.weight": GgmlType.Q6_K}
@@ -76,12 +79,16 @@ def _rank(rank, world, q_uid, q_out, kv_type, fused, arch, wtype, device_load=Fa
                                                                  (0, False, "qwen3moe", GgmlType.Q4_K, False),
                                                                  (0, False, "qwen2moe", GgmlType.Q8_0, False),
                                                                  (0, False, "qwen3", GgmlType.Q4_K, True),
-                                                                 (0, False, "qwen3moe", GgmlType.Q4_K, True)],
-                         ids=["f16", "turbo4", "fused", "moe_ep", "moe_ep_shared", "device_load", "moe_device_load"])
+                                                                 (0, False, "qwen3moe", GgmlType.Q4_K, True),
+                                                                 (0, False, "qwen3_kv1", GgmlType.Q4_K, False),
+                                                                 (2, False, "qwen3_kv1", GgmlType.Q4_K, True)],
+                         ids=["f16", "turbo4", "fused", "moe_ep", "moe_ep_shared", "device_load", "moe_device_load",
+                              "kv_replicated", "kv_replicated_turbo4_device_load"])
 def test_tp2_forward_matches_oracle(kv_type, fused, arch, wtype, device_load):
     """fused: the all-reduce pushed over NVLink by the GEMVs instead of NCCL; moe: experts
     split across the two ranks (expert parallelism), the shared expert on rank 0; device_load:
-    every matrix handed over in device memory (rcu_model_set_tensor_device cuts the shards)."""
+    every matrix handed over in device memory (rcu_model_set_tensor_device cuts the shards);
+    kv_replicated: one KV head, held by both ranks, each with half of its query heads."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

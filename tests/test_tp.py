@@ -79,6 +79,54 @@ def test_shards_reassemble(arch, wtype, world):
             assert all(np.array_equal(p[0], full) for p in parts), name
 
 
+@pytest.mark.parametrize("arch,wtype", [("qwen2", GgmlType.Q8_0), ("phi3", GgmlType.Q8_0), ("qwen3moe", GgmlType.Q8_0)])
+def test_kv_heads_replicated_when_fewer_than_ranks(arch, wtype):
+    """2 KV heads over 4 ranks: ranks 0-1 keep KV head 0 and ranks 2-3 KV head 1 (k / v rows,
+    biases, the k / v part of a fused q/k/v tensor); query heads still split four ways, and they
+    are the heads of the rank's KV group (8 query heads, 4 per KV head, 2 per rank)."""
+    spec = tp_spec(arch, wtype)
+    spec.n_head_kv = 2
+    cfg = spec.config()
+    world, hd = 4, spec.head_dim
+    qd, kvd = spec.n_head * hd, spec.n_head_kv * hd
+    rep = world // spec.n_head_kv
+    seen = set()
+    for name, t, rows, cols, data in tensors(spec):
+        full = raw(data)
+        rb = full.size // rows
+        parts = [M.tp_shard(cfg, name, t, rows, cols, data, r, world) for r in range(world)]
+        kv = name.endswith((".attn_k.weight", ".attn_v.weight", ".attn_k.bias", ".attn_v.bias"))
+        if kv:
+            seen.add(name.split(".", 2)[2])
+            es = full.size // (cols if rows == 1 else rows)  # bytes per row (or per bias element)
+            for r, p in enumerate(parts):
+                h = r // rep
+                assert (p[2] if rows == 1 else p[1]) == hd, name
+                assert np.array_equal(p[0], full[h * hd * es:(h + 1) * hd * es]), (name, r)
+        elif name.endswith("attn_qkv.weight"):
+            seen.add("attn_qkv.weight")
+            nq = qd // world
+            for r, p in enumerate(parts):
+                h = r // rep
+                assert p[1] == nq + 2 * hd, name
+                assert np.array_equal(p[0][: nq * rb], full[r * nq * rb:(r + 1) * nq * rb]), name
+                assert np.array_equal(p[0][nq * rb:(nq + hd) * rb], full[(qd + h * hd) * rb:(qd + (h + 1) * hd) * rb]), name
+                k0 = qd + kvd + h * hd
+                assert np.array_equal(p[0][(nq + hd) * rb:], full[k0 * rb:(k0 + hd) * rb]), name
+        elif name.endswith(".attn_q.weight"):
+            assert all(p[1] == qd // world for p in parts), name
+    assert seen, "no k / v tensors in the spec"
+
+
+def test_kv_heads_that_do_not_split_are_an_error():
+    spec = tp_spec("qwen2", GgmlType.Q8_0)
+    spec.n_head, spec.n_head_kv = 12, 3  # 3 KV heads over 4 ranks: neither divides the other
+    cfg = spec.config()
+    w = O.Rng(2).weight(int(GgmlType.Q8_0), 3 * spec.head_dim, spec.n_embd)
+    with pytest.raises(RuntimeError):
+        M.tp_shard(cfg, "blk.0.attn_k.weight", GgmlType.Q8_0, 3 * spec.head_dim, spec.n_embd, w, 0, 4)
+
+
 @pytest.mark.parametrize("wtype", [GgmlType.Q4_0, GgmlType.Q4_K, GgmlType.Q6_K])
 def test_row_parallel_partials_add_up(wtype):
     """Splitting K at block boundaries keeps every activation block: the ranks' partial
