@@ -1093,7 +1093,7 @@ def cpu_prefill_sample(seconds: float, threads: int):
 
 
 # ---- workload: config 5 as a whole model: Llama-3.1-70B-shape decode, Q4_0, turbo4 KV ------
-# (BASELINE.json names hidden 8192, 80 layers, 64/8 heads x 128, context 32768, Q4_0 weight
+# (benchmark configuration 5 names hidden 8192, 80 layers, 64/8 heads x 128, context 32768, Q4_0 weight
 # GEMVs tensor-parallel over 8 GPUs; FFN 28672 and vocabulary 128256 are the public
 # Llama-3.1-70B values, RoPE base 500000, RMS eps 1e-5)
 LLAMA70B = dict(arch="llama", n_vocab=128256, n_embd=8192, n_layer=80, n_head=64, n_head_kv=8, head_dim=128,
