@@ -265,7 +265,7 @@ class CudaBackend:
     def forward(self, tokens, pos: int, all_logits: bool = False) -> np.ndarray:
         tok = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
         rows = tok.size if all_logits else 1
-        out = np.zeros((rows, self.n_vocab), dtype=np.float32)
+        out = np.empty((rows, self.n_vocab), dtype=np.float32)  # every value is written by the call
         _check(self.ctx.ptr, _lib.load().rcu_backend_forward(self.ptr, tok.ctypes.data_as(C.c_void_p), tok.size, pos,
                                                              int(all_logits), out.ctypes.data_as(C.c_void_p),
                                                              out.size))
