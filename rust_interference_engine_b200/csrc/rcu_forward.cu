@@ -65,6 +65,10 @@ struct rcu_backend {
     // (token, choice) pair in the expert-sorted order, source token of every slot, expert
     // offsets on the device and their host copy (pinned)
     uint32_t *moe_slot = nullptr, *moe_row = nullptr, *moe_off = nullptr, *moe_off_host = nullptr;
+    // pinned staging of rcu_backend_forward's host tokens (max_batch) and one row of logits, so
+    // that both copies run as DMA instead of through the driver's pageable staging
+    uint32_t *tok_pin = nullptr;
+    float *logits_pin = nullptr;
     uint32_t ep_e0 = 0, ep_n = 0xffffffffu;  // experts of this rank: [ep_e0, ep_e0 + ep_n)
     rcu_acts *acts2 = nullptr;
     bool ar_ok = false;
@@ -1667,6 +1671,8 @@ void rcu_backend_free(rcu_backend *b) {
     if (b->ev_out) cudaEventDestroy(b->ev_out);
     if (b->ev_plan) cudaEventDestroy(b->ev_plan);
     if (b->moe_off_host) cudaFreeHost(b->moe_off_host);
+    if (b->tok_pin) cudaFreeHost(b->tok_pin);
+    if (b->logits_pin) cudaFreeHost(b->logits_pin);
     if (b->stream) cudaStreamDestroy(b->stream);
     for (auto *kv : b->kv) rcu_kv_free(kv);
     rcu_acts_free(b->acts);
@@ -1756,9 +1762,23 @@ int32_t rcu_backend_forward(rcu_backend *b, const uint32_t *tokens, uint64_t n, 
     for (uint64_t i = 0; i < n; i++)
         if (tokens[i] >= b->embd->rows) return set_err(b->ctx, RCU_ERR_RUNTIME, "token id " + std::to_string(tokens[i]) + " out of range");
     rcu_ctx *ctx = b->ctx;
-    if (int32_t st = run_forward(b, tokens, true, n, pos, all_logits != 0, b->logits)) return st;
-    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(logits, b->logits, rows * b->m->cfg.n_vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
-    return rcu_sync(ctx);
+    const uint64_t nv = b->m->cfg.n_vocab;
+    if (!b->tok_pin) RCU_CUDA_TRY(ctx, cudaMallocHost(&b->tok_pin, b->max_batch * sizeof(uint32_t)));
+    if (rows == 1 && !b->logits_pin) RCU_CUDA_TRY(ctx, cudaMallocHost(&b->logits_pin, nv * sizeof(float)));
+    // the previous call synchronised before returning, so the staging buffers are free
+    std::memcpy(b->tok_pin, tokens, n * sizeof(uint32_t));
+    if (int32_t st = run_forward(b, b->tok_pin, true, n, pos, all_logits != 0, b->logits)) {
+        cudaStreamSynchronize(b->stream);  // a token copy already queued must finish before the next call refills tok_pin
+        return st;
+    }
+    if (rows > 1) {  // prompt logits of every token: straight into the caller's buffer
+        RCU_CUDA_TRY(ctx, cudaMemcpyAsync(logits, b->logits, rows * nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        return rcu_sync(ctx);
+    }
+    RCU_CUDA_TRY(ctx, cudaMemcpyAsync(b->logits_pin, b->logits, nv * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (int32_t st = rcu_sync(ctx)) return st;
+    std::memcpy(logits, b->logits_pin, nv * 4);
+    return RCU_OK;
 }
 
 int32_t rcu_backend_forward_device(rcu_backend *b, const uint32_t *tokens_dev, uint64_t n, uint64_t pos,
